@@ -1,0 +1,27 @@
+"""pytest configuration for the kvboost_b200 suite.
+
+Markers:
+  gpu   -- needs an sm_100a GPU and the built CUDA library; run with ``-m gpu``.
+  slow  -- long CPU tests (multi-process, larger oracle sizes).
+"""
+
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs an sm_100a GPU and the built kvboost_b200 CUDA library")
+    config.addinivalue_line("markers", "slow: long-running CPU test")
+
+
+@pytest.fixture(scope="session")
+def golden_dir():
+    return GOLDEN

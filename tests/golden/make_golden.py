@@ -1,0 +1,211 @@
+"""Generate golden vectors by running the KVBoost reference itself on the CPU.
+
+Run from the repository root in a checkout that has the reference source
+(``KVBOOST_REF_SRC`` points at its ``src`` directory)::
+
+    KVBOOST_REF_SRC=/root/reference/src python tests/golden/make_golden.py
+
+Writes ``tests/golden/*.npz`` / ``*.json``.  The fixtures are small (well
+under 2 MB together) and are what ``tests/test_oracle_golden.py`` pins the
+oracle against; the GPU parity tests then compare the CUDA path to the
+pinned oracle.  Nothing at test time or on a GPU host needs the reference.
+
+Reference entry points exercised (file:line in the KVBoost project):
+
+* ``_kvboost_flash_attn`` CPU path -> SDPA (``flash_attn_ext.py:68-103``),
+  called exactly as a reuse prefill reaches it: GQA expanded with
+  ``repeat_interleave`` and HF's bottom-right boolean mask.
+* ``quantize_kv`` / ``dequantize_kv`` int8 (``kv_quantize.py:73-109,194-222``).
+* ``BlockAllocator`` / ``ChunkBlockMapper`` / ``append_kv_to_blocks`` /
+  ``read_kv`` / ``paged_attention_fwd`` (``cpu_paged/``).
+* ``chained_hash`` / ``content_hash_from_tokens`` (``models.py:131-148``) and
+  ``ChunkRegistry`` fixed split (``chunk_registry.py:98-110``).
+"""
+
+from __future__ import annotations
+
+import json
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _ref():
+    src = os.environ.get("KVBOOST_REF_SRC")
+    if not src or not os.path.isdir(src):
+        raise SystemExit("set KVBOOST_REF_SRC to the reference's src/ directory")
+    sys.path.insert(0, src)
+    import kvboost.flash_attn_ext as fae            # noqa: E402
+    import kvboost.kv_quantize as kq                 # noqa: E402
+    import kvboost.models as models                  # noqa: E402
+    import kvboost.chunk_registry as cr              # noqa: E402
+    from kvboost.cpu_paged import block_allocator, chunk_to_blocks, paged_attn_cpu  # noqa: E402
+    return fae, kq, models, cr, block_allocator, chunk_to_blocks, paged_attn_cpu
+
+
+def _store(t: torch.Tensor) -> np.ndarray:
+    """float32 as is; 16-bit floats as their raw uint16 bit patterns (exact, half the size)."""
+    if t.dtype == torch.float32:
+        return t.numpy()
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def attention_cases(fae):
+    """Each case: inputs (float32 exact values), dtype, and the reference output."""
+    cases = [
+        # name, B, Hq, Hkv, Sq, Skv, D, dtype, causal
+        ("square_causal_f32", 1, 2, 2, 100, 100, 64, torch.float32, True),
+        ("square_noncausal_f32", 2, 2, 2, 16, 16, 64, torch.float32, False),
+        ("seq1_f32", 1, 4, 4, 1, 1, 64, torch.float32, True),
+        ("cross_noncausal_f32", 1, 4, 4, 8, 128, 64, torch.float32, False),
+        ("reuse_gqa4_f32", 1, 8, 2, 24, 88, 128, torch.float32, True),
+        ("reuse_gqa4_bf16", 1, 8, 2, 40, 168, 128, torch.bfloat16, True),
+        ("reuse_mha_d96_f16", 1, 2, 2, 33, 97, 96, torch.float16, True),
+        ("square_d64_bf16", 2, 4, 4, 64, 64, 64, torch.bfloat16, True),
+        ("suffix_longer_than_prefix_bf16", 1, 4, 1, 130, 200, 64, torch.bfloat16, True),
+    ]
+    out = {}
+    for i, (name, B, Hq, Hkv, Sq, Skv, D, dt, causal) in enumerate(cases):
+        g = torch.Generator().manual_seed(1000 + i)
+        q = torch.randn(B, Hq, Sq, D, generator=g).to(dt)
+        k = torch.randn(B, Hkv, Skv, D, generator=g).to(dt)
+        v = torch.randn(B, Hkv, Skv, D, generator=g).to(dt)
+        scale = 1.0 / math.sqrt(D)
+        rep = Hq // Hkv
+        ke = k.repeat_interleave(rep, dim=1)
+        ve = v.repeat_interleave(rep, dim=1)
+        if causal and Sq != Skv:
+            mask = torch.ones(Sq, Skv, dtype=torch.bool).tril(Skv - Sq)
+            o = fae._kvboost_flash_attn(q, ke, ve, scale, True, attn_mask=mask)
+        else:
+            o = fae._kvboost_flash_attn(q, ke, ve, scale, causal)
+        out[name + "/q"] = _store(q)
+        out[name + "/k"] = _store(k)
+        out[name + "/v"] = _store(v)
+        out[name + "/o"] = _store(o)
+        out[name + "/meta"] = np.array([B, Hq, Hkv, Sq, Skv, D, int(causal),
+                                        {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[dt]],
+                                       dtype=np.int64)
+    return out
+
+
+def quant_cases(kq):
+    out = {}
+    g = torch.Generator().manual_seed(7)
+    for i, (H, S, D) in enumerate([(2, 128, 64), (2, 128, 128), (1, 100, 96)]):
+        key = torch.randn(1, H, S, D, generator=g).to(torch.float16)
+        val = (torch.randn(1, H, S, D, generator=g) * 3).to(torch.float16)
+        if i == 1:
+            key[0, 0, 5] = 0  # an all-zero row exercises the clamp(min=1e-8)
+        qkv = kq.quantize_kv(((key, val),), bits=8)
+        layer = qkv.layers[0]
+        deq = kq.dequantize_kv(qkv)[0]
+        p = f"q{i}/"
+        out[p + "key"] = key.numpy()
+        out[p + "val"] = val.numpy()
+        out[p + "key_q"] = layer.key_q.numpy()
+        out[p + "key_scale"] = layer.key_scale.numpy()
+        out[p + "val_q"] = layer.val_q.numpy()
+        out[p + "val_scale"] = layer.val_scale.numpy()
+        out[p + "key_deq"] = deq[0].numpy()
+        out[p + "val_deq"] = deq[1].numpy()
+    return out
+
+
+def paged_cases(block_allocator, chunk_to_blocks, paged_attn_cpu, models):
+    """Scripted allocator/mapper history plus gathers and paged attention."""
+    BA = block_allocator.BlockAllocator
+    CBM = chunk_to_blocks.ChunkBlockMapper
+    tables = {}
+    a = BA(num_layers=1, num_heads=2, head_dim=8, num_blocks=40, block_size=16, dtype=torch.float32)
+    m = CBM(a)
+
+    def chunk(cid, length, seed):
+        g = torch.Generator().manual_seed(seed)
+        kv = ((torch.randn(1, 2, length, 8, generator=g), torch.randn(1, 2, length, 8, generator=g)),)
+        return models.CachedChunk(chunk_id=cid, text="", token_ids=list(range(length)),
+                                  past_key_values=kv, position_start=0, position_end=length,
+                                  prefix_hash=cid, content_hash=cid + "c")
+
+    c1, c2, c3 = chunk("c1", 128, 1), chunk("c2", 100, 2), chunk("c3", 40, 3)
+    tables["load_c1"] = m.load_chunk(c1)
+    tables["load_c2"] = m.load_chunk(c2)
+    tables["reload_c1"] = m.load_chunk(c1)
+    asm = models.AssembledPrompt(full_token_ids=[], cached_past_kv=None, cached_length=268,
+                                 live_token_ids=[], live_position_ids=[], chunk_boundaries=[],
+                                 cache_hit_ratio=0.0)
+    tbl, clen = m.build_block_table(asm, [c1, c2, c3])
+    tables["build_c1_c2_c3"] = tbl
+    tables["build_cached_len"] = clen
+    m.on_evict("c2")
+    tables["after_evict_alloc3"] = a.allocate(3)
+    shared = a.fork(tables["load_c1"][:2])
+    tables["cow_first"] = a.ensure_writable(shared[0])
+    new_tbl, new_off = paged_attn_cpu.append_kv_to_blocks(
+        a, 0, list(tables["load_c1"]), 128, torch.randn(2, 20, 8), torch.randn(2, 20, 8))
+    tables["append_20_after_128"] = new_tbl
+    tables["append_new_offset"] = new_off
+    tables["free_blocks_end"] = a.free_blocks
+    tables["free_list_end"] = list(a._free)
+
+    arrays = {}
+    # read_kv over a permuted table of a random pool
+    b2 = BA(num_layers=1, num_heads=3, head_dim=16, num_blocks=24, block_size=16, dtype=torch.float32)
+    g = torch.Generator().manual_seed(11)
+    b2.pools[0].copy_(torch.randn(b2.pools[0].shape, generator=g))
+    table = torch.randperm(24, generator=g)[:7].tolist()
+    k, v = b2.read_kv(0, table, 100)
+    arrays["read/pool"] = b2.pools[0].numpy()
+    arrays["read/table"] = np.array(table, dtype=np.int64)
+    arrays["read/k"] = k.numpy()
+    arrays["read/v"] = v.numpy()
+    # paged_attention_fwd: GQA 6 q heads over 3 kv heads, batch of 2 + an empty history
+    q = torch.randn(3, 6, 5, 16, generator=g)
+    out = paged_attn_cpu.paged_attention_fwd(q, b2, [table, table[:3], []], [100, 37, 0], 0,
+                                             causal=True)
+    arrays["pattn/q"] = q.numpy()
+    arrays["pattn/o"] = out.numpy()
+    arrays["pattn/seq_lens"] = np.array([100, 37, 0], dtype=np.int64)
+    arrays["pattn/table_b1_len"] = np.array([3], dtype=np.int64)
+    return tables, arrays
+
+
+def hash_cases(models, cr):
+    rng = np.random.default_rng(5)
+    out = {"content": [], "chained": [], "splits": []}
+    for n in (0, 1, 5, 128, 300):
+        ids = rng.integers(0, 151936, size=n).tolist()
+        out["content"].append({"ids": ids, "hash": models.content_hash_from_tokens(ids)})
+    parent = None
+    ids = rng.integers(0, 151936, size=4096).tolist()
+    reg = cr.ChunkRegistry(chunk_size=128)
+    for s, e, sl in reg.split(ids):
+        h = models.chained_hash(sl, parent)
+        out["chained"].append({"start": s, "end": e, "parent": parent, "hash": h})
+        parent = h
+    out["chained_ids"] = ids
+    for n in (31, 32, 100, 159, 160, 161, 300, 4096):
+        out["splits"].append({"n": n, "spans": [(s, e) for s, e, _ in reg.split(list(range(n)))]})
+    return out
+
+
+def main():
+    fae, kq, models, cr, ba, c2b, pac = _ref()
+    np.savez_compressed(os.path.join(HERE, "attention.npz"), **attention_cases(fae))
+    np.savez_compressed(os.path.join(HERE, "kv_quant.npz"), **quant_cases(kq))
+    tables, arrays = paged_cases(ba, c2b, pac, models)
+    np.savez_compressed(os.path.join(HERE, "paged.npz"), **arrays)
+    with open(os.path.join(HERE, "paged_tables.json"), "w") as f:
+        json.dump(tables, f, indent=1)
+    with open(os.path.join(HERE, "hashes.json"), "w") as f:
+        json.dump(hash_cases(models, cr), f)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

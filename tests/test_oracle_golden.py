@@ -1,0 +1,164 @@
+"""Pin the CPU oracle against golden vectors produced by the reference itself.
+
+The fixtures in ``tests/golden/`` were made by ``tests/golden/make_golden.py``
+running KVBoost's own code (SDPA dispatch, KIVI int8, the paged allocator,
+chunk hashing).  These tests need no GPU and no reference checkout.
+"""
+
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+from oracle import attention as oattn
+from oracle import hashing as ohash
+from oracle import kv_quant as oq
+from oracle import paged as opaged
+
+
+def _load(golden_dir, name):
+    return np.load(os.path.join(golden_dir, name))
+
+
+def _vals(arr, dtype_code):
+    """Stored 16-bit floats are raw bit patterns; return their exact float32 values."""
+    if dtype_code == 0:
+        return arr.astype(np.float32)
+    if dtype_code == 1:
+        return oq.bf16_bits_to_f32(arr)
+    return arr.view(np.float16).astype(np.float32)
+
+
+ATTN_CASES = [
+    "square_causal_f32", "square_noncausal_f32", "seq1_f32", "cross_noncausal_f32",
+    "reuse_gqa4_f32", "reuse_gqa4_bf16", "reuse_mha_d96_f16", "square_d64_bf16",
+    "suffix_longer_than_prefix_bf16",
+]
+
+
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_attention_oracle_matches_reference(golden_dir, case):
+    d = _load(golden_dir, "attention.npz")
+    B, Hq, Hkv, Sq, Skv, D, causal, dt = d[case + "/meta"].tolist()
+    q, k, v, o_ref = (_vals(d[f"{case}/{n}"], dt) for n in "qkvo")
+    o, lse = oattn.attention(q, k, v, 1.0 / math.sqrt(D), bool(causal))
+    # The reference output was rounded to the input dtype by SDPA; the oracle
+    # computes in float64.  fp32 agrees to 1e-5, 16-bit outputs to one ulp-ish.
+    tol = {0: 1e-5, 1: 2e-2, 2: 4e-3}[dt]
+    assert o.shape == o_ref.shape
+    assert np.max(np.abs(o - o_ref)) <= tol
+    assert np.all(np.isfinite(lse))
+
+
+def test_offset_mask_is_hf_tril():
+    m = oattn.visible_mask(3, 7, True)
+    expect = np.tril(np.ones((3, 7), dtype=bool), k=4)
+    assert np.array_equal(m, expect)
+    assert np.array_equal(oattn.visible_mask(5, 5, True), np.tril(np.ones((5, 5), dtype=bool)))
+
+
+def test_lse_matches_definition():
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((1, 2, 5, 16))
+    k = rng.standard_normal((1, 2, 9, 16))
+    v = rng.standard_normal((1, 2, 9, 16))
+    _, lse = oattn.attention(q, k, v, 0.25, True)
+    s = np.einsum("bhqd,bhkd->bhqk", q, k) * 0.25
+    s = np.where(oattn.visible_mask(5, 9, True), s, -np.inf)
+    ref = np.log(np.exp(s).sum(-1))
+    assert np.allclose(lse, ref, atol=1e-6)
+
+
+def test_empty_rows_give_zero_and_neg_inf():
+    q = np.ones((1, 1, 4, 8))
+    k = np.ones((1, 1, 2, 8))
+    v = np.ones((1, 1, 2, 8))
+    o, lse = oattn.attention(q, k, v, 1.0, True)  # q_len > kv_len: first 2 rows see nothing
+    assert np.all(o[0, 0, :2] == 0) and np.all(np.isneginf(lse[0, 0, :2]))
+    assert np.all(np.isfinite(lse[0, 0, 2:]))
+
+
+@pytest.mark.parametrize("i", [0, 1, 2])
+def test_int8_quant_bit_exact(golden_dir, i):
+    d = _load(golden_dir, "kv_quant.npz")
+    p = f"q{i}/"
+    key_q, key_scale, val_q, val_scale = oq.quantize_int8(d[p + "key"], d[p + "val"])
+    assert np.array_equal(key_q, d[p + "key_q"])
+    assert np.array_equal(key_scale.view(np.uint16), d[p + "key_scale"].view(np.uint16))
+    assert np.array_equal(val_q, d[p + "val_q"])
+    assert np.array_equal(val_scale.view(np.uint16), d[p + "val_scale"].view(np.uint16))
+    kd = oq.dequantize_int8(d[p + "key_q"], d[p + "key_scale"])
+    vd = oq.dequantize_int8(d[p + "val_q"], d[p + "val_scale"])
+    assert np.array_equal(kd.view(np.uint16), d[p + "key_deq"].view(np.uint16))
+    assert np.array_equal(vd.view(np.uint16), d[p + "val_deq"].view(np.uint16))
+
+
+def test_block_tables_bit_exact(golden_dir):
+    with open(os.path.join(golden_dir, "paged_tables.json")) as f:
+        t = json.load(f)
+    a = opaged.AllocatorModel(40)
+    m = opaged.MapperModel(a, 16)
+    assert m.load_chunk("c1", 128) == t["load_c1"]
+    assert m.load_chunk("c2", 100) == t["load_c2"]
+    assert m.load_chunk("c1", 128) == t["reload_c1"]
+    assert m.build_block_table([("c1", 128), ("c2", 100), ("c3", 40)]) == t["build_c1_c2_c3"]
+    m.on_evict("c2")
+    assert a.allocate(3) == t["after_evict_alloc3"]
+    shared = a.fork(t["load_c1"][:2])
+    assert a.ensure_writable(shared[0]) == t["cow_first"]
+    # append 20 tokens at slot 128 of c1's table: one new block, CoW on shared ids
+    table = list(t["load_c1"])
+    for slot in range(128, 148):
+        bi = slot // 16
+        if bi >= len(table):
+            table.extend(a.allocate(1))
+        table[bi] = a.ensure_writable(table[bi])
+    assert table == t["append_20_after_128"]
+    assert len(a.free_list) == t["free_blocks_end"]
+    assert a.free_list == t["free_list_end"]
+
+
+def test_read_kv_gather_exact(golden_dir):
+    d = _load(golden_dir, "paged.npz")
+    k, v = opaged.gather(d["read/pool"], d["read/table"].tolist(), 100)
+    assert np.array_equal(k, d["read/k"]) and np.array_equal(v, d["read/v"])
+
+
+def test_paged_attention_topleft(golden_dir):
+    d = _load(golden_dir, "paged.npz")
+    table = d["read/table"].tolist()
+    hist_k, hist_v = [], []
+    for tb, n in ((table, 100), (table[:3], 37), ([], 0)):
+        if n:
+            k, v = opaged.gather(d["read/pool"], tb, n)
+        else:
+            k = v = np.zeros((3, 0, 16), np.float32)
+        hist_k.append(k)
+        hist_v.append(v)
+    o = oattn.paged_attention_topleft(d["pattn/q"], hist_k, hist_v, causal=True)
+    assert np.max(np.abs(o - d["pattn/o"])) < 1e-5
+
+
+def test_hashes_and_split_bit_exact(golden_dir):
+    with open(os.path.join(golden_dir, "hashes.json")) as f:
+        h = json.load(f)
+    for c in h["content"]:
+        assert ohash.content_hash(c["ids"]) == c["hash"]
+    ids = h["chained_ids"]
+    parent = None
+    spans = ohash.fixed_split(ids)
+    assert len(spans) == len(h["chained"])
+    for (s, e, sl), c in zip(spans, h["chained"]):
+        assert (s, e) == (c["start"], c["end"]) and c["parent"] == parent
+        parent = ohash.chained_hash(sl, parent)
+        assert parent == c["hash"]
+    for sp in h["splits"]:
+        assert [(s, e) for s, e, _ in ohash.fixed_split(list(range(sp["n"])))] == [tuple(x) for x in sp["spans"]]
+
+
+def test_flop_count_config2():
+    # 4 * 128 * 32 * 4 * (256*896 + 256*257/2) = 17.19 GFLOP
+    f = oattn.attention_flops([256] * 4, [1152] * 4, 32, 128)
+    assert f == 4 * 128 * 32 * 4 * (256 * 896 + 256 * 257 // 2)
