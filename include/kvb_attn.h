@@ -1,0 +1,145 @@
+/*
+ * kvb_attn.h -- C ABI of the kvboost_b200 prefill-attention library
+ * (libkvb_attn: kvboost_b200/_kvb_attn.so), B200 / sm_100a only.
+ *
+ * Plain pointers, sizes and a CUDA stream handle (cudaStream_t passed as
+ * void*); no framework types.  Every entry point validates its arguments on
+ * the host before launching anything and returns
+ *
+ *     KVB_OK (0)            launched (asynchronous: nothing is synchronised)
+ *     KVB_ERR_INVALID (1)   bad argument; nothing launched
+ *     KVB_ERR_UNSUPPORTED(2) well-formed but outside what the kernels support
+ *     KVB_ERR_CUDA (-1)     the CUDA runtime refused the launch
+ *
+ * with a human-readable reason available from kvb_last_error() (per host
+ * thread).  Device-side waits are bounded: a kernel that gives up on a wait
+ * ORs a non-zero code into the optional caller-owned `status` word
+ * (KVB_STATUS_*) and exits cleanly instead of hanging.
+ *
+ * Attention semantics (all entry points): O = softmax(Q K^T * scale) V per
+ * query head, query head h reading KV head h / (num_q_heads / num_kv_heads)
+ * (GQA grouping as KVBoost's repeat_interleave, cpu_paged/paged_attn_cpu.py:87-88).
+ * causal = 1 (KVB_CAUSAL_BOTTOM_RIGHT): key j is visible to query i iff
+ * j <= i + (kv_len - q_len), i.e. HuggingFace's reuse-prefill mask; for
+ * q_len == kv_len it equals the reference kernel's mask
+ * (csrc/flash_attn_kernel.cu:148,193).  causal = 2 (KVB_CAUSAL_TOP_LEFT):
+ * j <= i, torch SDPA's is_causal, which the reference's paged path applies
+ * (cpu_paged/paged_attn_cpu.py:103).  causal = 0: no mask.  LSE is log(sum_j exp(scale*q.k_j))
+ * in natural log (flash_attn_kernel.cu:236-245); rows with no visible key
+ * get O = 0 and LSE = -inf.
+ */
+#ifndef KVB_ATTN_H_
+#define KVB_ATTN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVB_ABI_VERSION 1
+
+enum {
+  KVB_DTYPE_BF16 = 0,
+  KVB_DTYPE_FP16 = 1
+};
+
+enum {
+  KVB_CAUSAL_NONE = 0,
+  KVB_CAUSAL_BOTTOM_RIGHT = 1,
+  KVB_CAUSAL_TOP_LEFT = 2
+};
+
+enum {
+  KVB_OK = 0,
+  KVB_ERR_INVALID = 1,
+  KVB_ERR_UNSUPPORTED = 2,
+  KVB_ERR_CUDA = -1
+};
+
+/* Bits a kernel ORs into `status` when a bounded wait gives up. */
+enum {
+  KVB_STATUS_LOAD_WAIT = 1,    /* producer waited too long for a free stage   */
+  KVB_STATUS_MMA_WAIT = 2,     /* MMA issuer waited too long for operands     */
+  KVB_STATUS_SOFTMAX_WAIT = 4, /* softmax warps waited too long for scores    */
+  KVB_STATUS_EPILOGUE_WAIT = 8 /* epilogue waited too long for the output     */
+};
+
+/*
+ * kvb_flash_attn_fwd -- drop-in for the reference extension's
+ * flash_attn_fwd_dispatch(Q, K, V, O, L, scale, causal)
+ * (src/kvboost/csrc/flash_attn.h:5-12, flash_attn_kernel.cu:250-294) together
+ * with its argument checks (flash_attn.cpp:16-54), behind the Python op
+ * kvboost._flash_attn_cuda.flash_attn_fwd (flash_attn.cpp:85-102).
+ *
+ * q, k, v, o : contiguous [batch, heads, seqlen, head_dim], dtype KVB_DTYPE_*
+ * lse        : contiguous float32 [batch, heads, seqlen] (may be NULL)
+ * head_dim   : 64, 96 or 128.  Same q and kv length, same head count (as the
+ *              reference requires).  Launched on `stream` (the reference used
+ *              the legacy default stream).
+ */
+int kvb_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                       int batch, int heads, int seqlen, int head_dim, int dtype,
+                       float softmax_scale, int causal, void* stream);
+
+/*
+ * Extended prefill: GQA, q_len != kv_len (reuse prefill over a cached
+ * prefix), arbitrary row/head/batch strides, and packed variable-length
+ * batches.  Replaces the SDPA call that KVBoost's reuse prefill reaches
+ * through HF's attention registry (flash_attn_ext.py:86-103 and
+ * transformers integrations/sdpa_attention.py).
+ *
+ * Dense mode (cu_seqlens_q == NULL): q/o are [batch, q_len] rows per head,
+ * k/v [batch, kv_len]; element (b, h, i, d) of q sits at
+ *   q + b*q_batch_stride + h*q_head_stride + i*q_row_stride + d.
+ * lse (optional) element (b, h, i) at lse + b*lse_batch_stride + h*lse_head_stride + i.
+ *
+ * Varlen mode (cu_seqlens_q and cu_seqlens_k set, device int32 [batch+1]):
+ * q/o are packed [total_q, heads, head_dim] (batch stride ignored), k/v
+ * [total_k, kv_heads, head_dim]; sequence b owns rows cu[b]..cu[b+1]-1;
+ * q_len / kv_len carry the maxima over sequences; lse element (h, row) at
+ * lse + h*lse_head_stride + row.
+ *
+ * Requirements: innermost stride 1; row/head/batch strides multiples of 8
+ * elements; base pointers 16-byte aligned.
+ */
+typedef struct KvbPrefillParams {
+  int32_t dtype;
+  int32_t head_dim;
+  int32_t batch;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t q_len;
+  int32_t kv_len;
+  int32_t causal;
+  float softmax_scale;
+  int32_t total_q; /* varlen only: rows of q/o */
+  int32_t total_k; /* varlen only: rows of k/v */
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;
+  int64_t q_batch_stride, q_head_stride, q_row_stride;
+  int64_t k_batch_stride, k_head_stride, k_row_stride;
+  int64_t v_batch_stride, v_head_stride, v_row_stride;
+  int64_t o_batch_stride, o_head_stride, o_row_stride;
+  int64_t lse_batch_stride, lse_head_stride;
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_seqlens_k;
+  int32_t* status;
+} KvbPrefillParams;
+
+int kvb_prefill_fwd(const KvbPrefillParams* params, void* stream);
+
+/* Human-readable reason for the last non-zero return on this host thread. */
+const char* kvb_last_error(void);
+
+/* KVB_ABI_VERSION of the loaded library. */
+int kvb_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVB_ATTN_H_ */

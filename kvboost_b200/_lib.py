@@ -1,0 +1,100 @@
+"""ctypes binding of the C ABI in ``include/kvb_attn.h``.
+
+The library is loaded from the package directory (built in-tree by
+``kvboost_b200._build``).  There is no fallback: if the library is missing
+or fails to load, every op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import threading
+
+from . import _build
+
+KVB_DTYPE_BF16 = 0
+KVB_DTYPE_FP16 = 1
+KVB_OK = 0
+KVB_ERR_INVALID = 1
+KVB_ERR_UNSUPPORTED = 2
+KVB_ERR_CUDA = -1
+
+_i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+
+
+class KvbPrefillParams(ctypes.Structure):
+    """Mirror of ``KvbPrefillParams`` (field order and types must match the header)."""
+
+    _fields_ = [
+        ("dtype", _i32), ("head_dim", _i32), ("batch", _i32),
+        ("num_q_heads", _i32), ("num_kv_heads", _i32),
+        ("q_len", _i32), ("kv_len", _i32), ("causal", _i32),
+        ("softmax_scale", _f32), ("total_q", _i32), ("total_k", _i32),
+        ("q", _vp), ("k", _vp), ("v", _vp), ("o", _vp), ("lse", _vp),
+        ("q_batch_stride", _i64), ("q_head_stride", _i64), ("q_row_stride", _i64),
+        ("k_batch_stride", _i64), ("k_head_stride", _i64), ("k_row_stride", _i64),
+        ("v_batch_stride", _i64), ("v_head_stride", _i64), ("v_row_stride", _i64),
+        ("o_batch_stride", _i64), ("o_head_stride", _i64), ("o_row_stride", _i64),
+        ("lse_batch_stride", _i64), ("lse_head_stride", _i64),
+        ("cu_seqlens_q", _vp), ("cu_seqlens_k", _vp), ("status", _vp),
+    ]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def lib_path() -> str:
+    return _build.LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the CUDA library; raises if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = lib_path()
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"kvboost_b200 CUDA library not found at {path}; build it with "
+                "`python -m kvboost_b200._build` (nvcc, sm_100a)")
+        lib = ctypes.CDLL(path)
+        lib.kvb_prefill_fwd.argtypes = [ctypes.POINTER(KvbPrefillParams), _vp]
+        lib.kvb_prefill_fwd.restype = ctypes.c_int
+        lib.kvb_flash_attn_fwd.argtypes = [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int,
+                                           ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32,
+                                           ctypes.c_int, _vp]
+        lib.kvb_flash_attn_fwd.restype = ctypes.c_int
+        lib.kvb_last_error.argtypes = []
+        lib.kvb_last_error.restype = ctypes.c_char_p
+        lib.kvb_abi_version.argtypes = []
+        lib.kvb_abi_version.restype = ctypes.c_int
+        _lib = lib
+        return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != KVB_OK:
+        msg = load().kvb_last_error().decode("utf-8", "replace")
+        kind = {KVB_ERR_INVALID: "invalid argument", KVB_ERR_UNSUPPORTED: "unsupported",
+                KVB_ERR_CUDA: "CUDA error"}.get(rc, f"error {rc}")
+        raise RuntimeError(f"{what}: {kind}: {msg}")
+
+
+def header_symbols(header_dir: str = None):
+    """Function names declared in ``include/*.h`` (used to check the exports)."""
+    header_dir = header_dir or _build.INCLUDE
+    names = []
+    for fn in sorted(os.listdir(header_dir)):
+        if not fn.endswith(".h"):
+            continue
+        text = open(os.path.join(header_dir, fn)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(kvb_\w+)\s*\(", text, re.M):
+            names.append(m.group(1))
+    return sorted(set(names))

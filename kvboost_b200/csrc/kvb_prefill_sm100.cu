@@ -1,0 +1,677 @@
+// Offset-causal prefill attention for B200 (sm_100a).
+//
+// One CTA computes one 128-row query tile of one query head against the
+// visible part of its KV head:
+//
+//   warps 0-3  softmax / correction / epilogue.  Thread t owns query row t,
+//              which is TMEM lane t, so scores and the output row are read
+//              and written with 32x32b tcgen05.ld/st and no shuffles.
+//   warp 4     TMA producer: Q once, then K_j / V_j tiles (128 x D, 128-byte
+//              swizzle) into an NS-deep shared-memory ring.
+//   warp 5     MMA issuer (one thread) and TMEM owner:
+//                S_j  = Q K_j^T        tcgen05.mma SS, fp32 accumulator in TMEM
+//                O   += P_j V_j        tcgen05.mma TS, P read from TMEM
+//
+// TMEM (256 columns): S at [0,128); P is written back over S as packed
+// 16-bit pairs in [0,64); O at [128, 128+DP).  256 columns and <=97 KB of
+// shared memory let two CTAs share an SM, so one CTA's MMAs overlap the
+// other's softmax.
+//
+// Online softmax runs in the log2 domain on scaled scores.  The running row
+// maximum is only raised when it grows by more than 8 (a factor of 256), so
+// most tiles skip the O rescale; the final normalisation uses the same
+// maximum, so this is exact up to rounding.
+//
+// Causality is bottom-right (key j visible to query i iff
+// j <= i + kv_len - q_len) or, on request, top-left (j <= i); key tiles entirely above the diagonal are never
+// loaded, and only the tiles crossing the diagonal or the end of the keys
+// are masked element by element.
+//
+// Every mbarrier wait is bounded (KVB_WAIT_NS); a wait that gives up sets a
+// CTA-wide abort flag and ORs a code into the caller's status word, after
+// which every role drains its in-flight copies / MMAs and the CTA frees its
+// TMEM and exits.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include <cmath>
+#include <mutex>
+#include <string>
+
+#include "kvb_attn.h"
+#include "kvb_sm100_ptx.cuh"
+
+#ifndef KVB_WAIT_NS
+#define KVB_WAIT_NS 2000000000ull  // 2 s: far above any legitimate wait
+#endif
+
+namespace kvb {
+
+constexpr int BM = 128;  // query rows per CTA (= TMEM lanes)
+constexpr int BN = 128;  // keys per tile
+constexpr int kThreads = 192;
+constexpr int kSoftmaxThreads = 128;
+
+template <int D>
+struct Geo {
+  static constexpr int DP = (D + 63) / 64 * 64;  // head_dim padded to whole 64-element atoms
+  static constexpr int NATOM = DP / 64;          // 128-byte swizzle atoms per row
+  static constexpr int ATOM_BYTES = 128 * 128;   // 128 rows x 128 bytes
+  static constexpr int TILE_BYTES = NATOM * ATOM_BYTES;
+  static constexpr int NS = (D <= 64) ? 2 : 1;   // K/V ring depth
+  static constexpr int TMEM_COLS = 256;
+  static constexpr int S_COL = 0;
+  static constexpr int O_COL = 128;
+  static constexpr int QK_STEPS = D / 16;        // K-steps of S = Q K^T
+  static constexpr int PV_STEPS = BN / 16;       // K-steps of O += P V
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = 1024 + TILE_BYTES * (1 + 2 * NS) + BAR_BYTES;
+};
+
+// Barrier slots
+enum {
+  BAR_Q_FULL = 0,
+  BAR_S_FULL = 1,
+  BAR_P_FULL = 2,
+  BAR_O_FULL = 3,
+  BAR_DRAIN = 4,
+  BAR_K_FULL = 5,   // + stage
+  BAR_K_EMPTY = 7,  // + stage
+  BAR_V_FULL = 9,   // + stage
+  BAR_V_EMPTY = 11, // + stage
+  BAR_COUNT = 13
+};
+
+struct DenseArgs {
+  void* o;
+  float* lse;
+  int64_t o_bs, o_hs, o_rs;
+  int64_t lse_bs, lse_hs;
+  const int* cu_q;
+  const int* cu_k;
+  int q_len, kv_len;
+  int group;  // num_q_heads / num_kv_heads
+  int causal;
+  float scale_log2;
+  int* status;
+};
+
+struct SharedCtl {
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// Bounded wait: spins on try_wait, then checks the CTA abort flag and the
+// global timer.  Returns false if the CTA is aborting or the limit passed.
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                         int* status, int code) {
+#pragma unroll 1
+  for (int i = 0; i < 128; ++i)
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = ptx::globaltimer_ns();
+#pragma unroll 1
+  while (true) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (ptx::globaltimer_ns() - t0 > KVB_WAIT_NS) {
+      *abort_flag = 1;
+      if (status) atomicOr(status, code);
+      return false;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T>
+__host__ __device__ constexpr int ab_format() {
+  return std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 2)
+    kvb_prefill_dense_kernel(const __grid_constant__ CUtensorMap tm_q,
+                             const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v, const DenseArgs a) {
+  using G = Geo<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + G::TILE_BYTES;
+  uint8_t* sV = sK + G::NS * G::TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + G::NS * G::TILE_BYTES);
+  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(bars + 16);
+  volatile int* abort_flag = &ctl->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---- work item --------------------------------------------------------
+  const int tile_m = gridDim.x - 1 - blockIdx.x;  // heaviest (last) tiles first
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int kvh = h / a.group;
+  int q_len = a.q_len, kv_len = a.kv_len, q_base = 0, k_base = 0, tb = b;
+  if (a.cu_q != nullptr) {
+    q_base = a.cu_q[b];
+    q_len = a.cu_q[b + 1] - q_base;
+    k_base = a.cu_k[b];
+    kv_len = a.cu_k[b + 1] - k_base;
+    tb = 0;
+  }
+  const int q0 = tile_m * BM;
+  if (q0 >= q_len) return;  // uniform across the CTA, before any barrier use
+  const int q_rows = min(BM, q_len - q0);
+  // causal 1: bottom-right (j <= i + kv_len - q_len); 2: top-left (j <= i)
+  const int off = (a.causal == 2) ? 0 : kv_len - q_len;
+  int kv_end = a.causal ? min(kv_len, q0 + q_rows + off) : kv_len;
+  kv_end = max(kv_end, 0);
+  const int n_tiles = (kv_end + BN - 1) / BN;
+
+  auto bar = [&](int i) { return ptx::smem_u32(&bars[i]); };
+
+  // ---- setup --------------------------------------------------------------
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(bar(BAR_Q_FULL), 1);
+    ptx::mbar_init(bar(BAR_S_FULL), 1);
+    ptx::mbar_init(bar(BAR_P_FULL), kSoftmaxThreads);
+    ptx::mbar_init(bar(BAR_O_FULL), 1);
+    ptx::mbar_init(bar(BAR_DRAIN), 1);
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(bar(BAR_K_FULL + s), 1);
+      ptx::mbar_init(bar(BAR_K_EMPTY + s), 1);
+      ptx::mbar_init(bar(BAR_V_FULL + s), 1);
+      ptx::mbar_init(bar(BAR_V_EMPTY + s), 1);
+    }
+    ctl->abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    ptx::prefetch_tmap(&tm_q);
+    ptx::prefetch_tmap(&tm_k);
+    ptx::prefetch_tmap(&tm_v);
+  }
+  if (warp == 5) {
+    ptx::tmem_alloc(ptx::smem_u32(&ctl->tmem_base), G::TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 4) {
+    // ================================================================ TMA
+    if (lane == 0 && n_tiles > 0) {
+      const int qy = q_base + q0;
+      ptx::mbar_arrive_expect_tx(bar(BAR_Q_FULL), G::TILE_BYTES);
+#pragma unroll
+      for (int at = 0; at < G::NATOM; ++at)
+        ptx::tma_load_4d(ptx::smem_u32(sQ + at * G::ATOM_BYTES), &tm_q, at * 64, qy, h, tb,
+                         bar(BAR_Q_FULL));
+      int issued = 0;
+#pragma unroll 1
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j % G::NS;
+        const uint32_t ph = (j / G::NS) & 1;
+        const int ky = k_base + j * BN;
+        if (!wait_bar(bar(BAR_K_EMPTY + s), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
+          break;
+        ptx::mbar_arrive_expect_tx(bar(BAR_K_FULL + s), G::TILE_BYTES);
+#pragma unroll
+        for (int at = 0; at < G::NATOM; ++at)
+          ptx::tma_load_4d(ptx::smem_u32(sK + s * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_k,
+                           at * 64, ky, kvh, tb, bar(BAR_K_FULL + s));
+        if (!wait_bar(bar(BAR_V_EMPTY + s), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
+          break;
+        ptx::mbar_arrive_expect_tx(bar(BAR_V_FULL + s), G::TILE_BYTES);
+#pragma unroll
+        for (int at = 0; at < G::NATOM; ++at)
+          ptx::tma_load_4d(ptx::smem_u32(sV + s * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_v,
+                           at * 64, ky, kvh, tb, bar(BAR_V_FULL + s));
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        // Drain: wait (bounded) for the loads of the last ring round to land.
+        for (int j = max(0, issued - G::NS); j < issued; ++j) {
+          const int s = j % G::NS;
+          const uint32_t ph = (j / G::NS) & 1;
+          wait_bar(bar(BAR_K_FULL + s), ph, abort_flag, nullptr, 0);
+          wait_bar(bar(BAR_V_FULL + s), ph, abort_flag, nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ================================================================ MMA
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idesc_s = ptx::idesc_f16(BM, BN, ab_format<T>(), 0, 0);
+      constexpr uint32_t idesc_o = ptx::idesc_f16(BM, G::DP, ab_format<T>(), 0, 1);
+      const uint32_t tS = tmem + G::S_COL;
+      const uint32_t tO = tmem + G::O_COL;
+      const uint32_t sQa = ptx::smem_u32(sQ);
+      const uint32_t sKa = ptx::smem_u32(sK);
+      const uint32_t sVa = ptx::smem_u32(sV);
+      bool ok = wait_bar(bar(BAR_Q_FULL), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
+
+      auto issue_s = [&](int j) {
+        const int s = j % G::NS;
+        const uint32_t kb = sKa + s * G::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < G::QK_STEPS; ++kk) {
+          const uint32_t off_b = (kk >> 2) * G::ATOM_BYTES + (kk & 3) * 32;
+          const uint64_t da = ptx::smem_desc_sw128(sQa + off_b, 16, 1024);
+          const uint64_t db = ptx::smem_desc_sw128(kb + off_b, 16, 1024);
+          ptx::mma_ss(tS, da, db, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(bar(BAR_K_EMPTY + s));
+        ptx::mma_commit(bar(BAR_S_FULL));
+      };
+
+      if (ok) ok = wait_bar(bar(BAR_K_FULL + 0), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
+      if (ok) {
+        ptx::tc_fence_after();
+        issue_s(0);
+      }
+#pragma unroll 1
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int s = j % G::NS;
+        const uint32_t ph = (j / G::NS) & 1;
+        if (!wait_bar(bar(BAR_P_FULL), j & 1, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) break;
+        if (!wait_bar(bar(BAR_V_FULL + s), ph, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) break;
+        ptx::tc_fence_after();
+        const uint32_t vb = sVa + s * G::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < G::PV_STEPS; ++kk) {
+          const uint64_t dv = ptx::smem_desc_sw128(vb + kk * 16 * 128, G::ATOM_BYTES, 1024);
+          ptx::mma_ts(tO, tS + kk * 8, dv, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        ptx::mma_commit(bar(BAR_V_EMPTY + s));
+        if (j + 1 < n_tiles) {
+          const int s1 = (j + 1) % G::NS;
+          const uint32_t ph1 = ((j + 1) / G::NS) & 1;
+          if (!wait_bar(bar(BAR_K_FULL + s1), ph1, abort_flag, a.status, KVB_STATUS_MMA_WAIT))
+            break;
+          ptx::tc_fence_after();
+          issue_s(j + 1);
+        }
+      }
+      ptx::mma_commit(bar(BAR_O_FULL));
+      // Drain: all MMAs issued above complete before TMEM can be freed.
+      ptx::mma_commit(bar(BAR_DRAIN));
+      wait_bar(bar(BAR_DRAIN), 0, abort_flag, nullptr, 0);
+    }
+  } else {
+    // ============================================================ softmax
+    const int t = threadIdx.x;  // row within the tile == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tS = tmem + lane_base + G::S_COL;
+    const uint32_t tO = tmem + lane_base + G::O_COL;
+    const int qi = q0 + t;
+    const float sl2 = a.scale_log2;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+
+#pragma unroll 1
+    for (int j = 0; j < n_tiles; ++j) {
+      ok = wait_bar(bar(BAR_S_FULL), j & 1, abort_flag, a.status, KVB_STATUS_SOFTMAX_WAIT);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      ptx::tc_fence_after();
+
+      // Pass 1: row maximum over the tile, 32 columns at a time (keeps the
+      // live register set small enough for two CTAs per SM).
+      const int kv0 = j * BN;
+      const bool need_mask = (kv0 + BN > kv_len) || (a.causal && kv0 + BN - 1 > q0 + off);
+      const int lim = (a.causal ? min(kv_len - 1, qi + off) : kv_len - 1) - kv0;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        ptx::tmem_ld32(tS + c, r);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float v = (need_mask && c + i > lim) ? -INFINITY : __uint_as_float(r[i]);
+          mx = fmaxf(mx, v);
+        }
+      }
+      const float m_tile = mx * sl2;
+      float alpha = 1.f;
+      const bool raise = m_tile > m_run + 8.0f;
+      if (raise) {
+        alpha = ptx::ex2(m_run - m_tile);
+        m_run = m_tile;
+      }
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+
+      // O rescale (after PV_{j-1}, which completed before S_j was committed)
+      const bool rescale = raise && j > 0;
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float f = rescale ? alpha : 1.f;
+#pragma unroll
+        for (int c = 0; c < G::DP; c += 32) {
+          uint32_t r[32];
+          ptx::tmem_ld32(tO + c, r);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+          ptx::tmem_st32(tO + c, r);
+        }
+      }
+
+      // Pass 2: P = exp2(s * scale*log2e - m), packed to 16-bit pairs and
+      // written back over the already-consumed S columns: S columns
+      // [c, c+32) become P columns [c/2, c/2+16).
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        ptx::tmem_ld32(tS + c, r);
+        ptx::tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const bool m0 = need_mask && c + 2 * i > lim;
+          const bool m1 = need_mask && c + 2 * i + 1 > lim;
+          const float p0 = m0 ? 0.f : ptx::ex2(fmaf(__uint_as_float(r[2 * i]), sl2, -m_use));
+          const float p1 = m1 ? 0.f : ptx::ex2(fmaf(__uint_as_float(r[2 * i + 1]), sl2, -m_use));
+          sum += p0 + p1;
+          pk[i] = pack2<T>(p0, p1);
+        }
+        ptx::tmem_st16(tS + c / 2, pk);
+      }
+      l_run = l_run * alpha + sum;
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(BAR_P_FULL));
+    }
+
+    // ---- epilogue --------------------------------------------------------
+    bool have_o = n_tiles > 0 && ok;
+    if (have_o) {
+      have_o = wait_bar(bar(BAR_O_FULL), 0, abort_flag, a.status, KVB_STATUS_EPILOGUE_WAIT);
+      have_o = __all_sync(0xffffffffu, have_o);
+      ptx::tc_fence_after();
+    }
+    const bool row_valid = t < q_rows;
+    const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+    T* orow = reinterpret_cast<T*>(a.o) +
+              (a.cu_q ? (int64_t)(q_base + qi) * a.o_rs + (int64_t)h * a.o_hs
+                      : (int64_t)b * a.o_bs + (int64_t)h * a.o_hs + (int64_t)qi * a.o_rs);
+#pragma unroll
+    for (int c = 0; c < D; c += 32) {
+      uint32_t r[32];
+      if (n_tiles > 0) {
+        ptx::tmem_ld32(tO + c, r);
+        ptx::tmem_wait_ld();
+      }
+      if (row_valid) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float o0 = have_o ? __uint_as_float(r[2 * i]) * inv_l : 0.f;
+          const float o1 = have_o ? __uint_as_float(r[2 * i + 1]) * inv_l : 0.f;
+          pk[i] = pack2<T>(o0, o1);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      }
+    }
+    if (row_valid && a.lse != nullptr) {
+      const float lse = (l_run > 0.f && have_o) ? (m_run + ptx::lg2(l_run)) * 0.69314718055994531f
+                                                : -INFINITY;
+      if (a.cu_q)
+        a.lse[(int64_t)h * a.lse_hs + q_base + qi] = lse;
+      else
+        a.lse[(int64_t)b * a.lse_bs + (int64_t)h * a.lse_hs + qi] = lse;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, G::TMEM_COLS);
+  }
+}
+
+// ============================================================================
+// Host side
+// ============================================================================
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 4-D map over (head_dim, rows, heads, batch) with a 64 x 128 x 1 x 1 box and
+// 128-byte swizzle.  Strides are in elements.
+static bool make_map(CUtensorMap* m, const void* base, int dtype, int head_dim, int64_t rows,
+                     int64_t heads, int64_t batch, int64_t row_stride, int64_t head_stride,
+                     int64_t batch_stride, std::string* err) {
+  auto enc = tensor_map_encoder();
+  if (!enc) {
+    *err = "cuTensorMapEncodeTiled unavailable from the CUDA driver";
+    return false;
+  }
+  cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)rows, (cuuint64_t)heads,
+                        (cuuint64_t)batch};
+  cuuint64_t strides[3] = {(cuuint64_t)row_stride * 2, (cuuint64_t)head_stride * 2,
+                           (cuuint64_t)batch_stride * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)BM, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m,
+                   dtype == KVB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r);
+    return false;
+  }
+  return true;
+}
+
+template <typename T, int D>
+static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
+  using G = Geo<D>;
+  const bool varlen = p.cu_seqlens_q != nullptr;
+  CUtensorMap tq, tk, tv;
+  std::string err;
+  const int64_t qrows = varlen ? p.total_q : p.q_len;
+  const int64_t krows = varlen ? p.total_k : p.kv_len;
+  const int64_t nb = varlen ? 1 : p.batch;
+  // batch stride of a 1-batch varlen map only has to be a valid multiple of 16 bytes
+  const int64_t qbs = varlen ? 8 : p.q_batch_stride;
+  const int64_t kbs = varlen ? 8 : p.k_batch_stride;
+  const int64_t vbs = varlen ? 8 : p.v_batch_stride;
+  if (!make_map(&tq, p.q, p.dtype, D, qrows, p.num_q_heads, nb, p.q_row_stride, p.q_head_stride,
+                qbs, &err) ||
+      !make_map(&tk, p.k, p.dtype, D, krows, p.num_kv_heads, nb, p.k_row_stride, p.k_head_stride,
+                kbs, &err) ||
+      !make_map(&tv, p.v, p.dtype, D, krows, p.num_kv_heads, nb, p.v_row_stride, p.v_head_stride,
+                vbs, &err))
+    return fail(KVB_ERR_INVALID, err);
+
+  DenseArgs a;
+  a.o = p.o;
+  a.lse = p.lse;
+  a.o_bs = p.o_batch_stride;
+  a.o_hs = p.o_head_stride;
+  a.o_rs = p.o_row_stride;
+  a.lse_bs = p.lse_batch_stride;
+  a.lse_hs = p.lse_head_stride;
+  a.cu_q = p.cu_seqlens_q;
+  a.cu_k = p.cu_seqlens_k;
+  a.q_len = p.q_len;
+  a.kv_len = p.kv_len;
+  a.group = p.num_q_heads / p.num_kv_heads;
+  a.causal = p.causal;
+  a.scale_log2 = p.softmax_scale * 1.4426950408889634f;
+  a.status = p.status;
+
+  auto kern = kvb_prefill_dense_kernel<T, D>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         G::SMEM_BYTES);
+    if (e != cudaSuccess)
+      return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    configured_device = dev;
+  }
+  dim3 grid((p.q_len + BM - 1) / BM, p.num_q_heads, p.batch);
+  kern<<<grid, kThreads, G::SMEM_BYTES, stream>>>(tq, tk, tv, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return fail(KVB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  return KVB_OK;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int validate(const KvbPrefillParams& p) {
+  if (p.dtype != KVB_DTYPE_BF16 && p.dtype != KVB_DTYPE_FP16)
+    return fail(KVB_ERR_INVALID, "dtype must be KVB_DTYPE_BF16 or KVB_DTYPE_FP16");
+  if (p.head_dim != 64 && p.head_dim != 96 && p.head_dim != 128)
+    return fail(KVB_ERR_INVALID,
+                "head_dim must be one of 64, 96, 128, got " + std::to_string(p.head_dim));
+  if (p.batch < 1 || p.num_q_heads < 1 || p.num_kv_heads < 1)
+    return fail(KVB_ERR_INVALID, "batch and head counts must be positive");
+  if (p.num_q_heads % p.num_kv_heads)
+    return fail(KVB_ERR_INVALID, "num_q_heads (" + std::to_string(p.num_q_heads) +
+                                     ") must be divisible by num_kv_heads (" +
+                                     std::to_string(p.num_kv_heads) + ")");
+  if (p.batch > 65535 || p.num_q_heads > 65535)
+    return fail(KVB_ERR_UNSUPPORTED, "batch and num_q_heads must be <= 65535");
+  if (p.causal < 0 || p.causal > 2)
+    return fail(KVB_ERR_INVALID, "causal must be 0 (none), 1 (bottom-right) or 2 (top-left)");
+  if (p.q_len < 0 || p.kv_len < 0)
+    return fail(KVB_ERR_INVALID, "sequence lengths must be non-negative");
+  if (!p.q || !p.k || !p.v || !p.o)
+    return fail(KVB_ERR_INVALID, "q, k, v and o must be non-null");
+  if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v) || !aligned16(p.o))
+    return fail(KVB_ERR_INVALID, "q, k, v and o must be 16-byte aligned");
+  const bool varlen = p.cu_seqlens_q != nullptr;
+  if (varlen != (p.cu_seqlens_k != nullptr))
+    return fail(KVB_ERR_INVALID, "cu_seqlens_q and cu_seqlens_k must both be set or both NULL");
+  if (varlen && (p.total_q < 0 || p.total_k < 0))
+    return fail(KVB_ERR_INVALID, "total_q/total_k must be non-negative in varlen mode");
+  const int64_t st[] = {p.q_head_stride, p.q_row_stride, p.k_head_stride, p.k_row_stride,
+                        p.v_head_stride, p.v_row_stride, p.o_head_stride, p.o_row_stride};
+  for (int64_t s : st)
+    if (s <= 0 || (s % 8) != 0)
+      return fail(KVB_ERR_INVALID, "row and head strides must be positive multiples of 8 elements");
+  if (!varlen) {
+    const int64_t bst[] = {p.q_batch_stride, p.k_batch_stride, p.v_batch_stride, p.o_batch_stride};
+    for (int64_t s : bst)
+      if ((p.batch > 1 && s <= 0) || (s % 8) != 0)
+        return fail(KVB_ERR_INVALID, "batch strides must be positive multiples of 8 elements");
+  }
+  return KVB_OK;
+}
+
+}  // namespace kvb
+
+// ============================================================================
+// C ABI
+// ============================================================================
+using namespace kvb;
+
+extern "C" int kvb_prefill_fwd(const KvbPrefillParams* params, void* stream) {
+  if (!params) return fail(KVB_ERR_INVALID, "params is NULL");
+  const KvbPrefillParams& p = *params;
+  int rc = validate(p);
+  if (rc != KVB_OK) return rc;
+  if (p.q_len == 0) return KVB_OK;
+  const bool varlen = p.cu_seqlens_q != nullptr;
+  if (varlen && (p.total_q == 0)) return KVB_OK;
+  // The TMA maps need at least one row; an empty key side is handled by the
+  // kernel (no tiles) but the map must still be encodable.
+  KvbPrefillParams q = p;
+  if (!varlen && q.kv_len == 0) {
+    q.k = p.q; q.v = p.q;
+    q.k_head_stride = p.q_head_stride; q.k_row_stride = p.q_row_stride;
+    q.k_batch_stride = p.q_batch_stride;
+    q.v_head_stride = p.q_head_stride; q.v_row_stride = p.q_row_stride;
+    q.v_batch_stride = p.q_batch_stride;
+  }
+  if (varlen && q.total_k == 0) q.total_k = 1;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool bf = p.dtype == KVB_DTYPE_BF16;
+  switch (p.head_dim) {
+    case 64: return bf ? launch_dense<__nv_bfloat16, 64>(q, s) : launch_dense<__half, 64>(q, s);
+    case 96: return bf ? launch_dense<__nv_bfloat16, 96>(q, s) : launch_dense<__half, 96>(q, s);
+    default: return bf ? launch_dense<__nv_bfloat16, 128>(q, s) : launch_dense<__half, 128>(q, s);
+  }
+}
+
+extern "C" int kvb_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                                  int batch, int heads, int seqlen, int head_dim, int dtype,
+                                  float softmax_scale, int causal, void* stream) {
+  KvbPrefillParams p = {};
+  p.dtype = dtype;
+  p.head_dim = head_dim;
+  p.batch = batch;
+  p.num_q_heads = heads;
+  p.num_kv_heads = heads;
+  p.q_len = seqlen;
+  p.kv_len = seqlen;
+  p.causal = causal;
+  p.softmax_scale = softmax_scale;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.o = o;
+  p.lse = lse;
+  const int64_t rs = head_dim, hs = (int64_t)seqlen * head_dim, bs = (int64_t)heads * hs;
+  p.q_row_stride = p.k_row_stride = p.v_row_stride = p.o_row_stride = rs;
+  p.q_head_stride = p.k_head_stride = p.v_head_stride = p.o_head_stride = hs > 0 ? hs : rs;
+  p.q_batch_stride = p.k_batch_stride = p.v_batch_stride = p.o_batch_stride = bs > 0 ? bs : rs;
+  p.lse_head_stride = seqlen;
+  p.lse_batch_stride = (int64_t)heads * seqlen;
+  return kvb_prefill_fwd(&p, stream);
+}
+
+extern "C" const char* kvb_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int kvb_abi_version(void) { return KVB_ABI_VERSION; }

@@ -35,11 +35,14 @@ def _as_f(x, dtype):
     return x.astype(dtype, copy=False)
 
 
-def visible_mask(q_len: int, kv_len: int, causal: bool) -> np.ndarray:
-    """Boolean ``[q_len, kv_len]`` mask; True = key visible (bottom-right causal)."""
+def visible_mask(q_len: int, kv_len: int, causal: bool, top_left: bool = False) -> np.ndarray:
+    """Boolean ``[q_len, kv_len]`` mask; True = key visible.
+
+    Bottom-right causal by default; ``top_left=True`` is SDPA's ``is_causal``.
+    """
     if not causal:
         return np.ones((q_len, kv_len), dtype=bool)
-    off = kv_len - q_len
+    off = 0 if top_left else kv_len - q_len
     qi = np.arange(q_len)[:, None]
     kj = np.arange(kv_len)[None, :]
     return kj <= qi + off
@@ -60,7 +63,8 @@ def _attend_head(q, k, v, scale, mask):
 
 
 def attention(q, k, v, scale: Optional[float] = None, causal: bool = True,
-              compute_dtype=np.float64, q_chunk: int = 1024) -> Tuple[np.ndarray, np.ndarray]:
+              compute_dtype=np.float64, q_chunk: int = 1024,
+              top_left: bool = False) -> Tuple[np.ndarray, np.ndarray]:
     """Dense attention oracle.
 
     q: [B, Hq, Sq, D]; k, v: [B, Hkv, Skv, D] (any float dtype, values taken
@@ -76,7 +80,7 @@ def attention(q, k, v, scale: Optional[float] = None, causal: bool = True,
     g = Hq // Hkv
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    mask = visible_mask(Sq, Skv, causal)
+    mask = visible_mask(Sq, Skv, causal, top_left)
     o = np.zeros((B, Hq, Sq, D), dtype=np.float32)
     lse = np.full((B, Hq, Sq), -np.inf, dtype=np.float32)
     for b in range(B):

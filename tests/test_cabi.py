@@ -1,0 +1,85 @@
+"""The C-ABI library loads and exports every symbol ``include/*.h`` declares.
+
+CPU only: nothing here launches a kernel.  Argument validation happens on
+the host before any CUDA call, so invalid calls can be checked without a GPU.
+"""
+
+import ctypes
+import os
+import subprocess
+
+import pytest
+
+from kvboost_b200 import _build, _lib
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(_build.LIB_PATH):
+        _build.build(verbose=False)
+    return _lib.load()
+
+
+def test_header_declares_expected_entry_points():
+    names = _lib.header_symbols()
+    for n in ("kvb_flash_attn_fwd", "kvb_prefill_fwd", "kvb_last_error", "kvb_abi_version"):
+        assert n in names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", _build.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    for name in _lib.header_symbols():
+        assert name in exported, f"{name} declared in include/ but not exported"
+        assert hasattr(lib, name)
+
+
+def test_abi_version(lib):
+    assert lib.kvb_abi_version() == 1
+
+
+def test_ctypes_struct_matches_header_size():
+    # 11 x int32/float = 44 -> padded to 48, 5 pointers, 14 int64, 3 pointers
+    assert ctypes.sizeof(_lib.KvbPrefillParams) == 48 + 5 * 8 + 14 * 8 + 3 * 8
+
+
+def _params(**kw):
+    p = _lib.KvbPrefillParams()
+    p.dtype, p.head_dim, p.batch, p.num_q_heads, p.num_kv_heads = 0, 128, 1, 4, 2
+    p.q_len, p.kv_len, p.causal, p.softmax_scale = 16, 32, 1, 0.088
+    p.q = p.k = p.v = p.o = 4096
+    for s in ("q", "k", "v", "o"):
+        setattr(p, f"{s}_row_stride", 128)
+        setattr(p, f"{s}_head_stride", 128 * 64)
+        setattr(p, f"{s}_batch_stride", 128 * 64 * 8)
+    for k_, v_ in kw.items():
+        setattr(p, k_, v_)
+    return p
+
+
+@pytest.mark.parametrize("field,value,needle", [
+    ("head_dim", 80, "head_dim"),
+    ("dtype", 7, "dtype"),
+    ("num_kv_heads", 3, "divisible"),
+    ("causal", 5, "causal"),
+    ("q_len", -1, "non-negative"),
+    ("q", 0, "non-null"),
+    ("k", 4097, "aligned"),
+    ("q_row_stride", 100, "multiples of 8"),
+])
+def test_host_validation_rejects_before_launch(lib, field, value, needle):
+    p = _params(**{field: value})
+    rc = lib.kvb_prefill_fwd(ctypes.byref(p), None)
+    assert rc == _lib.KVB_ERR_INVALID
+    assert needle in lib.kvb_last_error().decode()
+
+
+def test_null_params_rejected(lib):
+    assert lib.kvb_prefill_fwd(None, None) == _lib.KVB_ERR_INVALID
+
+
+def test_compat_entry_validates_head_dim(lib):
+    rc = lib.kvb_flash_attn_fwd(4096, 4096, 4096, 4096, None, 1, 2, 8, 48, 0, 0.1, 1, None)
+    assert rc == _lib.KVB_ERR_INVALID
+    assert b"head_dim" in lib.kvb_last_error()
