@@ -39,6 +39,7 @@
 #include <cudaTypedefs.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <cmath>
 #include <mutex>
 #include <string>
@@ -144,6 +145,115 @@ __host__ __device__ constexpr int ab_format() {
   return std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
 }
 
+// Packed fp32 pair helpers (sm_100 f32x2 ALU forms).
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ float f2lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Convert a pair of probabilities to the MMA operand type, low half = first.
+template <typename T>
+__device__ __forceinline__ uint32_t cvt_pair(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t cvt_pair<__nv_bfloat16>(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+template <>
+__device__ __forceinline__ uint32_t cvt_pair<__half>(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// Row maximum of the raw scores of one 128-column S tile held in TMEM.
+template <bool MASK>
+__device__ __forceinline__ float tile_row_max(uint32_t tS, int lim) {
+  float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    ptx::tmem_ld32(tS + c, r);
+    ptx::tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      float x[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        x[e] = (MASK && c + i + e > lim) ? -INFINITY : __uint_as_float(r[i + e]);
+      m0 = fmax3(m0, x[0], x[1]);
+      m1 = fmax3(m1, x[2], x[3]);
+      m2 = fmax3(m2, x[4], x[5]);
+      m3 = fmax3(m3, x[6], x[7]);
+    }
+  }
+  return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+}
+
+// P = exp2(s * sl2 - m) for one S tile: written back into TMEM over the
+// consumed S columns as 16-bit pairs (S columns [c, c+32) -> P columns
+// [c/2, c/2+16)).  Returns the row sum of P (fp32, before rounding) and the
+// raw row maximum seen (for the stale-maximum check).  The 32-column chunk
+// loop is kept rolled so the live set stays near 100 registers (two CTAs
+// per SM).
+template <typename T, bool MASK>
+__device__ __forceinline__ float tile_exp_store(uint32_t tS, float sl2, float m_use, int lim,
+                                                float* raw_max) {
+  const uint64_t sc2 = f2pack(sl2, sl2);
+  const uint64_t nm2 = f2pack(-m_use, -m_use);
+  uint64_t acc0 = 0, acc1 = 0;  // two packed partial sums
+  float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    ptx::tmem_ld32(tS + c, r);
+    ptx::tmem_wait_ld();
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float x0 = __uint_as_float(r[2 * i]);
+      float x1 = __uint_as_float(r[2 * i + 1]);
+      if (MASK) {
+        if (c + 2 * i > lim) x0 = -INFINITY;
+        if (c + 2 * i + 1 > lim) x1 = -INFINITY;
+      }
+      if (i & 1)
+        m1 = fmax3(m1, x0, x1);
+      else
+        m0 = fmax3(m0, x0, x1);
+      const uint64_t a = ffma2(f2pack(x0, x1), sc2, nm2);
+      const float p0 = ptx::ex2(f2lo(a));
+      const float p1 = ptx::ex2(f2hi(a));
+      if (i & 1)
+        acc1 = fadd2(acc1, f2pack(p0, p1));
+      else
+        acc0 = fadd2(acc0, f2pack(p0, p1));
+      pk[i] = cvt_pair<T>(p0, p1);
+    }
+    ptx::tmem_st16(tS + c / 2, pk);
+  }
+  *raw_max = fmaxf(m0, m1);
+  const uint64_t t = fadd2(acc0, acc1);
+  return f2lo(t) + f2hi(t);
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 2)
     kvb_prefill_dense_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -191,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (threadIdx.x == 0) {
     ptx::mbar_init(bar(BAR_Q_FULL), 1);
     ptx::mbar_init(bar(BAR_S_FULL), 1);
-    ptx::mbar_init(bar(BAR_P_FULL), kSoftmaxThreads);
+    ptx::mbar_init(bar(BAR_P_FULL), kSoftmaxThreads / 32);
     ptx::mbar_init(bar(BAR_O_FULL), 1);
     ptx::mbar_init(bar(BAR_DRAIN), 1);
     for (int s = 0; s < 2; ++s) {
@@ -336,36 +446,37 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!ok) break;
       ptx::tc_fence_after();
 
-      // Pass 1: row maximum over the tile, 32 columns at a time (keeps the
-      // live register set small enough for two CTAs per SM).
       const int kv0 = j * BN;
       const bool need_mask = (kv0 + BN > kv_len) || (a.causal && kv0 + BN - 1 > q0 + off);
       const int lim = (a.causal ? min(kv_len - 1, qi + off) : kv_len - 1) - kv0;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        ptx::tmem_ld32(tS + c, r);
-        ptx::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float v = (need_mask && c + i > lim) ? -INFINITY : __uint_as_float(r[i]);
-          mx = fmaxf(mx, v);
-        }
-      }
-      const float m_tile = mx * sl2;
-      float alpha = 1.f;
-      const bool raise = m_tile > m_run + 8.0f;
-      if (raise) {
-        alpha = ptx::ex2(m_run - m_tile);
-        m_run = m_tile;
-      }
-      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
 
+      // Stale-maximum softmax: exponentiate against the running maximum in
+      // one pass; only when some row's tile maximum exceeds it by more than
+      // 8 (log2 units) is the maximum raised, O rescaled and the tile redone.
+      // A row with no maximum yet (first tile) takes the two-pass path.
+      float alpha = 1.f;
+      float sum = 0.f;
+      float raw_mx;
+      bool raise = false;
+      const bool two_pass = __any_sync(0xffffffffu, m_run == -INFINITY);
+      if (two_pass) {
+        raw_mx = need_mask ? tile_row_max<true>(tS, lim) : tile_row_max<false>(tS, lim);
+        raise = raw_mx * sl2 > m_run + 8.0f || (m_run == -INFINITY && raw_mx > -INFINITY);
+      } else {
+        const float m_use = m_run;
+        sum = need_mask ? tile_exp_store<T, true>(tS, sl2, m_use, lim, &raw_mx)
+                        : tile_exp_store<T, false>(tS, sl2, m_use, lim, &raw_mx);
+        raise = raw_mx * sl2 > m_run + 8.0f;
+      }
+      const bool redo = two_pass || __any_sync(0xffffffffu, raise);
+      if (raise) {
+        const float m_new = raw_mx * sl2;
+        alpha = ptx::ex2(m_run - m_new);
+        m_run = m_new;
+      }
       // O rescale (after PV_{j-1}, which completed before S_j was committed)
-      const bool rescale = raise && j > 0;
-      if (__any_sync(0xffffffffu, rescale)) {
-        const float f = rescale ? alpha : 1.f;
+      if (j > 0 && __any_sync(0xffffffffu, raise)) {
+        const float f = raise ? alpha : 1.f;
 #pragma unroll
         for (int c = 0; c < G::DP; c += 32) {
           uint32_t r[32];
@@ -376,32 +487,17 @@ __global__ void __launch_bounds__(kThreads, 2)
           ptx::tmem_st32(tO + c, r);
         }
       }
-
-      // Pass 2: P = exp2(s * scale*log2e - m), packed to 16-bit pairs and
-      // written back over the already-consumed S columns: S columns
-      // [c, c+32) become P columns [c/2, c/2+16).
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        ptx::tmem_ld32(tS + c, r);
-        ptx::tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const bool m0 = need_mask && c + 2 * i > lim;
-          const bool m1 = need_mask && c + 2 * i + 1 > lim;
-          const float p0 = m0 ? 0.f : ptx::ex2(fmaf(__uint_as_float(r[2 * i]), sl2, -m_use));
-          const float p1 = m1 ? 0.f : ptx::ex2(fmaf(__uint_as_float(r[2 * i + 1]), sl2, -m_use));
-          sum += p0 + p1;
-          pk[i] = pack2<T>(p0, p1);
-        }
-        ptx::tmem_st16(tS + c / 2, pk);
+      if (redo) {
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        float dummy;
+        sum = need_mask ? tile_exp_store<T, true>(tS, sl2, m_use, lim, &dummy)
+                        : tile_exp_store<T, false>(tS, sl2, m_use, lim, &dummy);
       }
       l_run = l_run * alpha + sum;
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
-      ptx::mbar_arrive(bar(BAR_P_FULL));
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(BAR_P_FULL));
     }
 
     // ---- epilogue --------------------------------------------------------
@@ -517,7 +613,7 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
   CUtensorMap tq, tk, tv;
   std::string err;
   const int64_t qrows = varlen ? p.total_q : p.q_len;
-  const int64_t krows = varlen ? p.total_k : p.kv_len;
+  const int64_t krows = std::max<int64_t>(1, varlen ? p.total_k : p.kv_len);
   const int64_t nb = varlen ? 1 : p.batch;
   // batch stride of a 1-batch varlen map only has to be a valid multiple of 16 bytes
   const int64_t qbs = varlen ? 8 : p.q_batch_stride;
@@ -587,11 +683,13 @@ static int validate(const KvbPrefillParams& p) {
     return fail(KVB_ERR_INVALID, "causal must be 0 (none), 1 (bottom-right) or 2 (top-left)");
   if (p.q_len < 0 || p.kv_len < 0)
     return fail(KVB_ERR_INVALID, "sequence lengths must be non-negative");
-  if (!p.q || !p.k || !p.v || !p.o)
+  const bool varlen = p.cu_seqlens_q != nullptr;
+  // An empty key side may come with null k/v (an empty tensor's data pointer).
+  const bool no_keys = varlen ? p.total_k == 0 : p.kv_len == 0;
+  if (!p.q || !p.o || (!no_keys && (!p.k || !p.v)))
     return fail(KVB_ERR_INVALID, "q, k, v and o must be non-null");
   if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v) || !aligned16(p.o))
     return fail(KVB_ERR_INVALID, "q, k, v and o must be 16-byte aligned");
-  const bool varlen = p.cu_seqlens_q != nullptr;
   if (varlen != (p.cu_seqlens_k != nullptr))
     return fail(KVB_ERR_INVALID, "cu_seqlens_q and cu_seqlens_k must both be set or both NULL");
   if (varlen && (p.total_q < 0 || p.total_k < 0))
@@ -628,14 +726,15 @@ extern "C" int kvb_prefill_fwd(const KvbPrefillParams* params, void* stream) {
   // The TMA maps need at least one row; an empty key side is handled by the
   // kernel (no tiles) but the map must still be encodable.
   KvbPrefillParams q = p;
-  if (!varlen && q.kv_len == 0) {
+  if (varlen ? q.total_k == 0 : q.kv_len == 0) {
+    // No keys: no tile is ever loaded, but the K/V maps must still encode.
     q.k = p.q; q.v = p.q;
     q.k_head_stride = p.q_head_stride; q.k_row_stride = p.q_row_stride;
     q.k_batch_stride = p.q_batch_stride;
     q.v_head_stride = p.q_head_stride; q.v_row_stride = p.q_row_stride;
     q.v_batch_stride = p.q_batch_stride;
+    if (varlen) q.total_k = 1;
   }
-  if (varlen && q.total_k == 0) q.total_k = 1;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool bf = p.dtype == KVB_DTYPE_BF16;
   switch (p.head_dim) {
