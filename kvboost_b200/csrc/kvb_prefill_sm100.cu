@@ -47,16 +47,53 @@
 #include "kvb_attn.h"
 #include "kvb_sm100_ptx.cuh"
 
+// Share of exponent pairs computed on the FMA pipe: pair i of each 32-column
+// chunk uses the polynomial when (i % 4) < KVB_POLY_PAIRS_OF_4.  Measured on
+// B200 the softmax is issue/latency bound rather than MUFU bound, and every
+// non-zero share was slower, so the default keeps all exponentials on MUFU.
+#ifndef KVB_POLY_PAIRS_OF_4
+#define KVB_POLY_PAIRS_OF_4 0
+#endif
+// 1: pack bf16 probabilities with integer round-half-up + byte permute
+// instead of the cvt.rn.bf16x2.f32 conversion.
+#ifndef KVB_PACK_INT
+#define KVB_PACK_INT 0
+#endif
+
 #ifndef KVB_WAIT_NS
 #define KVB_WAIT_NS 2000000000ull  // 2 s: far above any legitimate wait
 #endif
 
 namespace kvb {
 
-constexpr int BM = 128;  // query rows per CTA (= TMEM lanes)
-constexpr int BN = 128;  // keys per tile
-constexpr int kThreads = 192;
-constexpr int kSoftmaxThreads = 128;
+// Optional per-CTA phase timestamps (SM clock) for pipeline studies; compiled
+// only with -DKVB_TRACE, never in the shipped library.
+#ifdef KVB_TRACE
+__device__ long long* g_kvb_trace;
+#define KVB_TRACE_AT(slot)                                 \
+  do {                                                     \
+    if (kvb_trace_row) kvb_trace_row[(slot)] = clock64();  \
+  } while (0)
+#define KVB_TRACE_SETUP()                                                                      \
+  long long* kvb_trace_row =                                                                   \
+      g_kvb_trace ? g_kvb_trace + 256ull * (blockIdx.x +                                       \
+                                            gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) \
+                  : nullptr
+#else
+#define KVB_TRACE_SETUP() \
+  do {                    \
+  } while (0)
+#define KVB_TRACE_AT(slot) \
+  do {                     \
+  } while (0)
+#endif
+
+constexpr int BM = 128;        // query rows per slot (= TMEM lanes)
+constexpr int BN = 128;        // keys per tile
+constexpr int kSlots = 2;      // query tiles per CTA, processed in ping-pong
+constexpr int kThreads = 320;  // warps 0-3 / 4-7 softmax of slot 0 / 1, warp 8 TMA, warp 9 MMA
+constexpr int kWarpTma = 8;
+constexpr int kWarpMma = 9;
 
 template <int D>
 struct Geo {
@@ -64,28 +101,28 @@ struct Geo {
   static constexpr int NATOM = DP / 64;          // 128-byte swizzle atoms per row
   static constexpr int ATOM_BYTES = 128 * 128;   // 128 rows x 128 bytes
   static constexpr int TILE_BYTES = NATOM * ATOM_BYTES;
-  static constexpr int NS = (D <= 64) ? 2 : 1;   // K/V ring depth
-  static constexpr int TMEM_COLS = 256;
-  static constexpr int S_COL = 0;
-  static constexpr int O_COL = 128;
+  static constexpr int NS = (D <= 64) ? 4 : 2;   // K/V ring depth
+  static constexpr int TMEM_COLS = 512;          // S0 S1 O0 O1, 128 columns each
   static constexpr int QK_STEPS = D / 16;        // K-steps of S = Q K^T
   static constexpr int PV_STEPS = BN / 16;       // K-steps of O += P V
-  static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = 1024 + TILE_BYTES * (1 + 2 * NS) + BAR_BYTES;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM_BYTES = 1024 + TILE_BYTES * (kSlots + 2 * NS) + BAR_BYTES;
+  __host__ __device__ static constexpr uint32_t s_col(int slot) { return slot * 128; }
+  __host__ __device__ static constexpr uint32_t o_col(int slot) { return 256 + slot * 128; }
 };
 
-// Barrier slots
+// Barrier slots (per-slot barriers at +slot, ring barriers at +stage)
 enum {
   BAR_Q_FULL = 0,
-  BAR_S_FULL = 1,
-  BAR_P_FULL = 2,
-  BAR_O_FULL = 3,
-  BAR_DRAIN = 4,
-  BAR_K_FULL = 5,   // + stage
-  BAR_K_EMPTY = 7,  // + stage
-  BAR_V_FULL = 9,   // + stage
-  BAR_V_EMPTY = 11, // + stage
-  BAR_COUNT = 13
+  BAR_S_FULL = 2,
+  BAR_P_FULL = 4,
+  BAR_O_FULL = 6,
+  BAR_DRAIN = 8,
+  BAR_K_FULL = 9,
+  BAR_K_EMPTY = 13,
+  BAR_V_FULL = 17,
+  BAR_V_EMPTY = 21,
+  BAR_COUNT = 25
 };
 
 struct DenseArgs {
@@ -96,7 +133,9 @@ struct DenseArgs {
   const int* cu_q;
   const int* cu_k;
   int q_len, kv_len;
-  int group;  // num_q_heads / num_kv_heads
+  int group;       // num_q_heads / num_kv_heads
+  int pair_heads;  // 1: slots are heads 2y, 2y+1 (same KV head) on one query tile;
+                   // 0: slots are query tiles 2x, 2x+1 of one head
   int causal;
   float scale_log2;
   int* status;
@@ -111,6 +150,7 @@ struct SharedCtl {
 // global timer.  Returns false if the CTA is aborting or the limit passed.
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                          int* status, int code) {
+  if (ptx::mbar_test_wait(bar, parity)) return true;
 #pragma unroll 1
   for (int i = 0; i < 128; ++i)
     if (ptx::mbar_try_wait(bar, parity)) return true;
@@ -161,10 +201,41 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
+}
+
+// 2^x for a pair on the FMA pipe, to take load off the MUFU unit (which
+// would otherwise bound the softmax at one ex2 per lane per 8 cycles).
+// Cody-Waite style split x = j + f with j = round-to-nearest(x) obtained by
+// adding 1.5 * 2^23 (the integer lands in the low mantissa bits), f in
+// [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted here by a Remez
+// exchange for minimax relative error on [-0.5, 0.5] (max 7.5e-5, below the
+// half-ulp of bf16 and fp16 probabilities); the result's exponent field is
+// then advanced by j.  Inputs are clamped to >= -126 so the result stays a
+// normal float; used only for unmasked columns, where that clamp only
+// replaces values below 2^-126.
+__device__ __forceinline__ void ex2_poly_pair(uint64_t x, float& p0, float& p1) {
+  const uint64_t magic = f2pack(12582912.f, 12582912.f);
+  const uint64_t c3 = f2pack(0.0551716685295105f, 0.0551716685295105f);
+  const uint64_t c2 = f2pack(0.2426111251115799f, 0.2426111251115799f);
+  const uint64_t c1 = f2pack(0.6932609677314758f, 0.6932609677314758f);
+  const uint64_t c0 = f2pack(0.9999280571937561f, 0.9999280571937561f);
+  x = f2pack(fmaxf(f2lo(x), -126.f), fmaxf(f2hi(x), -126.f));
+  const uint64_t t = fadd2(x, magic);
+  const uint64_t f = fsub2(x, fsub2(t, magic));
+  uint64_t p = ffma2(c3, f, c2);
+  p = ffma2(p, f, c1);
+  p = ffma2(p, f, c0);
+  p0 = __uint_as_float(static_cast<uint32_t>(p) + (static_cast<uint32_t>(t) << 23));
+  p1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(t >> 32) << 23));
 }
 
 // Convert a pair of probabilities to the MMA operand type, low half = first.
@@ -173,7 +244,15 @@ __device__ __forceinline__ uint32_t cvt_pair(float lo, float hi);
 template <>
 __device__ __forceinline__ uint32_t cvt_pair<__nv_bfloat16>(float lo, float hi) {
   uint32_t d;
+#if KVB_PACK_INT
+  // Probabilities are finite and non-negative: adding half an ulp of the
+  // 16-bit result and keeping the high halves rounds to nearest (ties up).
+  asm("prmt.b32 %0, %1, %2, 0x7632;"
+      : "=r"(d)
+      : "r"(__float_as_uint(lo) + 0x8000u), "r"(__float_as_uint(hi) + 0x8000u));
+#else
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+#endif
   return d;
 }
 template <>
@@ -207,55 +286,78 @@ __device__ __forceinline__ float tile_row_max(uint32_t tS, int lim) {
   return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
 }
 
-// P = exp2(s * sl2 - m) for one S tile: written back into TMEM over the
-// consumed S columns as 16-bit pairs (S columns [c, c+32) -> P columns
-// [c/2, c/2+16)).  Returns the row sum of P (fp32, before rounding) and the
-// raw row maximum seen (for the stale-maximum check).  The 32-column chunk
-// loop is kept rolled so the live set stays near 100 registers (two CTAs
-// per SM).
+// Softmax work on one 32-column chunk already in registers: P pairs packed
+// into pk, partial sums updated.
 template <typename T, bool MASK>
-__device__ __forceinline__ float tile_exp_store(uint32_t tS, float sl2, float m_use, int lim,
-                                                float* raw_max) {
+__device__ __forceinline__ void chunk_exp(const uint32_t (&r)[32], int c, int lim, uint64_t sc2,
+                                          uint64_t nm2, uint64_t& acc0, uint64_t& acc1,
+                                          uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float x0 = __uint_as_float(r[2 * i]);
+    float x1 = __uint_as_float(r[2 * i + 1]);
+    if (MASK) {
+      if (c + 2 * i > lim) x0 = -INFINITY;
+      if (c + 2 * i + 1 > lim) x1 = -INFINITY;
+    }
+    const uint64_t a = ffma2(f2pack(x0, x1), sc2, nm2);
+    float p0, p1;
+    if (!MASK && (i & 3) < KVB_POLY_PAIRS_OF_4) {
+      ex2_poly_pair(a, p0, p1);
+    } else {
+      p0 = ptx::ex2(f2lo(a));
+      p1 = ptx::ex2(f2hi(a));
+    }
+    if (i & 1)
+      acc1 = fadd2(acc1, f2pack(p0, p1));
+    else
+      acc0 = fadd2(acc0, f2pack(p0, p1));
+    pk[i] = cvt_pair<T>(p0, p1);
+  }
+}
+
+// P = exp2(s * sl2 - m) for one 128-column S tile, packed as 16-bit pairs
+// into pk (64 words; pair i of S columns 2i, 2i+1).  The four 32-column
+// chunks are double-buffered: the TMEM load of chunk k+1 is in flight while
+// chunk k is exponentiated.  S in TMEM is left intact (the caller stores P
+// only once the row sums pass the range check).  Returns the row sum of P
+// (fp32, before rounding).
+template <typename T, bool MASK>
+__device__ __forceinline__ float tile_exp(uint32_t tS, float sl2, float m_use, int lim,
+                                          uint32_t (&pk)[64]) {
   const uint64_t sc2 = f2pack(sl2, sl2);
   const uint64_t nm2 = f2pack(-m_use, -m_use);
-  uint64_t acc0 = 0, acc1 = 0;  // two packed partial sums
-  float m0 = -INFINITY, m1 = -INFINITY;
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
-    uint32_t r[32];
-    ptx::tmem_ld32(tS + c, r);
-    ptx::tmem_wait_ld();
-    uint32_t pk[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float x0 = __uint_as_float(r[2 * i]);
-      float x1 = __uint_as_float(r[2 * i + 1]);
-      if (MASK) {
-        if (c + 2 * i > lim) x0 = -INFINITY;
-        if (c + 2 * i + 1 > lim) x1 = -INFINITY;
-      }
-      if (i & 1)
-        m1 = fmax3(m1, x0, x1);
-      else
-        m0 = fmax3(m0, x0, x1);
-      const uint64_t a = ffma2(f2pack(x0, x1), sc2, nm2);
-      const float p0 = ptx::ex2(f2lo(a));
-      const float p1 = ptx::ex2(f2hi(a));
-      if (i & 1)
-        acc1 = fadd2(acc1, f2pack(p0, p1));
-      else
-        acc0 = fadd2(acc0, f2pack(p0, p1));
-      pk[i] = cvt_pair<T>(p0, p1);
-    }
-    ptx::tmem_st16(tS + c / 2, pk);
-  }
-  *raw_max = fmaxf(m0, m1);
+  uint64_t acc0 = 0, acc1 = 0;
+  uint32_t ra[32], rb[32];
+  ptx::tmem_ld32(tS + 0, ra);
+  ptx::tmem_wait_ld();
+  ptx::tmem_ld32(tS + 32, rb);
+  chunk_exp<T, MASK>(ra, 0, lim, sc2, nm2, acc0, acc1,
+                     *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
+  ptx::tmem_wait_ld();
+  ptx::tmem_ld32(tS + 64, ra);
+  chunk_exp<T, MASK>(rb, 32, lim, sc2, nm2, acc0, acc1,
+                     *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
+  ptx::tmem_wait_ld();
+  ptx::tmem_ld32(tS + 96, rb);
+  chunk_exp<T, MASK>(ra, 64, lim, sc2, nm2, acc0, acc1,
+                     *reinterpret_cast<uint32_t(*)[16]>(&pk[32]));
+  ptx::tmem_wait_ld();
+  chunk_exp<T, MASK>(rb, 96, lim, sc2, nm2, acc0, acc1,
+                     *reinterpret_cast<uint32_t(*)[16]>(&pk[48]));
   const uint64_t t = fadd2(acc0, acc1);
   return f2lo(t) + f2hi(t);
 }
 
+// Write the packed P of one tile over the (already consumed) S columns:
+// S columns [c, c+32) -> P columns [c/2, c/2+16).
+__device__ __forceinline__ void tile_store_p(uint32_t tS, const uint32_t (&pk)[64]) {
+  ptx::tmem_st32(tS + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+  ptx::tmem_st32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+}
+
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads)
     kvb_prefill_dense_kernel(const __grid_constant__ CUtensorMap tm_q,
                              const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v, const DenseArgs a) {
@@ -263,21 +365,32 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + G::TILE_BYTES;
-  uint8_t* sV = sK + G::NS * G::TILE_BYTES;
+  uint8_t* sQ = smem;                                  // kSlots tiles
+  uint8_t* sK = sQ + kSlots * G::TILE_BYTES;           // NS tiles
+  uint8_t* sV = sK + G::NS * G::TILE_BYTES;            // NS tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + G::NS * G::TILE_BYTES);
-  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(bars + 16);
+  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(bars + 32);
   volatile int* abort_flag = &ctl->abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  KVB_TRACE_SETUP();
 
-  // ---- work item --------------------------------------------------------
-  const int tile_m = gridDim.x - 1 - blockIdx.x;  // heaviest (last) tiles first
-  const int h = blockIdx.y;
+  // ---- work item: two query tiles sharing one KV head ---------------------
   const int b = blockIdx.z;
-  const int kvh = h / a.group;
+  int head[kSlots], mtile[kSlots];
+  if (a.pair_heads) {
+    const int m = gridDim.x - 1 - blockIdx.x;  // heaviest (last) query tiles first
+    head[0] = 2 * blockIdx.y;
+    head[1] = 2 * blockIdx.y + 1;
+    mtile[0] = mtile[1] = m;
+  } else {
+    const int x = gridDim.x - 1 - blockIdx.x;
+    head[0] = head[1] = blockIdx.y;
+    mtile[0] = 2 * x;
+    mtile[1] = 2 * x + 1;
+  }
+  const int kvh = head[0] / a.group;
   int q_len = a.q_len, kv_len = a.kv_len, q_base = 0, k_base = 0, tb = b;
   if (a.cu_q != nullptr) {
     q_base = a.cu_q[b];
@@ -286,39 +399,46 @@ __global__ void __launch_bounds__(kThreads, 2)
     kv_len = a.cu_k[b + 1] - k_base;
     tb = 0;
   }
-  const int q0 = tile_m * BM;
-  if (q0 >= q_len) return;  // uniform across the CTA, before any barrier use
-  const int q_rows = min(BM, q_len - q0);
   // causal 1: bottom-right (j <= i + kv_len - q_len); 2: top-left (j <= i)
   const int off = (a.causal == 2) ? 0 : kv_len - q_len;
-  int kv_end = a.causal ? min(kv_len, q0 + q_rows + off) : kv_len;
-  kv_end = max(kv_end, 0);
-  const int n_tiles = (kv_end + BN - 1) / BN;
+  int q0[kSlots], q_rows[kSlots], n_t[kSlots];
+#pragma unroll
+  for (int sl = 0; sl < kSlots; ++sl) {
+    q0[sl] = mtile[sl] * BM;
+    q_rows[sl] = max(0, min(BM, q_len - q0[sl]));
+    int kv_end = a.causal ? min(kv_len, q0[sl] + q_rows[sl] + off) : kv_len;
+    kv_end = max(kv_end, 0);
+    n_t[sl] = q_rows[sl] > 0 ? (kv_end + BN - 1) / BN : 0;
+  }
+  if (q_rows[0] == 0 && q_rows[1] == 0) return;  // uniform, before any barrier use
+  const int n_max = max(n_t[0], n_t[1]);
 
   auto bar = [&](int i) { return ptx::smem_u32(&bars[i]); };
 
   // ---- setup --------------------------------------------------------------
   if (threadIdx.x == 0) {
-    ptx::mbar_init(bar(BAR_Q_FULL), 1);
-    ptx::mbar_init(bar(BAR_S_FULL), 1);
-    ptx::mbar_init(bar(BAR_P_FULL), kSoftmaxThreads / 32);
-    ptx::mbar_init(bar(BAR_O_FULL), 1);
+    for (int sl = 0; sl < kSlots; ++sl) {
+      ptx::mbar_init(bar(BAR_Q_FULL + sl), 1);
+      ptx::mbar_init(bar(BAR_S_FULL + sl), 1);
+      ptx::mbar_init(bar(BAR_P_FULL + sl), 4);  // one arrive per softmax warp
+      ptx::mbar_init(bar(BAR_O_FULL + sl), 1);
+    }
     ptx::mbar_init(bar(BAR_DRAIN), 1);
-    for (int s = 0; s < 2; ++s) {
-      ptx::mbar_init(bar(BAR_K_FULL + s), 1);
-      ptx::mbar_init(bar(BAR_K_EMPTY + s), 1);
-      ptx::mbar_init(bar(BAR_V_FULL + s), 1);
-      ptx::mbar_init(bar(BAR_V_EMPTY + s), 1);
+    for (int st = 0; st < G::NS; ++st) {
+      ptx::mbar_init(bar(BAR_K_FULL + st), 1);
+      ptx::mbar_init(bar(BAR_K_EMPTY + st), 1);
+      ptx::mbar_init(bar(BAR_V_FULL + st), 1);
+      ptx::mbar_init(bar(BAR_V_EMPTY + st), 1);
     }
     ctl->abort_flag = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == kWarpTma && lane == 0) {
     ptx::prefetch_tmap(&tm_q);
     ptx::prefetch_tmap(&tm_k);
     ptx::prefetch_tmap(&tm_v);
   }
-  if (warp == 5) {
+  if (warp == kWarpMma) {
     ptx::tmem_alloc(ptx::smem_u32(&ctl->tmem_base), G::TMEM_COLS);
     ptx::tmem_relinquish();
   }
@@ -326,193 +446,254 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
+  if (threadIdx.x == 0) KVB_TRACE_AT(0);
 
-  if (warp == 4) {
+  if (warp == kWarpTma) {
     // ================================================================ TMA
-    if (lane == 0 && n_tiles > 0) {
-      const int qy = q_base + q0;
-      ptx::mbar_arrive_expect_tx(bar(BAR_Q_FULL), G::TILE_BYTES);
+    if (lane == 0 && n_max > 0) {
 #pragma unroll
-      for (int at = 0; at < G::NATOM; ++at)
-        ptx::tma_load_4d(ptx::smem_u32(sQ + at * G::ATOM_BYTES), &tm_q, at * 64, qy, h, tb,
-                         bar(BAR_Q_FULL));
+      for (int sl = 0; sl < kSlots; ++sl) {
+        if (n_t[sl] == 0) continue;
+        ptx::mbar_arrive_expect_tx(bar(BAR_Q_FULL + sl), G::TILE_BYTES);
+#pragma unroll
+        for (int at = 0; at < G::NATOM; ++at)
+          ptx::tma_load_4d(ptx::smem_u32(sQ + sl * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_q,
+                           at * 64, q_base + q0[sl], head[sl], tb, bar(BAR_Q_FULL + sl));
+      }
       int issued = 0;
 #pragma unroll 1
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j % G::NS;
+      for (int j = 0; j < n_max; ++j) {
+        const int st = j % G::NS;
         const uint32_t ph = (j / G::NS) & 1;
         const int ky = k_base + j * BN;
-        if (!wait_bar(bar(BAR_K_EMPTY + s), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
+        if (!wait_bar(bar(BAR_K_EMPTY + st), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
           break;
-        ptx::mbar_arrive_expect_tx(bar(BAR_K_FULL + s), G::TILE_BYTES);
+        if (j < 16) KVB_TRACE_AT(16 + j);
+        ptx::mbar_arrive_expect_tx(bar(BAR_K_FULL + st), G::TILE_BYTES);
 #pragma unroll
         for (int at = 0; at < G::NATOM; ++at)
-          ptx::tma_load_4d(ptx::smem_u32(sK + s * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_k,
-                           at * 64, ky, kvh, tb, bar(BAR_K_FULL + s));
-        if (!wait_bar(bar(BAR_V_EMPTY + s), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
+          ptx::tma_load_4d(ptx::smem_u32(sK + st * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_k,
+                           at * 64, ky, kvh, tb, bar(BAR_K_FULL + st));
+        if (!wait_bar(bar(BAR_V_EMPTY + st), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
           break;
-        ptx::mbar_arrive_expect_tx(bar(BAR_V_FULL + s), G::TILE_BYTES);
+        if (j < 16) KVB_TRACE_AT(32 + j);
+        ptx::mbar_arrive_expect_tx(bar(BAR_V_FULL + st), G::TILE_BYTES);
 #pragma unroll
         for (int at = 0; at < G::NATOM; ++at)
-          ptx::tma_load_4d(ptx::smem_u32(sV + s * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_v,
-                           at * 64, ky, kvh, tb, bar(BAR_V_FULL + s));
+          ptx::tma_load_4d(ptx::smem_u32(sV + st * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_v,
+                           at * 64, ky, kvh, tb, bar(BAR_V_FULL + st));
         issued = j + 1;
       }
       if (*abort_flag) {
         // Drain: wait (bounded) for the loads of the last ring round to land.
         for (int j = max(0, issued - G::NS); j < issued; ++j) {
-          const int s = j % G::NS;
+          const int st = j % G::NS;
           const uint32_t ph = (j / G::NS) & 1;
-          wait_bar(bar(BAR_K_FULL + s), ph, abort_flag, nullptr, 0);
-          wait_bar(bar(BAR_V_FULL + s), ph, abort_flag, nullptr, 0);
+          wait_bar(bar(BAR_K_FULL + st), ph, abort_flag, nullptr, 0);
+          wait_bar(bar(BAR_V_FULL + st), ph, abort_flag, nullptr, 0);
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kWarpMma) {
     // ================================================================ MMA
-    if (lane == 0 && n_tiles > 0) {
+    if (lane == 0 && n_max > 0) {
       constexpr uint32_t idesc_s = ptx::idesc_f16(BM, BN, ab_format<T>(), 0, 0);
       constexpr uint32_t idesc_o = ptx::idesc_f16(BM, G::DP, ab_format<T>(), 0, 1);
-      const uint32_t tS = tmem + G::S_COL;
-      const uint32_t tO = tmem + G::O_COL;
       const uint32_t sQa = ptx::smem_u32(sQ);
       const uint32_t sKa = ptx::smem_u32(sK);
       const uint32_t sVa = ptx::smem_u32(sV);
-      bool ok = wait_bar(bar(BAR_Q_FULL), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
 
-      auto issue_s = [&](int j) {
-        const int s = j % G::NS;
-        const uint32_t kb = sKa + s * G::TILE_BYTES;
+      // Descriptor words are built once; between instructions only the low
+      // word advances (one add per operand), which keeps the single issuing
+      // thread ahead of the tensor pipe.
+      constexpr uint32_t hi = ptx::desc_hi_sw128(1024);
+      const uint32_t q_lo = ptx::desc_lo(sQa, 16);
+      const uint32_t k_lo = ptx::desc_lo(sKa, 16);
+      const uint32_t v_lo = ptx::desc_lo(sVa, G::ATOM_BYTES);
+      constexpr uint32_t TILE16 = G::TILE_BYTES >> 4;
+
+      auto issue_s = [&](int sl, int j) {
+        if (j < 16) KVB_TRACE_AT(48 + 96 * sl + j);
+        const uint32_t qa = q_lo + sl * TILE16;
+        const uint32_t kb = k_lo + (j % G::NS) * TILE16;
+        const uint32_t tS = tmem + G::s_col(sl);
 #pragma unroll
         for (int kk = 0; kk < G::QK_STEPS; ++kk) {
-          const uint32_t off_b = (kk >> 2) * G::ATOM_BYTES + (kk & 3) * 32;
-          const uint64_t da = ptx::smem_desc_sw128(sQa + off_b, 16, 1024);
-          const uint64_t db = ptx::smem_desc_sw128(kb + off_b, 16, 1024);
-          ptx::mma_ss(tS, da, db, idesc_s, kk > 0 ? 1u : 0u);
+          const uint32_t off16 = ((kk >> 2) * G::ATOM_BYTES + (kk & 3) * 32) >> 4;
+          ptx::mma_ss_lohi(tS, qa + off16, hi, kb + off16, hi, idesc_s, kk > 0 ? 1u : 0u);
         }
-        ptx::mma_commit(bar(BAR_K_EMPTY + s));
-        ptx::mma_commit(bar(BAR_S_FULL));
+        ptx::mma_commit(bar(BAR_S_FULL + sl));
+        if (sl == 0 && j < 16) KVB_TRACE_AT(224 + j);
+      };
+      auto issue_pv = [&](int sl, int j) {
+        if (j < 16) KVB_TRACE_AT(96 + 96 * sl + j);
+        const uint32_t vb = v_lo + (j % G::NS) * TILE16;
+        const uint32_t tP = tmem + G::s_col(sl);
+        const uint32_t tO = tmem + G::o_col(sl);
+#pragma unroll
+        for (int kk = 0; kk < G::PV_STEPS; ++kk)
+          ptx::mma_ts_lohi(tO, tP + kk * 8, vb + ((kk * 16 * 128) >> 4), hi, idesc_o,
+                           (j > 0 || kk > 0) ? 1u : 0u);
+        if (sl == 0 && j < 16) KVB_TRACE_AT(240 + j);
       };
 
-      if (ok) ok = wait_bar(bar(BAR_K_FULL + 0), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
-      if (ok) {
-        ptx::tc_fence_after();
-        issue_s(0);
-      }
-#pragma unroll 1
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int s = j % G::NS;
-        const uint32_t ph = (j / G::NS) & 1;
-        if (!wait_bar(bar(BAR_P_FULL), j & 1, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) break;
-        if (!wait_bar(bar(BAR_V_FULL + s), ph, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) break;
-        ptx::tc_fence_after();
-        const uint32_t vb = sVa + s * G::TILE_BYTES;
+      bool ok = wait_bar(bar(BAR_K_FULL), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
 #pragma unroll
-        for (int kk = 0; kk < G::PV_STEPS; ++kk) {
-          const uint64_t dv = ptx::smem_desc_sw128(vb + kk * 16 * 128, G::ATOM_BYTES, 1024);
-          ptx::mma_ts(tO, tS + kk * 8, dv, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        ptx::mma_commit(bar(BAR_V_EMPTY + s));
-        if (j + 1 < n_tiles) {
-          const int s1 = (j + 1) % G::NS;
-          const uint32_t ph1 = ((j + 1) / G::NS) & 1;
-          if (!wait_bar(bar(BAR_K_FULL + s1), ph1, abort_flag, a.status, KVB_STATUS_MMA_WAIT))
-            break;
-          ptx::tc_fence_after();
-          issue_s(j + 1);
-        }
+      for (int sl = 0; sl < kSlots && ok; ++sl) {
+        if (n_t[sl] == 0) continue;
+        ok = wait_bar(bar(BAR_Q_FULL + sl), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        issue_s(sl, 0);
       }
-      ptx::mma_commit(bar(BAR_O_FULL));
-      // Drain: all MMAs issued above complete before TMEM can be freed.
+      if (ok) ptx::mma_commit(bar(BAR_K_EMPTY));
+#pragma unroll 1
+      for (int j = 0; ok && j < n_max; ++j) {
+        const int st = j % G::NS;
+        const uint32_t ph = (j / G::NS) & 1;
+        const int st1 = (j + 1) % G::NS;
+        const uint32_t ph1 = ((j + 1) / G::NS) & 1;
+        bool v_ready = false, k_next_ready = false;
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl) {
+          if (j >= n_t[sl]) continue;
+          if (!wait_bar(bar(BAR_P_FULL + sl), j & 1, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) {
+            ok = false;
+            break;
+          }
+          if (sl == 0 && j < 16) KVB_TRACE_AT(112 + j);
+          if (!v_ready) {
+            if (!wait_bar(bar(BAR_V_FULL + st), ph, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) {
+              ok = false;
+              break;
+            }
+            v_ready = true;
+          }
+          if (sl == 0 && j < 16) KVB_TRACE_AT(128 + j);
+          ptx::tc_fence_after();
+          issue_pv(sl, j);
+          if (j + 1 < n_t[sl]) {
+            if (!k_next_ready) {
+              if (!wait_bar(bar(BAR_K_FULL + st1), ph1, abort_flag, a.status,
+                            KVB_STATUS_MMA_WAIT)) {
+                ok = false;
+                break;
+              }
+              k_next_ready = true;
+            }
+            issue_s(sl, j + 1);
+          } else {
+            ptx::mma_commit(bar(BAR_O_FULL + sl));  // this slot's last PV
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit(bar(BAR_V_EMPTY + st));
+        if (k_next_ready) ptx::mma_commit(bar(BAR_K_EMPTY + st1));
+      }
+      // Drain: every MMA issued above completes before TMEM can be freed.
       ptx::mma_commit(bar(BAR_DRAIN));
       wait_bar(bar(BAR_DRAIN), 0, abort_flag, nullptr, 0);
     }
   } else {
     // ============================================================ softmax
-    const int t = threadIdx.x;  // row within the tile == TMEM lane
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tS = tmem + lane_base + G::S_COL;
-    const uint32_t tO = tmem + lane_base + G::O_COL;
-    const int qi = q0 + t;
+    const int sl = warp >> 2;                     // slot of this warpgroup
+    const int t = threadIdx.x & 127;              // row within the tile == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + G::s_col(sl);
+    const uint32_t tO = tmem + lane_base + G::o_col(sl);
+    const int h = head[sl];
+    const int q0s = q0[sl];
+    const int n_tiles = n_t[sl];
+    const int qi = q0s + t;
     const float sl2 = a.scale_log2;
+    constexpr float kSumLimit = std::is_same<T, __half>::value ? 32768.f : 1.0995116e12f;
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
 
 #pragma unroll 1
     for (int j = 0; j < n_tiles; ++j) {
-      ok = wait_bar(bar(BAR_S_FULL), j & 1, abort_flag, a.status, KVB_STATUS_SOFTMAX_WAIT);
+      ok = wait_bar(bar(BAR_S_FULL + sl), j & 1, abort_flag, a.status, KVB_STATUS_SOFTMAX_WAIT);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       ptx::tc_fence_after();
+      if (t == 0 && j < 16) KVB_TRACE_AT(64 + 96 * sl + j);
 
       const int kv0 = j * BN;
-      const bool need_mask = (kv0 + BN > kv_len) || (a.causal && kv0 + BN - 1 > q0 + off);
+      const bool need_mask = (kv0 + BN > kv_len) || (a.causal && kv0 + BN - 1 > q0s + off);
       const int lim = (a.causal ? min(kv_len - 1, qi + off) : kv_len - 1) - kv0;
 
-      // Stale-maximum softmax: exponentiate against the running maximum in
-      // one pass; only when some row's tile maximum exceeds it by more than
-      // 8 (log2 units) is the maximum raised, O rescaled and the tile redone.
-      // A row with no maximum yet (first tile) takes the two-pass path.
+      // Stale-maximum softmax.  After the first tile, each tile is
+      // exponentiated against the running maximum in one pass with no max
+      // tracking.  The maximum only has to be raised before a probability
+      // could leave the range of the P operand (2^40 keeps bf16 P and the
+      // fp32 sums far from overflow; fp16 P tops out at 65504, so 2^15
+      // there).  Every probability is bounded by the row sum, so the sum is
+      // the check.  Rows that fail it, and rows without a maximum yet, take
+      // the exact path: tile maximum, O rescale, redo.  The final
+      // normalisation uses the same maximum as the exponentials, so the
+      // result is exact up to rounding.
       float alpha = 1.f;
       float sum = 0.f;
-      float raw_mx;
       bool raise = false;
+      uint32_t pk[64];
       const bool two_pass = __any_sync(0xffffffffu, m_run == -INFINITY);
-      if (two_pass) {
-        raw_mx = need_mask ? tile_row_max<true>(tS, lim) : tile_row_max<false>(tS, lim);
-        raise = raw_mx * sl2 > m_run + 8.0f || (m_run == -INFINITY && raw_mx > -INFINITY);
-      } else {
-        const float m_use = m_run;
-        sum = need_mask ? tile_exp_store<T, true>(tS, sl2, m_use, lim, &raw_mx)
-                        : tile_exp_store<T, false>(tS, sl2, m_use, lim, &raw_mx);
-        raise = raw_mx * sl2 > m_run + 8.0f;
+      if (!two_pass) {
+        sum = need_mask ? tile_exp<T, true>(tS, sl2, m_run, lim, pk)
+                        : tile_exp<T, false>(tS, sl2, m_run, lim, pk);
+        raise = !(sum <= kSumLimit);  // also catches inf / NaN
       }
-      const bool redo = two_pass || __any_sync(0xffffffffu, raise);
-      if (raise) {
-        const float m_new = raw_mx * sl2;
-        alpha = ptx::ex2(m_run - m_new);
-        m_run = m_new;
-      }
-      // O rescale (after PV_{j-1}, which completed before S_j was committed)
-      if (j > 0 && __any_sync(0xffffffffu, raise)) {
-        const float f = raise ? alpha : 1.f;
-#pragma unroll
-        for (int c = 0; c < G::DP; c += 32) {
-          uint32_t r[32];
-          ptx::tmem_ld32(tO + c, r);
-          ptx::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-          ptx::tmem_st32(tO + c, r);
+      const bool exact = two_pass || __any_sync(0xffffffffu, raise);
+      if (exact) {
+        const float raw_mx =
+            need_mask ? tile_row_max<true>(tS, lim) : tile_row_max<false>(tS, lim);
+        const float m_tile = raw_mx * sl2;
+        raise = m_tile > m_run && raw_mx > -INFINITY && (raise || m_run == -INFINITY);
+        if (raise) {
+          alpha = ptx::ex2(m_run - m_tile);
+          m_run = m_tile;
         }
-      }
-      if (redo) {
+        // O rescale (PV_{j-1} completed before S_j was committed)
+        if (j > 0 && __any_sync(0xffffffffu, raise)) {
+          const float f = raise ? alpha : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < G::DP; c += 32) {
+            uint32_t r[32];
+            ptx::tmem_ld32(tO + c, r);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+            ptx::tmem_st32(tO + c, r);
+          }
+        }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        float dummy;
-        sum = need_mask ? tile_exp_store<T, true>(tS, sl2, m_use, lim, &dummy)
-                        : tile_exp_store<T, false>(tS, sl2, m_use, lim, &dummy);
+        sum = need_mask ? tile_exp<T, true>(tS, sl2, m_use, lim, pk)
+                        : tile_exp<T, false>(tS, sl2, m_use, lim, pk);
       }
+      tile_store_p(tS, pk);
       l_run = l_run * alpha + sum;
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar(BAR_P_FULL));
+      if (lane == 0) ptx::mbar_arrive(bar(BAR_P_FULL + sl));
+      if (lane == 0 && warp == 3 && j < 16) KVB_TRACE_AT(208 + j);
+      if (t == 0 && j < 16) KVB_TRACE_AT(80 + 96 * sl + j);
     }
 
     // ---- epilogue --------------------------------------------------------
     bool have_o = n_tiles > 0 && ok;
     if (have_o) {
-      have_o = wait_bar(bar(BAR_O_FULL), 0, abort_flag, a.status, KVB_STATUS_EPILOGUE_WAIT);
+      have_o = wait_bar(bar(BAR_O_FULL + sl), 0, abort_flag, a.status, KVB_STATUS_EPILOGUE_WAIT);
       have_o = __all_sync(0xffffffffu, have_o);
       ptx::tc_fence_after();
     }
-    const bool row_valid = t < q_rows;
+    if (t == 0 && sl == 0) KVB_TRACE_AT(2);
+    const bool row_valid = t < q_rows[sl];
     const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
     T* orow = reinterpret_cast<T*>(a.o) +
               (a.cu_q ? (int64_t)(q_base + qi) * a.o_rs + (int64_t)h * a.o_hs
                       : (int64_t)b * a.o_bs + (int64_t)h * a.o_hs + (int64_t)qi * a.o_rs);
-#pragma unroll
+#pragma unroll 1
     for (int c = 0; c < D; c += 32) {
       uint32_t r[32];
       if (n_tiles > 0) {
@@ -545,7 +726,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (threadIdx.x == 0) KVB_TRACE_AT(3);
+  if (warp == kWarpMma) {
     __syncwarp();
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, G::TMEM_COLS);
@@ -640,6 +822,7 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
   a.q_len = p.q_len;
   a.kv_len = p.kv_len;
   a.group = p.num_q_heads / p.num_kv_heads;
+  a.pair_heads = (a.group % 2 == 0) ? 1 : 0;
   a.causal = p.causal;
   a.scale_log2 = p.softmax_scale * 1.4426950408889634f;
   a.status = p.status;
@@ -655,7 +838,9 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
       return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured_device = dev;
   }
-  dim3 grid((p.q_len + BM - 1) / BM, p.num_q_heads, p.batch);
+  const int q_tiles = (p.q_len + BM - 1) / BM;
+  dim3 grid = a.pair_heads ? dim3(q_tiles, p.num_q_heads / 2, p.batch)
+                           : dim3((q_tiles + 1) / 2, p.num_q_heads, p.batch);
   kern<<<grid, kThreads, G::SMEM_BYTES, stream>>>(tq, tk, tv, a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
@@ -774,3 +959,9 @@ extern "C" int kvb_flash_attn_fwd(const void* q, const void* k, const void* v, v
 extern "C" const char* kvb_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" int kvb_abi_version(void) { return KVB_ABI_VERSION; }
+
+#ifdef KVB_TRACE
+extern "C" int kvb_debug_set_trace(void* dev_ptr) {
+  return cudaMemcpyToSymbol(kvb::g_kvb_trace, &dev_ptr, sizeof(dev_ptr)) == cudaSuccess ? 0 : -1;
+}
+#endif

@@ -219,3 +219,20 @@ def test_repeatable_bitwise():
     o2, l2 = prefill_attention(q, k, v)
     torch.cuda.synchronize()
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_running_max_raises_late(dtype):
+    """Scores that grow along the keys force the exact path (max raise + O rescale)."""
+    from kvboost_b200.ops import prefill_attention
+    g = torch.Generator().manual_seed(17)
+    B, H, Sq, Skv, D = 1, 4, 130, 1000, 128
+    q = _rand((B, H, Sq, D), dtype, g)
+    ramp = torch.linspace(0.05, 3.0, Skv).view(1, 1, Skv, 1)
+    k = (torch.randn(B, H, Skv, D, generator=g) * ramp).to(dtype)
+    v = _rand((B, H, Skv, D), dtype, g)
+    # one very strong key late in the sequence for query row 3
+    k[0, 0, 900] = (q[0, 0, 3].float() * 0.9).to(dtype)
+    o, lse = prefill_attention(q.cuda(), k.cuda(), v.cuda(), 1.0 / math.sqrt(D), True)
+    torch.cuda.synchronize()
+    _check(o, lse, q, k, v, 1.0 / math.sqrt(D), True, dtype)
