@@ -43,8 +43,8 @@ WORKLOADS = {
 }
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one prefill launch from the
-# committed ncu capture (profiles/), per workload; None until captured.
-NCU_TRAFFIC_BYTES = {}
+# committed ncu capture (profiles/prefill_dense_reuse_b4h32kv8_d128.md).
+NCU_TRAFFIC_BYTES = {"reuse_prefill": 27335168}
 
 
 def parse():
