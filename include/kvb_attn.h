@@ -62,7 +62,8 @@ enum {
   KVB_STATUS_LOAD_WAIT = 1,    /* producer waited too long for a free stage   */
   KVB_STATUS_MMA_WAIT = 2,     /* MMA issuer waited too long for operands     */
   KVB_STATUS_SOFTMAX_WAIT = 4, /* softmax warps waited too long for scores    */
-  KVB_STATUS_EPILOGUE_WAIT = 8 /* epilogue waited too long for the output     */
+  KVB_STATUS_EPILOGUE_WAIT = 8,/* epilogue waited too long for the output     */
+  KVB_STATUS_BAD_BLOCK = 16     /* a block-table entry was outside the pool    */
 };
 
 /*
@@ -131,6 +132,64 @@ typedef struct KvbPrefillParams {
 } KvbPrefillParams;
 
 int kvb_prefill_fwd(const KvbPrefillParams* params, void* stream);
+
+/*
+ * Reuse prefill over an int8 paged prefix: the suffix's queries attend to
+ * the cached prefix (KVBoost's 128-token chunks, KIVI int8, stored in
+ * 16-token blocks) followed by the suffix's own fresh K/V, bottom-right
+ * causal.  Replaces the host path that dequantises each cached chunk
+ * (kv_quantize.py:102-109), gathers it through the block table
+ * (cpu_paged/block_allocator.py:178-206, cpu_paged/chunk_to_blocks.py:57-125)
+ * and concatenates it before SDPA (cache_manager.py:460-471): here the
+ * gather and the dequantisation happen in the kernel's K/V load stage.
+ *
+ * Pool layout (one layer): kv_pool int8 [num_blocks, 2, num_kv_heads, 16,
+ * head_dim] (index 0 = K, 1 = V; the reference pool's layout,
+ * block_allocator.py:67-73); k_scale float32 [num_blocks, num_kv_heads, 16]
+ * (the per-token K scale of each slot); v_scale float32 [num_blocks,
+ * num_kv_heads, head_dim] (the per-channel V scale of the chunk the block
+ * belongs to).  Scales are the reference's float16 values widened to
+ * float32.  Logical token t of sequence b lives in block
+ * block_tables[b * max_blocks_per_seq + t / 16], slot t % 16.  Dequantised
+ * values are q * scale rounded once to the compute dtype.
+ *
+ * q/o: [batch, num_q_heads, q_len, head_dim] strided; k_new/v_new: the
+ * suffix's K/V [batch, num_kv_heads, q_len, head_dim] strided.  Sequence b
+ * has kv_len = prefix_len_b + q_len.  block_size must be 16.  Block ids
+ * outside [0, num_blocks) read as zeros and set KVB_STATUS_BAD_BLOCK.
+ */
+typedef struct KvbPagedPrefillParams {
+  int32_t dtype;
+  int32_t head_dim;
+  int32_t batch;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t q_len;
+  int32_t causal;
+  float softmax_scale;
+  const void* q;
+  void* o;
+  float* lse;
+  int64_t q_batch_stride, q_head_stride, q_row_stride;
+  int64_t o_batch_stride, o_head_stride, o_row_stride;
+  int64_t lse_batch_stride, lse_head_stride;
+  const void* k_new;
+  const void* v_new;
+  int64_t k_new_batch_stride, k_new_head_stride, k_new_row_stride;
+  int64_t v_new_batch_stride, v_new_head_stride, v_new_row_stride;
+  const int8_t* kv_pool;
+  const float* k_scale;
+  const float* v_scale;
+  int32_t num_blocks;
+  int32_t block_size;
+  const int32_t* block_tables;
+  int32_t max_blocks_per_seq;
+  int32_t prefix_len;           /* uniform (or maximum) cached tokens        */
+  const int32_t* prefix_lens;   /* device [batch] per-sequence, or NULL      */
+  int32_t* status;
+} KvbPagedPrefillParams;
+
+int kvb_paged_prefill_fwd(const KvbPagedPrefillParams* params, void* stream);
 
 /* Human-readable reason for the last non-zero return on this host thread. */
 const char* kvb_last_error(void);

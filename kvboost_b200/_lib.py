@@ -42,6 +42,27 @@ class KvbPrefillParams(ctypes.Structure):
     ]
 
 
+class KvbPagedPrefillParams(ctypes.Structure):
+    """Mirror of ``KvbPagedPrefillParams`` (field order and types must match the header)."""
+
+    _fields_ = [
+        ("dtype", _i32), ("head_dim", _i32), ("batch", _i32),
+        ("num_q_heads", _i32), ("num_kv_heads", _i32), ("q_len", _i32), ("causal", _i32),
+        ("softmax_scale", _f32),
+        ("q", _vp), ("o", _vp), ("lse", _vp),
+        ("q_batch_stride", _i64), ("q_head_stride", _i64), ("q_row_stride", _i64),
+        ("o_batch_stride", _i64), ("o_head_stride", _i64), ("o_row_stride", _i64),
+        ("lse_batch_stride", _i64), ("lse_head_stride", _i64),
+        ("k_new", _vp), ("v_new", _vp),
+        ("k_new_batch_stride", _i64), ("k_new_head_stride", _i64), ("k_new_row_stride", _i64),
+        ("v_new_batch_stride", _i64), ("v_new_head_stride", _i64), ("v_new_row_stride", _i64),
+        ("kv_pool", _vp), ("k_scale", _vp), ("v_scale", _vp),
+        ("num_blocks", _i32), ("block_size", _i32),
+        ("block_tables", _vp), ("max_blocks_per_seq", _i32), ("prefix_len", _i32),
+        ("prefix_lens", _vp), ("status", _vp),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -70,6 +91,8 @@ def load() -> ctypes.CDLL:
                                            ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32,
                                            ctypes.c_int, _vp]
         lib.kvb_flash_attn_fwd.restype = ctypes.c_int
+        lib.kvb_paged_prefill_fwd.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]
+        lib.kvb_paged_prefill_fwd.restype = ctypes.c_int
         lib.kvb_last_error.argtypes = []
         lib.kvb_last_error.restype = ctypes.c_char_p
         lib.kvb_abi_version.argtypes = []

@@ -91,9 +91,18 @@ __device__ long long* g_kvb_trace;
 constexpr int BM = 128;        // query rows per slot (= TMEM lanes)
 constexpr int BN = 128;        // keys per tile
 constexpr int kSlots = 2;      // query tiles per CTA, processed in ping-pong
-constexpr int kThreads = 320;  // warps 0-3 / 4-7 softmax of slot 0 / 1, warp 8 TMA, warp 9 MMA
-constexpr int kWarpTma = 8;
-constexpr int kWarpMma = 9;
+// Warp roles.  Dense: warps 0-3 / 4-7 softmax of slot 0 / 1, warp 8 TMA,
+// warp 9 MMA (320 threads).  Paged: warps 8-10 gather + dequantise K/V into
+// shared memory (warp 8 lane 0 also issues the Q TMA), warp 11 MMA (384
+// threads).  Either way no SM sub-partition holds more than 3 warps, which
+// leaves 168 registers per thread.
+template <bool PAGED>
+struct Roles {
+  static constexpr int kThreads = PAGED ? 384 : 320;
+  static constexpr int kWarpTma = 8;
+  static constexpr int kWarpMma = PAGED ? 11 : 9;
+  static constexpr int kConvWarps = PAGED ? 3 : 0;
+};
 
 template <int D>
 struct Geo {
@@ -139,6 +148,22 @@ struct DenseArgs {
   int causal;
   float scale_log2;
   int* status;
+};
+
+// Reused-prefix K/V in the int8 paged pool plus the suffix's own fresh K/V.
+struct PagedArgs {
+  const int8_t* pool;     // [num_blocks, 2, num_kv_heads, 16, D] int8 (K then V)
+  const float* k_scale;   // [num_blocks, num_kv_heads, 16]  per-token K scale
+  const float* v_scale;   // [num_blocks, num_kv_heads, D]   per-channel V scale of the block's chunk
+  const int* block_table; // [batch, max_blocks]
+  const int* prefix_lens; // [batch] cached tokens, or null -> prefix_len
+  const void* k_new;      // suffix K (compute dtype), element (b, h, i, d) at
+  const void* v_new;      //   b*bs + h*hs + i*rs + d
+  int64_t kn_bs, kn_hs, kn_rs, vn_bs, vn_hs, vn_rs;
+  int max_blocks;
+  int num_blocks;
+  int num_kv_heads;
+  int prefix_len;
 };
 
 struct SharedCtl {
@@ -356,12 +381,99 @@ __device__ __forceinline__ void tile_store_p(uint32_t tS, const uint32_t (&pk)[6
   ptx::tmem_st32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
 }
 
+// Gather one 128-token K or V tile for the paged path into the swizzled
+// shared-memory layout the MMA reads (the same layout a 128-byte-swizzle TMA
+// box produces: row r, 16-byte unit u of a 64-element atom lands at
+// atom*16K + r*128 + ((u ^ (r & 7)) * 16)).  Tokens below the cached prefix
+// come from the int8 pool through the block table and are dequantised as
+// q * scale in fp32, rounded once to the compute type; tokens of the suffix
+// are copied from the fresh K/V; rows past the end (and padding columns past
+// head_dim) are zero.  Block ids outside the pool, and table positions past
+// max_blocks (a per-sequence prefix longer than the table), read as zeros
+// and set KVB_STATUS_BAD_BLOCK.
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads)
-    kvb_prefill_dense_kernel(const __grid_constant__ CUtensorMap tm_q,
-                             const __grid_constant__ CUtensorMap tm_k,
-                             const __grid_constant__ CUtensorMap tm_v, const DenseArgs a) {
+__device__ __forceinline__ void gather_kv_tile(uint8_t* dst, const PagedArgs& pa, int b, int kvh,
+                                               int tok0, int P, int kv_len, int kv, int ct,
+                                               int nct, int* status) {
   using G = Geo<D>;
+  constexpr int NCH = G::DP / 16;  // 16-element chunks per row (padding included)
+  const T* fresh = reinterpret_cast<const T*>(kv ? pa.v_new : pa.k_new);
+  const int64_t f_bs = kv ? pa.vn_bs : pa.kn_bs;
+  const int64_t f_hs = kv ? pa.vn_hs : pa.kn_hs;
+  const int64_t f_rs = kv ? pa.vn_rs : pa.kn_rs;
+#pragma unroll 1
+  for (int idx = ct; idx < BN * NCH; idx += nct) {
+    const int row = idx / NCH;
+    const int ch = idx - row * NCH;
+    const int tok = tok0 + row;
+    uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
+    if (ch * 16 < D && tok < kv_len) {
+      if (tok < P) {
+        const int bi = tok >> 4;
+        const int blk =
+            bi < pa.max_blocks ? __ldg(pa.block_table + (int64_t)b * pa.max_blocks + bi) : -1;
+        if (blk < 0 || blk >= pa.num_blocks) {
+          if (status) atomicOr(status, KVB_STATUS_BAD_BLOCK);
+        } else {
+          const int slot = tok & 15;
+          const int64_t hb = (int64_t)blk * pa.num_kv_heads + kvh;
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(
+              pa.pool + (((int64_t)blk * 2 + kv) * pa.num_kv_heads + kvh) * 16 * D +
+              (int64_t)slot * D + ch * 16));
+          float sc[16];
+          if (kv == 0) {
+            const float s = __ldg(pa.k_scale + hb * 16 + slot);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) sc[e] = s;
+          } else {
+            const float4* sp = reinterpret_cast<const float4*>(pa.v_scale + hb * D + ch * 16);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float4 f = __ldg(sp + e);
+              sc[4 * e] = f.x; sc[4 * e + 1] = f.y; sc[4 * e + 2] = f.z; sc[4 * e + 3] = f.w;
+            }
+          }
+          // int8 -> fp32 exactly: bias the byte to unsigned, drop it into the
+          // mantissa of 2^23, subtract 2^23 + 128.
+          const uint32_t qw[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u,
+                                  q.w ^ 0x80808080u};
+          uint32_t o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t word = qw[e >> 1];
+            const int sh = (e & 1) * 2;
+            const float f0 = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7650 + sh)) -
+                             8388736.f;
+            const float f1 = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7651 + sh)) -
+                             8388736.f;
+            o[e] = pack2<T>(f0 * sc[2 * e], f1 * sc[2 * e + 1]);
+          }
+          w0 = make_uint4(o[0], o[1], o[2], o[3]);
+          w1 = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+      } else {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            fresh + (int64_t)b * f_bs + (int64_t)kvh * f_hs + (int64_t)(tok - P) * f_rs + ch * 16);
+        w0 = __ldg(src);
+        w1 = __ldg(src + 1);
+      }
+    }
+    uint8_t* rowp = dst + (ch >> 2) * G::ATOM_BYTES + row * 128;
+    const int u = (ch & 3) * 2;
+    *reinterpret_cast<uint4*>(rowp + ((u ^ (row & 7)) << 4)) = w0;
+    *reinterpret_cast<uint4*>(rowp + (((u + 1) ^ (row & 7)) << 4)) = w1;
+  }
+}
+
+template <typename T, int D, bool PAGED>
+__global__ void __launch_bounds__(Roles<PAGED>::kThreads)
+    kvb_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const DenseArgs a,
+                       const PagedArgs pa) {
+  using G = Geo<D>;
+  constexpr int kWarpTma = Roles<PAGED>::kWarpTma;
+  constexpr int kWarpMma = Roles<PAGED>::kWarpMma;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -392,7 +504,11 @@ __global__ void __launch_bounds__(kThreads)
   }
   const int kvh = head[0] / a.group;
   int q_len = a.q_len, kv_len = a.kv_len, q_base = 0, k_base = 0, tb = b;
-  if (a.cu_q != nullptr) {
+  int P = 0;  // paged: cached-prefix tokens of this sequence
+  if (PAGED) {
+    P = pa.prefix_lens ? pa.prefix_lens[b] : pa.prefix_len;
+    kv_len = P + q_len;
+  } else if (a.cu_q != nullptr) {
     q_base = a.cu_q[b];
     q_len = a.cu_q[b + 1] - q_base;
     k_base = a.cu_k[b];
@@ -425,9 +541,9 @@ __global__ void __launch_bounds__(kThreads)
     }
     ptx::mbar_init(bar(BAR_DRAIN), 1);
     for (int st = 0; st < G::NS; ++st) {
-      ptx::mbar_init(bar(BAR_K_FULL + st), 1);
+      ptx::mbar_init(bar(BAR_K_FULL + st), PAGED ? Roles<PAGED>::kConvWarps : 1);
       ptx::mbar_init(bar(BAR_K_EMPTY + st), 1);
-      ptx::mbar_init(bar(BAR_V_FULL + st), 1);
+      ptx::mbar_init(bar(BAR_V_FULL + st), PAGED ? Roles<PAGED>::kConvWarps : 1);
       ptx::mbar_init(bar(BAR_V_EMPTY + st), 1);
     }
     ctl->abort_flag = 0;
@@ -435,8 +551,10 @@ __global__ void __launch_bounds__(kThreads)
   }
   if (warp == kWarpTma && lane == 0) {
     ptx::prefetch_tmap(&tm_q);
-    ptx::prefetch_tmap(&tm_k);
-    ptx::prefetch_tmap(&tm_v);
+    if (!PAGED) {
+      ptx::prefetch_tmap(&tm_k);
+      ptx::prefetch_tmap(&tm_v);
+    }
   }
   if (warp == kWarpMma) {
     ptx::tmem_alloc(ptx::smem_u32(&ctl->tmem_base), G::TMEM_COLS);
@@ -448,7 +566,49 @@ __global__ void __launch_bounds__(kThreads)
   const uint32_t tmem = ctl->tmem_base;
   if (threadIdx.x == 0) KVB_TRACE_AT(0);
 
-  if (warp == kWarpTma) {
+  if (PAGED && warp >= kWarpTma && warp < kWarpTma + Roles<PAGED>::kConvWarps) {
+    // ===================================================== paged gather
+    const int ct = threadIdx.x - kWarpTma * 32;
+    constexpr int nct = Roles<PAGED>::kConvWarps * 32;
+    if (n_max > 0) {
+      if (ct == 0) {
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl) {
+          if (n_t[sl] == 0) continue;
+          ptx::mbar_arrive_expect_tx(bar(BAR_Q_FULL + sl), G::TILE_BYTES);
+#pragma unroll
+          for (int at = 0; at < G::NATOM; ++at)
+            ptx::tma_load_4d(ptx::smem_u32(sQ + sl * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_q,
+                             at * 64, q0[sl], head[sl], b, bar(BAR_Q_FULL + sl));
+        }
+      }
+#pragma unroll 1
+      for (int j = 0; j < n_max; ++j) {
+        const int st = j % G::NS;
+        const uint32_t ph = (j / G::NS) & 1;
+        bool ok = wait_bar(bar(BAR_K_EMPTY + st), ph ^ 1, abort_flag, a.status,
+                           KVB_STATUS_LOAD_WAIT);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        gather_kv_tile<T, D>(sK + st * G::TILE_BYTES, pa, b, kvh, j * BN, P, kv_len, 0, ct, nct,
+                             a.status);
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(BAR_K_FULL + st));
+        ok = wait_bar(bar(BAR_V_EMPTY + st), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        gather_kv_tile<T, D>(sV + st * G::TILE_BYTES, pa, b, kvh, j * BN, P, kv_len, 1, ct, nct,
+                             a.status);
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(BAR_V_FULL + st));
+      }
+      if (*abort_flag && ct == 0) {
+        // Drain the Q loads this thread issued before leaving.
+        for (int sl = 0; sl < kSlots; ++sl)
+          if (n_t[sl] > 0) wait_bar(bar(BAR_Q_FULL + sl), 0, abort_flag, nullptr, 0);
+      }
+    }
+  } else if (!PAGED && warp == kWarpTma) {
     // ================================================================ TMA
     if (lane == 0 && n_max > 0) {
 #pragma unroll
@@ -827,7 +987,7 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
   a.scale_log2 = p.softmax_scale * 1.4426950408889634f;
   a.status = p.status;
 
-  auto kern = kvb_prefill_dense_kernel<T, D>;
+  auto kern = kvb_prefill_kernel<T, D, false>;
   static thread_local int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -841,7 +1001,71 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
   const int q_tiles = (p.q_len + BM - 1) / BM;
   dim3 grid = a.pair_heads ? dim3(q_tiles, p.num_q_heads / 2, p.batch)
                            : dim3((q_tiles + 1) / 2, p.num_q_heads, p.batch);
-  kern<<<grid, kThreads, G::SMEM_BYTES, stream>>>(tq, tk, tv, a);
+  PagedArgs none = {};
+  kern<<<grid, Roles<false>::kThreads, G::SMEM_BYTES, stream>>>(tq, tk, tv, a, none);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return fail(KVB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  return KVB_OK;
+}
+
+template <typename T, int D>
+static int launch_paged(const KvbPagedPrefillParams& p, cudaStream_t stream) {
+  using G = Geo<D>;
+  CUtensorMap tq;
+  std::string err;
+  if (!make_map(&tq, p.q, p.dtype, D, p.q_len, p.num_q_heads, p.batch, p.q_row_stride,
+                p.q_head_stride, p.batch > 1 ? p.q_batch_stride : 8, &err))
+    return fail(KVB_ERR_INVALID, err);
+  DenseArgs a = {};
+  a.o = p.o;
+  a.lse = p.lse;
+  a.o_bs = p.o_batch_stride;
+  a.o_hs = p.o_head_stride;
+  a.o_rs = p.o_row_stride;
+  a.lse_bs = p.lse_batch_stride;
+  a.lse_hs = p.lse_head_stride;
+  a.q_len = p.q_len;
+  a.kv_len = p.prefix_len + p.q_len;
+  a.group = p.num_q_heads / p.num_kv_heads;
+  a.pair_heads = (a.group % 2 == 0) ? 1 : 0;
+  a.causal = p.causal;
+  a.scale_log2 = p.softmax_scale * 1.4426950408889634f;
+  a.status = p.status;
+  PagedArgs pa;
+  pa.pool = p.kv_pool;
+  pa.k_scale = p.k_scale;
+  pa.v_scale = p.v_scale;
+  pa.block_table = p.block_tables;
+  pa.prefix_lens = p.prefix_lens;
+  pa.k_new = p.k_new;
+  pa.v_new = p.v_new;
+  pa.kn_bs = p.k_new_batch_stride;
+  pa.kn_hs = p.k_new_head_stride;
+  pa.kn_rs = p.k_new_row_stride;
+  pa.vn_bs = p.v_new_batch_stride;
+  pa.vn_hs = p.v_new_head_stride;
+  pa.vn_rs = p.v_new_row_stride;
+  pa.max_blocks = p.max_blocks_per_seq;
+  pa.num_blocks = p.num_blocks;
+  pa.num_kv_heads = p.num_kv_heads;
+  pa.prefix_len = p.prefix_len;
+
+  auto kern = kvb_prefill_kernel<T, D, true>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         G::SMEM_BYTES);
+    if (e != cudaSuccess)
+      return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    configured_device = dev;
+  }
+  const int q_tiles = (p.q_len + BM - 1) / BM;
+  dim3 grid = a.pair_heads ? dim3(q_tiles, p.num_q_heads / 2, p.batch)
+                           : dim3((q_tiles + 1) / 2, p.num_q_heads, p.batch);
+  kern<<<grid, Roles<true>::kThreads, G::SMEM_BYTES, stream>>>(tq, tq, tq, a, pa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return fail(KVB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
@@ -954,6 +1178,59 @@ extern "C" int kvb_flash_attn_fwd(const void* q, const void* k, const void* v, v
   p.lse_head_stride = seqlen;
   p.lse_batch_stride = (int64_t)heads * seqlen;
   return kvb_prefill_fwd(&p, stream);
+}
+
+static int validate_paged(const KvbPagedPrefillParams& p) {
+  if (p.dtype != KVB_DTYPE_BF16 && p.dtype != KVB_DTYPE_FP16)
+    return fail(KVB_ERR_INVALID, "dtype must be KVB_DTYPE_BF16 or KVB_DTYPE_FP16");
+  if (p.head_dim != 64 && p.head_dim != 96 && p.head_dim != 128)
+    return fail(KVB_ERR_INVALID,
+                "head_dim must be one of 64, 96, 128, got " + std::to_string(p.head_dim));
+  if (p.batch < 1 || p.num_q_heads < 1 || p.num_kv_heads < 1)
+    return fail(KVB_ERR_INVALID, "batch and head counts must be positive");
+  if (p.num_q_heads % p.num_kv_heads)
+    return fail(KVB_ERR_INVALID, "num_q_heads must be divisible by num_kv_heads");
+  if (p.batch > 65535 || p.num_q_heads > 65535)
+    return fail(KVB_ERR_UNSUPPORTED, "batch and num_q_heads must be <= 65535");
+  if (p.causal < 0 || p.causal > 2)
+    return fail(KVB_ERR_INVALID, "causal must be 0 (none), 1 (bottom-right) or 2 (top-left)");
+  if (p.q_len < 0 || p.prefix_len < 0)
+    return fail(KVB_ERR_INVALID, "q_len and prefix_len must be non-negative");
+  if (p.block_size != 16)
+    return fail(KVB_ERR_UNSUPPORTED, "block_size must be 16");
+  if (p.num_blocks < 1 || p.max_blocks_per_seq < 0)
+    return fail(KVB_ERR_INVALID, "num_blocks must be positive");
+  if ((int64_t)p.max_blocks_per_seq * 16 < p.prefix_len)
+    return fail(KVB_ERR_INVALID, "block table too short for prefix_len");
+  if (!p.q || !p.o || !p.kv_pool || !p.k_scale || !p.v_scale || !p.block_tables)
+    return fail(KVB_ERR_INVALID, "q, o, kv_pool, scales and block_tables must be non-null");
+  if (p.q_len > 0 && (!p.k_new || !p.v_new))
+    return fail(KVB_ERR_INVALID, "k_new and v_new must be non-null when q_len > 0");
+  if (!aligned16(p.q) || !aligned16(p.o) || !aligned16(p.kv_pool) || !aligned16(p.v_scale) ||
+      (p.k_new && !aligned16(p.k_new)) || (p.v_new && !aligned16(p.v_new)))
+    return fail(KVB_ERR_INVALID, "q, o, k_new, v_new, kv_pool and v_scale must be 16-byte aligned");
+  const int64_t st[] = {p.q_head_stride, p.q_row_stride, p.o_head_stride, p.o_row_stride,
+                        p.k_new_head_stride, p.k_new_row_stride, p.v_new_head_stride,
+                        p.v_new_row_stride};
+  for (int64_t s : st)
+    if (s <= 0 || (s % 8) != 0)
+      return fail(KVB_ERR_INVALID, "row and head strides must be positive multiples of 8 elements");
+  return KVB_OK;
+}
+
+extern "C" int kvb_paged_prefill_fwd(const KvbPagedPrefillParams* params, void* stream) {
+  if (!params) return fail(KVB_ERR_INVALID, "params is NULL");
+  const KvbPagedPrefillParams& p = *params;
+  int rc = validate_paged(p);
+  if (rc != KVB_OK) return rc;
+  if (p.q_len == 0) return KVB_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool bf = p.dtype == KVB_DTYPE_BF16;
+  switch (p.head_dim) {
+    case 64: return bf ? launch_paged<__nv_bfloat16, 64>(p, s) : launch_paged<__half, 64>(p, s);
+    case 96: return bf ? launch_paged<__nv_bfloat16, 96>(p, s) : launch_paged<__half, 96>(p, s);
+    default: return bf ? launch_paged<__nv_bfloat16, 128>(p, s) : launch_paged<__half, 128>(p, s);
+  }
 }
 
 extern "C" const char* kvb_last_error(void) { return g_last_error.c_str(); }

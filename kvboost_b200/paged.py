@@ -1,0 +1,295 @@
+"""Device-resident int8 paged KV pool and the paged reuse-prefill op.
+
+The bookkeeping mirrors KVBoost's CPU pool so block tables are identical:
+
+* ``DeviceBlockAllocator`` -- ``BlockAllocator`` (``cpu_paged/block_allocator.py``):
+  free list ``[0 .. num_blocks-1]`` popped from the end (``:76``, ``:93``), ref
+  counts, ``fork`` (``:109-119``), copy-on-write ``ensure_writable``
+  (``:121-141``), ``free`` (``:98-107``), ``free_blocks`` / ``used_blocks`` /
+  ``utilization``.  The storage is on the GPU and int8: per layer
+  ``[num_blocks, 2, num_kv_heads, 16, head_dim]`` (the reference pool's
+  layout, ``:67-73``) plus per-block scales.
+* ``DeviceChunkMapper`` -- ``ChunkBlockMapper`` (``cpu_paged/chunk_to_blocks.py:57-139``):
+  ``ceil(len/16)`` fresh blocks per new chunk, a fork of the same ids for a
+  chunk already loaded, tables concatenated in chunk order, ``on_evict``.
+
+Chunks are stored KIVI int8 exactly as ``quantize_kv(bits=8)`` produces them
+(``kv_quantize.py:73-100``): K with one float16 scale per token, V with one
+float16 scale per channel of the chunk.  ``quantize_chunk_int8`` reproduces
+that arithmetic on the GPU bit for bit (torch float16 ops round each result
+like the reference's CPU ops).  The kernel reads the scales as float32
+copies of those float16 values.
+
+``paged_prefill_attention`` runs the suffix prefill over the pool with the
+block-table gather and the int8 dequantisation fused into the kernel's K/V
+load stage (``kvb_paged_prefill_fwd``).
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from .ops import _DTYPES, _check_tensor, _stream_handle, status_word
+
+BLOCK_SIZE = 16
+
+
+def quantize_chunk_int8(key: torch.Tensor, val: torch.Tensor):
+    """KIVI int8 of one chunk, same arithmetic as ``_quantize_int8`` (``kv_quantize.py:73-100``).
+
+    key/val: ``[..., S, D]`` float16.  Returns ``(key_q int8, key_scale fp16 [...,S,1],
+    val_q int8, val_scale fp16 [...,1,D])``.
+    """
+    key = key.to(torch.float16)
+    val = val.to(torch.float16)
+    key_amax = key.abs().amax(dim=-1, keepdim=True).clamp(min=1e-8)
+    key_scale = key_amax / 127.0
+    key_q = (key / key_scale).round().clamp(-128, 127).to(torch.int8)
+    val_amax = val.abs().amax(dim=-2, keepdim=True).clamp(min=1e-8)
+    val_scale = val_amax / 127.0
+    val_q = (val / val_scale).round().clamp(-128, 127).to(torch.int8)
+    return key_q, key_scale.to(torch.float16), val_q, val_scale.to(torch.float16)
+
+
+class DeviceBlockAllocator:
+    """Block allocator over a GPU int8 KV pool (``BlockAllocator`` semantics)."""
+
+    def __init__(self, num_layers: int, num_heads: int, head_dim: int, num_blocks: int = 4096,
+                 block_size: int = BLOCK_SIZE, device="cuda") -> None:
+        if block_size != BLOCK_SIZE:
+            raise ValueError("the paged kernels use 16-token blocks")
+        self.num_layers = num_layers
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.num_blocks = num_blocks
+        self.block_size = block_size
+        self.device = torch.device(device)
+        self.pools: List[torch.Tensor] = [
+            torch.zeros(num_blocks, 2, num_heads, block_size, head_dim, dtype=torch.int8,
+                        device=self.device) for _ in range(num_layers)]
+        # float16 scales as the reference stores them, and the float32 copies the kernel reads
+        self.k_scale16 = [torch.zeros(num_blocks, num_heads, block_size, dtype=torch.float16,
+                                      device=self.device) for _ in range(num_layers)]
+        self.v_scale16 = [torch.zeros(num_blocks, num_heads, head_dim, dtype=torch.float16,
+                                      device=self.device) for _ in range(num_layers)]
+        self.k_scale = [torch.zeros(num_blocks, num_heads, block_size, dtype=torch.float32,
+                                    device=self.device) for _ in range(num_layers)]
+        self.v_scale = [torch.zeros(num_blocks, num_heads, head_dim, dtype=torch.float32,
+                                    device=self.device) for _ in range(num_layers)]
+        self._free: List[int] = list(range(num_blocks))
+        self._ref_count: Dict[int, int] = {}
+        self._lock = threading.Lock()
+
+    # ── allocation (block_allocator.py:85-141) ─────────────────────────────────
+    def allocate(self, n: int) -> List[int]:
+        with self._lock:
+            if len(self._free) < n:
+                raise RuntimeError(
+                    f"BlockAllocator OOM: requested {n} blocks but only "
+                    f"{len(self._free)} free (pool size {self.num_blocks}).")
+            ids = [self._free.pop() for _ in range(n)]
+            for b in ids:
+                self._ref_count[b] = 1
+            return ids
+
+    def free(self, block_ids: List[int]) -> None:
+        with self._lock:
+            for b in block_ids:
+                rc = self._ref_count.get(b, 0)
+                if rc <= 1:
+                    self._ref_count.pop(b, None)
+                    self._free.append(b)
+                else:
+                    self._ref_count[b] = rc - 1
+
+    def fork(self, block_ids: List[int]) -> List[int]:
+        with self._lock:
+            for b in block_ids:
+                self._ref_count[b] = self._ref_count.get(b, 1) + 1
+        return list(block_ids)
+
+    def ensure_writable(self, block_id: int) -> int:
+        with self._lock:
+            rc = self._ref_count.get(block_id, 1)
+            if rc <= 1:
+                return block_id
+            if not self._free:
+                raise RuntimeError("BlockAllocator OOM during copy-on-write.")
+            new_id = self._free.pop()
+            self._ref_count[new_id] = 1
+            self._ref_count[block_id] = rc - 1
+        for t in (*self.pools, *self.k_scale16, *self.v_scale16, *self.k_scale, *self.v_scale):
+            t[new_id].copy_(t[block_id])
+        return new_id
+
+    @property
+    def free_blocks(self) -> int:
+        return len(self._free)
+
+    @property
+    def used_blocks(self) -> int:
+        return self.num_blocks - len(self._free)
+
+    def utilization(self) -> float:
+        return self.used_blocks / self.num_blocks
+
+    # ── storage ────────────────────────────────────────────────────────────────
+    def write_chunk_int8(self, layer: int, block_ids: List[int], key_q: torch.Tensor,
+                         key_scale: torch.Tensor, val_q: torch.Tensor,
+                         val_scale: torch.Tensor) -> None:
+        """Store one quantised chunk (``[1 or H.., S, D]`` as ``quantize_kv`` returns it).
+
+        Token t of the chunk goes to ``block_ids[t // 16]``, slot ``t % 16``; every
+        block of the chunk gets the chunk's per-channel V scale.
+        """
+        H, D, bs = self.num_heads, self.head_dim, self.block_size
+        kq = key_q.reshape(H, -1, D)
+        S = kq.shape[1]
+        n = len(block_ids)
+        if n * bs < S:
+            raise ValueError(f"{n} blocks cannot hold {S} tokens")
+        idx = torch.as_tensor(block_ids, dtype=torch.long, device=self.device)
+
+        def blocked(t, last):  # [H, S, last] -> [n, H, bs, last], zero padded
+            pad = torch.zeros(H, n * bs, last, dtype=t.dtype, device=self.device)
+            pad[:, :S] = t.to(self.device)
+            return pad.view(H, n, bs, last).permute(1, 0, 2, 3)
+
+        pool = self.pools[layer]
+        pool[idx, 0] = blocked(kq, D)
+        pool[idx, 1] = blocked(val_q.reshape(H, -1, D), D)
+        ks = blocked(key_scale.reshape(H, -1, 1).to(torch.float16), 1)[..., 0]   # [n, H, bs]
+        self.k_scale16[layer][idx] = ks
+        self.k_scale[layer][idx] = ks.float()
+        vs = val_scale.reshape(H, D).to(torch.float16).to(self.device)
+        self.v_scale16[layer][idx] = vs.unsqueeze(0).expand(n, H, D)
+        self.v_scale[layer][idx] = vs.float().unsqueeze(0).expand(n, H, D)
+
+    def read_dequant(self, layer: int, block_ids: List[int], seq_len: int):
+        """float16 K/V ``[H, seq_len, D]`` exactly as the reference's dequantise+gather."""
+        idx = torch.as_tensor(block_ids, dtype=torch.long, device=self.device)
+        g = self.pools[layer][idx]                                 # [n, 2, H, bs, D]
+        n, H, bs, D = g.shape[0], self.num_heads, self.block_size, self.head_dim
+        kq = g[:, 0].permute(1, 0, 2, 3).reshape(H, n * bs, D)[:, :seq_len]
+        vq = g[:, 1].permute(1, 0, 2, 3).reshape(H, n * bs, D)[:, :seq_len]
+        ks = self.k_scale16[layer][idx].permute(1, 0, 2).reshape(H, n * bs)[:, :seq_len]
+        vs = self.v_scale16[layer][idx][torch.arange(seq_len, device=self.device) // bs]
+        k = kq.to(torch.float16) * ks.unsqueeze(-1)
+        v = vq.to(torch.float16) * vs.permute(1, 0, 2)
+        return k, v
+
+
+class DeviceChunkMapper:
+    """``ChunkBlockMapper`` over a ``DeviceBlockAllocator``."""
+
+    def __init__(self, allocator: DeviceBlockAllocator) -> None:
+        self.allocator = allocator
+        self._chunk_blocks: Dict[str, List[int]] = {}
+        self._lock = threading.Lock()
+
+    def load_chunk(self, chunk_id: str, layers_kv: Sequence[Tuple[torch.Tensor, torch.Tensor]],
+                   quantized: Optional[Sequence[tuple]] = None) -> List[int]:
+        """Store a chunk (per layer (K, V) ``[1, H, S, D]``, or already-quantised
+        layers ``(key_q, key_scale, val_q, val_scale)``) and return its blocks."""
+        with self._lock:
+            if chunk_id in self._chunk_blocks:
+                return self.allocator.fork(self._chunk_blocks[chunk_id])
+        if quantized is None:
+            quantized = [quantize_chunk_int8(k, v) for k, v in layers_kv]
+        S = quantized[0][0].shape[-2]
+        bs = self.allocator.block_size
+        block_ids = self.allocator.allocate((S + bs - 1) // bs)
+        for layer, (kq, ks, vq, vs) in enumerate(quantized):
+            self.allocator.write_chunk_int8(layer, block_ids, kq, ks, vq, vs)
+        with self._lock:
+            self._chunk_blocks[chunk_id] = block_ids
+        return list(block_ids)
+
+    def build_block_table(self, chunks) -> List[int]:
+        """Concatenate the chunks' block lists in order (``chunk_to_blocks.py:105-125``)."""
+        table: List[int] = []
+        for chunk_id, layers_kv in chunks:
+            table.extend(self.load_chunk(chunk_id, layers_kv))
+        return table
+
+    def on_evict(self, chunk_id: str) -> None:
+        with self._lock:
+            ids = self._chunk_blocks.pop(chunk_id, None)
+        if ids is not None:
+            self.allocator.free(ids)
+
+    def loaded_chunks(self) -> int:
+        return len(self._chunk_blocks)
+
+
+def block_table_tensor(tables: Sequence[Sequence[int]], device) -> torch.Tensor:
+    """Pad per-sequence tables into a device int32 ``[B, max_blocks]`` array."""
+    mb = max(1, max(len(t) for t in tables))
+    out = torch.zeros(len(tables), mb, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        if t:
+            out[i, :len(t)] = torch.as_tensor(t, dtype=torch.int32)
+    return out.to(device)
+
+
+def paged_prefill_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                            allocator: DeviceBlockAllocator, layer: int,
+                            block_tables: torch.Tensor, prefix_len: int,
+                            prefix_lens: Optional[torch.Tensor] = None,
+                            softmax_scale: Optional[float] = None, causal: bool = True,
+                            out: Optional[torch.Tensor] = None, return_lse: bool = True):
+    """Suffix prefill over an int8 paged prefix (``kvb_paged_prefill_fwd``).
+
+    q: ``[B, Hq, q_len, D]``; k_new/v_new: the suffix's own ``[B, Hkv, q_len, D]``;
+    block_tables: device int32 ``[B, max_blocks]``; ``prefix_len``: cached tokens
+    (``prefix_lens`` device int32 ``[B]`` for per-sequence lengths, with
+    ``prefix_len`` their maximum).  Sequence b attends to its prefix followed by
+    its suffix, bottom-right causal.  Returns ``(o, lse)``.
+    """
+    _check_tensor("q", q, 4)
+    _check_tensor("k_new", k_new, 4)
+    _check_tensor("v_new", v_new, 4)
+    B, Hq, Sq, D = q.shape
+    if k_new.shape != v_new.shape or k_new.shape[0] != B or k_new.shape[2] != Sq or k_new.shape[3] != D:
+        raise RuntimeError("k_new/v_new must be [B, Hkv, q_len, D] matching q")
+    Hkv = k_new.shape[1]
+    if Hkv != allocator.num_heads or D != allocator.head_dim:
+        raise RuntimeError("pool heads / head_dim do not match the query")
+    if block_tables.dtype != torch.int32 or not block_tables.is_cuda or block_tables.dim() != 2 \
+            or not block_tables.is_contiguous():
+        raise RuntimeError("block_tables must be a contiguous 2-D int32 CUDA tensor")
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty_like(q)
+    lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device) if return_lse else None
+    p = _lib.KvbPagedPrefillParams()
+    p.dtype = _DTYPES[q.dtype]
+    p.head_dim, p.batch, p.num_q_heads, p.num_kv_heads = D, B, Hq, Hkv
+    p.q_len, p.causal, p.softmax_scale = Sq, 1 if causal else 0, float(softmax_scale)
+    p.q, p.o = q.data_ptr(), out.data_ptr()
+    p.lse = lse.data_ptr() if lse is not None else None
+    p.q_batch_stride, p.q_head_stride, p.q_row_stride = q.stride(0), q.stride(1), q.stride(2)
+    p.o_batch_stride, p.o_head_stride, p.o_row_stride = out.stride(0), out.stride(1), out.stride(2)
+    if lse is not None:
+        p.lse_batch_stride, p.lse_head_stride = lse.stride(0), lse.stride(1)
+    p.k_new, p.v_new = k_new.data_ptr(), v_new.data_ptr()
+    p.k_new_batch_stride, p.k_new_head_stride, p.k_new_row_stride = k_new.stride()[:3]
+    p.v_new_batch_stride, p.v_new_head_stride, p.v_new_row_stride = v_new.stride()[:3]
+    p.kv_pool = allocator.pools[layer].data_ptr()
+    p.k_scale = allocator.k_scale[layer].data_ptr()
+    p.v_scale = allocator.v_scale[layer].data_ptr()
+    p.num_blocks, p.block_size = allocator.num_blocks, allocator.block_size
+    p.block_tables, p.max_blocks_per_seq = block_tables.data_ptr(), block_tables.shape[1]
+    p.prefix_len = int(prefix_len)
+    p.prefix_lens = prefix_lens.data_ptr() if prefix_lens is not None else None
+    p.status = status_word(q.device).data_ptr()
+    with torch.cuda.device(q.device):
+        rc = _lib.load().kvb_paged_prefill_fwd(p, _stream_handle(q.device))
+    _lib.check(rc, "kvb_paged_prefill_fwd")
+    return out, lse

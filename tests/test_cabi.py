@@ -83,3 +83,26 @@ def test_compat_entry_validates_head_dim(lib):
     rc = lib.kvb_flash_attn_fwd(4096, 4096, 4096, 4096, None, 1, 2, 8, 48, 0, 0.1, 1, None)
     assert rc == _lib.KVB_ERR_INVALID
     assert b"head_dim" in lib.kvb_last_error()
+
+
+def test_ctypes_layouts_match_c_compiler(tmp_path):
+    """sizeof/offsetof of both parameter structs as gcc sees the header."""
+    from kvboost_b200._build import INCLUDE
+    structs = {"KvbPrefillParams": _lib.KvbPrefillParams,
+               "KvbPagedPrefillParams": _lib.KvbPagedPrefillParams}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "kvb_attn.h"', 'int main(){']
+    for name, cls in structs.items():
+        lines.append(f'printf("{name} %zu\\n", sizeof({name}));')
+        for f, _ in cls._fields_:
+            lines.append(f'printf("{name}.{f} %zu\\n", offsetof({name}, {f}));')
+    lines.append('return 0;}')
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", INCLUDE, "-o", str(exe), str(src)], check=True)
+    got = dict(l.split() for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                  check=True).stdout.splitlines())
+    for name, cls in structs.items():
+        assert int(got[name]) == ctypes.sizeof(cls)
+        for f, _ in cls._fields_:
+            assert int(got[f"{name}.{f}"]) == getattr(cls, f).offset, f"{name}.{f}"

@@ -1,0 +1,145 @@
+"""GPU parity of the int8 paged reuse prefill (config-5 semantics).
+
+The cached prefix is KIVI-int8 quantised per 128-token chunk, stored in
+16-token blocks of a device pool at a seeded random permutation of block ids,
+and attended to together with the suffix's own fresh K/V.  The oracle is the
+reference's host path restated: dequantise (``float16(q * scale)``), gather by
+the block table, cast to the compute dtype, concatenate, bottom-right causal
+attention.  Tolerances: max-abs 2e-2 (bf16), 1e-2 (fp16), LSE 2e-3.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oattn
+from oracle import kv_quant as oq
+from oracle import paged as opaged
+
+pytestmark = pytest.mark.gpu
+TOL = {torch.bfloat16: 2e-2, torch.float16: 1e-2}
+
+
+@pytest.fixture(autouse=True)
+def _gpu():
+    if not torch.cuda.is_available() or torch.cuda.get_device_capability()[0] != 10:
+        pytest.skip("needs an sm_100 (B200) device")
+    from kvboost_b200 import ops
+    ops.read_status(torch.device("cuda"))
+    yield
+
+
+def test_gpu_quantiser_matches_reference_bit_exact():
+    """quantize_chunk_int8 on the GPU == the reference's _quantize_int8 (kv_quantize.py:73-100)."""
+    from kvboost_b200.paged import quantize_chunk_int8
+    g = torch.Generator().manual_seed(3)
+    for H, L, D in ((2, 128, 128), (8, 128, 64), (1, 100, 96)):
+        k = torch.randn(1, H, L, D, generator=g).to(torch.bfloat16).to(torch.float16)
+        v = (torch.randn(1, H, L, D, generator=g) * 3).to(torch.float16)
+        kq, ks, vq, vs = quantize_chunk_int8(k.cuda(), v.cuda())
+        rk, rks, rv, rvs = oq.quantize_int8(k.numpy(), v.numpy())
+        assert np.array_equal(kq.cpu().numpy(), rk) and np.array_equal(vq.cpu().numpy(), rv)
+        assert np.array_equal(ks.cpu().numpy().view(np.uint16), rks.view(np.uint16))
+        assert np.array_equal(vs.cpu().numpy().view(np.uint16), rvs.view(np.uint16))
+
+
+def _oracle_prefix(alloc, tbl, P):
+    pool = alloc.pools[0].cpu().numpy()
+    ks = alloc.k_scale16[0].cpu().numpy()
+    vs = alloc.v_scale16[0].cpu().numpy()
+    return opaged.dequant_gather(pool, ks, vs, tbl, P, 16)   # float16 [H, P, D]
+
+
+def _run_case(B, Hq, Hkv, D, chunk_sets, Sq, dtype, seed, num_blocks=512, rows=None):
+    from kvboost_b200.paged import (DeviceBlockAllocator, block_table_tensor,
+                                    paged_prefill_attention, quantize_chunk_int8)
+    g = torch.Generator().manual_seed(seed + 1)
+    # one pool shared by the batch, chunks stored at a seeded permutation of block ids
+    total = sum((L + 15) // 16 for cs in chunk_sets for L in cs)
+    assert total <= num_blocks
+    perm = torch.randperm(num_blocks, generator=g).tolist()
+    alloc = DeviceBlockAllocator(1, Hkv, D, num_blocks)
+    tables, pos = [], 0
+    for cs in chunk_sets:
+        tb = []
+        for L in cs:
+            n = (L + 15) // 16
+            ids = perm[pos:pos + n]
+            pos += n
+            k = torch.randn(1, Hkv, L, D, generator=g).to(torch.float16)
+            v = torch.randn(1, Hkv, L, D, generator=g).to(torch.float16)
+            alloc.write_chunk_int8(0, ids, *quantize_chunk_int8(k.cuda(), v.cuda()))
+            tb.extend(ids)
+        tables.append(tb)
+    prefix = [sum(cs) for cs in chunk_sets]
+    P = max(prefix)
+    q = torch.randn(B, Hq, Sq, D, generator=g).to(dtype)
+    kn = torch.randn(B, Hkv, Sq, D, generator=g).to(dtype)
+    vn = torch.randn(B, Hkv, Sq, D, generator=g).to(dtype)
+    bt = block_table_tensor(tables, "cuda")
+    pl = torch.tensor(prefix, dtype=torch.int32, device="cuda")
+    o, lse = paged_prefill_attention(q.cuda(), kn.cuda(), vn.cuda(), alloc, 0, bt, P,
+                                     prefix_lens=pl, softmax_scale=1.0 / math.sqrt(D))
+    torch.cuda.synchronize()
+    from kvboost_b200 import ops
+    assert ops.read_status(torch.device("cuda")) == 0
+    for b in range(B):
+        kp, vp = _oracle_prefix(alloc, tables[b], prefix[b]) if prefix[b] else (
+            np.zeros((Hkv, 0, D), np.float16), np.zeros((Hkv, 0, D), np.float16))
+        # the reference casts the float16 dequantised K/V to the model dtype
+        kp = torch.from_numpy(kp).to(dtype).float().numpy()
+        vp = torch.from_numpy(vp).to(dtype).float().numpy()
+        k_all = np.concatenate([kp, kn[b].float().numpy()], axis=1)[None]
+        v_all = np.concatenate([vp, vn[b].float().numpy()], axis=1)[None]
+        qb = q[b:b + 1].float().numpy()
+        ob = o[b:b + 1].float().cpu().numpy()
+        lb = lse[b:b + 1].cpu().numpy()
+        if rows is not None:  # the last `rows` queries only (same bottom-right offsets)
+            qb, ob, lb = qb[:, :, -rows:], ob[:, :, -rows:], lb[:, :, -rows:]
+        o_ref, l_ref = oattn.attention(qb, k_all, v_all, 1.0 / math.sqrt(D), True,
+                                       compute_dtype=np.float32)
+        err = np.abs(ob - o_ref).max()
+        assert err <= TOL[dtype], f"batch {b}: max-abs {err}"
+        assert np.abs(lb - l_ref).max() <= 2e-3
+
+
+def test_paged_config5_shape_reduced():
+    """GQA 8, D128, bf16: 8 cached chunks at a random block permutation + 200 new tokens."""
+    _run_case(1, 16, 2, 128, [[128] * 8], 200, torch.bfloat16, seed=5)
+
+
+def test_paged_ragged_batch():
+    """Per-sequence prefixes: full chunks, a partial last chunk, and no prefix at all."""
+    _run_case(3, 8, 2, 128, [[128, 128, 128], [128, 100], []], 130, torch.bfloat16, seed=6)
+
+
+@pytest.mark.parametrize("D,dtype", [(64, torch.float16), (96, torch.float16), (128, torch.float16),
+                                     (64, torch.bfloat16)])
+def test_paged_head_dims(D, dtype):
+    _run_case(2, 8, 4, D, [[128] * 3, [128] * 2], 77, dtype, seed=D)
+
+
+def test_paged_suffix_shorter_than_tile_mha():
+    _run_case(1, 4, 4, 128, [[128] * 5], 16, torch.bfloat16, seed=9)
+
+
+def test_paged_config5_full_size_last_rows():
+    """Full config 5 on one GPU: P=32768 int8 prefix in an 8192-block pool, 2048 new
+    tokens, Hq 64 / Hkv 8, D 128; the last 64 query rows of every head are checked."""
+    _run_case(1, 64, 8, 128, [[128] * 256], 2048, torch.bfloat16, seed=50, num_blocks=8192,
+              rows=64)
+
+
+def test_bad_block_id_is_reported_not_read():
+    from kvboost_b200 import ops
+    from kvboost_b200.paged import DeviceBlockAllocator, paged_prefill_attention
+    alloc = DeviceBlockAllocator(1, 2, 64, 8)
+    bt = torch.tensor([[0, 99]], dtype=torch.int32, device="cuda")  # 99 is outside the pool
+    q = torch.randn(1, 2, 8, 64, device="cuda", dtype=torch.bfloat16)
+    kn = torch.randn(1, 2, 8, 64, device="cuda", dtype=torch.bfloat16)
+    o, _ = paged_prefill_attention(q, kn, kn.clone(), alloc, 0, bt, 32)
+    torch.cuda.synchronize()
+    assert ops.read_status(torch.device("cuda")) & 16
+    assert torch.isfinite(o.float()).all()
