@@ -1,20 +1,27 @@
 """Prefill-attention benchmark (one JSON line on rank 0).
 
-Default workload ("reuse_prefill"): KVBoost's prefix-reuse prefill op --
-batch 4, 32 query heads over 8 KV heads (GQA 4), head_dim 128, bf16, a cached
-prefix of 7 chunks x 128 = 896 tokens plus a 256-token suffix (kv_len 1152,
-bottom-right causal offset 896), all N(0,1) from a seed.  One step = one
-launch of the prefill kernel over one such batch.
-
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
     python bench.py --impl reference ...   # the CPU restatement on host cores
 
-Timing: K steps are captured in one CUDA graph and replayed between two
-events on the launching stream (W warm-up steps replayed first).  The steps
-rotate over enough distinct input sets that the inputs touched (>126 MB) do
-not fit in L2, so every step reads cold data.  With N > 1 (torchrun) every
-rank runs its own batch (weak scaling, no collective on the data path); the
-elapsed time is the max over ranks.
+Workloads (seeded N(0,1) inputs with the shapes of the configs the
+reference's metric is defined on; the public datasets are not available):
+
+* ``reuse_prefill`` (default) -- prefix-reuse prefill op: batch 4, 32 query
+  heads over 8 KV heads, head_dim 128, bf16, 7 cached chunks x 128 = 896
+  tokens + 256 new tokens (kv_len 1152, bottom-right offset 896).
+* ``causal_op`` -- single causal op: batch 2, 16 heads, S 1024, D 64, bf16.
+* ``varlen_d96`` -- 64 requests, suffix ~ U{16..512}, prefix ~ 128*U{0..64},
+  32 heads MHA, D 96, fp16, packed varlen.
+* ``paged_long`` -- 32768-token int8 paged prefix (KIVI per 128-token chunk,
+  16-token blocks of an 8192-block pool at a seeded permutation) + 2048 new
+  tokens, 64 query / 8 KV heads, D 128, bf16.  With N GPUs the KV heads are
+  split across ranks (strong scaling; each rank holds its heads' pool shard).
+
+One step = one kernel launch over one batch.  K steps are captured in one
+CUDA graph and replayed between two events on the launching stream after W
+graph-replayed warm-up steps.  Steps rotate over enough input sets that the
+bytes touched exceed L2 (126 MB).  With N > 1 (torchrun) the elapsed time is
+the max over ranks; only that scalar crosses ranks (no data-path collective).
 """
 
 from __future__ import annotations
@@ -33,17 +40,8 @@ sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
 
-WORKLOADS = {
-    # name: (B, Hq, Hkv, Sq, P (cached prefix), D, dtype)
-    "reuse_prefill": dict(B=4, Hq=32, Hkv=8, Sq=256, P=896, D=128, dtype="bf16",
-                          desc="prefix-reuse prefill op: B4 Hq32/Hkv8 D128 bf16, "
-                               "7 cached chunks (896) + 256 new tokens"),
-    "causal_op": dict(B=2, Hq=16, Hkv=16, Sq=1024, P=0, D=64, dtype="bf16",
-                      desc="single causal op: B2 H16 S1024 D64 bf16"),
-}
-
-# dram__bytes_read.sum + dram__bytes_write.sum of one prefill launch from the
-# committed ncu capture (profiles/prefill_dense_reuse_b4h32kv8_d128.md).
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch from the committed
+# ncu captures (profiles/*.md), per workload.
 NCU_TRAFFIC_BYTES = {"reuse_prefill": 27335168}
 
 
@@ -53,22 +51,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kvboost", choices=["kvboost", "reference"])
-    ap.add_argument("--workload", default="reuse_prefill", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="reuse_prefill",
+                    choices=["reuse_prefill", "causal_op", "varlen_d96", "paged_long"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
     return ap.parse_args()
-
-
-def flops_of(w):
-    from oracle.attention import attention_flops
-    kv = w["P"] + w["Sq"]
-    return attention_flops([w["Sq"]] * w["B"], [kv] * w["B"], w["Hq"], w["D"], causal=True)
-
-
-def bytes_of(w):
-    s = 2
-    kv = w["P"] + w["Sq"]
-    return w["B"] * (2 * w["Hq"] * w["Sq"] * w["D"] * s + 2 * w["Hkv"] * kv * w["D"] * s)
 
 
 def measured_peaks():
@@ -80,6 +67,300 @@ def measured_peaks():
     return 1590.0, 6650.0, "fallback"
 
 
+# ───────────────────────────────────────────────────────────── workloads ──
+
+class Dense:
+    """Dense ``[B, H, S, D]`` prefill (configs 1 and 2)."""
+
+    def __init__(self, name, B, Hq, Hkv, Sq, P, D, dtype, desc):
+        self.name, self.B, self.Hq, self.Hkv, self.Sq, self.P, self.D = name, B, Hq, Hkv, Sq, P, D
+        self.dtype_name, self.desc = dtype, desc
+        self.kv = P + Sq
+        self.scaling = "weak"
+        self.bound = "tensor"
+
+    def flops(self):
+        from oracle.attention import attention_flops
+        return attention_flops([self.Sq] * self.B, [self.kv] * self.B, self.Hq, self.D)
+
+    def bytes(self):
+        return self.B * 2 * (2 * self.Hq * self.Sq * self.D + 2 * self.Hkv * self.kv * self.D)
+
+    def tokens(self):
+        return self.B * self.Sq
+
+    def config(self):
+        return {"batch": self.B, "q_heads": self.Hq, "kv_heads": self.Hkv, "q_len": self.Sq,
+                "kv_len": self.kv, "head_dim": self.D}
+
+    def setup(self, torch, dev, rank, world):
+        from kvboost_b200 import ops
+        dt = torch.bfloat16 if self.dtype_name == "bf16" else torch.float16
+        self.dt = dt
+        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        R = max(2, math.ceil(2 * L2_BYTES / self.bytes()))
+        self.sets_desc = f"inputs rotate over {R} sets ({R * self.bytes() / 2**20:.0f} MiB > L2)"
+        sets = []
+        for _ in range(R):
+            q = torch.randn(self.B, self.Hq, self.Sq, self.D, generator=g, device=dev).to(dt)
+            k = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(dt)
+            v = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(dt)
+            sets.append((q, k, v, torch.empty_like(q)))
+        scale = 1.0 / math.sqrt(self.D)
+
+        def step(i):
+            q, k, v, o = sets[i % R]
+            ops.prefill_attention(q, k, v, scale, True, out=o, return_lse=False)
+        return step
+
+    def e2e(self, torch, dev):
+        from kvboost_b200 import ops
+        hq = torch.randn(self.B, self.Hq, self.Sq, self.D).to(self.dt).pin_memory()
+        hk = torch.randn(self.B, self.Hkv, self.kv, self.D).to(self.dt).pin_memory()
+        hv = torch.randn(self.B, self.Hkv, self.kv, self.D).to(self.dt).pin_memory()
+        ho = torch.empty(self.B, self.Hq, self.Sq, self.D, dtype=self.dt).pin_memory()
+        scale = 1.0 / math.sqrt(self.D)
+
+        def step():
+            dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+            o, _ = ops.prefill_attention(dq, dk, dv, scale, True, return_lse=False)
+            ho.copy_(o, non_blocking=True)
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+        return step, h2d, ho.numel() * ho.element_size()
+
+    def cpu_sample(self, np):
+        """One batch element through the oracle (numpy float32)."""
+        from oracle.attention import attention, attention_flops
+        g = np.random.default_rng(0)
+        q = g.standard_normal((1, self.Hq, self.Sq, self.D), dtype=np.float32)
+        k = g.standard_normal((1, self.Hkv, self.kv, self.D), dtype=np.float32)
+        v = g.standard_normal((1, self.Hkv, self.kv, self.D), dtype=np.float32)
+        fl = attention_flops([self.Sq], [self.kv], self.Hq, self.D)
+
+        def run():
+            attention(q, k, v, 1.0 / math.sqrt(self.D), True, compute_dtype=np.float32)
+        return run, fl, f"1 of {self.B} batch elements"
+
+
+class Varlen:
+    """Config 4: packed varlen, 32 heads MHA, head_dim 96, fp16."""
+
+    def __init__(self):
+        import torch
+        self.name, self.Hq, self.Hkv, self.D, self.dtype_name = "varlen_d96", 32, 32, 96, "fp16"
+        g = torch.Generator().manual_seed(0)
+        self.sq, self.pre = [], []
+        for _ in range(64):
+            self.sq.append(int(torch.randint(16, 513, (1,), generator=g)))
+            self.pre.append(128 * int(torch.randint(0, 65, (1,), generator=g)))
+        self.skv = [a + b for a, b in zip(self.sq, self.pre)]
+        self.desc = ("varlen: 64 requests, suffix U{16..512}, prefix 128*U{0..64}, "
+                     "32 heads MHA, D96, fp16")
+        self.scaling = "weak"
+        self.bound = "hbm"
+
+    def flops(self):
+        from oracle.attention import attention_flops
+        return attention_flops(self.sq, self.skv, self.Hq, self.D)
+
+    def bytes(self):
+        return 2 * self.D * (2 * self.Hq * sum(self.sq) + 2 * self.Hkv * sum(self.skv))
+
+    def tokens(self):
+        return sum(self.sq)
+
+    def config(self):
+        return {"requests": 64, "q_heads": self.Hq, "kv_heads": self.Hkv, "head_dim": self.D,
+                "total_q": sum(self.sq), "total_kv": sum(self.skv)}
+
+    def _packed(self, torch, dev, g):
+        import numpy as np
+        cu_q = torch.tensor(np.concatenate([[0], np.cumsum(self.sq)]), dtype=torch.int32, device=dev)
+        cu_k = torch.tensor(np.concatenate([[0], np.cumsum(self.skv)]), dtype=torch.int32, device=dev)
+        q = torch.randn(sum(self.sq), self.Hq, self.D, generator=g, device=dev).half()
+        k = torch.randn(sum(self.skv), self.Hkv, self.D, generator=g, device=dev).half()
+        v = torch.randn(sum(self.skv), self.Hkv, self.D, generator=g, device=dev).half()
+        return q, k, v, cu_q, cu_k
+
+    def setup(self, torch, dev, rank, world):
+        from kvboost_b200 import ops
+        g = torch.Generator(device=dev).manual_seed(4 + rank)
+        R = 2  # one set is already > L2; two keep consecutive steps on distinct data
+        self.sets_desc = f"inputs rotate over {R} sets ({R * self.bytes() / 2**30:.1f} GiB > L2)"
+        sets = [self._packed(torch, dev, g) for _ in range(R)]
+        outs = [torch.empty_like(s[0]) for s in sets]
+
+        def step(i):
+            q, k, v, cq, ck = sets[i % R]
+            ops.prefill_attention_varlen(q, k, v, cq, ck, max(self.sq), max(self.skv),
+                                         1.0 / math.sqrt(self.D), True, out=outs[i % R],
+                                         return_lse=False)
+        return step
+
+    def e2e(self, torch, dev):
+        from kvboost_b200 import ops
+        q, k, v, cq, ck = self._packed(torch, "cpu", torch.Generator().manual_seed(9))
+        hq, hk, hv = (t.pin_memory() for t in (q, k, v))
+        ho = torch.empty_like(hq).pin_memory()
+        cq, ck = cq.to(dev), ck.to(dev)
+
+        def step():
+            dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+            o, _ = ops.prefill_attention_varlen(dq, dk, dv, cq, ck, max(self.sq), max(self.skv),
+                                                1.0 / math.sqrt(self.D), True, return_lse=False)
+            ho.copy_(o, non_blocking=True)
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+        return step, h2d, ho.numel() * ho.element_size()
+
+    def cpu_sample(self, np):
+        from oracle.attention import attention_varlen, attention_flops
+        n = 3  # the first 3 requests
+        g = np.random.default_rng(0)
+        sq, skv = self.sq[:n], self.skv[:n]
+        q = g.standard_normal((sum(sq), self.Hq, self.D), dtype=np.float32)
+        k = g.standard_normal((sum(skv), self.Hkv, self.D), dtype=np.float32)
+        v = g.standard_normal((sum(skv), self.Hkv, self.D), dtype=np.float32)
+        cq = np.concatenate([[0], np.cumsum(sq)])
+        ck = np.concatenate([[0], np.cumsum(skv)])
+        fl = attention_flops(sq, skv, self.Hq, self.D)
+
+        def run():
+            attention_varlen(q, k, v, cq, ck, 1.0 / math.sqrt(self.D), True,
+                             compute_dtype=np.float32)
+        return run, fl, f"the first {n} of 64 requests"
+
+
+class PagedLong:
+    """Config 5: int8 paged 32K prefix + 2048 new tokens, heads split over ranks."""
+
+    def __init__(self):
+        self.name = "paged_long"
+        self.B, self.Hq, self.Hkv, self.D, self.Sq, self.P = 1, 64, 8, 128, 2048, 32768
+        self.num_blocks = 8192
+        self.dtype_name = "bf16"
+        self.desc = ("paged int8 reuse: P 32768 (KIVI int8, 16-token blocks, 8192-block pool, "
+                     "seeded permutation) + 2048 new tokens, Hq64/Hkv8, D128, bf16")
+        self.scaling = "strong"
+        self.bound = "tensor"
+        self.world = 1
+
+    def local_heads(self, rank, world):
+        if self.Hkv % world:
+            raise SystemExit(f"paged_long splits 8 KV heads; --gpus {world} does not divide 8")
+        hk = self.Hkv // world
+        return hk, hk * (self.Hq // self.Hkv)
+
+    def flops(self):
+        from oracle.attention import attention_flops
+        _, hq = self.local_heads(0, self.world)
+        return attention_flops([self.Sq], [self.P + self.Sq], hq, self.D)
+
+    def bytes(self):
+        hk, hq = self.local_heads(0, self.world)
+        nblk = self.P // 16
+        pool = nblk * hk * (2 * 16 * self.D + 4 * 16 + 4 * self.D)   # int8 K/V + fp32 scales
+        return pool + 2 * (2 * hq * self.Sq * self.D + 2 * hk * self.Sq * self.D)
+
+    def tokens(self):
+        return self.Sq
+
+    def config(self):
+        return {"batch": 1, "q_heads": self.Hq, "kv_heads": self.Hkv, "head_dim": self.D,
+                "prefix_tokens": self.P, "q_len": self.Sq, "pool_blocks": self.num_blocks,
+                "block_size": 16, "kv_storage": "int8 KIVI, fp32 copies of fp16 scales"}
+
+    def _pool(self, torch, dev, hk, seed):
+        from kvboost_b200.paged import DeviceBlockAllocator, quantize_chunk_int8
+        g = torch.Generator(device=dev).manual_seed(seed)
+        alloc = DeviceBlockAllocator(1, hk, self.D, self.num_blocks, device=dev)
+        perm = torch.randperm(self.num_blocks, generator=torch.Generator().manual_seed(seed))
+        table = perm[: self.P // 16].tolist()
+        for c in range(self.P // 128):
+            k = torch.randn(1, hk, 128, self.D, generator=g, device=dev).to(torch.bfloat16).half()
+            v = torch.randn(1, hk, 128, self.D, generator=g, device=dev).to(torch.bfloat16).half()
+            alloc.write_chunk_int8(0, table[8 * c: 8 * c + 8], *quantize_chunk_int8(k, v))
+        bt = torch.tensor([table], dtype=torch.int32, device=dev)
+        return alloc, bt
+
+    def setup(self, torch, dev, rank, world):
+        from kvboost_b200.paged import paged_prefill_attention
+        self.world = world
+        hk, hq = self.local_heads(rank, world)
+        R = 2
+        sets = []
+        for r in range(R):
+            alloc, bt = self._pool(torch, dev, hk, seed=100 + 7 * rank + r)
+            g = torch.Generator(device=dev).manual_seed(200 + rank + r)
+            q = torch.randn(1, hq, self.Sq, self.D, generator=g, device=dev).to(torch.bfloat16)
+            kn = torch.randn(1, hk, self.Sq, self.D, generator=g, device=dev).to(torch.bfloat16)
+            vn = torch.randn(1, hk, self.Sq, self.D, generator=g, device=dev).to(torch.bfloat16)
+            sets.append((q, kn, vn, alloc, bt, torch.empty_like(q)))
+        self.sets_desc = (f"{R} pools x {self.bytes() / 2**20:.0f} MiB touched per step > L2; "
+                          f"rank holds KV heads {rank * hk}..{(rank + 1) * hk - 1}")
+        self.e2e_set = sets[0]
+
+        def step(i):
+            q, kn, vn, alloc, bt, o = sets[i % R]
+            paged_prefill_attention(q, kn, vn, alloc, 0, bt, self.P, out=o, return_lse=False)
+        return step
+
+    def e2e(self, torch, dev):
+        """Suffix Q/K/V and the block table come from pinned host memory; the int8
+        pool is the device-resident chunk cache."""
+        from kvboost_b200.paged import paged_prefill_attention
+        q, kn, vn, alloc, bt, _ = self.e2e_set
+        hq, hk_, hv = (t.cpu().pin_memory() for t in (q, kn, vn))
+        hbt = bt.cpu().pin_memory()
+        ho = torch.empty_like(hq).pin_memory()
+
+        def step():
+            dq, dk, dv, dbt = (t.to(dev, non_blocking=True) for t in (hq, hk_, hv, hbt))
+            o, _ = paged_prefill_attention(dq, dk, dv, alloc, 0, dbt, self.P, return_lse=False)
+            ho.copy_(o, non_blocking=True)
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk_, hv, hbt))
+        return step, h2d, ho.numel() * ho.element_size()
+
+    def cpu_sample(self, np):
+        """One query head of the full workload with its KV head: dequantise + gather by
+        the block table + attention, the reference's host path (numpy float32)."""
+        from oracle.attention import attention, attention_flops
+        from oracle.kv_quant import dequantize_int8
+        g = np.random.default_rng(0)
+        nblk = self.P // 16
+        kq = g.integers(-127, 128, size=(1, self.P, self.D), dtype=np.int8)
+        vq = g.integers(-127, 128, size=(1, self.P, self.D), dtype=np.int8)
+        ks = (np.abs(g.standard_normal((1, self.P, 1))) / 40 + 1e-3).astype(np.float16)
+        vs = (np.abs(g.standard_normal((1, self.P // 128, self.D))) / 40 + 1e-3).astype(np.float16)
+        perm = g.permutation(nblk)
+        q = g.standard_normal((1, 1, self.Sq, self.D), dtype=np.float32)
+        kn = g.standard_normal((1, 1, self.Sq, self.D), dtype=np.float32)
+        vn = g.standard_normal((1, 1, self.Sq, self.D), dtype=np.float32)
+        fl = attention_flops([self.Sq], [self.P + self.Sq], 1, self.D)
+
+        def run():
+            tok = (perm[np.arange(self.P) // 16] * 16 + np.arange(self.P) % 16) % self.P
+            k = dequantize_int8(kq[:, tok], ks[:, tok]).astype(np.float32)
+            v = dequantize_int8(vq[:, tok], np.repeat(vs, 128, axis=1)[:, tok]).astype(np.float32)
+            K = np.concatenate([k[None], kn], axis=2)
+            V = np.concatenate([v[None], vn], axis=2)
+            attention(q, K, V, 1.0 / math.sqrt(self.D), True, compute_dtype=np.float32)
+        return run, fl, "1 of 64 query heads (its KV head gathered and dequantised)"
+
+
+def make_workload(name):
+    if name == "reuse_prefill":
+        return Dense(name, 4, 32, 8, 256, 896, 128, "bf16",
+                     "prefix-reuse prefill op: B4 Hq32/Hkv8 D128 bf16, 7 cached chunks (896) + "
+                     "256 new tokens")
+    if name == "causal_op":
+        return Dense(name, 2, 16, 16, 1024, 0, 64, "bf16", "single causal op: B2 H16 S1024 D64 bf16")
+    if name == "varlen_d96":
+        return Varlen()
+    return PagedLong()
+
+
+# ─────────────────────────────────────────────────────────── helpers ──
+
 class ClockSampler:
     """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
 
@@ -90,6 +371,7 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.lines = []
 
     def __enter__(self):
         try:
@@ -103,7 +385,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -117,7 +398,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
+        for l in self.lines:
             parts = [x.strip() for x in l.split(",")]
             if len(parts) < 9:
                 continue
@@ -133,68 +414,50 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(w, budget_s=12.0, sample_batches=1):
-    """The oracle (numpy float32, all host threads) on `sample_batches` batch elements."""
-    import numpy as np
-    from oracle.attention import attention, attention_flops
-    try:
-        from threadpoolctl import threadpool_limits
-        limiter = threadpool_limits(limits=os.cpu_count())
-    except Exception:  # pragma: no cover
-        limiter = None
-    g = np.random.default_rng(0)
-    b = sample_batches
-    kv = w["P"] + w["Sq"]
-    q = g.standard_normal((b, w["Hq"], w["Sq"], w["D"]), dtype=np.float32)
-    k = g.standard_normal((b, w["Hkv"], kv, w["D"]), dtype=np.float32)
-    v = g.standard_normal((b, w["Hkv"], kv, w["D"]), dtype=np.float32)
-    scale = 1.0 / math.sqrt(w["D"])
-    fl = attention_flops([w["Sq"]] * b, [kv] * b, w["Hq"], w["D"], True)
+def time_cpu(run, fl, budget_s=12.0, max_iters=50):
+    run()  # warm
     n, t0 = 0, time.perf_counter()
     while True:
-        attention(q, k, v, scale, True, compute_dtype=np.float32)
+        run()
         n += 1
         el = time.perf_counter() - t0
-        if el > budget_s or n >= 50:
-            break
-    if limiter is not None:
-        limiter.unregister() if hasattr(limiter, "unregister") else None
-    return {"value": fl * n / el / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(),
-            "kind": "port",
-            "sample": f"{n} x {b} of {w['B']} batch elements of the workload, numpy float32 "
-                      f"oracle (oracle/attention.py), {el:.1f} s"}
+        if el > budget_s or n >= max_iters:
+            return fl * n / el / 1e12, n, el
 
 
-def run_reference(args, w):
-    """--impl reference: the CPU restatement timed on the host (rank 0 only)."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=os.cpu_count())
+    except Exception:  # pragma: no cover
+        pass
+    return os.cpu_count()
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (restated: numpy, all host threads)."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return
     import numpy as np
-    from oracle.attention import attention, attention_flops
-    kv = w["P"] + w["Sq"]
-    g = np.random.default_rng(0)
-    q = g.standard_normal((1, w["Hq"], w["Sq"], w["D"]), dtype=np.float32)
-    k = g.standard_normal((1, w["Hkv"], kv, w["D"]), dtype=np.float32)
-    v = g.standard_normal((1, w["Hkv"], kv, w["D"]), dtype=np.float32)
-    scale = 1.0 / math.sqrt(w["D"])
-    fl = attention_flops([w["Sq"]], [kv], w["Hq"], w["D"], True)
+    w = make_workload(args.workload)
+    cores = cpu_threads()
+    run, fl, sample = w.cpu_sample(np)
     for _ in range(max(0, args.warmup)):
-        attention(q, k, v, scale, True, compute_dtype=np.float32)
+        run()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        attention(q, k, v, scale, True, compute_dtype=np.float32)
+        run()
     el = time.perf_counter() - t0
     val = fl * args.steps / el / 1e12
     line = {
         "impl": "reference", "metric": "prefill attention TFLOP/s", "value": val,
         "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": w.scaling,
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "desc": w["desc"], "sample": "1 batch element per step"},
-        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": "1 of %d batch elements per step, numpy float32 oracle "
-                                   "(no runnable reference CUDA path exists)" % w["B"]},
+        "config": {"workload": args.workload, "desc": w.desc, "sample": sample + " per step"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": sample + " per step, numpy float32 restatement of the "
+                                   "reference's CPU path (oracle/)"},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -202,9 +465,8 @@ def run_reference(args, w):
 
 def main():
     args = parse()
-    w = WORKLOADS[args.workload]
     if args.impl == "reference":
-        run_reference(args, w)
+        run_reference(args)
         return
 
     import torch
@@ -218,29 +480,11 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
 
-    dtype = torch.bfloat16 if w["dtype"] == "bf16" else torch.float16
-    B, Hq, Hkv, Sq, P, D = w["B"], w["Hq"], w["Hkv"], w["Sq"], w["P"], w["D"]
-    kv = P + Sq
-    scale = 1.0 / math.sqrt(D)
-    per_set = bytes_of(w)
-    R = max(2, math.ceil(2 * L2_BYTES / per_set))
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    sets = []
-    for _ in range(R):
-        q = torch.randn(B, Hq, Sq, D, generator=g, device=dev, dtype=torch.float32).to(dtype)
-        k = torch.randn(B, Hkv, kv, D, generator=g, device=dev, dtype=torch.float32).to(dtype)
-        v = torch.randn(B, Hkv, kv, D, generator=g, device=dev, dtype=torch.float32).to(dtype)
-        o = torch.empty(B, Hq, Sq, D, device=dev, dtype=dtype)
-        sets.append((q, k, v, o))
-
-    def step(i):
-        q, k, v, o = sets[i % R]
-        ops.prefill_attention(q, k, v, scale, True, out=o, return_lse=False)
-
-    # one eager call (allocates the status word), then capture
-    step(0)
+    w = make_workload(args.workload)
+    step = w.setup(torch, dev, rank, world)
+    step(0)  # eager call: allocates the status word before capture
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
@@ -257,9 +501,9 @@ def main():
     with ClockSampler(local) as clk:
         with torch.cuda.stream(stream):
             gw.replay()
+            torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
-            torch.cuda.synchronize()
             ev0.record(stream)
             gt.replay()
             ev1.record(stream)
@@ -272,24 +516,14 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     status = ops.read_status(dev)
-    fl = flops_of(w)
+    fl = w.flops()                     # per rank per step
     per_launch_s = ms / 1e3 / args.steps
     value = world * fl * args.steps / (ms / 1e3) / 1e12
-    tok_s = world * B * Sq * args.steps / (ms / 1e3)
+    units = w.tokens() * (world if w.scaling == "weak" else 1)
+    tok_s = units * args.steps / (ms / 1e3)
 
-    # ---- e2e: public API with pinned host buffers, copies inside the timed region
-    hq = torch.randn(B, Hq, Sq, D, dtype=torch.float32).to(dtype).pin_memory()
-    hk = torch.randn(B, Hkv, kv, D, dtype=torch.float32).to(dtype).pin_memory()
-    hv = torch.randn(B, Hkv, kv, D, dtype=torch.float32).to(dtype).pin_memory()
-    ho = torch.empty(B, Hq, Sq, D, dtype=dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
-    d2h = ho.numel() * ho.element_size()
-
-    def e2e_step():
-        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
-        o, _ = ops.prefill_attention(dq, dk, dv, scale, True, return_lse=False)
-        ho.copy_(o, non_blocking=True)
-
+    # ---- e2e through the public op with pinned host buffers ------------------
+    e2e_step, h2d, d2h = w.e2e(torch, dev)
     for _ in range(3):
         e2e_step()
     torch.cuda.synchronize()
@@ -309,35 +543,42 @@ def main():
     e2e_value = world * fl * args.e2e_steps / (ems / 1e3) / 1e12
 
     peak_tf, peak_bw, peak_src = measured_peaks()
-    achieved = fl / per_launch_s / 1e12
-    traffic = NCU_TRAFFIC_BYTES.get(args.workload)
+    if w.bound == "tensor":
+        achieved, peak, unit = fl / per_launch_s / 1e12, peak_tf, "TFLOP/s"
+        psrc = f"{peak_src} bf16 dense (burst)"
+    else:
+        achieved, peak, unit = w.bytes() / per_launch_s / 1e9, peak_bw, "GB/s"
+        psrc = f"{peak_src} HBM copy"
+    cfg = {"workload": w.name, "desc": w.desc, **w.config(),
+           "parallelism": (f"KV heads split over {world} ranks" if w.scaling == "strong"
+                           else f"independent batches x{world}") if world > 1 else "single",
+           "l2": w.sets_desc, "timing": "CUDA graph of K launches between events"}
     line = {
         "metric": "prefill attention TFLOP/s", "value": value, "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
-        "config": {"workload": args.workload, "desc": w["desc"], "batch": B, "q_heads": Hq,
-                   "kv_heads": Hkv, "q_len": Sq, "kv_len": kv, "head_dim": D,
-                   "parallelism": f"independent batches x{world}" if world > 1 else "single",
-                   "l2": f"inputs rotate over {R} sets ({R * per_set / 2**20:.0f} MiB > L2)",
-                   "timing": "CUDA graph of K launches between events"},
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": w.scaling,
+        "vs_baseline": None, "dtype": w.dtype_name, "data": "synthetic", "config": cfg,
         "tokens_per_s": tok_s,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ems / args.e2e_steps},
         "gpu_launches": args.steps,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf,
-                     "unit": "TFLOP/s", "frac": achieved / peak_tf, "traffic": traffic,
-                     "peak_source": f"{peak_src} bf16 (burst)",
-                     "algorithmic_bytes": bytes_of(w)},
+        "roofline": {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES.get(w.name),
+                     "peak_source": psrc, "algorithmic_flops": fl, "algorithmic_bytes": w.bytes()},
         "clocks": clk.summary(),
         "device_status": status,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(w)
+        import numpy as np
+        cores = cpu_threads()
+        run, sfl, sample = w.cpu_sample(np)
+        v, n, el = time_cpu(run, sfl)
+        line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                                "sample": f"{n} x {sample}, numpy float32 oracle, {el:.1f} s"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    del gw, gt
     if world > 1:
-        del gw, gt
         dist.barrier()
         dist.destroy_process_group()
 
