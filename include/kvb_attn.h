@@ -187,7 +187,21 @@ typedef struct KvbPagedPrefillParams {
   int32_t prefix_len;           /* uniform (or maximum) cached tokens        */
   const int32_t* prefix_lens;   /* device [batch] per-sequence, or NULL      */
   int32_t* status;
+  void* workspace;              /* optional device scratch, see below        */
+  int64_t workspace_bytes;
 } KvbPagedPrefillParams;
+
+/*
+ * When many CTAs would read (and dequantise) each KV tile -- long suffixes
+ * under GQA, e.g. 2048 new tokens over 8 query heads per KV head -- the
+ * library can instead dequantise the prefix once into a dense workspace and
+ * run the dense kernel over it.  kvb_paged_prefill_workspace_bytes returns the
+ * bytes that strategy needs for these params (0 when the fused path is the
+ * right one); pass at least that much as params->workspace to enable it.
+ * Without a (large enough) workspace the fused path runs; results agree to
+ * rounding either way.
+ */
+int64_t kvb_paged_prefill_workspace_bytes(const KvbPagedPrefillParams* params);
 
 int kvb_paged_prefill_fwd(const KvbPagedPrefillParams* params, void* stream);
 

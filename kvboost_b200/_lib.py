@@ -60,6 +60,7 @@ class KvbPagedPrefillParams(ctypes.Structure):
         ("num_blocks", _i32), ("block_size", _i32),
         ("block_tables", _vp), ("max_blocks_per_seq", _i32), ("prefix_len", _i32),
         ("prefix_lens", _vp), ("status", _vp),
+        ("workspace", _vp), ("workspace_bytes", _i64),
     ]
 
 
@@ -93,6 +94,8 @@ def load() -> ctypes.CDLL:
         lib.kvb_flash_attn_fwd.restype = ctypes.c_int
         lib.kvb_paged_prefill_fwd.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]
         lib.kvb_paged_prefill_fwd.restype = ctypes.c_int
+        lib.kvb_paged_prefill_workspace_bytes.argtypes = [ctypes.POINTER(KvbPagedPrefillParams)]
+        lib.kvb_paged_prefill_workspace_bytes.restype = ctypes.c_int64
         lib.kvb_last_error.argtypes = []
         lib.kvb_last_error.restype = ctypes.c_char_p
         lib.kvb_abi_version.argtypes = []

@@ -148,6 +148,9 @@ struct DenseArgs {
   int causal;
   float scale_log2;
   int* status;
+  // Dense layout with per-sequence key counts: sequence b uses the first
+  // kv_prefix[b] + q_len rows of its K/V (the rest may be padding).
+  const int* kv_prefix;
 };
 
 // Reused-prefix K/V in the int8 paged pool plus the suffix's own fresh K/V.
@@ -465,6 +468,83 @@ __device__ __forceinline__ void gather_kv_tile(uint8_t* dst, const PagedArgs& pa
   }
 }
 
+// Materialise the paged prefix (dequantised) and the fresh suffix of every
+// sequence into a dense workspace K/V [batch, num_kv_heads, kv_pad, D] of the
+// compute dtype, for the strategy used when many CTAs would otherwise each
+// dequantise the same tiles (long suffixes under GQA).  One thread per 16
+// elements; token rows in [kv_len_b, kv_len_b rounded up to 128) are zeroed so
+// the attention kernel never reads uninitialised padding.
+template <typename T, int D>
+__global__ void __launch_bounds__(256)
+    kvb_paged_materialize_kernel(PagedArgs pa, T* wk, T* wv, int q_len, int kv_pad, int* status) {
+  constexpr int NCH = D / 16;
+  const int b = blockIdx.z;
+  const int kvh = blockIdx.y;
+  const int P = pa.prefix_lens ? pa.prefix_lens[b] : pa.prefix_len;
+  const int kv_len = P + q_len;
+  const int kv_end = min(kv_pad, (kv_len + BN - 1) / BN * BN);
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)kv_end * NCH * 2) return;
+  const int kv = (int)(idx / ((int64_t)kv_end * NCH));       // 0 = K, 1 = V
+  const int rem = (int)(idx - (int64_t)kv * kv_end * NCH);
+  const int tok = rem / NCH;
+  const int ch = rem - tok * NCH;
+  uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
+  if (tok < kv_len) {
+    if (tok < P) {
+      const int bi = tok >> 4;
+      const int blk =
+          bi < pa.max_blocks ? __ldg(pa.block_table + (int64_t)b * pa.max_blocks + bi) : -1;
+      if (blk < 0 || blk >= pa.num_blocks) {
+        if (status) atomicOr(status, KVB_STATUS_BAD_BLOCK);
+      } else {
+        const int slot = tok & 15;
+        const int64_t hb = (int64_t)blk * pa.num_kv_heads + kvh;
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(
+            pa.pool + (((int64_t)blk * 2 + kv) * pa.num_kv_heads + kvh) * 16 * D +
+            (int64_t)slot * D + ch * 16));
+        float sc[16];
+        if (kv == 0) {
+          const float sk = __ldg(pa.k_scale + hb * 16 + slot);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) sc[e] = sk;
+        } else {
+          const float4* sp = reinterpret_cast<const float4*>(pa.v_scale + hb * D + ch * 16);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float4 f = __ldg(sp + e);
+            sc[4 * e] = f.x; sc[4 * e + 1] = f.y; sc[4 * e + 2] = f.z; sc[4 * e + 3] = f.w;
+          }
+        }
+        const uint32_t qw[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u,
+                                q.w ^ 0x80808080u};
+        uint32_t o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t word = qw[e >> 1];
+          const int sh = (e & 1) * 2;
+          const float f0 = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7650 + sh)) - 8388736.f;
+          const float f1 = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7651 + sh)) - 8388736.f;
+          o[e] = pack2<T>(f0 * sc[2 * e], f1 * sc[2 * e + 1]);
+        }
+        w0 = make_uint4(o[0], o[1], o[2], o[3]);
+        w1 = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+    } else {
+      const T* fresh = reinterpret_cast<const T*>(kv ? pa.v_new : pa.k_new);
+      const int64_t bs = kv ? pa.vn_bs : pa.kn_bs, hs = kv ? pa.vn_hs : pa.kn_hs,
+                    rs = kv ? pa.vn_rs : pa.kn_rs;
+      const uint4* src = reinterpret_cast<const uint4*>(
+          fresh + (int64_t)b * bs + (int64_t)kvh * hs + (int64_t)(tok - P) * rs + ch * 16);
+      w0 = __ldg(src);
+      w1 = __ldg(src + 1);
+    }
+  }
+  T* dst = (kv ? wv : wk) + (((int64_t)b * pa.num_kv_heads + kvh) * kv_pad + tok) * D + ch * 16;
+  reinterpret_cast<uint4*>(dst)[0] = w0;
+  reinterpret_cast<uint4*>(dst)[1] = w1;
+}
+
 template <typename T, int D, bool PAGED>
 __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     kvb_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -508,6 +588,8 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   if (PAGED) {
     P = pa.prefix_lens ? pa.prefix_lens[b] : pa.prefix_len;
     kv_len = P + q_len;
+  } else if (a.kv_prefix != nullptr) {
+    kv_len = a.kv_prefix[b] + q_len;
   } else if (a.cu_q != nullptr) {
     q_base = a.cu_q[b];
     q_len = a.cu_q[b + 1] - q_base;
@@ -949,6 +1031,33 @@ static bool make_map(CUtensorMap* m, const void* base, int dtype, int head_dim, 
 }
 
 template <typename T, int D>
+static int launch_dense_core(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                             const DenseArgs& a, int batch, int num_q_heads, int q_len,
+                             cudaStream_t stream) {
+  using G = Geo<D>;
+  auto kern = kvb_prefill_kernel<T, D, false>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         G::SMEM_BYTES);
+    if (e != cudaSuccess)
+      return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    configured_device = dev;
+  }
+  const int q_tiles = (q_len + BM - 1) / BM;
+  dim3 grid = a.pair_heads ? dim3(q_tiles, num_q_heads / 2, batch)
+                           : dim3((q_tiles + 1) / 2, num_q_heads, batch);
+  PagedArgs none = {};
+  kern<<<grid, Roles<false>::kThreads, G::SMEM_BYTES, stream>>>(tq, tk, tv, a, none);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return fail(KVB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  return KVB_OK;
+}
+
+template <typename T, int D>
 static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
   using G = Geo<D>;
   const bool varlen = p.cu_seqlens_q != nullptr;
@@ -969,7 +1078,7 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
                 vbs, &err))
     return fail(KVB_ERR_INVALID, err);
 
-  DenseArgs a;
+  DenseArgs a = {};
   a.o = p.o;
   a.lse = p.lse;
   a.o_bs = p.o_batch_stride;
@@ -987,26 +1096,22 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
   a.scale_log2 = p.softmax_scale * 1.4426950408889634f;
   a.status = p.status;
 
-  auto kern = kvb_prefill_kernel<T, D, false>;
-  static thread_local int configured_device = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         G::SMEM_BYTES);
-    if (e != cudaSuccess)
-      return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    configured_device = dev;
-  }
+  return launch_dense_core<T, D>(tq, tk, tv, a, p.batch, p.num_q_heads, p.q_len, stream);
+}
+
+// Workspace the paged path uses to dequantise the prefix once instead of in
+// every CTA: chosen when each KV tile would be read (and dequantised) by at
+// least kMaterializeMinReaders CTAs.  0 = the fused path is used.
+constexpr int kMaterializeMinReaders = 4;
+
+static int64_t paged_workspace_bytes(const KvbPagedPrefillParams& p) {
+  if (p.q_len <= 0 || p.num_kv_heads <= 0 || p.num_q_heads % p.num_kv_heads) return 0;
+  const int group = p.num_q_heads / p.num_kv_heads;
   const int q_tiles = (p.q_len + BM - 1) / BM;
-  dim3 grid = a.pair_heads ? dim3(q_tiles, p.num_q_heads / 2, p.batch)
-                           : dim3((q_tiles + 1) / 2, p.num_q_heads, p.batch);
-  PagedArgs none = {};
-  kern<<<grid, Roles<false>::kThreads, G::SMEM_BYTES, stream>>>(tq, tk, tv, a, none);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess)
-    return fail(KVB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
-  return KVB_OK;
+  const int64_t readers = (group % 2 == 0) ? (int64_t)q_tiles * (group / 2) : (q_tiles + 1) / 2;
+  if (readers < kMaterializeMinReaders) return 0;
+  const int64_t kv_pad = (int64_t)(p.prefix_len + p.q_len + BN - 1) / BN * BN;
+  return 2 * (int64_t)p.batch * p.num_kv_heads * kv_pad * p.head_dim * 2;
 }
 
 template <typename T, int D>
@@ -1050,6 +1155,31 @@ static int launch_paged(const KvbPagedPrefillParams& p, cudaStream_t stream) {
   pa.num_blocks = p.num_blocks;
   pa.num_kv_heads = p.num_kv_heads;
   pa.prefix_len = p.prefix_len;
+
+  const int64_t need = paged_workspace_bytes(p);
+  if (need > 0 && p.workspace != nullptr && p.workspace_bytes >= need) {
+    // Many CTAs read each KV tile: dequantise the prefix once into the
+    // workspace, then run the dense kernel over it.
+    const int kv_pad = (p.prefix_len + p.q_len + BN - 1) / BN * BN;
+    T* wk = reinterpret_cast<T*>(p.workspace);
+    T* wv = wk + (int64_t)p.batch * p.num_kv_heads * kv_pad * D;
+    const int64_t threads = (int64_t)kv_pad * (D / 16) * 2;
+    dim3 mgrid((unsigned)((threads + 255) / 256), p.num_kv_heads, p.batch);
+    kvb_paged_materialize_kernel<T, D><<<mgrid, 256, 0, stream>>>(pa, wk, wv, p.q_len, kv_pad,
+                                                                  p.status);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+      return fail(KVB_ERR_CUDA, std::string("materialize launch: ") + cudaGetErrorString(e));
+    CUtensorMap tk, tv;
+    const int64_t hs = (int64_t)kv_pad * D, bs = (int64_t)p.num_kv_heads * kv_pad * D;
+    if (!make_map(&tk, wk, p.dtype, D, kv_pad, p.num_kv_heads, p.batch, D, hs, bs, &err) ||
+        !make_map(&tv, wv, p.dtype, D, kv_pad, p.num_kv_heads, p.batch, D, hs, bs, &err))
+      return fail(KVB_ERR_INVALID, err);
+    if (p.prefix_lens != nullptr) {
+      a.kv_prefix = p.prefix_lens;
+    }
+    return launch_dense_core<T, D>(tq, tk, tv, a, p.batch, p.num_q_heads, p.q_len, stream);
+  }
 
   auto kern = kvb_prefill_kernel<T, D, true>;
   static thread_local int configured_device = -1;
@@ -1216,6 +1346,11 @@ static int validate_paged(const KvbPagedPrefillParams& p) {
     if (s <= 0 || (s % 8) != 0)
       return fail(KVB_ERR_INVALID, "row and head strides must be positive multiples of 8 elements");
   return KVB_OK;
+}
+
+extern "C" int64_t kvb_paged_prefill_workspace_bytes(const KvbPagedPrefillParams* params) {
+  if (!params || validate_paged(*params) != KVB_OK) return 0;
+  return paged_workspace_bytes(*params);
 }
 
 extern "C" int kvb_paged_prefill_fwd(const KvbPagedPrefillParams* params, void* stream) {

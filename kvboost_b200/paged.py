@@ -227,6 +227,19 @@ class DeviceChunkMapper:
         return len(self._chunk_blocks)
 
 
+_workspaces: Dict[int, torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device scratch for the materialised-prefix strategy (grown, never shrunk)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{idx}")
+        _workspaces[idx] = ws
+    return ws
+
+
 def block_table_tensor(tables: Sequence[Sequence[int]], device) -> torch.Tensor:
     """Pad per-sequence tables into a device int32 ``[B, max_blocks]`` array."""
     mb = max(1, max(len(t) for t in tables))
@@ -242,8 +255,13 @@ def paged_prefill_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.T
                             block_tables: torch.Tensor, prefix_len: int,
                             prefix_lens: Optional[torch.Tensor] = None,
                             softmax_scale: Optional[float] = None, causal: bool = True,
-                            out: Optional[torch.Tensor] = None, return_lse: bool = True):
+                            out: Optional[torch.Tensor] = None, return_lse: bool = True,
+                            fused_only: bool = False):
     """Suffix prefill over an int8 paged prefix (``kvb_paged_prefill_fwd``).
+
+    When each KV tile would be dequantised by many CTAs (long suffixes under
+    GQA) the library asks for a workspace and dequantises the prefix once
+    into it; ``fused_only=True`` forces the fused gather+dequant path.
 
     q: ``[B, Hq, q_len, D]``; k_new/v_new: the suffix's own ``[B, Hkv, q_len, D]``;
     block_tables: device int32 ``[B, max_blocks]``; ``prefix_len``: cached tokens
@@ -289,7 +307,12 @@ def paged_prefill_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.T
     p.prefix_len = int(prefix_len)
     p.prefix_lens = prefix_lens.data_ptr() if prefix_lens is not None else None
     p.status = status_word(q.device).data_ptr()
+    lib = _lib.load()
+    need = int(lib.kvb_paged_prefill_workspace_bytes(p)) if fused_only is False else 0
+    if need > 0:
+        ws = _workspace(q.device, need)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
     with torch.cuda.device(q.device):
-        rc = _lib.load().kvb_paged_prefill_fwd(p, _stream_handle(q.device))
+        rc = lib.kvb_paged_prefill_fwd(p, _stream_handle(q.device))
     _lib.check(rc, "kvb_paged_prefill_fwd")
     return out, lse

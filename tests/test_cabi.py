@@ -106,3 +106,21 @@ def test_ctypes_layouts_match_c_compiler(tmp_path):
         assert int(got[name]) == ctypes.sizeof(cls)
         for f, _ in cls._fields_:
             assert int(got[f"{name}.{f}"]) == getattr(cls, f).offset, f"{name}.{f}"
+
+
+def test_paged_strategy_selection():
+    """The workspace strategy is chosen only when many CTAs read each KV tile."""
+    from kvboost_b200 import _lib
+    lib = _lib.load()
+    p = _lib.KvbPagedPrefillParams()
+    p.dtype, p.head_dim, p.batch, p.num_q_heads, p.num_kv_heads = 0, 128, 1, 64, 8
+    p.q_len, p.causal, p.softmax_scale = 2048, 1, 0.088
+    p.q = p.o = p.k_new = p.v_new = p.kv_pool = p.k_scale = p.v_scale = p.block_tables = 4096
+    for f in ("q", "o", "k_new", "v_new"):
+        setattr(p, f"{f}_head_stride", 128 * 2048)
+        setattr(p, f"{f}_row_stride", 128)
+    p.num_blocks, p.block_size, p.max_blocks_per_seq, p.prefix_len = 8192, 16, 2048, 32768
+    assert lib.kvb_paged_prefill_workspace_bytes(p) == 2 * 8 * (32768 + 2048) * 128 * 2
+    p.q_len = 16  # a seam-recompute-sized suffix stays fused (reads int8 once)
+    p.num_q_heads = 16
+    assert lib.kvb_paged_prefill_workspace_bytes(p) == 0

@@ -52,7 +52,8 @@ def _oracle_prefix(alloc, tbl, P):
     return opaged.dequant_gather(pool, ks, vs, tbl, P, 16)   # float16 [H, P, D]
 
 
-def _run_case(B, Hq, Hkv, D, chunk_sets, Sq, dtype, seed, num_blocks=512, rows=None):
+def _run_case(B, Hq, Hkv, D, chunk_sets, Sq, dtype, seed, num_blocks=512, rows=None,
+              fused_only=False):
     from kvboost_b200.paged import (DeviceBlockAllocator, block_table_tensor,
                                     paged_prefill_attention, quantize_chunk_int8)
     g = torch.Generator().manual_seed(seed + 1)
@@ -81,7 +82,8 @@ def _run_case(B, Hq, Hkv, D, chunk_sets, Sq, dtype, seed, num_blocks=512, rows=N
     bt = block_table_tensor(tables, "cuda")
     pl = torch.tensor(prefix, dtype=torch.int32, device="cuda")
     o, lse = paged_prefill_attention(q.cuda(), kn.cuda(), vn.cuda(), alloc, 0, bt, P,
-                                     prefix_lens=pl, softmax_scale=1.0 / math.sqrt(D))
+                                     prefix_lens=pl, softmax_scale=1.0 / math.sqrt(D),
+                                     fused_only=fused_only)
     torch.cuda.synchronize()
     from kvboost_b200 import ops
     assert ops.read_status(torch.device("cuda")) == 0
@@ -105,41 +107,52 @@ def _run_case(B, Hq, Hkv, D, chunk_sets, Sq, dtype, seed, num_blocks=512, rows=N
         assert np.abs(lb - l_ref).max() <= 2e-3
 
 
-def test_paged_config5_shape_reduced():
+# fused: gather + dequantise inside the attention kernel's load stage;
+# materialised: one dequantise pass into a workspace, then the dense kernel.
+STRATEGIES = [pytest.param(True, id="fused"), pytest.param(False, id="auto")]
+
+
+@pytest.mark.parametrize("fused_only", STRATEGIES)
+def test_paged_config5_shape_reduced(fused_only):
     """GQA 8, D128, bf16: 8 cached chunks at a random block permutation + 200 new tokens."""
-    _run_case(1, 16, 2, 128, [[128] * 8], 200, torch.bfloat16, seed=5)
+    _run_case(1, 16, 2, 128, [[128] * 8], 200, torch.bfloat16, seed=5, fused_only=fused_only)
 
 
-def test_paged_ragged_batch():
+@pytest.mark.parametrize("fused_only", STRATEGIES)
+def test_paged_ragged_batch(fused_only):
     """Per-sequence prefixes: full chunks, a partial last chunk, and no prefix at all."""
-    _run_case(3, 8, 2, 128, [[128, 128, 128], [128, 100], []], 130, torch.bfloat16, seed=6)
+    _run_case(3, 8, 2, 128, [[128, 128, 128], [128, 100], []], 330, torch.bfloat16, seed=6,
+              fused_only=fused_only)
 
 
+@pytest.mark.parametrize("fused_only", STRATEGIES)
 @pytest.mark.parametrize("D,dtype", [(64, torch.float16), (96, torch.float16), (128, torch.float16),
                                      (64, torch.bfloat16)])
-def test_paged_head_dims(D, dtype):
-    _run_case(2, 8, 4, D, [[128] * 3, [128] * 2], 77, dtype, seed=D)
+def test_paged_head_dims(D, dtype, fused_only):
+    _run_case(2, 16, 2, D, [[128] * 3, [128] * 2], 277, dtype, seed=D, fused_only=fused_only)
 
 
 def test_paged_suffix_shorter_than_tile_mha():
     _run_case(1, 4, 4, 128, [[128] * 5], 16, torch.bfloat16, seed=9)
 
 
-def test_paged_config5_full_size_last_rows():
+@pytest.mark.parametrize("fused_only", STRATEGIES)
+def test_paged_config5_full_size_last_rows(fused_only):
     """Full config 5 on one GPU: P=32768 int8 prefix in an 8192-block pool, 2048 new
     tokens, Hq 64 / Hkv 8, D 128; the last 64 query rows of every head are checked."""
     _run_case(1, 64, 8, 128, [[128] * 256], 2048, torch.bfloat16, seed=50, num_blocks=8192,
-              rows=64)
+              rows=64, fused_only=fused_only)
 
 
-def test_bad_block_id_is_reported_not_read():
+@pytest.mark.parametrize("fused_only", STRATEGIES)
+def test_bad_block_id_is_reported_not_read(fused_only):
     from kvboost_b200 import ops
     from kvboost_b200.paged import DeviceBlockAllocator, paged_prefill_attention
     alloc = DeviceBlockAllocator(1, 2, 64, 8)
     bt = torch.tensor([[0, 99]], dtype=torch.int32, device="cuda")  # 99 is outside the pool
-    q = torch.randn(1, 2, 8, 64, device="cuda", dtype=torch.bfloat16)
-    kn = torch.randn(1, 2, 8, 64, device="cuda", dtype=torch.bfloat16)
-    o, _ = paged_prefill_attention(q, kn, kn.clone(), alloc, 0, bt, 32)
+    q = torch.randn(1, 16, 256, 64, device="cuda", dtype=torch.bfloat16)
+    kn = torch.randn(1, 2, 256, 64, device="cuda", dtype=torch.bfloat16)
+    o, _ = paged_prefill_attention(q, kn, kn.clone(), alloc, 0, bt, 32, fused_only=fused_only)
     torch.cuda.synchronize()
     assert ops.read_status(torch.device("cuda")) & 16
     assert torch.isfinite(o.float()).all()
