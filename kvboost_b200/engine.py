@@ -1,0 +1,487 @@
+"""KVBoost engine with a device-resident chunk store (chunk KV reuse on B200).
+
+Mirrors the CHUNK_KV_REUSE path of KVBoost's ``InferenceEngine``
+(``src/kvboost/engine.py``) with the same public calls -- ``warm``,
+``generate``, ``generate_batch``, ``reset_cache``, ``GenerationResult``,
+``WarmResult`` -- and the same host logic:
+
+* prompts split into fixed 128-token chunks, tails shorter than 32 tokens
+  dropped (``chunk_registry.py:98-110``);
+* chunks keyed by the prefix-chained SHA-256 hash (``models.py:137-148``);
+* each chunk encoded on its own at its absolute positions, with no
+  preceding context (``engine.py:829-850``);
+* reuse = the longest run of cached chunks from position 0, found by chained
+  lookups (``cache_manager.py:358-393``, ``prompt_assembler.py:99-176``);
+* seam repair with ``recompute_strategy="selective"``: the last
+  ``recompute_overlap`` tokens before each seam re-encoded over the prefix
+  (``selective_recompute.py:99-184``);
+* suffix prefill with the cached K/V as ``past_key_values`` at positions
+  ``cached_len..`` then greedy / sampled decode (``engine.py:634-753``);
+  batched prompts share a common chunk prefix broadcast over the batch
+  (``engine.py:235-365``, ``batch.py``).
+
+What changes is where things live and run: chunk K/V stay in GPU memory
+(no per-request host->device copy of the reused prefix, which dominates the
+reference's TTFT), and every attention call of every forward -- chunk
+encoding, seam recompute, suffix prefill, decode -- runs on the sm_100a
+prefill kernels through ``install_flash_attention``.
+"""
+
+from __future__ import annotations
+
+import enum
+import hashlib
+import logging
+import struct
+import time
+from collections import OrderedDict
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple, Union
+
+import torch
+
+from .flash_attn_ext import install_flash_attention
+
+log = logging.getLogger(__name__)
+
+TokenIds = List[int]
+
+
+class GenerationMode(str, enum.Enum):
+    BASELINE = "baseline"
+    CHUNK_KV_REUSE = "chunk_kv_reuse"
+
+
+class RecomputeStrategy(str, enum.Enum):
+    SELECTIVE = "selective"
+    NONE = "none"
+
+
+@dataclass
+class GenerationResult:
+    """Same fields as ``engine.py:61-73``."""
+    mode: str
+    prompt: str
+    output_text: str
+    generated_tokens: int
+    ttft_ms: float
+    total_ms: float
+    tokens_per_sec: float
+    kv_reuse_ratio: float
+    prompt_tokens: int
+    cached_tokens: int
+    first_token_logits: Optional[object] = None
+    generated_ids: Optional[List[int]] = None
+
+
+@dataclass
+class WarmResult:
+    """Same fields as ``models.py:115-126``."""
+    chunks_stored: int
+    token_count: int
+    chunk_size: int
+    chunk_boundary_aligned: bool
+    partial_tail_tokens: int
+    alignment_warning: Optional[str] = None
+
+
+# ── chunk keys and split (bit-identical to the reference) ─────────────────────
+
+def _token_bytes(ids: Sequence[int]) -> bytes:
+    return struct.pack("<%dI" % len(ids), *[int(t) & 0xFFFFFFFF for t in ids])
+
+
+def chained_hash(token_ids: Sequence[int], parent_hash: Optional[str] = None) -> str:
+    """``models.py:137-148``: SHA-256 of (parent or "root") + little-endian int32 tokens."""
+    return hashlib.sha256((parent_hash or "root").encode("utf-8") + _token_bytes(token_ids)).hexdigest()
+
+
+def content_hash_from_tokens(token_ids: Sequence[int]) -> str:
+    """``models.py:131-134``."""
+    return hashlib.sha256(_token_bytes(token_ids)).hexdigest()
+
+
+def fixed_split(token_ids: Sequence[int], chunk_size: int = 128,
+                min_chunk_tokens: int = 32) -> List[Tuple[int, int, List[int]]]:
+    """``ChunkRegistry._fixed_split`` (``chunk_registry.py:98-110``)."""
+    out, pos, n = [], 0, len(token_ids)
+    while pos < n:
+        end = min(pos + chunk_size, n)
+        if end - pos >= min_chunk_tokens:
+            out.append((pos, end, list(token_ids[pos:end])))
+        pos = end
+    return out
+
+
+def find_common_chunk_prefix(all_token_ids: List[TokenIds], chunk_size: int) -> int:
+    """``batch.py:31-54``."""
+    if not all_token_ids or len(all_token_ids) < 2:
+        return len(all_token_ids[0]) if all_token_ids else 0
+    min_len = min(len(ids) for ids in all_token_ids)
+    common = 0
+    for i in range(0, min_len, chunk_size):
+        end = i + chunk_size
+        if end > min_len:
+            break
+        ref = all_token_ids[0][i:end]
+        if all(ids[i:end] == ref for ids in all_token_ids[1:]):
+            common = end
+        else:
+            break
+    return common
+
+
+# ── device-resident chunk store ───────────────────────────────────────────────
+
+@dataclass
+class DeviceChunk:
+    chunk_id: str
+    token_ids: List[int]
+    position_start: int
+    position_end: int
+    keys: torch.Tensor     # [layers, kv_heads, len, head_dim] on the GPU
+    values: torch.Tensor
+    hits: int = 0
+
+    @property
+    def length(self) -> int:
+        return self.position_end - self.position_start
+
+    def nbytes(self) -> int:
+        return self.keys.numel() * self.keys.element_size() * 2
+
+
+class DeviceChunkStore:
+    """Byte-budgeted LRU store of chunk K/V in GPU memory, keyed by prefix hash.
+
+    Plays the role of ``KVCacheManager``'s hot tier (``cache_manager.py:141-292``)
+    without the CPU round trip: ``get`` / ``store`` / ``lookup`` chained by parent
+    hash, LRU eviction when the byte budget is exceeded, hit/miss stats.
+    """
+
+    def __init__(self, max_bytes: int):
+        self.max_bytes = int(max_bytes)
+        self._chunks: "OrderedDict[str, DeviceChunk]" = OrderedDict()
+        self.bytes = 0
+        self.hits = self.misses = self.evictions = 0
+
+    def get(self, chunk_id: str) -> Optional[DeviceChunk]:
+        c = self._chunks.get(chunk_id)
+        if c is not None:
+            self._chunks.move_to_end(chunk_id)
+        return c
+
+    def lookup(self, token_ids: Sequence[int], parent_hash: Optional[str]) -> Optional[DeviceChunk]:
+        c = self.get(chained_hash(token_ids, parent_hash))
+        if c is None:
+            self.misses += 1
+        else:
+            self.hits += 1
+            c.hits += 1
+        return c
+
+    def store(self, chunk: DeviceChunk) -> bool:
+        size = chunk.nbytes()
+        if size > self.max_bytes:
+            return False
+        while self.bytes + size > self.max_bytes and self._chunks:
+            _, old = self._chunks.popitem(last=False)
+            self.bytes -= old.nbytes()
+            self.evictions += 1
+        self._chunks[chunk.chunk_id] = chunk
+        self.bytes += size
+        return True
+
+    def clear(self) -> None:
+        self._chunks.clear()
+        self.bytes = 0
+        self.hits = self.misses = self.evictions = 0
+
+    def __len__(self) -> int:
+        return len(self._chunks)
+
+    def stats(self) -> Dict[str, float]:
+        total = self.hits + self.misses
+        return {"chunks": len(self._chunks), "bytes": self.bytes, "max_bytes": self.max_bytes,
+                "hits": self.hits, "misses": self.misses, "evictions": self.evictions,
+                "hit_rate": self.hits / total if total else 0.0}
+
+
+def plan_reuse(token_ids: Sequence[int], store: DeviceChunkStore, chunk_size: int = 128,
+               min_chunk_tokens: int = 32):
+    """Longest contiguous run of cached chunks from position 0.
+
+    Chained lookups as ``find_matching_chunks`` (``cache_manager.py:358-393``),
+    then the contiguous-from-0 stitching of ``_chunk_reuse``
+    (``prompt_assembler.py:99-176``).  Returns ``(chunks, cached_len,
+    boundaries)``.
+    """
+    matches = []
+    parent = None
+    for start, end, ids in fixed_split(token_ids, chunk_size, min_chunk_tokens):
+        c = store.lookup(ids, parent)
+        if c is not None:
+            matches.append((start, c))
+            parent = chained_hash(ids, parent)
+        else:
+            parent = None
+    chunks, boundaries, covered = [], [], 0
+    for start, c in sorted(matches, key=lambda x: x[0]):
+        if start != covered:
+            break
+        chunks.append(c)
+        boundaries.append((start, start + c.length))
+        covered = start + c.length
+    return chunks, covered, boundaries
+
+
+# ── engine ────────────────────────────────────────────────────────────────────
+
+class KVBoost:
+    """Chunk-level KV reuse over a HuggingFace causal LM, on the sm_100a kernels."""
+
+    def __init__(self, model, tokenizer=None, *, max_cache_bytes: int = 16 << 30,
+                 chunk_size: int = 128, min_chunk_tokens: int = 32,
+                 recompute_overlap: int = 16,
+                 recompute_strategy: Union[str, RecomputeStrategy] = RecomputeStrategy.SELECTIVE,
+                 device: str = "cuda"):
+        self.device = torch.device(device)
+        self.model = model.to(self.device).eval()
+        self.tokenizer = tokenizer
+        self.chunk_size = chunk_size
+        self.min_chunk_tokens = min_chunk_tokens
+        self.recompute_overlap = recompute_overlap
+        self.recompute_strategy = RecomputeStrategy(recompute_strategy)
+        self.store = DeviceChunkStore(max_cache_bytes)
+        self._flash_attn_patched = install_flash_attention(self.model)
+
+    @classmethod
+    def from_pretrained(cls, model_name: str, dtype=torch.bfloat16, **kwargs) -> "KVBoost":
+        from transformers import AutoModelForCausalLM, AutoTokenizer
+        tok = AutoTokenizer.from_pretrained(model_name)
+        if tok.pad_token is None:
+            tok.pad_token = tok.eos_token
+        model = AutoModelForCausalLM.from_pretrained(model_name, dtype=dtype,
+                                                     attn_implementation="sdpa")
+        return cls(model, tok, **kwargs)
+
+    # ── helpers ───────────────────────────────────────────────────────────────
+    def _encode(self, prompt: Union[str, Sequence[int]]) -> TokenIds:
+        if isinstance(prompt, str):
+            if self.tokenizer is None:
+                raise ValueError("a tokenizer is needed for text prompts")
+            return self.tokenizer.encode(prompt, add_special_tokens=True)
+        return [int(t) for t in prompt]
+
+    def _decode_text(self, ids: List[int]) -> str:
+        if self.tokenizer is None:
+            return " ".join(str(i) for i in ids)
+        return self.tokenizer.decode(ids, skip_special_tokens=True)
+
+    @property
+    def _eos(self) -> Optional[int]:
+        return getattr(self.tokenizer, "eos_token_id", None) if self.tokenizer else None
+
+    @staticmethod
+    def _layers(cache) -> List[Tuple[torch.Tensor, torch.Tensor]]:
+        if hasattr(cache, "layers"):
+            return [(l.keys, l.values) for l in cache.layers]
+        return [(k, v) for k, v in zip(cache.key_cache, cache.value_cache)]
+
+    @staticmethod
+    def _cache_from(keys: torch.Tensor, values: torch.Tensor, batch: int = 1):
+        """DynamicCache from stacked [layers, kv_heads, len, D] K/V, broadcast over batch."""
+        from transformers import DynamicCache
+        cache = DynamicCache()
+        for l in range(keys.shape[0]):
+            k = keys[l].unsqueeze(0).expand(batch, -1, -1, -1)
+            v = values[l].unsqueeze(0).expand(batch, -1, -1, -1)
+            cache.update(k, v, l)
+        return cache
+
+    def _forward(self, ids: torch.Tensor, pos: torch.Tensor, cache=None):
+        with torch.no_grad():
+            return self.model(input_ids=ids, position_ids=pos, past_key_values=cache,
+                              use_cache=True, logits_to_keep=1)
+
+    def _encode_to_kv(self, ids: List[int], position_offset: int):
+        """One chunk on its own at its absolute positions (``engine.py:829-850``)."""
+        x = torch.tensor([ids], dtype=torch.long, device=self.device)
+        pos = torch.arange(position_offset, position_offset + len(ids), device=self.device)[None]
+        from transformers import DynamicCache
+        out = self._forward(x, pos, DynamicCache())
+        layers = self._layers(out.past_key_values)
+        return (torch.stack([k[0] for k, _ in layers]), torch.stack([v[0] for _, v in layers]))
+
+    def _sample(self, logits: torch.Tensor, temperature: float, do_sample: bool) -> torch.Tensor:
+        if do_sample:
+            probs = torch.softmax(logits.float() / max(temperature, 1e-5), dim=-1)
+            return torch.multinomial(probs, 1)[..., 0]
+        return logits.argmax(dim=-1)
+
+    # ── cache population ─────────────────────────────────────────────────────
+    def warm(self, text: Union[str, Sequence[int]], position_offset: int = 0) -> WarmResult:
+        """Encode and cache every fixed-size chunk of ``text`` (``engine.py:415-507``)."""
+        token_ids = self._encode(text)
+        added, pos, parent = 0, position_offset, None
+        for _, _, ids in fixed_split(token_ids, self.chunk_size, self.min_chunk_tokens):
+            key = chained_hash(ids, parent)
+            if self.store.get(key) is None:
+                k, v = self._encode_to_kv(ids, pos)
+                if self.store.store(DeviceChunk(key, ids, pos, pos + len(ids), k, v)):
+                    added += 1
+            parent = key
+            pos += len(ids)
+        n = len(token_ids)
+        tail = n % self.chunk_size
+        aligned = tail == 0 or tail < self.min_chunk_tokens
+        warning = None if aligned else (
+            f"Prompt length {n} tokens is not a multiple of chunk_size {self.chunk_size}. "
+            f"The last {tail} tokens will not be cached and must be recomputed on every "
+            f"generate() call.")
+        return WarmResult(added, n, self.chunk_size, aligned, tail, warning)
+
+    def _store_prompt_chunks(self, token_ids: TokenIds) -> None:
+        """Cache the prompt's not-yet-cached chunks (``engine.py:919-979``)."""
+        self.warm(token_ids)
+
+    def reset_cache(self) -> None:
+        self.store.clear()
+
+    # ── assembly and seam repair ─────────────────────────────────────────────
+    def _assemble(self, token_ids: TokenIds):
+        chunks, cached_len, boundaries = plan_reuse(token_ids, self.store, self.chunk_size,
+                                                    self.min_chunk_tokens)
+        if not chunks:
+            return None, None, 0, boundaries
+        keys = torch.cat([c.keys for c in chunks], dim=2)
+        values = torch.cat([c.values for c in chunks], dim=2)
+        if self.recompute_strategy == RecomputeStrategy.SELECTIVE and len(boundaries) > 1:
+            keys, values = self._recompute_seams(token_ids, keys, values, boundaries[:-1])
+        return keys, values, cached_len, boundaries
+
+    def _recompute_seams(self, token_ids, keys, values, seams):
+        """``selective_recompute.py:99-184``: re-encode the last ``recompute_overlap``
+        tokens before each seam with the (already repaired) prefix as context."""
+        for _, end in seams:
+            start = max(0, end - self.recompute_overlap)
+            if start >= end:
+                continue
+            cache = self._cache_from(keys[:, :, :start].contiguous(),
+                                     values[:, :, :start].contiguous())
+            x = torch.tensor([token_ids[start:end]], dtype=torch.long, device=self.device)
+            pos = torch.arange(start, end, device=self.device)[None]
+            out = self._forward(x, pos, cache)
+            layers = self._layers(out.past_key_values)
+            fresh_k = torch.stack([k[0, :, start:end] for k, _ in layers])
+            fresh_v = torch.stack([v[0, :, start:end] for _, v in layers])
+            keys = torch.cat([keys[:, :, :start], fresh_k, keys[:, :, end:]], dim=2)
+            values = torch.cat([values[:, :, :start], fresh_v, values[:, :, end:]], dim=2)
+        return keys, values
+
+    # ── generation ────────────────────────────────────────────────────────────
+    def generate(self, prompt: Union[str, Sequence[int]], max_new_tokens: int = 64,
+                 mode: Union[str, GenerationMode] = GenerationMode.CHUNK_KV_REUSE,
+                 temperature: float = 1.0, do_sample: bool = False) -> GenerationResult:
+        torch.cuda.synchronize(self.device)
+        t_start = time.perf_counter()
+        token_ids = self._encode(prompt)
+        mode = GenerationMode(mode)
+        if mode == GenerationMode.CHUNK_KV_REUSE:
+            keys, values, cached_len, _ = self._assemble(token_ids)
+        else:
+            keys = values = None
+            cached_len = 0
+        res = self._decode_batch([token_ids], keys, values, cached_len, max_new_tokens,
+                                 temperature, do_sample, mode.value,
+                                 prompts=[prompt if isinstance(prompt, str) else ""],
+                                 t_start=t_start)[0]
+        if mode == GenerationMode.CHUNK_KV_REUSE:
+            self._store_prompt_chunks(token_ids)
+        return res
+
+    def generate_batch(self, prompts: List[Union[str, Sequence[int]]], max_new_tokens: int = 64,
+                       temperature: float = 1.0, do_sample: bool = False) -> List[GenerationResult]:
+        """Prompts sharing a chunk-aligned prefix: the shared K/V is assembled once and
+        broadcast over the batch (``engine.py:235-365``)."""
+        if len(prompts) == 1:
+            return [self.generate(prompts[0], max_new_tokens, temperature=temperature,
+                                  do_sample=do_sample)]
+        torch.cuda.synchronize(self.device)
+        t_start = time.perf_counter()
+        all_ids = [self._encode(p) for p in prompts]
+        common = find_common_chunk_prefix(all_ids, self.chunk_size)
+        keys = values = None
+        cached_len = 0
+        if common > 0:
+            keys, values, cached_len, _ = self._assemble(all_ids[0][:common + 1])
+        res = self._decode_batch(all_ids, keys, values, cached_len, max_new_tokens, temperature,
+                                 do_sample, "chunk_kv_reuse_batch",
+                                 prompts=[p if isinstance(p, str) else "" for p in prompts],
+                                 t_start=t_start)
+        for ids in all_ids:
+            self._store_prompt_chunks(ids)
+        return res
+
+    def _decode_batch(self, all_ids: List[TokenIds], keys, values, cached_len: int,
+                      max_new_tokens: int, temperature: float, do_sample: bool, mode_name: str,
+                      prompts: List[str], t_start: float) -> List[GenerationResult]:
+        """Suffix prefill over the reused prefix, then decode (``engine.py:634-753``).
+
+        ``ttft_ms`` runs from the start of the ``generate`` call (so it includes
+        prefix assembly and seam repair, which the reference's clock at
+        ``engine.py:648`` leaves out) to the first sampled token on the host.
+        The batch's suffixes must have equal length (as in the reference's batched
+        prefill, which passes no padding mask to the model)."""
+        B = len(all_ids)
+        suffixes = [ids[cached_len:] for ids in all_ids]
+        if len({len(s) for s in suffixes}) != 1:
+            raise NotImplementedError("batched prompts need suffixes of equal length")
+        t0 = t_start
+        live = suffixes[0]
+        if live:
+            cache = self._cache_from(keys, values, B) if keys is not None else None
+            x = torch.tensor(suffixes, dtype=torch.long, device=self.device)
+            pos = torch.arange(cached_len, cached_len + len(live), device=self.device)
+            pos = pos[None].expand(B, -1)
+        else:  # everything cached: re-feed the last token (engine.py:688-712)
+            cache = self._cache_from(keys[:, :, :cached_len - 1].contiguous(),
+                                     values[:, :, :cached_len - 1].contiguous(), B)
+            x = torch.tensor([[ids[-1]] for ids in all_ids], dtype=torch.long, device=self.device)
+            pos = torch.full((B, 1), cached_len - 1, dtype=torch.long, device=self.device)
+        from transformers import DynamicCache
+        out = self._forward(x, pos, cache if cache is not None else DynamicCache())
+        nxt = self._sample(out.logits[:, -1, :], temperature, do_sample)
+        first_logits = out.logits[:, -1, :].float()
+        generated = [[int(t)] for t in nxt.tolist()]          # .tolist() synchronises
+        t_first = time.perf_counter()
+        cache = out.past_key_values
+        cur = cached_len + len(live)
+        done = [g[-1] == self._eos for g in generated]
+        while len(generated[0]) < max_new_tokens and not all(done):
+            x = nxt[:, None]
+            pos = torch.full((B, 1), cur, dtype=torch.long, device=self.device)
+            out = self._forward(x, pos, cache)
+            cache = out.past_key_values
+            nxt = self._sample(out.logits[:, -1, :], temperature, do_sample)
+            for b, t in enumerate(nxt.tolist()):
+                if not done[b]:
+                    generated[b].append(int(t))
+                    done[b] = int(t) == self._eos
+            cur += 1
+        t1 = time.perf_counter()
+        results = []
+        for b in range(B):
+            n = len(all_ids[b])
+            results.append(GenerationResult(
+                mode=mode_name, prompt=prompts[b], output_text=self._decode_text(generated[b]),
+                generated_tokens=len(generated[b]), ttft_ms=(t_first - t0) * 1e3,
+                total_ms=(t1 - t0) * 1e3,
+                tokens_per_sec=len(generated[b]) / max(t1 - t0, 1e-9),
+                kv_reuse_ratio=cached_len / max(n, 1), prompt_tokens=n,
+                cached_tokens=cached_len, first_token_logits=first_logits[b].cpu().numpy(),
+                generated_ids=generated[b]))
+        return results
+
+    def stats(self) -> Dict[str, float]:
+        return self.store.stats()

@@ -207,5 +207,60 @@ def main():
     print("golden fixtures written to", HERE)
 
 
+
+
+def assembly_cases(models, cr):
+    """Reference KVCacheManager + PromptAssembler on toy chunks: what gets reused."""
+    import kvboost.cache_manager as cm
+    import kvboost.prompt_assembler as pa
+    cache = cm.KVCacheManager(max_cache_bytes=1 << 30, device="cpu")
+    reg = cr.ChunkRegistry(chunk_size=128)
+    asm = pa.PromptAssembler(cache_manager=cache, chunk_registry=reg, mode=pa.AssemblyMode.CHUNK_REUSE)
+    rng = np.random.default_rng(21)
+    base = rng.integers(0, 50000, size=1000).tolist()
+
+    def put(ids):
+        parent, pos = None, 0
+        for s, e, sl in reg.split(ids):
+            h = models.chained_hash(sl, parent)
+            kv = ((torch.zeros(1, 1, len(sl), 4), torch.zeros(1, 1, len(sl), 4)),)
+            cache.store(models.CachedChunk(chunk_id=h, text="", token_ids=sl, past_key_values=kv,
+                                           position_start=s, position_end=e, prefix_hash=h,
+                                           content_hash=models.content_hash_from_tokens(sl)))
+            parent = h
+
+    put(base[:640])                     # 5 chunks cached
+    other = rng.integers(0, 50000, size=300).tolist()
+    put(other)                          # an unrelated document (2 chunks + a 44-token tail)
+    prompts = {
+        "full_prefix_plus_tail": base[:640] + rng.integers(0, 50000, size=77).tolist(),
+        "partial_prefix": base[:300] + rng.integers(0, 50000, size=200).tolist(),
+        "diverges_in_chunk_3": base[:256] + [7] + base[257:700],
+        "no_match": rng.integers(0, 50000, size=400).tolist(),
+        "other_doc_tail": other[:300] + [1, 2, 3],
+        "short": base[:20],
+    }
+    out = {}
+    for name, ids in prompts.items():
+        a = asm.assemble(ids, chunk_splits=reg.split(ids))
+        out[name] = {"ids": ids, "cached_length": a.cached_length,
+                     "boundaries": [list(b) for b in a.chunk_boundaries],
+                     "live": len(a.live_token_ids)}
+    import kvboost.batch as kb
+    groups = [[base[:512] + [1] * 40, base[:512] + [2] * 40], [base[:300], base[:200] + [5] * 100],
+              [base[:128] * 2, base[:256]]]
+    out["common_prefix"] = [{"ids": g, "common": kb.find_common_chunk_prefix(g, 128)} for g in groups]
+    out["stored"] = {"base": base[:640], "other": other}
+    return out
+
+
+def main_assembly():
+    fae, kq, models, cr, ba, c2b, pac = _ref()
+    with open(os.path.join(HERE, "assembly.json"), "w") as f:
+        json.dump(assembly_cases(models, cr), f)
+    print("assembly fixture written")
+
+
 if __name__ == "__main__":
     main()
+    main_assembly()
