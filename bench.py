@@ -12,6 +12,10 @@ reference's metric is defined on; the public datasets are not available):
 * ``causal_op`` -- single causal op: batch 2, 16 heads, S 1024, D 64, bf16.
 * ``varlen_d96`` -- 64 requests, suffix ~ U{16..512}, prefix ~ 128*U{0..64},
   32 heads MHA, D 96, fp16, packed varlen.
+* ``ttft_reuse`` -- TTFT at 75% prefix reuse through the engine
+  (``generate_batch``) on a random-init Qwen2.5-3B-architecture decoder, 8
+  prompts x 4096 tokens sharing a warmed 3072-token prefix (its own timing
+  loop; see ``run_ttft``).
 * ``paged_long`` -- 32768-token int8 paged prefix (KIVI per 128-token chunk,
   16-token blocks of an 8192-block pool at a seeded permutation) + 2048 new
   tokens, 64 query / 8 KV heads, D 128, bf16.  With N GPUs the KV heads are
@@ -52,7 +56,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kvboost", choices=["kvboost", "reference"])
     ap.add_argument("--workload", default="reuse_prefill",
-                    choices=["reuse_prefill", "causal_op", "varlen_d96", "paged_long"])
+                    choices=["reuse_prefill", "causal_op", "varlen_d96", "paged_long",
+                             "ttft_reuse"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
     return ap.parse_args()
@@ -347,6 +352,216 @@ class PagedLong:
         return run, fl, "1 of 64 query heads (its KV head gathered and dequantised)"
 
 
+class TtftReuse:
+    """Config 3: TTFT at 75% prefix reuse through the engine on a random-init
+    Qwen2.5-3B-architecture decoder (36 layers, hidden 2048, 16 q / 2 KV heads,
+    D 128, MLP 11008, vocab 151936, bf16).  8 prompts x 4096 seeded token ids share
+    a 3072-token prefix (24 chunks) warmed first; each step is one
+    ``generate_batch`` call with a fresh 1024-token suffix per prompt and greedy
+    decode of 64 tokens.  With N GPUs every rank serves its own batch (replicas)."""
+
+    name = "ttft_reuse"
+    B, PREFIX, SUFFIX, NEW = 8, 3072, 1024, 64
+    LAYERS, HQ, HKV, D, HIDDEN, MLP, VOCAB = 36, 16, 2, 128, 2048, 11008, 151936
+    dtype_name = "bf16"
+    scaling = "weak"
+    desc = ("TTFT at 75% reuse: random-init Qwen2.5-3B architecture (36 layers, hidden 2048, "
+            "Hq16/Hkv2, D128, MLP 11008, vocab 151936, bf16), 8 prompts x 4096 tokens sharing "
+            "a warmed 3072-token prefix, greedy decode of 64 tokens")
+
+    def attn_flops(self):
+        """Algorithmic FLOPs of one layer's suffix-prefill attention (one launch)."""
+        from oracle.attention import attention_flops
+        return attention_flops([self.SUFFIX] * self.B, [self.PREFIX + self.SUFFIX] * self.B,
+                               self.HQ, self.D)
+
+    def config(self):
+        return {"batch": self.B, "prompt_tokens": self.PREFIX + self.SUFFIX,
+                "shared_prefix": self.PREFIX, "suffix_tokens": self.SUFFIX,
+                "new_tokens": self.NEW, "layers": self.LAYERS, "q_heads": self.HQ,
+                "kv_heads": self.HKV, "head_dim": self.D, "hidden": self.HIDDEN,
+                "intermediate": self.MLP, "vocab": self.VOCAB}
+
+    def cpu_sample(self, np):
+        """Attention of the suffix prefill for one prompt, one layer and one KV-head
+        group (8 query heads over 1 KV head) through the oracle; the projection to
+        the whole batch multiplies by prompts x layers x KV heads."""
+        from oracle.attention import attention, attention_flops
+        g = np.random.default_rng(0)
+        grp = self.HQ // self.HKV
+        q = g.standard_normal((1, grp, self.SUFFIX, self.D), dtype=np.float32)
+        k = g.standard_normal((1, 1, self.PREFIX + self.SUFFIX, self.D), dtype=np.float32)
+        v = g.standard_normal((1, 1, self.PREFIX + self.SUFFIX, self.D), dtype=np.float32)
+        fl = attention_flops([self.SUFFIX], [self.PREFIX + self.SUFFIX], grp, self.D)
+
+        def run():
+            attention(q, k, v, 1.0 / math.sqrt(self.D), True, compute_dtype=np.float32)
+        return run, fl, "suffix-prefill attention of 1 prompt x 1 layer x 1 KV-head group"
+
+    def projection(self):
+        return self.B * self.LAYERS * self.HKV
+
+    def model(self, torch, dev):
+        from transformers import Qwen2Config, Qwen2ForCausalLM
+        cfg = Qwen2Config(vocab_size=self.VOCAB, hidden_size=self.HIDDEN,
+                          intermediate_size=self.MLP, num_hidden_layers=self.LAYERS,
+                          num_attention_heads=self.HQ, num_key_value_heads=self.HKV,
+                          max_position_embeddings=32768, rms_norm_eps=1e-6, rope_theta=1e6,
+                          tie_word_embeddings=True, initializer_range=0.02,
+                          attn_implementation="sdpa")
+        torch.manual_seed(0)
+        old = torch.get_default_dtype()
+        torch.set_default_dtype(torch.bfloat16)
+        try:
+            with torch.device(dev):
+                m = Qwen2ForCausalLM(cfg)
+        finally:
+            torch.set_default_dtype(old)
+        with torch.no_grad():   # weights N(0, 0.02), norms 1, biases 0
+            for n, p in m.named_parameters():
+                if p.dim() >= 2:
+                    p.normal_(0.0, 0.02)
+        return m.eval()
+
+    def prompts(self, step, rank):
+        import numpy as np
+        g = np.random.default_rng(1000 + rank)
+        prefix = g.integers(0, self.VOCAB, self.PREFIX).tolist()
+        h = np.random.default_rng(10_000 * (rank + 1) + step)
+        return prefix, [prefix + h.integers(0, self.VOCAB, self.SUFFIX).tolist()
+                        for _ in range(self.B)]
+
+
+def run_ttft(args, torch, dist, rank, world, local, dev):
+    """Config 3 through the engine: TTFT (ms, lower is better)."""
+    import numpy as np
+    from kvboost_b200 import _lib, ops
+    from kvboost_b200.engine import KVBoost
+    w = TtftReuse()
+    eng = KVBoost(w.model(torch, dev), None, recompute_strategy="selective",
+                  max_cache_bytes=48 << 30, device=str(dev))
+    prefix, _ = w.prompts(0, rank)
+    eng.warm(prefix)
+
+    def allmax(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # device-side prefill: the cached prefix broadcast + 8 x 1024-token suffix forward
+    # (36 layers) + argmax, inputs resident, CUDA events on the current stream
+    keys, values, cached, _ = eng._assemble(prefix + [0], repair_seams=False)
+    _, pr = w.prompts(10**6, rank)
+    x = torch.tensor([p[cached:] for p in pr], device=dev)
+    pos = torch.arange(cached, cached + w.SUFFIX, device=dev)[None].expand(w.B, -1)
+
+    def prefill():
+        cache = eng._cache_from(keys, values, w.B)
+        out = eng._forward(x, pos, cache)
+        return out.logits[:, -1].argmax(-1)
+
+    for _ in range(max(3, args.warmup)):
+        prefill()
+    torch.cuda.synchronize()
+    # attention kernel launches timed inside one forward (events on the launching stream)
+    times = []
+    orig = ops.prefill_attention
+
+    def timed(*a, **k):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = orig(*a, **k)
+        e1.record()
+        times.append((e0, e1))
+        return r
+    ops.prefill_attention = timed
+    try:
+        prefill()
+    finally:
+        ops.prefill_attention = orig
+    torch.cuda.synchronize()
+    attn_ms = [a.elapsed_time(b) for a, b in times]
+    dev_ms = []
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            prefill()
+            e1.record()
+            torch.cuda.synchronize()
+            dev_ms.append(allmax(e0.elapsed_time(e1)))
+    # end to end: generate_batch from host token ids to host tokens
+    c0 = _lib.calls_ok
+    ttft, total = [], []
+    for s in range(args.warmup + args.e2e_steps):
+        _, pr = w.prompts(s + 1, rank)
+        if world > 1:
+            dist.barrier()
+        res = eng.generate_batch(pr, max_new_tokens=w.NEW)
+        assert all(r.cached_tokens == w.PREFIX for r in res)
+        if s >= args.warmup:
+            ttft.append(allmax(res[0].ttft_ms))
+            total.append(allmax(res[0].total_ms))
+    launches = (_lib.calls_ok - c0) // (args.warmup + args.e2e_steps)
+    # the same engine on stock SDPA, for the kernel's share of TTFT
+    from kvboost_b200.flash_attn_ext import install_flash_attention, uninstall_flash_attention
+    uninstall_flash_attention(eng.model)
+    sdpa = []
+    for s in range(3):
+        _, pr = w.prompts(500 + s, rank)
+        res = eng.generate_batch(pr, max_new_tokens=1)
+        sdpa.append(allmax(res[0].ttft_ms))
+    install_flash_attention(eng.model)
+
+    peak_tf, _, peak_src = measured_peaks()
+    per_launch = statistics.mean(attn_ms) / 1e3
+    afl = w.attn_flops()
+    value = statistics.mean(dev_ms)
+    e2e = statistics.mean(ttft)
+    line = {
+        "metric": "TTFT at 75% prefix reuse", "value": value, "unit": "ms",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": value, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded token ids, random-init)",
+        "config": {"workload": w.name, "desc": w.desc, **w.config(),
+                   "parallelism": f"replicas x{world}" if world > 1 else "single",
+                   "l2": "model weights 6.2 GB and per-layer K/V > L2",
+                   "timing": "value: CUDA events around the batched suffix prefill (cached "
+                             "prefix resident); e2e: generate_batch wall clock to the first "
+                             "token on the host"},
+        "prefill_tokens_per_s": world * w.B * (w.PREFIX + w.SUFFIX) / (value / 1e3),
+        "computed_tokens_per_s": world * w.B * w.SUFFIX / (value / 1e3),
+        "e2e": {"value": e2e, "unit": "ms", "h2d_bytes_per_step": w.B * w.SUFFIX * 8,
+                "d2h_bytes_per_step": w.B * w.NEW * 8, "total_ms": statistics.mean(total),
+                "ttft_ms_sdpa_engine": statistics.mean(sdpa),
+                "prompt_tokens_per_s": world * w.B * (w.PREFIX + w.SUFFIX) / (e2e / 1e3)},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "kernel": "suffix-prefill attention (per layer)",
+                     "achieved": afl / per_launch / 1e12, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": afl / per_launch / 1e12 / peak_tf, "traffic": None,
+                     "peak_source": f"{peak_src} bf16 dense (burst)",
+                     "algorithmic_flops": afl, "attention_ms_per_prefill": sum(attn_ms),
+                     "attention_share_of_prefill": sum(attn_ms) / statistics.mean(dev_ms)},
+        "clocks": clk.summary(),
+        "device_status": ops.read_status(dev),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cores = cpu_threads()
+        run, sfl, sample = w.cpu_sample(np)
+        _, n, el = time_cpu(run, sfl)
+        line["cpu_baseline"] = {
+            "value": el / n * w.projection() * 1e3, "unit": "ms (suffix-prefill attention only)",
+            "cores": cores, "kind": "port",
+            "sample": f"{n} x {sample}, numpy float32 oracle, {el:.1f} s; projected x"
+                      f"{w.projection()} (prompts x layers x KV heads)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def make_workload(name):
     if name == "reuse_prefill":
         return Dense(name, 4, 32, 8, 256, 896, 128, "bf16",
@@ -356,6 +571,8 @@ def make_workload(name):
         return Dense(name, 2, 16, 16, 1024, 0, 64, "bf16", "single causal op: B2 H16 S1024 D64 bf16")
     if name == "varlen_d96":
         return Varlen()
+    if name == "ttft_reuse":
+        return TtftReuse()
     return PagedLong()
 
 
@@ -448,6 +665,23 @@ def run_reference(args):
     for _ in range(args.steps):
         run()
     el = time.perf_counter() - t0
+    if isinstance(w, TtftReuse):
+        val = el / args.steps * w.projection() * 1e3
+        sample += f", projected x{w.projection()} (prompts x layers x KV heads)"
+        line = {
+            "impl": "reference", "metric": "TTFT at 75% prefix reuse", "value": val,
+            "unit": "ms", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": val, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "desc": w.desc,
+                       "sample": sample + " per step; attention of the suffix prefill only"},
+            "cpu_baseline": {"value": val, "unit": "ms (suffix-prefill attention only)",
+                             "cores": cores, "kind": "port",
+                             "sample": sample + ", numpy float32 restatement (oracle/)"},
+            "e2e": {"value": val, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
     val = fl * args.steps / el / 1e12
     line = {
         "impl": "reference", "metric": "prefill attention TFLOP/s", "value": val,
@@ -481,6 +715,13 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
+
+    if args.workload == "ttft_reuse":
+        run_ttft(args, torch, dist, rank, world, local, dev)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     w = make_workload(args.workload)
     step = w.setup(torch, dev, rank, world)

@@ -104,8 +104,14 @@ def load() -> ctypes.CDLL:
         return lib
 
 
+calls_ok = 0   # successful attention entry-point calls (each launches the kernels once)
+
+
 def check(rc: int, what: str) -> None:
-    if rc != KVB_OK:
+    global calls_ok
+    if rc == KVB_OK:
+        calls_ok += 1
+    else:
         msg = load().kvb_last_error().decode("utf-8", "replace")
         kind = {KVB_ERR_INVALID: "invalid argument", KVB_ERR_UNSUPPORTED: "unsupported",
                 KVB_ERR_CUDA: "CUDA error"}.get(rc, f"error {rc}")

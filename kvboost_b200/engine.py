@@ -349,14 +349,15 @@ class KVBoost:
         self.store.clear()
 
     # ── assembly and seam repair ─────────────────────────────────────────────
-    def _assemble(self, token_ids: TokenIds):
+    def _assemble(self, token_ids: TokenIds, repair_seams: bool = True):
         chunks, cached_len, boundaries = plan_reuse(token_ids, self.store, self.chunk_size,
                                                     self.min_chunk_tokens)
         if not chunks:
             return None, None, 0, boundaries
         keys = torch.cat([c.keys for c in chunks], dim=2)
         values = torch.cat([c.values for c in chunks], dim=2)
-        if self.recompute_strategy == RecomputeStrategy.SELECTIVE and len(boundaries) > 1:
+        if (repair_seams and self.recompute_strategy == RecomputeStrategy.SELECTIVE
+                and len(boundaries) > 1):
             keys, values = self._recompute_seams(token_ids, keys, values, boundaries[:-1])
         return keys, values, cached_len, boundaries
 
@@ -403,7 +404,13 @@ class KVBoost:
     def generate_batch(self, prompts: List[Union[str, Sequence[int]]], max_new_tokens: int = 64,
                        temperature: float = 1.0, do_sample: bool = False) -> List[GenerationResult]:
         """Prompts sharing a chunk-aligned prefix: the shared K/V is assembled once and
-        broadcast over the batch (``engine.py:235-365``)."""
+        broadcast over the batch (``engine.py:235-365``).
+
+        As in the reference, the batched path stitches the cached chunks without
+        seam repair.  Prompts whose suffixes differ in length run as separate
+        sub-batches of equal suffix length over the same shared prefix (the
+        reference right-pads them under a padding mask instead; the prefill
+        kernels take no padding mask)."""
         if len(prompts) == 1:
             return [self.generate(prompts[0], max_new_tokens, temperature=temperature,
                                   do_sample=do_sample)]
@@ -414,11 +421,20 @@ class KVBoost:
         keys = values = None
         cached_len = 0
         if common > 0:
-            keys, values, cached_len, _ = self._assemble(all_ids[0][:common + 1])
-        res = self._decode_batch(all_ids, keys, values, cached_len, max_new_tokens, temperature,
-                                 do_sample, "chunk_kv_reuse_batch",
-                                 prompts=[p if isinstance(p, str) else "" for p in prompts],
-                                 t_start=t_start)
+            keys, values, cached_len, _ = self._assemble(all_ids[0][:common + 1],
+                                                         repair_seams=False)
+        texts = [p if isinstance(p, str) else "" for p in prompts]
+        groups: Dict[int, List[int]] = {}
+        for i, ids in enumerate(all_ids):
+            groups.setdefault(len(ids) - cached_len, []).append(i)
+        res: List[Optional[GenerationResult]] = [None] * len(all_ids)
+        for idx in groups.values():
+            out = self._decode_batch([all_ids[i] for i in idx], keys, values, cached_len,
+                                     max_new_tokens, temperature, do_sample,
+                                     "chunk_kv_reuse_batch", prompts=[texts[i] for i in idx],
+                                     t_start=t_start)
+            for i, r in zip(idx, out):
+                res[i] = r
         for ids in all_ids:
             self._store_prompt_chunks(ids)
         return res
