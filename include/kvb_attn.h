@@ -205,6 +205,30 @@ int64_t kvb_paged_prefill_workspace_bytes(const KvbPagedPrefillParams* params);
 
 int kvb_paged_prefill_fwd(const KvbPagedPrefillParams* params, void* stream);
 
+/* Size of the static device scratch of kvb_paged_prefill_fwd_noalloc: 32 MiB. */
+#define KVB_NOALLOC_SCRATCH_BYTES (32ll << 20)
+
+/* Paged reuse prefill that allocates nothing.  No counterpart in the
+ * reference: it serves callers that must not allocate device memory while a
+ * request runs (a serving loop whose memory is planned up front, a caching
+ * allocator that must not grow between a pool reservation and its release).
+ *
+ * Same params, results and errors as kvb_paged_prefill_fwd, with the prefix
+ * always dequantised once into a fixed static device array of
+ * KVB_NOALLOC_SCRATCH_BYTES per device (params->workspace and
+ * params->workspace_bytes are ignored); the dense attention kernel then reads
+ * it.  Needs 2 * batch * num_kv_heads * round_up(prefix_len + q_len, 128) *
+ * head_dim * 2 bytes; larger requests return KVB_ERR_UNSUPPORTED with the
+ * sizes in kvb_last_error.  Nothing in the scratch needs to start at zero:
+ * the materialise kernel writes every row the attention kernel reads.
+ *
+ * The first call on a device looks up the scratch's address (which loads the
+ * library's module on that device); make it before any stream capture.  Calls
+ * share one scratch per device: two calls that overlap in time (different
+ * streams or host threads) race on it.
+ */
+int kvb_paged_prefill_fwd_noalloc(const KvbPagedPrefillParams* params, void* stream);
+
 /* Human-readable reason for the last non-zero return on this host thread. */
 const char* kvb_last_error(void);
 

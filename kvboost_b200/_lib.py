@@ -20,6 +20,7 @@ KVB_OK = 0
 KVB_ERR_INVALID = 1
 KVB_ERR_UNSUPPORTED = 2
 KVB_ERR_CUDA = -1
+KVB_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -94,6 +95,8 @@ def load() -> ctypes.CDLL:
         lib.kvb_flash_attn_fwd.restype = ctypes.c_int
         lib.kvb_paged_prefill_fwd.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]
         lib.kvb_paged_prefill_fwd.restype = ctypes.c_int
+        lib.kvb_paged_prefill_fwd_noalloc.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]
+        lib.kvb_paged_prefill_fwd_noalloc.restype = ctypes.c_int
         lib.kvb_paged_prefill_workspace_bytes.argtypes = [ctypes.POINTER(KvbPagedPrefillParams)]
         lib.kvb_paged_prefill_workspace_bytes.restype = ctypes.c_int64
         lib.kvb_last_error.argtypes = []

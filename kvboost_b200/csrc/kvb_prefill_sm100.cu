@@ -1104,18 +1104,27 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
 // least kMaterializeMinReaders CTAs.  0 = the fused path is used.
 constexpr int kMaterializeMinReaders = 4;
 
+// Bytes of the dense K/V copy the materialise kernel writes for these params:
+// K and V, [batch, num_kv_heads, kv_pad, D] each, 2-byte elements.
+static int64_t paged_materialize_bytes(const KvbPagedPrefillParams& p) {
+  const int64_t kv_pad = (int64_t)(p.prefix_len + p.q_len + BN - 1) / BN * BN;
+  return 2 * (int64_t)p.batch * p.num_kv_heads * kv_pad * p.head_dim * 2;
+}
+
 static int64_t paged_workspace_bytes(const KvbPagedPrefillParams& p) {
   if (p.q_len <= 0 || p.num_kv_heads <= 0 || p.num_q_heads % p.num_kv_heads) return 0;
   const int group = p.num_q_heads / p.num_kv_heads;
   const int q_tiles = (p.q_len + BM - 1) / BM;
   const int64_t readers = (group % 2 == 0) ? (int64_t)q_tiles * (group / 2) : (q_tiles + 1) / 2;
   if (readers < kMaterializeMinReaders) return 0;
-  const int64_t kv_pad = (int64_t)(p.prefix_len + p.q_len + BN - 1) / BN * BN;
-  return 2 * (int64_t)p.batch * p.num_kv_heads * kv_pad * p.head_dim * 2;
+  return paged_materialize_bytes(p);
 }
 
+// force_materialize: take the materialise strategy whatever the reader count
+// (the no-allocation entry point, whose workspace is always present).
 template <typename T, int D>
-static int launch_paged(const KvbPagedPrefillParams& p, cudaStream_t stream) {
+static int launch_paged(const KvbPagedPrefillParams& p, cudaStream_t stream,
+                        bool force_materialize = false) {
   using G = Geo<D>;
   CUtensorMap tq;
   std::string err;
@@ -1156,7 +1165,7 @@ static int launch_paged(const KvbPagedPrefillParams& p, cudaStream_t stream) {
   pa.num_kv_heads = p.num_kv_heads;
   pa.prefix_len = p.prefix_len;
 
-  const int64_t need = paged_workspace_bytes(p);
+  const int64_t need = force_materialize ? paged_materialize_bytes(p) : paged_workspace_bytes(p);
   if (need > 0 && p.workspace != nullptr && p.workspace_bytes >= need) {
     // Many CTAs read each KV tile: dequantise the prefix once into the
     // workspace, then run the dense kernel over it.
@@ -1367,6 +1376,37 @@ extern "C" int kvb_paged_prefill_fwd(const KvbPagedPrefillParams* params, void* 
     default: return bf ? launch_paged<__nv_bfloat16, 128>(p, s) : launch_paged<__half, 128>(p, s);
   }
 }
+
+// ── hooks for the no-allocation entry point (kvb_noalloc_sm100.cu) ──────────
+// Validate the params and return the workspace bytes the materialise strategy
+// needs, or a negative KVB_ERR_* code (the reason is in kvb_last_error).
+int64_t kvb_detail_paged_materialize_bytes(const KvbPagedPrefillParams& p) {
+  const int rc = validate_paged(p);
+  if (rc != KVB_OK) return -(int64_t)rc;
+  return p.q_len == 0 ? 0 : paged_materialize_bytes(p);
+}
+
+// Paged prefill with the prefix always materialised into `scratch`, which the
+// caller has checked holds kvb_detail_paged_materialize_bytes(p) bytes.
+int kvb_detail_paged_prefill_scratch(const KvbPagedPrefillParams& params, void* scratch,
+                                     int64_t scratch_bytes, cudaStream_t s) {
+  if (params.q_len == 0) return KVB_OK;
+  KvbPagedPrefillParams p = params;
+  p.workspace = scratch;
+  p.workspace_bytes = scratch_bytes;
+  const bool bf = p.dtype == KVB_DTYPE_BF16;
+  switch (p.head_dim) {
+    case 64:
+      return bf ? launch_paged<__nv_bfloat16, 64>(p, s, true) : launch_paged<__half, 64>(p, s, true);
+    case 96:
+      return bf ? launch_paged<__nv_bfloat16, 96>(p, s, true) : launch_paged<__half, 96>(p, s, true);
+    default:
+      return bf ? launch_paged<__nv_bfloat16, 128>(p, s, true)
+                : launch_paged<__half, 128>(p, s, true);
+  }
+}
+
+int kvb_detail_fail(int code, const std::string& msg) { return fail(code, msg); }
 
 extern "C" const char* kvb_last_error(void) { return g_last_error.c_str(); }
 

@@ -316,3 +316,70 @@ def paged_prefill_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.T
         rc = lib.kvb_paged_prefill_fwd(p, _stream_handle(q.device))
     _lib.check(rc, "kvb_paged_prefill_fwd")
     return out, lse
+
+
+def paged_prefill_attention_noalloc(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                                    allocator: DeviceBlockAllocator, layer: int,
+                                    block_tables: torch.Tensor, prefix_len: int,
+                                    out: torch.Tensor, lse: Optional[torch.Tensor] = None,
+                                    prefix_lens: Optional[torch.Tensor] = None,
+                                    softmax_scale: Optional[float] = None, causal: bool = True,
+                                    status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``paged_prefill_attention`` through ``kvb_paged_prefill_fwd_noalloc``.
+
+    For callers that must not allocate device memory while a request runs
+    (memory planned up front, or a caching-allocator pool that must not grow):
+    nothing is allocated here or in the library.  ``out`` (and ``lse``
+    ``[B, Hq, q_len]`` float32, if wanted) are the caller's; ``status`` is an
+    optional preallocated int32 word the kernels OR wait-timeout bits into.
+    The prefix is always dequantised into the library's static 32 MiB
+    per-device scratch, so ``2 * B * Hkv * round_up(prefix_len + q_len, 128) *
+    D * 2`` bytes must fit in it.  Calls that overlap in time share that
+    scratch and race; the first call on a device must precede any stream
+    capture.  Returns ``out``.
+    """
+    _check_tensor("q", q, 4)
+    _check_tensor("k_new", k_new, 4)
+    _check_tensor("v_new", v_new, 4)
+    _check_tensor("out", out, 4)
+    B, Hq, Sq, D = q.shape
+    if k_new.shape != v_new.shape or k_new.shape[0] != B or k_new.shape[2] != Sq or k_new.shape[3] != D:
+        raise RuntimeError("k_new/v_new must be [B, Hkv, q_len, D] matching q")
+    if out.shape != q.shape or out.dtype != q.dtype:
+        raise RuntimeError("out must match q in shape and dtype")
+    Hkv = k_new.shape[1]
+    if Hkv != allocator.num_heads or D != allocator.head_dim:
+        raise RuntimeError("pool heads / head_dim do not match the query")
+    if block_tables.dtype != torch.int32 or not block_tables.is_cuda or block_tables.dim() != 2 \
+            or not block_tables.is_contiguous():
+        raise RuntimeError("block_tables must be a contiguous 2-D int32 CUDA tensor")
+    if lse is not None and (lse.dtype != torch.float32 or tuple(lse.shape) != (B, Hq, Sq)
+                            or lse.stride(2) != 1):
+        raise RuntimeError("lse must be float32 [B, Hq, q_len] with contiguous rows")
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(D)
+    p = _lib.KvbPagedPrefillParams()
+    p.dtype = _DTYPES[q.dtype]
+    p.head_dim, p.batch, p.num_q_heads, p.num_kv_heads = D, B, Hq, Hkv
+    p.q_len, p.causal, p.softmax_scale = Sq, 1 if causal else 0, float(softmax_scale)
+    p.q, p.o = q.data_ptr(), out.data_ptr()
+    p.lse = lse.data_ptr() if lse is not None else None
+    p.q_batch_stride, p.q_head_stride, p.q_row_stride = q.stride(0), q.stride(1), q.stride(2)
+    p.o_batch_stride, p.o_head_stride, p.o_row_stride = out.stride(0), out.stride(1), out.stride(2)
+    if lse is not None:
+        p.lse_batch_stride, p.lse_head_stride = lse.stride(0), lse.stride(1)
+    p.k_new, p.v_new = k_new.data_ptr(), v_new.data_ptr()
+    p.k_new_batch_stride, p.k_new_head_stride, p.k_new_row_stride = k_new.stride()[:3]
+    p.v_new_batch_stride, p.v_new_head_stride, p.v_new_row_stride = v_new.stride()[:3]
+    p.kv_pool = allocator.pools[layer].data_ptr()
+    p.k_scale = allocator.k_scale[layer].data_ptr()
+    p.v_scale = allocator.v_scale[layer].data_ptr()
+    p.num_blocks, p.block_size = allocator.num_blocks, allocator.block_size
+    p.block_tables, p.max_blocks_per_seq = block_tables.data_ptr(), block_tables.shape[1]
+    p.prefix_len = int(prefix_len)
+    p.prefix_lens = prefix_lens.data_ptr() if prefix_lens is not None else None
+    p.status = status.data_ptr() if status is not None else None
+    with torch.cuda.device(q.device):
+        rc = _lib.load().kvb_paged_prefill_fwd_noalloc(p, _stream_handle(q.device))
+    _lib.check(rc, "kvb_paged_prefill_fwd_noalloc")
+    return out
