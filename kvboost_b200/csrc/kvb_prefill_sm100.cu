@@ -48,11 +48,9 @@
 #include "kvb_sm100_ptx.cuh"
 
 // Share of exponent pairs computed on the FMA pipe: pair i of each 32-column
-// chunk uses the polynomial when (i % 4) < KVB_POLY_PAIRS_OF_4.  Measured on
-// B200 the softmax is issue/latency bound rather than MUFU bound, and every
-// non-zero share was slower, so the default keeps all exponentials on MUFU.
-#ifndef KVB_POLY_PAIRS_OF_4
-#define KVB_POLY_PAIRS_OF_4 0
+// chunk uses the polynomial when (i % 8) < KVB_POLY_PAIRS_OF_8.
+#ifndef KVB_POLY_PAIRS_OF_8
+#define KVB_POLY_PAIRS_OF_8 0
 #endif
 // 1: pack bf16 probabilities with integer round-half-up + byte permute
 // instead of the cvt.rn.bf16x2.f32 conversion.
@@ -91,17 +89,20 @@ __device__ long long* g_kvb_trace;
 constexpr int BM = 128;        // query rows per slot (= TMEM lanes)
 constexpr int BN = 128;        // keys per tile
 constexpr int kSlots = 2;      // query tiles per CTA, processed in ping-pong
-// Warp roles.  Dense: warps 0-3 / 4-7 softmax of slot 0 / 1, warp 8 TMA,
-// warp 9 MMA (320 threads).  Paged: warps 8-10 gather + dequantise K/V into
-// shared memory (warp 8 lane 0 also issues the Q TMA), warp 11 MMA (384
-// threads).  Either way no SM sub-partition holds more than 3 warps, which
-// leaves 168 registers per thread.
+// Warp roles.  Dense: warps 0-15 softmax, two warpgroups per slot (slot s,
+// column half h -> warps 4*(2s+h) .. +3; each thread owns one row and half of
+// its columns), warp 16 TMA, warp 17 MMA (576 threads).  Paged: warps 0-3 /
+// 4-7 softmax of slot 0 / 1 (one warpgroup per slot, whole rows), warps 8-10
+// gather + dequantise K/V into shared memory (warp 8 lane 0 also issues the
+// Q TMA), warp 11 MMA (384 threads).
 template <bool PAGED>
 struct Roles {
-  static constexpr int kThreads = PAGED ? 384 : 320;
-  static constexpr int kWarpTma = 8;
-  static constexpr int kWarpMma = PAGED ? 11 : 9;
+  static constexpr int kHalves = PAGED ? 1 : 2;                 // softmax warpgroups per slot
+  static constexpr int kSoftmaxWarps = 4 * kSlots * kHalves;
+  static constexpr int kWarpTma = kSoftmaxWarps;
   static constexpr int kConvWarps = PAGED ? 3 : 0;
+  static constexpr int kWarpMma = PAGED ? kWarpTma + kConvWarps : kWarpTma + 1;
+  static constexpr int kThreads = (kWarpMma + 1) * 32;
 };
 
 template <int D>
@@ -115,7 +116,11 @@ struct Geo {
   static constexpr int QK_STEPS = D / 16;        // K-steps of S = Q K^T
   static constexpr int PV_STEPS = BN / 16;       // K-steps of O += P V
   static constexpr int BAR_BYTES = 512;
-  static constexpr int SMEM_BYTES = 1024 + TILE_BYTES * (kSlots + 2 * NS) + BAR_BYTES;
+  // Row-statistic exchange between the two column halves of a slot:
+  // running maxima and final row sums, [kSlots][2 halves][128 rows] each.
+  static constexpr int XCH_BYTES = 2 * kSlots * 2 * 128 * 4;
+  static constexpr int SMEM_BYTES =
+      1024 + TILE_BYTES * (kSlots + 2 * NS) + BAR_BYTES + XCH_BYTES;
   __host__ __device__ static constexpr uint32_t s_col(int slot) { return slot * 128; }
   __host__ __device__ static constexpr uint32_t o_col(int slot) { return 256 + slot * 128; }
 };
@@ -290,38 +295,46 @@ __device__ __forceinline__ uint32_t cvt_pair<__half>(float lo, float hi) {
   return d;
 }
 
-// Row maximum of the raw scores of one 128-column S tile held in TMEM.
-template <bool MASK>
-__device__ __forceinline__ float tile_row_max(uint32_t tS, int lim) {
-  float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
-    uint32_t r[32];
-    ptx::tmem_ld32(tS + c, r);
-    ptx::tmem_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 32; i += 8) {
-      float x[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        x[e] = (MASK && c + i + e > lim) ? -INFINITY : __uint_as_float(r[i + e]);
-      m0 = fmax3(m0, x[0], x[1]);
-      m1 = fmax3(m1, x[2], x[3]);
-      m2 = fmax3(m2, x[4], x[5]);
-      m3 = fmax3(m3, x[6], x[7]);
-    }
-  }
-  return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+// TMEM load of CW (16 or 32) consecutive columns of this warp's 32 lanes.
+template <int CW>
+__device__ __forceinline__ void tmem_ld_cw(uint32_t taddr, uint32_t (&r)[CW]) {
+  if constexpr (CW == 32)
+    ptx::tmem_ld32(taddr, r);
+  else
+    ptx::tmem_ld16(taddr, r);
 }
 
-// Softmax work on one 32-column chunk already in registers: P pairs packed
-// into pk, partial sums updated.
-template <typename T, bool MASK>
-__device__ __forceinline__ void chunk_exp(const uint32_t (&r)[32], int c, int lim, uint64_t sc2,
-                                          uint64_t nm2, uint64_t& acc0, uint64_t& acc1,
-                                          uint32_t (&pk)[16]) {
+// Row maximum of the raw scores in NCH chunks of CW S columns starting at TMEM
+// address tS (tile column c0).  Columns past `lim` are masked when MASK.
+template <bool MASK, int NCH, int CW>
+__device__ __forceinline__ float cols_row_max(uint32_t tS, int c0, int lim) {
+  float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll 1
+  for (int k = 0; k < NCH; ++k) {
+    uint32_t r[CW];
+    tmem_ld_cw<CW>(tS + k * CW, r);
+    ptx::tmem_wait_ld();
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < CW; i += 4) {
+      float x[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        x[e] = (MASK && c0 + k * CW + i + e > lim) ? -INFINITY : __uint_as_float(r[i + e]);
+      m0 = fmax3(m0, x[0], x[1]);
+      m1 = fmax3(m1, x[2], x[3]);
+    }
+  }
+  return fmaxf(m0, m1);
+}
+
+// Softmax work on one chunk of CW columns already in registers (tile column
+// c): P pairs packed into pk, partial sums updated.
+template <typename T, bool MASK, int CW>
+__device__ __forceinline__ void chunk_exp(const uint32_t (&r)[CW], int c, int lim, uint64_t sc2,
+                                          uint64_t nm2, uint64_t& acc0, uint64_t& acc1,
+                                          uint32_t (&pk)[CW / 2]) {
+#pragma unroll
+  for (int i = 0; i < CW / 2; ++i) {
     float x0 = __uint_as_float(r[2 * i]);
     float x1 = __uint_as_float(r[2 * i + 1]);
     if (MASK) {
@@ -330,7 +343,7 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&r)[32], int c, int li
     }
     const uint64_t a = ffma2(f2pack(x0, x1), sc2, nm2);
     float p0, p1;
-    if (!MASK && (i & 3) < KVB_POLY_PAIRS_OF_4) {
+    if (!MASK && (i & 7) < KVB_POLY_PAIRS_OF_8) {
       ex2_poly_pair(a, p0, p1);
     } else {
       p0 = ptx::ex2(f2lo(a));
@@ -344,44 +357,40 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&r)[32], int c, int li
   }
 }
 
-// P = exp2(s * sl2 - m) for one 128-column S tile, packed as 16-bit pairs
-// into pk (64 words; pair i of S columns 2i, 2i+1).  The four 32-column
-// chunks are double-buffered: the TMEM load of chunk k+1 is in flight while
-// chunk k is exponentiated.  S in TMEM is left intact (the caller stores P
-// only once the row sums pass the range check).  Returns the row sum of P
-// (fp32, before rounding).
-template <typename T, bool MASK>
-__device__ __forceinline__ float tile_exp(uint32_t tS, float sl2, float m_use, int lim,
-                                          uint32_t (&pk)[64]) {
+// P = exp2(s * sl2 - m) for NCH chunks of CW S columns starting at TMEM
+// address tS (tile column c0), packed as 16-bit pairs into pk (pair i of
+// columns c0+2i, c0+2i+1).  The chunks are double-buffered: the TMEM load of
+// chunk k+1 is in flight while chunk k is exponentiated.  S in TMEM is left
+// intact (the caller stores P only once the row sums pass the range check).
+// Returns the row sum of P over these columns (fp32, before rounding).
+template <typename T, bool MASK, int NCH, int CW>
+__device__ __forceinline__ float cols_exp(uint32_t tS, int c0, float sl2, float m_use, int lim,
+                                          uint32_t (&pk)[NCH * CW / 2]) {
   const uint64_t sc2 = f2pack(sl2, sl2);
   const uint64_t nm2 = f2pack(-m_use, -m_use);
   uint64_t acc0 = 0, acc1 = 0;
-  uint32_t ra[32], rb[32];
-  ptx::tmem_ld32(tS + 0, ra);
+  uint32_t ra[CW], rb[CW];
+  tmem_ld_cw<CW>(tS, ra);
   ptx::tmem_wait_ld();
-  ptx::tmem_ld32(tS + 32, rb);
-  chunk_exp<T, MASK>(ra, 0, lim, sc2, nm2, acc0, acc1,
-                     *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
-  ptx::tmem_wait_ld();
-  ptx::tmem_ld32(tS + 64, ra);
-  chunk_exp<T, MASK>(rb, 32, lim, sc2, nm2, acc0, acc1,
-                     *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
-  ptx::tmem_wait_ld();
-  ptx::tmem_ld32(tS + 96, rb);
-  chunk_exp<T, MASK>(ra, 64, lim, sc2, nm2, acc0, acc1,
-                     *reinterpret_cast<uint32_t(*)[16]>(&pk[32]));
-  ptx::tmem_wait_ld();
-  chunk_exp<T, MASK>(rb, 96, lim, sc2, nm2, acc0, acc1,
-                     *reinterpret_cast<uint32_t(*)[16]>(&pk[48]));
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    if (k + 1 < NCH) tmem_ld_cw<CW>(tS + (k + 1) * CW, (k & 1) ? ra : rb);
+    chunk_exp<T, MASK, CW>((k & 1) ? rb : ra, c0 + k * CW, lim, sc2, nm2, acc0, acc1,
+                           *reinterpret_cast<uint32_t(*)[CW / 2]>(&pk[k * CW / 2]));
+    if (k + 1 < NCH) ptx::tmem_wait_ld();
+  }
   const uint64_t t = fadd2(acc0, acc1);
   return f2lo(t) + f2hi(t);
 }
 
-// Write the packed P of one tile over the (already consumed) S columns:
-// S columns [c, c+32) -> P columns [c/2, c/2+16).
-__device__ __forceinline__ void tile_store_p(uint32_t tS, const uint32_t (&pk)[64]) {
-  ptx::tmem_st32(tS + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-  ptx::tmem_st32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+// Write packed P over S columns this thread has already consumed: S columns
+// [c, c+32) of its range become P columns [c/2, c/2+16) relative to the range
+// start tP (its own S columns, so the other half's S is never overwritten).
+template <int NW>
+__device__ __forceinline__ void store_p(uint32_t tP, const uint32_t (&pk)[NW]) {
+#pragma unroll
+  for (int k = 0; k < NW / 32; ++k)
+    ptx::tmem_st32(tP + 32 * k, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32 * k]));
 }
 
 // Gather one 128-token K or V tile for the paged path into the swizzled
@@ -562,6 +571,8 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   uint8_t* sV = sK + G::NS * G::TILE_BYTES;            // NS tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + G::NS * G::TILE_BYTES);
   SharedCtl* ctl = reinterpret_cast<SharedCtl*>(bars + 32);
+  float* xmax = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + G::BAR_BYTES);
+  float* xsum = xmax + kSlots * 2 * 128;
   volatile int* abort_flag = &ctl->abort_flag;
 
   const int warp = threadIdx.x >> 5;
@@ -618,7 +629,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     for (int sl = 0; sl < kSlots; ++sl) {
       ptx::mbar_init(bar(BAR_Q_FULL + sl), 1);
       ptx::mbar_init(bar(BAR_S_FULL + sl), 1);
-      ptx::mbar_init(bar(BAR_P_FULL + sl), 4);  // one arrive per softmax warp
+      ptx::mbar_init(bar(BAR_P_FULL + sl), 4 * Roles<PAGED>::kHalves);  // one per softmax warp
       ptx::mbar_init(bar(BAR_O_FULL + sl), 1);
     }
     ptx::mbar_init(bar(BAR_DRAIN), 1);
@@ -767,6 +778,9 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
         ptx::mma_commit(bar(BAR_S_FULL + sl));
         if (sl == 0 && j < 16) KVB_TRACE_AT(224 + j);
       };
+      // P of S columns [c, c+16) sits at P column (c / PC) * PC + (c % PC) / 2:
+      // each softmax warpgroup packs its PC columns over the start of its own range.
+      constexpr int PC = BN / Roles<PAGED>::kHalves;
       auto issue_pv = [&](int sl, int j) {
         if (j < 16) KVB_TRACE_AT(96 + 96 * sl + j);
         const uint32_t vb = v_lo + (j % G::NS) * TILE16;
@@ -774,8 +788,8 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
         const uint32_t tO = tmem + G::o_col(sl);
 #pragma unroll
         for (int kk = 0; kk < G::PV_STEPS; ++kk)
-          ptx::mma_ts_lohi(tO, tP + kk * 8, vb + ((kk * 16 * 128) >> 4), hi, idesc_o,
-                           (j > 0 || kk > 0) ? 1u : 0u);
+          ptx::mma_ts_lohi(tO, tP + (16 * kk / PC) * PC + (16 * kk % PC) / 2,
+                           vb + ((kk * 16 * 128) >> 4), hi, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         if (sl == 0 && j < 16) KVB_TRACE_AT(240 + j);
       };
 
@@ -838,11 +852,30 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     }
   } else {
     // ============================================================ softmax
-    const int sl = warp >> 2;                     // slot of this warpgroup
+    // Each row of a slot is owned by one thread per column half (kHalves
+    // warpgroups); the two threads of a row sit in the "pair" of warps
+    // w and w + 4 and agree on every decision that touches the row (running
+    // maximum, exact path, abort) through a 64-thread barrier reduction.
+    constexpr int H = Roles<PAGED>::kHalves;
+    constexpr int COLS = BN / H;                  // S columns per thread
+    constexpr int CW = (H == 1) ? 32 : 16;        // TMEM load width
+    constexpr int NCH = COLS / CW;
+    constexpr int DH = D / H;                     // O columns per thread
+    constexpr int OCW = (DH % 32 == 0) ? 32 : 16;
+    const int grp = warp >> 2;
+    const int sl = grp / H;                       // slot of this warpgroup
+    const int hf = grp % H;                       // column half
     const int t = threadIdx.x & 127;              // row within the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_base + G::s_col(sl);
-    const uint32_t tO = tmem + lane_base + G::o_col(sl);
+    const uint32_t tS = tmem + lane_base + G::s_col(sl) + hf * COLS;
+    const uint32_t tO = tmem + lane_base + G::o_col(sl) + hf * DH;
+    const uint32_t pair_bar = 1 + sl * 4 + (warp & 3);
+    auto pair_any = [&](bool v) -> bool {
+      if constexpr (H == 1)
+        return __any_sync(0xffffffffu, v);
+      else
+        return ptx::bar_red_or(pair_bar, 64, v);
+    };
     const int h = head[sl];
     const int q0s = q0[sl];
     const int n_tiles = n_t[sl];
@@ -850,16 +883,14 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     const float sl2 = a.scale_log2;
     constexpr float kSumLimit = std::is_same<T, __half>::value ? 32768.f : 1.0995116e12f;
     float m_run = -INFINITY;
-    float l_run = 0.f;
+    float l_run = 0.f;   // row sum over this thread's columns
     bool ok = true;
 
 #pragma unroll 1
     for (int j = 0; j < n_tiles; ++j) {
       ok = wait_bar(bar(BAR_S_FULL + sl), j & 1, abort_flag, a.status, KVB_STATUS_SOFTMAX_WAIT);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
       ptx::tc_fence_after();
-      if (t == 0 && j < 16) KVB_TRACE_AT(64 + 96 * sl + j);
+      if (t == 0 && hf == 0 && j < 16) KVB_TRACE_AT(64 + 96 * sl + j);
 
       const int kv0 = j * BN;
       const bool need_mask = (kv0 + BN > kv_len) || (a.causal && kv0 + BN - 1 > q0s + off);
@@ -870,56 +901,67 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       // tracking.  The maximum only has to be raised before a probability
       // could leave the range of the P operand (2^40 keeps bf16 P and the
       // fp32 sums far from overflow; fp16 P tops out at 65504, so 2^15
-      // there).  Every probability is bounded by the row sum, so the sum is
-      // the check.  Rows that fail it, and rows without a maximum yet, take
-      // the exact path: tile maximum, O rescale, redo.  The final
-      // normalisation uses the same maximum as the exponentials, so the
-      // result is exact up to rounding.
+      // there).  Every probability is bounded by the sum over the thread's
+      // columns, so that sum is the check.  Rows that fail it (in either
+      // half), and rows without a maximum yet, take the exact path: tile
+      // maximum, O rescale, redo.  The final normalisation uses the same
+      // maximum as the exponentials, so the result is exact up to rounding.
       float alpha = 1.f;
       float sum = 0.f;
-      bool raise = false;
-      uint32_t pk[64];
-      const bool two_pass = __any_sync(0xffffffffu, m_run == -INFINITY);
-      if (!two_pass) {
-        sum = need_mask ? tile_exp<T, true>(tS, sl2, m_run, lim, pk)
-                        : tile_exp<T, false>(tS, sl2, m_run, lim, pk);
-        raise = !(sum <= kSumLimit);  // also catches inf / NaN
+      uint32_t pk[COLS / 2];
+      bool need = !ok || m_run == -INFINITY;
+      if (!__any_sync(0xffffffffu, need)) {
+        sum = need_mask ? cols_exp<T, true, NCH, CW>(tS, hf * COLS, sl2, m_run, lim, pk)
+                        : cols_exp<T, false, NCH, CW>(tS, hf * COLS, sl2, m_run, lim, pk);
+        need = !(sum <= kSumLimit);  // also catches inf / NaN
       }
-      const bool exact = two_pass || __any_sync(0xffffffffu, raise);
-      if (exact) {
-        const float raw_mx =
-            need_mask ? tile_row_max<true>(tS, lim) : tile_row_max<false>(tS, lim);
+      if (pair_any(need)) {
+        if (pair_any(!ok)) {
+          ok = false;
+          break;
+        }
+        float raw_mx = need_mask ? cols_row_max<true, NCH, CW>(tS, hf * COLS, lim)
+                                 : cols_row_max<false, NCH, CW>(tS, hf * COLS, lim);
+        if constexpr (H == 2) {
+          xmax[(sl * 2 + hf) * 128 + t] = raw_mx;
+          ptx::bar_sync(pair_bar, 64);
+          raw_mx = fmaxf(raw_mx, xmax[(sl * 2 + (hf ^ 1)) * 128 + t]);
+        }
         const float m_tile = raw_mx * sl2;
-        raise = m_tile > m_run && raw_mx > -INFINITY && (raise || m_run == -INFINITY);
+        const bool raise = m_tile > m_run && raw_mx > -INFINITY;
         if (raise) {
           alpha = ptx::ex2(m_run - m_tile);
           m_run = m_tile;
         }
-        // O rescale (PV_{j-1} completed before S_j was committed)
+        // O rescale over this thread's columns (PV_{j-1} completed before S_j
+        // was committed)
         if (j > 0 && __any_sync(0xffffffffu, raise)) {
           const float f = raise ? alpha : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < G::DP; c += 32) {
-            uint32_t r[32];
-            ptx::tmem_ld32(tO + c, r);
+          for (int c = 0; c < DH; c += OCW) {
+            uint32_t r[OCW];
+            tmem_ld_cw<OCW>(tO + c, r);
             ptx::tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-            ptx::tmem_st32(tO + c, r);
+            for (int i = 0; i < OCW; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+            if constexpr (OCW == 32)
+              ptx::tmem_st32(tO + c, r);
+            else
+              ptx::tmem_st16(tO + c, r);
           }
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        sum = need_mask ? tile_exp<T, true>(tS, sl2, m_use, lim, pk)
-                        : tile_exp<T, false>(tS, sl2, m_use, lim, pk);
+        sum = need_mask ? cols_exp<T, true, NCH, CW>(tS, hf * COLS, sl2, m_use, lim, pk)
+                        : cols_exp<T, false, NCH, CW>(tS, hf * COLS, sl2, m_use, lim, pk);
       }
-      tile_store_p(tS, pk);
+      store_p<COLS / 2>(tS, pk);
       l_run = l_run * alpha + sum;
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(BAR_P_FULL + sl));
       if (lane == 0 && warp == 3 && j < 16) KVB_TRACE_AT(208 + j);
-      if (t == 0 && j < 16) KVB_TRACE_AT(80 + 96 * sl + j);
+      if (t == 0 && hf == 0 && j < 16) KVB_TRACE_AT(80 + 96 * sl + j);
     }
 
     // ---- epilogue --------------------------------------------------------
@@ -929,35 +971,41 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       have_o = __all_sync(0xffffffffu, have_o);
       ptx::tc_fence_after();
     }
-    if (t == 0 && sl == 0) KVB_TRACE_AT(2);
+    if (t == 0 && sl == 0 && hf == 0) KVB_TRACE_AT(2);
+    float l_tot = l_run;
+    if constexpr (H == 2) {  // both warps of the pair always reach this barrier once
+      xsum[(sl * 2 + hf) * 128 + t] = l_run;
+      ptx::bar_sync(pair_bar, 64);
+      l_tot += xsum[(sl * 2 + (hf ^ 1)) * 128 + t];
+    }
     const bool row_valid = t < q_rows[sl];
-    const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
-    T* orow = reinterpret_cast<T*>(a.o) +
+    const float inv_l = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
+    T* orow = reinterpret_cast<T*>(a.o) + hf * DH +
               (a.cu_q ? (int64_t)(q_base + qi) * a.o_rs + (int64_t)h * a.o_hs
                       : (int64_t)b * a.o_bs + (int64_t)h * a.o_hs + (int64_t)qi * a.o_rs);
 #pragma unroll 1
-    for (int c = 0; c < D; c += 32) {
-      uint32_t r[32];
+    for (int c = 0; c < DH; c += OCW) {
+      uint32_t r[OCW];
       if (n_tiles > 0) {
-        ptx::tmem_ld32(tO + c, r);
+        tmem_ld_cw<OCW>(tO + c, r);
         ptx::tmem_wait_ld();
       }
       if (row_valid) {
-        uint32_t pk[16];
+        uint32_t pk[OCW / 2];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < OCW / 2; ++i) {
           const float o0 = have_o ? __uint_as_float(r[2 * i]) * inv_l : 0.f;
           const float o1 = have_o ? __uint_as_float(r[2 * i + 1]) * inv_l : 0.f;
           pk[i] = pack2<T>(o0, o1);
         }
         uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < OCW / 8; ++i)
           dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
     }
-    if (row_valid && a.lse != nullptr) {
-      const float lse = (l_run > 0.f && have_o) ? (m_run + ptx::lg2(l_run)) * 0.69314718055994531f
+    if (hf == 0 && row_valid && a.lse != nullptr) {
+      const float lse = (l_tot > 0.f && have_o) ? (m_run + ptx::lg2(l_tot)) * 0.69314718055994531f
                                                 : -INFINITY;
       if (a.cu_q)
         a.lse[(int64_t)h * a.lse_hs + q_base + qi] = lse;
