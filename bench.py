@@ -45,8 +45,9 @@ sys.path.insert(0, ROOT)
 L2_BYTES = 126 * 1024 * 1024
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch from the committed
-# ncu captures (profiles/*.md), per workload.
-NCU_TRAFFIC_BYTES = {"reuse_prefill": 27335168}
+# ncu captures (profiles/*.md), per workload.  varlen_d96: the 16-request capture
+# (1 029.9 MB) scaled to the full launch by algorithmic bytes (3 535.4 / 1 004.1 MB).
+NCU_TRAFFIC_BYTES = {"reuse_prefill": 27322880, "varlen_d96": 3626150000}
 
 
 def parse():
@@ -60,6 +61,9 @@ def parse():
                              "ttft_reuse"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--small", action="store_true",
+                    help="a reduced case of the workload for profiler captures (paged_long: "
+                         "8192-token prefix + 1024 new tokens; varlen_d96: first 16 requests)")
     return ap.parse_args()
 
 
@@ -133,6 +137,24 @@ class Dense:
         h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
         return step, h2d, ho.numel() * ho.element_size()
 
+    def gpu_sdpa(self, torch, dev):
+        """The reference's GPU fallback on the same shapes: its ``torch_flash`` tier
+        runs ``F.scaled_dot_product_attention`` with K/V repeated to the query heads
+        and the bottom-right bool mask HF builds (``flash_attn_ext.py:86-103``)."""
+        import torch.nn.functional as F
+        g = torch.Generator(device=dev).manual_seed(77)
+        q = torch.randn(self.B, self.Hq, self.Sq, self.D, generator=g, device=dev).to(self.dt)
+        k = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(self.dt)
+        v = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(self.dt)
+        rep = self.Hq // self.Hkv
+        mask = torch.ones(self.Sq, self.kv, dtype=torch.bool, device=dev).tril(self.kv - self.Sq)
+
+        def run():
+            kk = k.repeat_interleave(rep, 1) if rep > 1 else k
+            vv = v.repeat_interleave(rep, 1) if rep > 1 else v
+            F.scaled_dot_product_attention(q, kk, vv, attn_mask=mask, scale=1.0 / math.sqrt(self.D))
+        return run
+
     def cpu_sample(self, np):
         """One batch element through the oracle (numpy float32)."""
         from oracle.attention import attention, attention_flops
@@ -150,7 +172,7 @@ class Dense:
 class Varlen:
     """Config 4: packed varlen, 32 heads MHA, head_dim 96, fp16."""
 
-    def __init__(self):
+    def __init__(self, small=False):
         import torch
         self.name, self.Hq, self.Hkv, self.D, self.dtype_name = "varlen_d96", 32, 32, 96, "fp16"
         g = torch.Generator().manual_seed(0)
@@ -158,6 +180,8 @@ class Varlen:
         for _ in range(64):
             self.sq.append(int(torch.randint(16, 513, (1,), generator=g)))
             self.pre.append(128 * int(torch.randint(0, 65, (1,), generator=g)))
+        if small:
+            self.sq, self.pre = self.sq[:16], self.pre[:16]
         self.skv = [a + b for a, b in zip(self.sq, self.pre)]
         self.desc = ("varlen: 64 requests, suffix U{16..512}, prefix 128*U{0..64}, "
                      "32 heads MHA, D96, fp16")
@@ -175,7 +199,7 @@ class Varlen:
         return sum(self.sq)
 
     def config(self):
-        return {"requests": 64, "q_heads": self.Hq, "kv_heads": self.Hkv, "head_dim": self.D,
+        return {"requests": len(self.sq), "q_heads": self.Hq, "kv_heads": self.Hkv, "head_dim": self.D,
                 "total_q": sum(self.sq), "total_kv": sum(self.skv)}
 
     def _packed(self, torch, dev, g):
@@ -238,10 +262,12 @@ class Varlen:
 class PagedLong:
     """Config 5: int8 paged 32K prefix + 2048 new tokens, heads split over ranks."""
 
-    def __init__(self):
+    def __init__(self, small=False):
         self.name = "paged_long"
         self.B, self.Hq, self.Hkv, self.D, self.Sq, self.P = 1, 64, 8, 128, 2048, 32768
         self.num_blocks = 8192
+        if small:
+            self.Sq, self.P, self.num_blocks = 1024, 8192, 2048
         self.dtype_name = "bf16"
         self.desc = ("paged int8 reuse: P 32768 (KIVI int8, 16-token blocks, 8192-block pool, "
                      "seeded permutation) + 2048 new tokens, Hq64/Hkv8, D128, bf16")
@@ -562,7 +588,7 @@ def run_ttft(args, torch, dist, rank, world, local, dev):
         print(json.dumps(line), flush=True)
 
 
-def make_workload(name):
+def make_workload(name, small=False):
     if name == "reuse_prefill":
         return Dense(name, 4, 32, 8, 256, 896, 128, "bf16",
                      "prefix-reuse prefill op: B4 Hq32/Hkv8 D128 bf16, 7 cached chunks (896) + "
@@ -570,10 +596,10 @@ def make_workload(name):
     if name == "causal_op":
         return Dense(name, 2, 16, 16, 1024, 0, 64, "bf16", "single causal op: B2 H16 S1024 D64 bf16")
     if name == "varlen_d96":
-        return Varlen()
+        return Varlen(small)
     if name == "ttft_reuse":
         return TtftReuse()
-    return PagedLong()
+    return PagedLong(small)
 
 
 # ─────────────────────────────────────────────────────────── helpers ──
@@ -723,7 +749,7 @@ def main():
             dist.destroy_process_group()
         return
 
-    w = make_workload(args.workload)
+    w = make_workload(args.workload, args.small)
     step = w.setup(torch, dev, rank, world)
     step(0)  # eager call: allocates the status word before capture
     torch.cuda.synchronize()
@@ -790,7 +816,8 @@ def main():
     else:
         achieved, peak, unit = w.bytes() / per_launch_s / 1e9, peak_bw, "GB/s"
         psrc = f"{peak_src} HBM copy"
-    cfg = {"workload": w.name, "desc": w.desc, **w.config(),
+    cfg = {"workload": w.name + (" (small profiling case)" if args.small else ""),
+           "desc": w.desc, **w.config(),
            "parallelism": (f"KV heads split over {world} ranks" if w.scaling == "strong"
                            else f"independent batches x{world}") if world > 1 else "single",
            "l2": w.sets_desc, "timing": "CUDA graph of K launches between events"}
@@ -809,6 +836,23 @@ def main():
         "clocks": clk.summary(),
         "device_status": status,
     }
+    if hasattr(w, "gpu_sdpa"):
+        run = w.gpu_sdpa(torch, dev)
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_sdpa = 20
+        s0.record()
+        for _ in range(n_sdpa):
+            run()
+        s1.record()
+        torch.cuda.synchronize()
+        sms = s0.elapsed_time(s1) / n_sdpa
+        line["gpu_reference_sdpa"] = {
+            "value": fl / (sms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": sms,
+            "what": "the reference's torch_flash tier on this GPU: F.scaled_dot_product_attention "
+                    "with repeat_interleave'd K/V and the bottom-right bool mask, same shapes"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import numpy as np
         cores = cpu_threads()
