@@ -99,6 +99,40 @@ def test_noncausal_and_causal(causal):
     _run(1, 8, 2, 77, 333, 64, torch.float16, causal=causal, seed=3)
 
 
+@pytest.mark.parametrize("D,dtype,Sq,Skv,causal,top_left", [
+    (128, torch.bfloat16, 100, 900, True, False),
+    (96, torch.float16, 128, 1000, True, False),
+    (64, torch.bfloat16, 37, 37, True, False),
+    (128, torch.float16, 50, 60, True, False),      # fewer keys than one half-tile
+    (128, torch.bfloat16, 20, 700, False, False),
+    (96, torch.bfloat16, 90, 400, True, True),
+    (64, torch.float16, 128, 129, True, False),
+])
+def test_single_query_tile_mha(D, dtype, Sq, Skv, causal, top_left):
+    """CTAs holding a single query tile (MHA: no second tile for the slot pair)."""
+    _run(1, 6, 6, Sq, Skv, D, dtype, causal=causal, top_left=top_left, seed=D + Sq + Skv)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_single_tile_running_max_raises_late(dtype):
+    """The exact path (max raise + O rescale) in a CTA with one query tile."""
+    from kvboost_b200.ops import prefill_attention
+    g = torch.Generator().manual_seed(18)
+    B, H, Sq, Skv, D = 1, 2, 90, 1100, 128
+    q = _rand((B, H, Sq, D), dtype, g)
+    ramp = torch.linspace(0.05, 3.0, Skv).view(1, 1, Skv, 1)
+    k = (torch.randn(B, H, Skv, D, generator=g) * ramp).to(dtype)
+    v = _rand((B, H, Skv, D), dtype, g)
+    k[0, 1, 1000] = (q[0, 1, 7].float() * 0.9).to(dtype)
+    k[0, 0, 600] = (q[0, 0, 2].float() * 0.9).to(dtype)
+    o, lse = prefill_attention(q.cuda(), k.cuda(), v.cuda(), 1.0 / math.sqrt(D), True)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = oattn.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                     1.0 / math.sqrt(D), True, compute_dtype=np.float32)
+    assert np.max(np.abs(o.float().cpu().numpy() - o_ref)) <= TOL[dtype]
+    assert np.max(np.abs(lse.cpu().numpy() - lse_ref)) <= LSE_TOL
+
+
 def test_top_left_alignment():
     """SDPA's is_causal alignment (used by the reference's paged path)."""
     _run(1, 4, 2, 40, 200, 128, torch.bfloat16, causal=True, top_left=True, seed=9)
