@@ -58,7 +58,7 @@ def parse():
     ap.add_argument("--impl", default="kvboost", choices=["kvboost", "reference"])
     ap.add_argument("--workload", default="reuse_prefill",
                     choices=["reuse_prefill", "causal_op", "varlen_d96", "paged_long",
-                             "ttft_reuse"])
+                             "ttft_reuse", "paged_long_cp"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--small", action="store_true",
@@ -458,6 +458,124 @@ class TtftReuse:
                         for _ in range(self.B)]
 
 
+def run_cp(args, torch, dist, rank, world, local, dev):
+    """Config 5 with the prefix chunks placed round-robin across the ranks (chunk c on
+    rank c % N): every step all-gathers the int8 pool shards and the suffix K/V
+    (NCCL over NVLink), dequantises prefix + suffix once, and runs this rank's
+    zig-zag query chunks over all 64 query heads.  Strong scaling: the work of one
+    prefill is split N ways."""
+    import numpy as np
+    from kvboost_b200 import context_parallel as cp
+    from kvboost_b200 import ops
+    from kvboost_b200.paged import DeviceBlockAllocator, block_table_tensor, quantize_chunk_int8
+    from oracle.attention import attention_flops
+    P, Sq, Hq, Hkv, D = (8192, 1024, 64, 8, 128) if args.small else (32768, 2048, 64, 8, 128)
+    C = P // 128
+    g = torch.Generator(device=dev).manual_seed(300 + rank)
+    local_pool = cp.make_shard_allocator(C, world, Hkv, D, dev)
+    for slot, c in enumerate(cp.local_chunk_slots(C, world, rank)):
+        k = torch.randn(1, Hkv, 128, D, generator=g, device=dev).to(torch.bfloat16).half()
+        v = torch.randn(1, Hkv, 128, D, generator=g, device=dev).to(torch.bfloat16).half()
+        local_pool.write_chunk_int8(0, list(range(slot * 8, slot * 8 + 8)), *quantize_chunk_int8(k, v))
+    full_pool = DeviceBlockAllocator(1, Hkv, D, world * local_pool.num_blocks, device=dev)
+    rows = 2 * (Sq // (2 * world))
+    q = torch.randn(1, Hq, rows, D, generator=g, device=dev).to(torch.bfloat16)
+    kl = torch.randn(1, Hkv, rows, D, generator=g, device=dev).to(torch.bfloat16)
+    vl = torch.randn(1, Hkv, rows, D, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    kv_pad = (P + Sq + 127) // 128 * 128
+    ws = torch.empty(2 * Hkv * kv_pad * D, dtype=torch.bfloat16, device=dev)
+    table = block_table_tensor([cp.gathered_block_table(C, world)], dev)
+    index = cp.zigzag_token_index(Sq, world).to(dev)
+
+    def step():
+        if world > 1:
+            cp.cp_reuse_prefill(q, kl, vl, local_pool, full_pool, P, Sq, None, None, out, ws,
+                                table, index)
+        else:   # one rank: the shard is the whole pool, the suffix is local
+            cp.cp_rank_prefill(q, local_pool, kl, vl, P, Sq, 1, 0, None, out, ws, table)
+
+    def timed(n):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    timed(max(3, args.warmup))
+    with ClockSampler(local) as clk:
+        ms = timed(args.steps)
+    fl_total = attention_flops([Sq], [P + Sq], Hq, D)
+    value = fl_total * args.steps / (ms / 1e3) / 1e12
+    # one untimed step with events around each phase (same stream)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    if world > 1:
+        dist.barrier()
+    ev[0].record()
+    if world > 1:
+        cp.gather_pool(local_pool, full_pool)
+        kf, vf = cp.gather_suffix_kv(kl, vl, Sq, None, index)
+    else:
+        kf, vf = kl, vl
+    ev[1].record()
+    from kvboost_b200.paged import paged_materialize
+    K, V = paged_materialize(full_pool if world > 1 else local_pool, 0, table, P, kf, vf,
+                             workspace=ws)
+    ev[2].record()
+    c = Sq // (2 * world)
+    for j, (s0, e0_) in enumerate(cp.zigzag_chunks(Sq, world, rank)):
+        ops.prefill_attention(q[:, :, j * c:(j + 1) * c], K[:, :, :P + e0_], V[:, :, :P + e0_],
+                              None, True, out=out[:, :, j * c:(j + 1) * c], return_lse=False)
+    ev[3].record()
+    torch.cuda.synchronize()
+    phases = [ev[i].elapsed_time(ev[i + 1]) for i in range(3)]
+    peak_tf, _, peak_src = measured_peaks()
+    rank_fl = fl_total / world       # zig-zag chunks give every rank the same causal work
+    achieved = rank_fl / (phases[2] / 1e3) / 1e12
+    gathered_bytes = (world - 1) * (local_pool.pools[0].numel() + 4 * local_pool.k_scale[0].numel()
+                                    + 4 * local_pool.v_scale[0].numel()
+                                    + 2 * 2 * kl.numel())
+    line = {
+        "metric": "prefill attention TFLOP/s", "value": value, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "paged_long_cp" + (" (small)" if args.small else ""),
+                   "desc": f"paged int8 reuse, prefix chunks round-robin over {world} ranks: "
+                           f"P {P} + {Sq} new tokens, Hq{Hq}/Hkv{Hkv}, D{D}, bf16; per step "
+                           "NCCL all-gather of pool shards + suffix K/V, dequantise once, "
+                           "zig-zag query chunks",
+                   "parallelism": f"context parallel x{world} (zig-zag query chunks)",
+                   "l2": "pool, workspace and outputs > L2",
+                   "timing": "CUDA events around K eager steps, max over ranks"},
+        "tokens_per_s": Sq * args.steps / (ms / 1e3),
+        "phase_ms": {"gather": phases[0], "materialize": phases[1], "prefill": phases[2]},
+        "gathered_bytes_per_rank": gathered_bytes,
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0,
+                "note": "inputs are device-resident shards by construction of this workload"},
+        "gpu_launches": 3 * args.steps,   # materialise + two prefill launches per step
+        "roofline": {"bound": "tensor", "kernel": "dense prefill over the rank's query chunks",
+                     "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": achieved / peak_tf, "traffic": None,
+                     "peak_source": f"{peak_src} bf16 dense (burst)"},
+        "clocks": clk.summary(),
+        "device_status": ops.read_status(dev),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_ttft(args, torch, dist, rank, world, local, dev):
     """Config 3 through the engine: TTFT (ms, lower is better)."""
     import numpy as np
@@ -742,8 +860,9 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
 
-    if args.workload == "ttft_reuse":
-        run_ttft(args, torch, dist, rank, world, local, dev)
+    if args.workload in ("ttft_reuse", "paged_long_cp"):
+        (run_ttft if args.workload == "ttft_reuse" else run_cp)(args, torch, dist, rank, world,
+                                                                 local, dev)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()

@@ -205,6 +205,19 @@ int64_t kvb_paged_prefill_workspace_bytes(const KvbPagedPrefillParams* params);
 
 int kvb_paged_prefill_fwd(const KvbPagedPrefillParams* params, void* stream);
 
+/* Dequantise and gather the paged prefix of every sequence, followed by its
+ * fresh suffix, into dense K and V: params->workspace receives K then V, each
+ * [batch, num_kv_heads, round_up(prefix_len + q_len, 128), head_dim] in the
+ * compute dtype (rows past a sequence's prefix_len_b + q_len, up to the next
+ * multiple of 128, are zeros; rows past that are left as they were).
+ * workspace_bytes must be at least 2 * batch * num_kv_heads * round_up(...) *
+ * head_dim * 2.  q, o and lse are not used.  The device form of the host path
+ * that gathers each sequence's blocks (cpu_paged/block_allocator.py:178-206),
+ * dequantises them (kv_quantize.py:102-109) and concatenates the chunks
+ * (cache_manager.py:460-471); used where the dense K/V feed several query
+ * ranges (context-parallel query chunks over one gathered pool). */
+int kvb_paged_materialize(const KvbPagedPrefillParams* params, void* stream);
+
 /* Size of the static device scratch of kvb_paged_prefill_fwd_noalloc: 32 MiB. */
 #define KVB_NOALLOC_SCRATCH_BYTES (32ll << 20)
 

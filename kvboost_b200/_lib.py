@@ -95,6 +95,8 @@ def load() -> ctypes.CDLL:
         lib.kvb_flash_attn_fwd.restype = ctypes.c_int
         lib.kvb_paged_prefill_fwd.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]
         lib.kvb_paged_prefill_fwd.restype = ctypes.c_int
+        lib.kvb_paged_materialize.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]
+        lib.kvb_paged_materialize.restype = ctypes.c_int
         lib.kvb_paged_prefill_fwd_noalloc.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]
         lib.kvb_paged_prefill_fwd_noalloc.restype = ctypes.c_int
         lib.kvb_paged_prefill_workspace_bytes.argtypes = [ctypes.POINTER(KvbPagedPrefillParams)]

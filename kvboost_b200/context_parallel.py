@@ -1,0 +1,176 @@
+"""Context-parallel reuse prefill over a chunk-sharded int8 paged pool.
+
+For one very long prompt whose cached 128-token chunks are spread over the GPUs
+of a box (chunk c on rank ``c % G``, at local chunk slot ``c // G``), every rank:
+
+1. all-gathers the pool shards (int8 K/V blocks and their fp32 scales) over
+   NVLink with NCCL, so each rank holds the whole reused prefix;
+2. all-gathers the suffix's own K/V (each rank projected the K/V of its own
+   query rows) and puts it back in token order;
+3. dequantises + gathers prefix and suffix once into dense K/V
+   (``kvb_paged_materialize``);
+4. runs the prefill for its causally balanced share of the query rows over all
+   heads: the suffix is cut into 2G equal chunks and rank r takes chunks r and
+   2G-1-r (zig-zag), each a dense launch whose key range ends at its own last
+   row (bottom-right causal over prefix + suffix).
+
+Outputs stay sharded by query rows.  When the pool is sharded by KV head
+instead, ``bench.py --workload paged_long`` splits the heads with no
+collective at all; this module serves pools placed by chunk.
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from .ops import prefill_attention
+from .paged import DeviceBlockAllocator, block_table_tensor, paged_materialize
+
+CHUNK_TOKENS = 128
+BLOCKS_PER_CHUNK = CHUNK_TOKENS // 16
+
+
+def local_chunk_slots(num_chunks: int, world: int, rank: int) -> List[int]:
+    """Global chunk ids this rank stores, in local slot order."""
+    return list(range(rank, num_chunks, world))
+
+
+def shard_chunks(num_chunks: int, world: int) -> int:
+    """Chunk slots every rank's shard reserves (the largest rank's count)."""
+    return (num_chunks + world - 1) // world
+
+
+def gathered_block_table(num_chunks: int, world: int) -> List[int]:
+    """Block ids of the prefix in the gathered pool, token order.
+
+    Rank r's shard occupies gathered blocks ``[r * n, (r + 1) * n)`` with
+    ``n = shard_chunks * 8``; chunk c sits at local slot ``c // world``.
+    """
+    nlb = shard_chunks(num_chunks, world) * BLOCKS_PER_CHUNK
+    table = []
+    for c in range(num_chunks):
+        base = (c % world) * nlb + (c // world) * BLOCKS_PER_CHUNK
+        table.extend(range(base, base + BLOCKS_PER_CHUNK))
+    return table
+
+
+def zigzag_chunks(q_len: int, world: int, rank: int) -> List[Tuple[int, int]]:
+    """This rank's two query-row ranges: chunks r and 2G-1-r of 2G equal chunks."""
+    n = 2 * world
+    if q_len % n:
+        raise ValueError(f"q_len {q_len} must split into {n} equal chunks")
+    c = q_len // n
+    return [(rank * c, (rank + 1) * c), ((n - 1 - rank) * c, (n - rank) * c)]
+
+
+def zigzag_token_index(q_len: int, world: int) -> torch.Tensor:
+    """Row index that puts all-gathered zig-zag rows (rank-major, two chunks per
+    rank) back in token order."""
+    n = 2 * world
+    c = q_len // n
+    src = torch.empty(q_len, dtype=torch.long)
+    for r in range(world):
+        for j, (s, e) in enumerate(zigzag_chunks(q_len, world, r)):
+            src[s:e] = torch.arange((2 * r + j) * c, (2 * r + j + 1) * c)
+    return src
+
+
+def make_shard_allocator(num_chunks: int, world: int, num_heads: int, head_dim: int,
+                         device) -> DeviceBlockAllocator:
+    """An empty one-layer pool sized for this rank's shard of ``num_chunks`` chunks."""
+    return DeviceBlockAllocator(1, num_heads, head_dim,
+                                shard_chunks(num_chunks, world) * BLOCKS_PER_CHUNK, device=device)
+
+
+def gather_pool(local: DeviceBlockAllocator, full: DeviceBlockAllocator, layer: int = 0,
+                group=None) -> None:
+    """All-gather every rank's shard of ``layer`` into ``full`` (layer 0), NCCL.
+
+    ``full`` must have ``world * local.num_blocks`` blocks.  The int8 blocks and
+    the fp32 scales the kernels read are gathered; the fp16 scale copies are not.
+    """
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    if full.num_blocks != world * local.num_blocks:
+        raise ValueError("full pool must hold world * local blocks")
+    _all_gather(full.pools[0], local.pools[layer], group)
+    _all_gather(full.k_scale[0], local.k_scale[layer], group)
+    _all_gather(full.v_scale[0], local.v_scale[layer], group)
+
+
+def _all_gather(out: torch.Tensor, inp: torch.Tensor, group=None) -> None:
+    """Concatenate every rank's ``inp`` along dim 0 into ``out`` (NCCL: one
+    all_gather_into_tensor; other backends: all_gather of a list)."""
+    import torch.distributed as dist
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, inp, group=group)
+    else:
+        dist.all_gather(list(out.chunk(dist.get_world_size(group))), inp, group=group)
+
+
+def gather_suffix_kv(k_local: torch.Tensor, v_local: torch.Tensor, q_len: int,
+                     group=None, index: Optional[torch.Tensor] = None):
+    """All-gather the suffix K/V rows of every rank's zig-zag chunks and return them
+    in token order, ``[1, Hkv, q_len, D]`` each."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    _, Hkv, rows, D = k_local.shape
+    kv = torch.stack([k_local[0], v_local[0]]).permute(2, 0, 1, 3).contiguous()  # [rows, 2, Hkv, D]
+    buf = torch.empty(world * rows, 2, Hkv, D, dtype=k_local.dtype, device=k_local.device)
+    _all_gather(buf, kv, group)
+    if index is None:
+        index = zigzag_token_index(q_len, world).to(k_local.device)
+    full = buf.index_select(0, index)                        # token order
+    full = full.permute(1, 2, 0, 3)                          # [2, Hkv, q_len, D]
+    return full[0].unsqueeze(0), full[1].unsqueeze(0)
+
+
+def cp_rank_prefill(q_local: torch.Tensor, full_pool: DeviceBlockAllocator,
+                    k_full: torch.Tensor, v_full: torch.Tensor, prefix_len: int, q_len: int,
+                    world: int, rank: int, softmax_scale: Optional[float] = None,
+                    out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
+                    table: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The compute of one rank once the pool and the suffix K/V are gathered:
+    dequantise prefix + suffix once, then one bottom-right-causal launch per
+    zig-zag query chunk, each over the keys up to its own last row."""
+    if prefix_len % CHUNK_TOKENS:
+        raise ValueError("the reused prefix is whole 128-token chunks")
+    if table is None:
+        table = block_table_tensor([gathered_block_table(prefix_len // CHUNK_TOKENS, world)],
+                                   q_local.device)
+    K, V = paged_materialize(full_pool, 0, table, prefix_len, k_full, v_full,
+                             workspace=workspace)
+    if out is None:
+        out = torch.empty_like(q_local)
+    c = q_len // (2 * world)
+    for j, (s, e) in enumerate(zigzag_chunks(q_len, world, rank)):
+        kv_len = prefix_len + e
+        prefill_attention(q_local[:, :, j * c:(j + 1) * c], K[:, :, :kv_len], V[:, :, :kv_len],
+                          softmax_scale, True, out=out[:, :, j * c:(j + 1) * c],
+                          return_lse=False)
+    return out
+
+
+def cp_reuse_prefill(q_local: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
+                     local_pool: DeviceBlockAllocator, full_pool: DeviceBlockAllocator,
+                     prefix_len: int, q_len: int, softmax_scale: Optional[float] = None,
+                     group=None, out: Optional[torch.Tensor] = None,
+                     workspace: Optional[torch.Tensor] = None,
+                     table: Optional[torch.Tensor] = None,
+                     index: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """This rank's share of a context-parallel reuse prefill.
+
+    q_local: ``[1, Hq, 2c, D]`` the rank's zig-zag query rows (chunk r then chunk
+    2G-1-r, c = q_len / 2G); k_local/v_local: ``[1, Hkv, 2c, D]`` the suffix K/V of
+    the same rows; ``local_pool``: this rank's shard of the prefix chunks;
+    ``full_pool``: receives the gathered pool.  Returns ``[1, Hq, 2c, D]``.
+    """
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    gather_pool(local_pool, full_pool, 0, group)
+    k_full, v_full = gather_suffix_kv(k_local, v_local, q_len, group, index)
+    return cp_rank_prefill(q_local, full_pool, k_full, v_full, prefix_len, q_len, world, rank,
+                           softmax_scale, out, workspace, table)

@@ -1168,6 +1168,46 @@ static int64_t paged_workspace_bytes(const KvbPagedPrefillParams& p) {
   return paged_materialize_bytes(p);
 }
 
+static PagedArgs paged_args(const KvbPagedPrefillParams& p) {
+  PagedArgs pa;
+  pa.pool = p.kv_pool;
+  pa.k_scale = p.k_scale;
+  pa.v_scale = p.v_scale;
+  pa.block_table = p.block_tables;
+  pa.prefix_lens = p.prefix_lens;
+  pa.k_new = p.k_new;
+  pa.v_new = p.v_new;
+  pa.kn_bs = p.k_new_batch_stride;
+  pa.kn_hs = p.k_new_head_stride;
+  pa.kn_rs = p.k_new_row_stride;
+  pa.vn_bs = p.v_new_batch_stride;
+  pa.vn_hs = p.v_new_head_stride;
+  pa.vn_rs = p.v_new_row_stride;
+  pa.max_blocks = p.max_blocks_per_seq;
+  pa.num_blocks = p.num_blocks;
+  pa.num_kv_heads = p.num_kv_heads;
+  pa.prefix_len = p.prefix_len;
+  return pa;
+}
+
+// Dense K and V of every sequence, [batch, num_kv_heads, kv_pad, D] each, into
+// the workspace: kv_pad = round_up(prefix_len + q_len, 128).
+template <typename T, int D>
+static int launch_materialize(const KvbPagedPrefillParams& p, cudaStream_t stream) {
+  const PagedArgs pa = paged_args(p);
+  const int kv_pad = (p.prefix_len + p.q_len + BN - 1) / BN * BN;
+  T* wk = reinterpret_cast<T*>(p.workspace);
+  T* wv = wk + (int64_t)p.batch * p.num_kv_heads * kv_pad * D;
+  const int64_t threads = (int64_t)kv_pad * (D / 16) * 2;
+  dim3 mgrid((unsigned)((threads + 255) / 256), p.num_kv_heads, p.batch);
+  kvb_paged_materialize_kernel<T, D><<<mgrid, 256, 0, stream>>>(pa, wk, wv, p.q_len, kv_pad,
+                                                                p.status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return fail(KVB_ERR_CUDA, std::string("materialize launch: ") + cudaGetErrorString(e));
+  return KVB_OK;
+}
+
 // force_materialize: take the materialise strategy whatever the reader count
 // (the no-allocation entry point, whose workspace is always present).
 template <typename T, int D>
@@ -1194,24 +1234,7 @@ static int launch_paged(const KvbPagedPrefillParams& p, cudaStream_t stream,
   a.causal = p.causal;
   a.scale_log2 = p.softmax_scale * 1.4426950408889634f;
   a.status = p.status;
-  PagedArgs pa;
-  pa.pool = p.kv_pool;
-  pa.k_scale = p.k_scale;
-  pa.v_scale = p.v_scale;
-  pa.block_table = p.block_tables;
-  pa.prefix_lens = p.prefix_lens;
-  pa.k_new = p.k_new;
-  pa.v_new = p.v_new;
-  pa.kn_bs = p.k_new_batch_stride;
-  pa.kn_hs = p.k_new_head_stride;
-  pa.kn_rs = p.k_new_row_stride;
-  pa.vn_bs = p.v_new_batch_stride;
-  pa.vn_hs = p.v_new_head_stride;
-  pa.vn_rs = p.v_new_row_stride;
-  pa.max_blocks = p.max_blocks_per_seq;
-  pa.num_blocks = p.num_blocks;
-  pa.num_kv_heads = p.num_kv_heads;
-  pa.prefix_len = p.prefix_len;
+  const PagedArgs pa = paged_args(p);
 
   const int64_t need = force_materialize ? paged_materialize_bytes(p) : paged_workspace_bytes(p);
   if (need > 0 && p.workspace != nullptr && p.workspace_bytes >= need) {
@@ -1422,6 +1445,53 @@ extern "C" int kvb_paged_prefill_fwd(const KvbPagedPrefillParams* params, void* 
     case 64: return bf ? launch_paged<__nv_bfloat16, 64>(p, s) : launch_paged<__half, 64>(p, s);
     case 96: return bf ? launch_paged<__nv_bfloat16, 96>(p, s) : launch_paged<__half, 96>(p, s);
     default: return bf ? launch_paged<__nv_bfloat16, 128>(p, s) : launch_paged<__half, 128>(p, s);
+  }
+}
+
+extern "C" int kvb_paged_materialize(const KvbPagedPrefillParams* params, void* stream) {
+  if (!params) return fail(KVB_ERR_INVALID, "params is NULL");
+  const KvbPagedPrefillParams& p = *params;
+  if (p.dtype != KVB_DTYPE_BF16 && p.dtype != KVB_DTYPE_FP16)
+    return fail(KVB_ERR_INVALID, "dtype must be KVB_DTYPE_BF16 or KVB_DTYPE_FP16");
+  if (p.head_dim != 64 && p.head_dim != 96 && p.head_dim != 128)
+    return fail(KVB_ERR_INVALID,
+                "head_dim must be one of 64, 96, 128, got " + std::to_string(p.head_dim));
+  if (p.batch < 1 || p.num_kv_heads < 1 || p.batch > 65535 || p.num_kv_heads > 65535)
+    return fail(KVB_ERR_INVALID, "batch and num_kv_heads must be in [1, 65535]");
+  if (p.q_len < 0 || p.prefix_len < 0)
+    return fail(KVB_ERR_INVALID, "q_len and prefix_len must be non-negative");
+  if (p.block_size != 16) return fail(KVB_ERR_UNSUPPORTED, "block_size must be 16");
+  if (p.num_blocks < 1 || p.max_blocks_per_seq < 0 ||
+      (int64_t)p.max_blocks_per_seq * 16 < p.prefix_len)
+    return fail(KVB_ERR_INVALID, "num_blocks must be positive and the table cover prefix_len");
+  if (!p.kv_pool || !p.k_scale || !p.v_scale || !p.block_tables)
+    return fail(KVB_ERR_INVALID, "kv_pool, scales and block_tables must be non-null");
+  if (p.q_len > 0 && (!p.k_new || !p.v_new))
+    return fail(KVB_ERR_INVALID, "k_new and v_new must be non-null when q_len > 0");
+  if (!aligned16(p.kv_pool) || !aligned16(p.v_scale) || !aligned16(p.workspace) ||
+      (p.k_new && !aligned16(p.k_new)) || (p.v_new && !aligned16(p.v_new)))
+    return fail(KVB_ERR_INVALID, "kv_pool, v_scale, k_new, v_new and workspace must be 16-byte aligned");
+  if (p.q_len > 0) {
+    const int64_t st[] = {p.k_new_head_stride, p.k_new_row_stride, p.v_new_head_stride,
+                          p.v_new_row_stride};
+    for (int64_t x : st)
+      if (x <= 0 || (x % 8) != 0)
+        return fail(KVB_ERR_INVALID, "k_new/v_new row and head strides must be positive multiples of 8");
+  }
+  const int64_t need = paged_materialize_bytes(p);
+  if (!p.workspace || p.workspace_bytes < need)
+    return fail(KVB_ERR_INVALID, "workspace must hold " + std::to_string(need) + " bytes");
+  if (p.prefix_len + p.q_len == 0) return KVB_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool bf = p.dtype == KVB_DTYPE_BF16;
+  switch (p.head_dim) {
+    case 64:
+      return bf ? launch_materialize<__nv_bfloat16, 64>(p, s) : launch_materialize<__half, 64>(p, s);
+    case 96:
+      return bf ? launch_materialize<__nv_bfloat16, 96>(p, s) : launch_materialize<__half, 96>(p, s);
+    default:
+      return bf ? launch_materialize<__nv_bfloat16, 128>(p, s)
+                : launch_materialize<__half, 128>(p, s);
   }
 }
 

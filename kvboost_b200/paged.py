@@ -383,3 +383,56 @@ def paged_prefill_attention_noalloc(q: torch.Tensor, k_new: torch.Tensor, v_new:
         rc = _lib.load().kvb_paged_prefill_fwd_noalloc(p, _stream_handle(q.device))
     _lib.check(rc, "kvb_paged_prefill_fwd_noalloc")
     return out
+
+
+def paged_materialize(allocator: DeviceBlockAllocator, layer: int, block_tables: torch.Tensor,
+                      prefix_len: int, k_new: torch.Tensor, v_new: torch.Tensor,
+                      prefix_lens: Optional[torch.Tensor] = None,
+                      workspace: Optional[torch.Tensor] = None):
+    """Dense K/V of each sequence: its paged int8 prefix dequantised, then its fresh
+    suffix (``kvb_paged_materialize``).
+
+    ``k_new``/``v_new``: ``[B, Hkv, q_len, D]`` in the compute dtype (q_len may be 0
+    with ``[B, Hkv, 0, D]`` tensors).  Returns ``(K, V)``, each ``[B, Hkv, kv_pad, D]``
+    with ``kv_pad = round_up(prefix_len + q_len, 128)``; sequence b's keys are rows
+    ``[0, prefix_len_b + q_len)``, zeros up to the next multiple of 128.  The device
+    form of the reference's ``read_kv`` + dequantise + concatenate.
+    """
+    _check_tensor("k_new", k_new, 4)
+    _check_tensor("v_new", v_new, 4)
+    if k_new.shape != v_new.shape:
+        raise RuntimeError("k_new and v_new must have the same shape")
+    B, Hkv, Sq, D = k_new.shape
+    if Hkv != allocator.num_heads or D != allocator.head_dim:
+        raise RuntimeError("pool heads / head_dim do not match k_new")
+    if block_tables.dtype != torch.int32 or not block_tables.is_cuda or block_tables.dim() != 2 \
+            or not block_tables.is_contiguous() or block_tables.shape[0] != B:
+        raise RuntimeError("block_tables must be a contiguous [B, max_blocks] int32 CUDA tensor")
+    kv_pad = (int(prefix_len) + Sq + 127) // 128 * 128
+    need = 2 * B * Hkv * kv_pad * D
+    if workspace is None:
+        workspace = torch.empty(need, dtype=k_new.dtype, device=k_new.device)
+    if workspace.dtype != k_new.dtype or workspace.numel() < need or not workspace.is_contiguous():
+        raise RuntimeError(f"workspace must be a contiguous {k_new.dtype} tensor of >= {need} elements")
+    p = _lib.KvbPagedPrefillParams()
+    p.dtype = _DTYPES[k_new.dtype]
+    p.head_dim, p.batch, p.num_q_heads, p.num_kv_heads = D, B, Hkv, Hkv
+    p.q_len = Sq
+    if Sq > 0:
+        p.k_new, p.v_new = k_new.data_ptr(), v_new.data_ptr()
+        p.k_new_batch_stride, p.k_new_head_stride, p.k_new_row_stride = k_new.stride()[:3]
+        p.v_new_batch_stride, p.v_new_head_stride, p.v_new_row_stride = v_new.stride()[:3]
+    p.kv_pool = allocator.pools[layer].data_ptr()
+    p.k_scale = allocator.k_scale[layer].data_ptr()
+    p.v_scale = allocator.v_scale[layer].data_ptr()
+    p.num_blocks, p.block_size = allocator.num_blocks, allocator.block_size
+    p.block_tables, p.max_blocks_per_seq = block_tables.data_ptr(), block_tables.shape[1]
+    p.prefix_len = int(prefix_len)
+    p.prefix_lens = prefix_lens.data_ptr() if prefix_lens is not None else None
+    p.status = status_word(k_new.device).data_ptr()
+    p.workspace, p.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    with torch.cuda.device(k_new.device):
+        rc = _lib.load().kvb_paged_materialize(p, _stream_handle(k_new.device))
+    _lib.check(rc, "kvb_paged_materialize")
+    kv = workspace[:need].view(2, B, Hkv, kv_pad, D)
+    return kv[0], kv[1]

@@ -156,3 +156,82 @@ def test_bad_block_id_is_reported_not_read(fused_only):
     torch.cuda.synchronize()
     assert ops.read_status(torch.device("cuda")) & 16
     assert torch.isfinite(o.float()).all()
+
+
+def test_context_parallel_emulated_two_ranks():
+    """Chunk-sharded pool gathered (here by concatenation, as the NCCL all-gather lays
+    it out) + zig-zag query split: each rank's rows equal the unsharded paged prefill."""
+    from kvboost_b200 import context_parallel as cp
+    from kvboost_b200.paged import (DeviceBlockAllocator, block_table_tensor,
+                                    paged_prefill_attention, quantize_chunk_int8)
+    world, Hq, Hkv, D, C, Sq = 2, 16, 2, 128, 9, 512
+    P = C * 128
+    g = torch.Generator().manual_seed(21)
+    full = DeviceBlockAllocator(1, Hkv, D, C * 8)
+    for c in range(C):
+        k = torch.randn(1, Hkv, 128, D, generator=g).to(torch.bfloat16).half()
+        v = torch.randn(1, Hkv, 128, D, generator=g).to(torch.bfloat16).half()
+        full.write_chunk_int8(0, list(range(c * 8, c * 8 + 8)), *quantize_chunk_int8(k.cuda(), v.cuda()))
+    q = torch.randn(1, Hq, Sq, D, generator=g).to(torch.bfloat16).cuda()
+    kn = torch.randn(1, Hkv, Sq, D, generator=g).to(torch.bfloat16).cuda()
+    vn = torch.randn(1, Hkv, Sq, D, generator=g).to(torch.bfloat16).cuda()
+    ref, _ = paged_prefill_attention(q, kn, vn, full, 0,
+                                     block_table_tensor([list(range(C * 8))], "cuda"), P)
+    # what the all-gather of the per-rank shards produces
+    nb = cp.shard_chunks(C, world) * 8
+    gathered = DeviceBlockAllocator(1, Hkv, D, world * nb)
+    for r in range(world):
+        for slot, c in enumerate(cp.local_chunk_slots(C, world, r)):
+            src, dst = slice(c * 8, c * 8 + 8), slice(r * nb + slot * 8, r * nb + slot * 8 + 8)
+            gathered.pools[0][dst] = full.pools[0][src]
+            gathered.k_scale[0][dst] = full.k_scale[0][src]
+            gathered.v_scale[0][dst] = full.v_scale[0][src]
+    out = torch.empty_like(q)
+    for r in range(world):
+        rows = torch.cat([torch.arange(s, e) for s, e in cp.zigzag_chunks(Sq, world, r)]).cuda()
+        o_local = cp.cp_rank_prefill(q[:, :, rows].contiguous(), gathered, kn, vn, P, Sq, world, r)
+        out[:, :, rows] = o_local
+    torch.cuda.synchronize()
+    assert (out.float() - ref.float()).abs().max().item() <= TOL[torch.bfloat16]
+
+
+def _pool_with_chunks(Hkv, D, chunk_sets, seed, num_blocks=256):
+    """A one-layer int8 pool holding each sequence's chunks at a seeded permutation."""
+    from kvboost_b200.paged import DeviceBlockAllocator, quantize_chunk_int8
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(num_blocks, generator=g).tolist()
+    alloc = DeviceBlockAllocator(1, Hkv, D, num_blocks)
+    tables, pos = [], 0
+    for cs in chunk_sets:
+        tb = []
+        for L in cs:
+            ids = perm[pos:pos + (L + 15) // 16]
+            pos += len(ids)
+            k = torch.randn(1, Hkv, L, D, generator=g).to(torch.float16)
+            v = torch.randn(1, Hkv, L, D, generator=g).to(torch.float16)
+            alloc.write_chunk_int8(0, ids, *quantize_chunk_int8(k.cuda(), v.cuda()))
+            tb.extend(ids)
+        tables.append(tb)
+    return alloc, tables, max(sum(cs) for cs in chunk_sets)
+
+
+def test_materialize_matches_oracle_gather():
+    """kvb_paged_materialize: prefix dequantised through the block table + suffix, rows
+    past the end zero up to the next 128."""
+    from kvboost_b200.paged import block_table_tensor, paged_materialize
+    alloc, tables, P = _pool_with_chunks(2, 64, [[128, 128, 100], [128]], seed=33)
+    kn = torch.randn(2, 2, 40, 64).to(torch.float16).cuda()
+    vn = torch.randn(2, 2, 40, 64).to(torch.float16).cuda()
+    plens = torch.tensor([356, 128], dtype=torch.int32, device="cuda")
+    bt = block_table_tensor(tables, "cuda")
+    K, V = paged_materialize(alloc, 0, bt, 356, kn, vn, prefix_lens=plens)
+    torch.cuda.synchronize()
+    for b, Pb in enumerate([356, 128]):
+        pre = _oracle_prefix(alloc, tables[b], Pb)            # float16 [H, P, D] K then V
+        Kb = K[b].float().cpu().numpy()
+        Vb = V[b].float().cpu().numpy()
+        assert np.array_equal(Kb[:, :Pb], pre[0].astype(np.float32))
+        assert np.array_equal(Vb[:, :Pb], pre[1].astype(np.float32))
+        assert np.array_equal(Kb[:, Pb:Pb + 40], kn[b].float().cpu().numpy())
+        pad_end = (Pb + 40 + 127) // 128 * 128
+        assert not Kb[:, Pb + 40:pad_end].any() and not Vb[:, Pb + 40:pad_end].any()

@@ -64,3 +64,70 @@ def test_head_split_rejects_non_divisor():
     w = bench.make_workload("paged_long")
     with pytest.raises(SystemExit):
         w.local_heads(0, 3)
+
+
+def _cp_worker(rank, world, port, q):
+    """Context-parallel host logic: gather a chunk-sharded int8 pool and the
+    zig-zag suffix K/V over gloo; both must equal the unsharded originals."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from kvboost_b200 import context_parallel as cp
+        from kvboost_b200.paged import DeviceBlockAllocator
+        H, D, C, Sq = 2, 64, 5, 16                      # 5 chunks of 128 tokens, 16-row suffix
+        g = torch.Generator().manual_seed(7)
+        pool = torch.randint(-127, 128, (C * 8, 2, H, 16, D), generator=g, dtype=torch.int8)
+        ks = torch.rand(C * 8, H, 16, generator=g)
+        vs = torch.rand(C * 8, H, D, generator=g)
+        local = cp.make_shard_allocator(C, world, H, D, "cpu")
+        for slot, c in enumerate(cp.local_chunk_slots(C, world, rank)):
+            dst = slice(slot * 8, slot * 8 + 8)
+            local.pools[0][dst] = pool[c * 8:c * 8 + 8]
+            local.k_scale[0][dst] = ks[c * 8:c * 8 + 8]
+            local.v_scale[0][dst] = vs[c * 8:c * 8 + 8]
+        full = DeviceBlockAllocator(1, H, D, world * local.num_blocks, device="cpu")
+        cp.gather_pool(local, full)
+        table = torch.tensor(cp.gathered_block_table(C, world))
+        ok_pool = (torch.equal(full.pools[0][table], pool) and torch.equal(full.k_scale[0][table], ks)
+                   and torch.equal(full.v_scale[0][table], vs))
+        kfull = torch.randn(1, H, Sq, D, generator=g)
+        vfull = torch.randn(1, H, Sq, D, generator=g)
+        rows = torch.cat([torch.arange(s, e) for s, e in cp.zigzag_chunks(Sq, world, rank)])
+        k2, v2 = cp.gather_suffix_kv(kfull[:, :, rows], vfull[:, :, rows], Sq)
+        ok_kv = torch.equal(k2, kfull) and torch.equal(v2, vfull)
+        flags = torch.tensor([int(ok_pool), int(ok_kv)])
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+        if rank == 0:
+            q.put(flags.tolist())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.slow
+def test_context_parallel_gathers_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    flags = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert flags == [1, 1]
+
+
+def test_zigzag_chunks_cover_and_balance():
+    from kvboost_b200 import context_parallel as cp
+    for world in (1, 2, 4, 8):
+        q_len = 2048
+        spans = [sp for r in range(world) for sp in cp.zigzag_chunks(q_len, world, r)]
+        covered = sorted(i for s, e in spans for i in range(s, e))
+        assert covered == list(range(q_len))
+        # causal work of rank r ~ sum of its rows' key counts: equal across ranks
+        work = [sum(e * (e + 1) // 2 - s * (s + 1) // 2 for s, e in cp.zigzag_chunks(q_len, world, r))
+                for r in range(world)]
+        assert max(work) == min(work)
+        idx = cp.zigzag_token_index(q_len, world)
+        assert sorted(idx.tolist()) == list(range(q_len))
