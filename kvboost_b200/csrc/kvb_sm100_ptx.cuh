@@ -73,8 +73,8 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 
-// 4-D tiled tensor load into this CTA's shared memory, completion counted in
-// bytes on `bar`.  No multicast.
+// 4-D tiled tensor load into this CTA's own shared memory only, completion
+// counted in bytes on `bar`.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* m, int x, int y,
                                             int z, int w, uint32_t bar) {
   asm volatile(
