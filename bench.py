@@ -61,6 +61,9 @@ def parse():
                              "ttft_reuse", "paged_long_cp"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cp-gather", default="peers", choices=["peers", "nccl"],
+                    help="paged_long_cp: read peers' shards in place over NVLink inside the "
+                         "dequantise kernel (peers) or all-gather them with NCCL first")
     ap.add_argument("--small", action="store_true",
                     help="a reduced case of the workload for profiler captures (paged_long: "
                          "8192-token prefix + 1024 new tokens; varlen_d96: first 16 requests)")
@@ -471,25 +474,40 @@ def run_cp(args, torch, dist, rank, world, local, dev):
     from oracle.attention import attention_flops
     P, Sq, Hq, Hkv, D = (8192, 1024, 64, 8, 128) if args.small else (32768, 2048, 64, 8, 128)
     C = P // 128
+    peers = args.cp_gather == "peers"
     g = torch.Generator(device=dev).manual_seed(300 + rank)
-    local_pool = cp.make_shard_allocator(C, world, Hkv, D, dev)
+    rows = 2 * (Sq // (2 * world))
+    if peers:
+        shards = cp.PeerShardBuffer(C, world, Hkv, D, Sq, torch.bfloat16, dev,
+                                    symmetric=world > 1)
+        local_pool = shards.alloc
+    else:
+        local_pool = cp.make_shard_allocator(C, world, Hkv, D, dev)
     for slot, c in enumerate(cp.local_chunk_slots(C, world, rank)):
         k = torch.randn(1, Hkv, 128, D, generator=g, device=dev).to(torch.bfloat16).half()
         v = torch.randn(1, Hkv, 128, D, generator=g, device=dev).to(torch.bfloat16).half()
         local_pool.write_chunk_int8(0, list(range(slot * 8, slot * 8 + 8)), *quantize_chunk_int8(k, v))
-    full_pool = DeviceBlockAllocator(1, Hkv, D, world * local_pool.num_blocks, device=dev)
-    rows = 2 * (Sq // (2 * world))
+    full_pool = None if peers else DeviceBlockAllocator(1, Hkv, D, world * local_pool.num_blocks,
+                                                        device=dev)
     q = torch.randn(1, Hq, rows, D, generator=g, device=dev).to(torch.bfloat16)
     kl = torch.randn(1, Hkv, rows, D, generator=g, device=dev).to(torch.bfloat16)
     vl = torch.randn(1, Hkv, rows, D, generator=g, device=dev).to(torch.bfloat16)
+    if peers:   # this rank's suffix rows live in its shard buffer
+        shards.suffix_k.copy_(kl[0])
+        shards.suffix_v.copy_(vl[0])
     out = torch.empty_like(q)
     kv_pad = (P + Sq + 127) // 128 * 128
     ws = torch.empty(2 * Hkv * kv_pad * D, dtype=torch.bfloat16, device=dev)
     table = block_table_tensor([cp.gathered_block_table(C, world)], dev)
     index = cp.zigzag_token_index(Sq, world).to(dev)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
 
     def step():
-        if world > 1:
+        if peers:
+            cp.cp_reuse_prefill_peers(q, shards, P, rank, None, out, ws, table)
+        elif world > 1:
             cp.cp_reuse_prefill(q, kl, vl, local_pool, full_pool, P, Sq, None, None, out, ws,
                                 table, index)
         else:   # one rank: the shard is the whole pool, the suffix is local
@@ -522,15 +540,22 @@ def run_cp(args, torch, dist, rank, world, local, dev):
     if world > 1:
         dist.barrier()
     ev[0].record()
-    if world > 1:
+    if peers:
+        shards.barrier()
+    elif world > 1:
         cp.gather_pool(local_pool, full_pool)
         kf, vf = cp.gather_suffix_kv(kl, vl, Sq, None, index)
     else:
         kf, vf = kl, vl
     ev[1].record()
     from kvboost_b200.paged import paged_materialize
-    K, V = paged_materialize(full_pool if world > 1 else local_pool, 0, table, P, kf, vf,
-                             workspace=ws)
+    if peers:
+        K, V = cp.materialize_from_peers(shards.bases, shards.shard_blocks, shards.zz_rows, Hkv,
+                                         D, torch.bfloat16, table, P, Sq,
+                                         world * shards.shard_blocks, ws)
+    else:
+        K, V = paged_materialize(full_pool if world > 1 else local_pool, 0, table, P, kf, vf,
+                                 workspace=ws)
     ev[2].record()
     c = Sq // (2 * world)
     for j, (s0, e0_) in enumerate(cp.zigzag_chunks(Sq, world, rank)):
@@ -553,14 +578,18 @@ def run_cp(args, torch, dist, rank, world, local, dev):
         "config": {"workload": "paged_long_cp" + (" (small)" if args.small else ""),
                    "desc": f"paged int8 reuse, prefix chunks round-robin over {world} ranks: "
                            f"P {P} + {Sq} new tokens, Hq{Hq}/Hkv{Hkv}, D{D}, bf16; per step "
-                           "NCCL all-gather of pool shards + suffix K/V, dequantise once, "
-                           "zig-zag query chunks",
+                           + ("one kernel reads every rank's shard over NVLink and dequantises"
+                              if peers else "NCCL all-gather of pool shards + suffix K/V, "
+                              "dequantise once") + ", zig-zag query chunks",
                    "parallelism": f"context parallel x{world} (zig-zag query chunks)",
                    "l2": "pool, workspace and outputs > L2",
                    "timing": "CUDA events around K eager steps, max over ranks"},
         "tokens_per_s": Sq * args.steps / (ms / 1e3),
-        "phase_ms": {"gather": phases[0], "materialize": phases[1], "prefill": phases[2]},
+        "phase_ms": {"gather" if not peers else "barrier": phases[0],
+                     "materialize" if not peers else "materialize_from_peers": phases[1],
+                     "prefill": phases[2]},
         "gathered_bytes_per_rank": gathered_bytes,
+        "cp_gather": args.cp_gather,
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0,
                 "note": "inputs are device-resident shards by construction of this workload"},

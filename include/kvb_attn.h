@@ -218,6 +218,41 @@ int kvb_paged_prefill_fwd(const KvbPagedPrefillParams* params, void* stream);
  * ranges (context-parallel query chunks over one gathered pool). */
 int kvb_paged_materialize(const KvbPagedPrefillParams* params, void* stream);
 
+/* Context-parallel shards read in place.  Each rank of a G-GPU group keeps,
+ * in a buffer peer-mapped into every rank (symmetric memory over NVLink), its
+ * shard of a prompt's paged prefix (the gathered block ids
+ * [r * shard_blocks, (r + 1) * shard_blocks)) and the suffix K/V of its
+ * zig-zag query rows (chunks r and 2G-1-r of 2G chunks of zigzag_rows rows),
+ * laid out by kvb_peer_shard_layout.  base[r] is rank r's buffer as mapped in
+ * the calling process. */
+typedef struct KvbPeerShards {
+  const void* base[8];
+  int32_t world;
+  int32_t shard_blocks;
+  int32_t zigzag_rows;
+  int32_t reserved0;
+} KvbPeerShards;
+
+/* Byte offsets of a shard buffer's five regions (pool int8 [shard_blocks, 2,
+ * Hkv, 16, D]; k_scale f32 [shard_blocks, Hkv, 16]; v_scale f32
+ * [shard_blocks, Hkv, D]; suffix K and suffix V [Hkv, 2 * zigzag_rows, D] in
+ * the 16-bit compute dtype) into offsets[0..4]; returns the buffer's size in
+ * bytes, or -1 for invalid arguments.  No counterpart in the reference. */
+int64_t kvb_peer_shard_layout(int num_kv_heads, int head_dim, int shard_blocks,
+                              int zigzag_rows, int64_t* offsets);
+
+/* kvb_paged_materialize for one sequence whose prefix blocks and suffix rows
+ * are spread over the ranks' shard buffers: every block and suffix row is
+ * read from its owner's buffer with plain loads (peer memory over NVLink), so
+ * the gather needs no separate collective.  params: batch 1, num_blocks =
+ * world * shard_blocks, block_tables in gathered ids, q_len = 2 * world *
+ * zigzag_rows, workspace as for kvb_paged_materialize; kv_pool, scales,
+ * k_new and v_new are not used.  The caller orders the peers' writes before
+ * this call (a cross-GPU barrier).  No counterpart in the reference, whose
+ * pool is one host process's memory. */
+int kvb_paged_materialize_peers(const KvbPagedPrefillParams* params,
+                                const KvbPeerShards* shards, void* stream);
+
 /* Size of the static device scratch of kvb_paged_prefill_fwd_noalloc: 32 MiB. */
 #define KVB_NOALLOC_SCRATCH_BYTES (32ll << 20)
 

@@ -43,6 +43,13 @@ class KvbPrefillParams(ctypes.Structure):
     ]
 
 
+class KvbPeerShards(ctypes.Structure):
+    """Mirror of ``KvbPeerShards``."""
+
+    _fields_ = [("base", _vp * 8), ("world", _i32), ("shard_blocks", _i32),
+                ("zigzag_rows", _i32), ("reserved0", _i32)]
+
+
 class KvbPagedPrefillParams(ctypes.Structure):
     """Mirror of ``KvbPagedPrefillParams`` (field order and types must match the header)."""
 
@@ -95,6 +102,12 @@ def load() -> ctypes.CDLL:
         lib.kvb_flash_attn_fwd.restype = ctypes.c_int
         lib.kvb_paged_prefill_fwd.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]
         lib.kvb_paged_prefill_fwd.restype = ctypes.c_int
+        lib.kvb_paged_materialize_peers.argtypes = [ctypes.POINTER(KvbPagedPrefillParams),
+                                                    ctypes.POINTER(KvbPeerShards), _vp]
+        lib.kvb_paged_materialize_peers.restype = ctypes.c_int
+        lib.kvb_peer_shard_layout.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int, ctypes.POINTER(ctypes.c_int64)]
+        lib.kvb_peer_shard_layout.restype = ctypes.c_int64
         lib.kvb_paged_materialize.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]
         lib.kvb_paged_materialize.restype = ctypes.c_int
         lib.kvb_paged_prefill_fwd_noalloc.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]

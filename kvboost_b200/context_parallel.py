@@ -21,11 +21,13 @@ collective at all; this module serves pools placed by chunk.
 
 from __future__ import annotations
 
+import ctypes
 from typing import List, Optional, Sequence, Tuple
 
 import torch
 
-from .ops import prefill_attention
+from . import _lib
+from .ops import _DTYPES, _stream_handle, prefill_attention, status_word
 from .paged import DeviceBlockAllocator, block_table_tensor, paged_materialize
 
 CHUNK_TOKENS = 128
@@ -142,6 +144,14 @@ def cp_rank_prefill(q_local: torch.Tensor, full_pool: DeviceBlockAllocator,
                                    q_local.device)
     K, V = paged_materialize(full_pool, 0, table, prefix_len, k_full, v_full,
                              workspace=workspace)
+    return zigzag_prefill(q_local, K, V, prefix_len, q_len, world, rank, softmax_scale, out)
+
+
+def zigzag_prefill(q_local: torch.Tensor, K: torch.Tensor, V: torch.Tensor, prefix_len: int,
+                   q_len: int, world: int, rank: int, softmax_scale: Optional[float] = None,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One bottom-right-causal launch per zig-zag query chunk of this rank, each over
+    the dense keys up to its own last row."""
     if out is None:
         out = torch.empty_like(q_local)
     c = q_len // (2 * world)
@@ -151,6 +161,117 @@ def cp_rank_prefill(q_local: torch.Tensor, full_pool: DeviceBlockAllocator,
                           softmax_scale, True, out=out[:, :, j * c:(j + 1) * c],
                           return_lse=False)
     return out
+
+
+class PeerShardBuffer:
+    """This rank's shard of a context-parallel prompt, in memory the other ranks
+    read directly over NVLink.
+
+    One buffer (``kvb_peer_shard_layout``) holds the rank's prefix chunks as an
+    int8 pool (``.alloc``, a one-layer ``DeviceBlockAllocator`` whose pool and
+    fp32 scales are views of the buffer) and the suffix K/V of its zig-zag query
+    rows (``.suffix_k`` / ``.suffix_v``, ``[Hkv, 2c, D]``).  With ``symmetric``
+    the buffer comes from torch's symmetric memory and is mapped into every rank
+    (``.bases`` = every rank's buffer address in this process); otherwise it is
+    plain device memory and the caller supplies the bases (one process holding
+    several ranks' shards).
+    """
+
+    def __init__(self, num_chunks: int, world: int, num_kv_heads: int, head_dim: int,
+                 q_len: int, dtype=torch.bfloat16, device="cuda", group=None,
+                 symmetric: bool = True):
+        self.world = world
+        self.num_chunks = num_chunks
+        self.shard_blocks = shard_chunks(num_chunks, world) * BLOCKS_PER_CHUNK
+        if q_len % (2 * world):
+            raise ValueError(f"q_len {q_len} must split into {2 * world} equal chunks")
+        self.zz_rows = q_len // (2 * world)
+        self.q_len, self.dtype = q_len, dtype
+        off = (ctypes.c_int64 * 5)()
+        total = _lib.load().kvb_peer_shard_layout(num_kv_heads, head_dim, self.shard_blocks,
+                                                  self.zz_rows, off)
+        if total < 0:
+            raise ValueError("unsupported shard geometry")
+        self.offsets = list(off)
+        self.handle = None
+        if symmetric:
+            import torch.distributed as dist
+            import torch.distributed._symmetric_memory as symm_mem
+            self.buf = symm_mem.empty(total, dtype=torch.uint8, device=device)
+            grp = group if group is not None else dist.group.WORLD
+            self.handle = symm_mem.rendezvous(self.buf, grp)
+            self.bases = [int(p) for p in self.handle.buffer_ptrs]
+        else:
+            self.buf = torch.zeros(total, dtype=torch.uint8, device=device)
+            self.bases = [self.buf.data_ptr()]
+        H, D, sb, r2 = num_kv_heads, head_dim, self.shard_blocks, 2 * self.zz_rows
+        b = self.buf
+        self.alloc = DeviceBlockAllocator(1, H, D, sb, device=device)
+        self.alloc.pools[0] = b[off[0]:off[1]].view(torch.int8).view(sb, 2, H, 16, D)
+        self.alloc.k_scale[0] = b[off[1]:off[2]].view(torch.float32).view(sb, H, 16)
+        self.alloc.v_scale[0] = b[off[2]:off[3]].view(torch.float32).view(sb, H, D)
+        self.suffix_k = b[off[3]:off[4]].view(dtype).view(H, r2, D)
+        self.suffix_v = b[off[4]:total].view(dtype).view(H, r2, D)
+
+    def barrier(self, timeout_ms: int = 2000) -> None:
+        """Every rank's writes to its shard buffer are visible to the others after this
+        (a device-side barrier over the peers' signal pads, bounded by the timeout)."""
+        if self.handle is not None:
+            self.handle.barrier(channel=0, timeout_ms=timeout_ms)
+
+
+def materialize_from_peers(bases: Sequence[int], shard_blocks: int, zz_rows: int,
+                           num_kv_heads: int, head_dim: int, dtype, table: torch.Tensor,
+                           prefix_len: int, q_len: int, num_blocks: int,
+                           workspace: Optional[torch.Tensor] = None):
+    """Dense K/V of the whole prompt read from every rank's shard buffer in place
+    (``kvb_paged_materialize_peers``); returns ``(K, V)`` ``[1, Hkv, kv_pad, D]``."""
+    world = len(bases)
+    kv_pad = (int(prefix_len) + q_len + 127) // 128 * 128
+    need = 2 * num_kv_heads * kv_pad * head_dim
+    dev = table.device
+    if workspace is None:
+        workspace = torch.empty(need, dtype=dtype, device=dev)
+    if workspace.dtype != dtype or workspace.numel() < need:
+        raise RuntimeError(f"workspace must be a {dtype} tensor of >= {need} elements")
+    p = _lib.KvbPagedPrefillParams()
+    p.dtype = _DTYPES[dtype]
+    p.head_dim, p.batch, p.num_q_heads, p.num_kv_heads = head_dim, 1, num_kv_heads, num_kv_heads
+    p.q_len, p.prefix_len = q_len, int(prefix_len)
+    p.num_blocks, p.block_size = num_blocks, 16
+    p.block_tables, p.max_blocks_per_seq = table.data_ptr(), table.shape[1]
+    p.status = status_word(dev).data_ptr()
+    p.workspace, p.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    sh = _lib.KvbPeerShards()
+    for r, ptr in enumerate(bases):
+        sh.base[r] = ptr
+    sh.world, sh.shard_blocks, sh.zigzag_rows = world, shard_blocks, zz_rows
+    with torch.cuda.device(dev):
+        rc = _lib.load().kvb_paged_materialize_peers(p, sh, _stream_handle(dev))
+    _lib.check(rc, "kvb_paged_materialize_peers")
+    kv = workspace[:need].view(2, 1, num_kv_heads, kv_pad, head_dim)
+    return kv[0], kv[1]
+
+
+def cp_reuse_prefill_peers(q_local: torch.Tensor, shards: PeerShardBuffer, prefix_len: int,
+                           rank: int, softmax_scale: Optional[float] = None,
+                           out: Optional[torch.Tensor] = None,
+                           workspace: Optional[torch.Tensor] = None,
+                           table: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """This rank's share of a context-parallel reuse prefill with the gather fused
+    into the dequantise pass: a cross-GPU barrier, one kernel that reads every
+    block and suffix row from its owner's buffer over NVLink into dense K/V, then
+    the zig-zag launches.  ``shards.suffix_k/v`` must hold this rank's rows."""
+    H, _, D = shards.suffix_k.shape
+    if table is None:
+        table = block_table_tensor([gathered_block_table(prefix_len // CHUNK_TOKENS, shards.world)],
+                                   q_local.device)
+    shards.barrier()
+    K, V = materialize_from_peers(shards.bases, shards.shard_blocks, shards.zz_rows, H, D,
+                                  shards.dtype, table, prefix_len, shards.q_len,
+                                  shards.world * shards.shard_blocks, workspace)
+    return zigzag_prefill(q_local, K, V, prefix_len, shards.q_len, shards.world, rank,
+                          softmax_scale, out)
 
 
 def cp_reuse_prefill(q_local: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,

@@ -483,9 +483,36 @@ __device__ __forceinline__ void gather_kv_tile(uint8_t* dst, const PagedArgs& pa
 // dequantise the same tiles (long suffixes under GQA).  One thread per 16
 // elements; token rows in [kv_len_b, kv_len_b rounded up to 128) are zeroed so
 // the attention kernel never reads uninitialised padding.
-template <typename T, int D>
+// Context-parallel shards read in place over NVLink: rank r's shard buffer
+// (peer-mapped into this process) holds its prefix blocks, their scales and
+// the suffix K/V of its zig-zag query rows:
+//   [pool int8  shard_blocks x 2 x Hkv x 16 x D]
+//   [k_scale f32 shard_blocks x Hkv x 16] [v_scale f32 shard_blocks x Hkv x D]
+//   [suffix K  Hkv x 2c x D] [suffix V  Hkv x 2c x D]   (c = zig-zag chunk rows)
+// Gathered block id blk lives on rank blk / shard_blocks; suffix row s lies in
+// zig-zag chunk n = s / c, owned by rank n (n < world) or 2 world - 1 - n.
+constexpr int kMaxPeers = 8;
+struct PeerArgs {
+  const uint8_t* base[kMaxPeers];
+  int world;
+  int shard_blocks;
+  int zz_rows;
+  int64_t kscale_off, vscale_off, suffix_off, suffix_v_off;
+};
+
+// peer.base[r] by a select chain, so the kernel parameter is read from
+// parameter space rather than copied to local memory for a dynamic index.
+__device__ __forceinline__ const uint8_t* peer_base(const PeerArgs& peer, int r) {
+  const uint8_t* b = peer.base[0];
+#pragma unroll
+  for (int i = 1; i < kMaxPeers; ++i) b = (r == i) ? peer.base[i] : b;
+  return b;
+}
+
+template <typename T, int D, bool PEER>
 __global__ void __launch_bounds__(256)
-    kvb_paged_materialize_kernel(PagedArgs pa, T* wk, T* wv, int q_len, int kv_pad, int* status) {
+    kvb_paged_materialize_kernel(PagedArgs pa, T* wk, T* wv, int q_len, int kv_pad, int* status,
+                                 PeerArgs peer) {
   constexpr int NCH = D / 16;
   const int b = blockIdx.z;
   const int kvh = blockIdx.y;
@@ -508,20 +535,33 @@ __global__ void __launch_bounds__(256)
         if (status) atomicOr(status, KVB_STATUS_BAD_BLOCK);
       } else {
         const int slot = tok & 15;
-        const int64_t hb = (int64_t)blk * pa.num_kv_heads + kvh;
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(
-            pa.pool + (((int64_t)blk * 2 + kv) * pa.num_kv_heads + kvh) * 16 * D +
-            (int64_t)slot * D + ch * 16));
+        const int8_t* pool = pa.pool;
+        const float* kscale = pa.k_scale;
+        const float* vscale = pa.v_scale;
+        int lb = blk;
+        if (PEER) {  // the owning rank's shard, read in place (plain loads over NVLink)
+          const int r = blk / peer.shard_blocks;
+          lb = blk - r * peer.shard_blocks;
+          const uint8_t* base = peer_base(peer, r);
+          pool = reinterpret_cast<const int8_t*>(base);
+          kscale = reinterpret_cast<const float*>(base + peer.kscale_off);
+          vscale = reinterpret_cast<const float*>(base + peer.vscale_off);
+        }
+        const int64_t hb = (int64_t)lb * pa.num_kv_heads + kvh;
+        const uint4* qp = reinterpret_cast<const uint4*>(
+            pool + (((int64_t)lb * 2 + kv) * pa.num_kv_heads + kvh) * 16 * D +
+            (int64_t)slot * D + ch * 16);
+        const uint4 q = PEER ? *qp : __ldg(qp);
         float sc[16];
         if (kv == 0) {
-          const float sk = __ldg(pa.k_scale + hb * 16 + slot);
+          const float sk = PEER ? kscale[hb * 16 + slot] : __ldg(kscale + hb * 16 + slot);
 #pragma unroll
           for (int e = 0; e < 16; ++e) sc[e] = sk;
         } else {
-          const float4* sp = reinterpret_cast<const float4*>(pa.v_scale + hb * D + ch * 16);
+          const float4* sp = reinterpret_cast<const float4*>(vscale + hb * D + ch * 16);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float4 f = __ldg(sp + e);
+            const float4 f = PEER ? sp[e] : __ldg(sp + e);
             sc[4 * e] = f.x; sc[4 * e + 1] = f.y; sc[4 * e + 2] = f.z; sc[4 * e + 3] = f.w;
           }
         }
@@ -539,6 +579,17 @@ __global__ void __launch_bounds__(256)
         w0 = make_uint4(o[0], o[1], o[2], o[3]);
         w1 = make_uint4(o[4], o[5], o[6], o[7]);
       }
+    } else if (PEER) {
+      const int sr = tok - P;
+      const int n = sr / peer.zz_rows;
+      const int r = n < peer.world ? n : 2 * peer.world - 1 - n;
+      const int row = (n < peer.world ? 0 : peer.zz_rows) + (sr - n * peer.zz_rows);
+      const T* fresh = reinterpret_cast<const T*>(
+          peer_base(peer, r) + (kv ? peer.suffix_v_off : peer.suffix_off));
+      const uint4* src = reinterpret_cast<const uint4*>(
+          fresh + ((int64_t)kvh * 2 * peer.zz_rows + row) * D + ch * 16);
+      w0 = src[0];
+      w1 = src[1];
     } else {
       const T* fresh = reinterpret_cast<const T*>(kv ? pa.v_new : pa.k_new);
       const int64_t bs = kv ? pa.vn_bs : pa.kn_bs, hs = kv ? pa.vn_hs : pa.kn_hs,
@@ -1193,15 +1244,20 @@ static PagedArgs paged_args(const KvbPagedPrefillParams& p) {
 // Dense K and V of every sequence, [batch, num_kv_heads, kv_pad, D] each, into
 // the workspace: kv_pad = round_up(prefix_len + q_len, 128).
 template <typename T, int D>
-static int launch_materialize(const KvbPagedPrefillParams& p, cudaStream_t stream) {
+static int launch_materialize(const KvbPagedPrefillParams& p, cudaStream_t stream,
+                              const PeerArgs* peer = nullptr) {
   const PagedArgs pa = paged_args(p);
   const int kv_pad = (p.prefix_len + p.q_len + BN - 1) / BN * BN;
   T* wk = reinterpret_cast<T*>(p.workspace);
   T* wv = wk + (int64_t)p.batch * p.num_kv_heads * kv_pad * D;
   const int64_t threads = (int64_t)kv_pad * (D / 16) * 2;
   dim3 mgrid((unsigned)((threads + 255) / 256), p.num_kv_heads, p.batch);
-  kvb_paged_materialize_kernel<T, D><<<mgrid, 256, 0, stream>>>(pa, wk, wv, p.q_len, kv_pad,
-                                                                p.status);
+  if (peer)
+    kvb_paged_materialize_kernel<T, D, true><<<mgrid, 256, 0, stream>>>(
+        pa, wk, wv, p.q_len, kv_pad, p.status, *peer);
+  else
+    kvb_paged_materialize_kernel<T, D, false><<<mgrid, 256, 0, stream>>>(
+        pa, wk, wv, p.q_len, kv_pad, p.status, PeerArgs{});
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return fail(KVB_ERR_CUDA, std::string("materialize launch: ") + cudaGetErrorString(e));
@@ -1245,8 +1301,8 @@ static int launch_paged(const KvbPagedPrefillParams& p, cudaStream_t stream,
     T* wv = wk + (int64_t)p.batch * p.num_kv_heads * kv_pad * D;
     const int64_t threads = (int64_t)kv_pad * (D / 16) * 2;
     dim3 mgrid((unsigned)((threads + 255) / 256), p.num_kv_heads, p.batch);
-    kvb_paged_materialize_kernel<T, D><<<mgrid, 256, 0, stream>>>(pa, wk, wv, p.q_len, kv_pad,
-                                                                  p.status);
+    kvb_paged_materialize_kernel<T, D, false><<<mgrid, 256, 0, stream>>>(
+        pa, wk, wv, p.q_len, kv_pad, p.status, PeerArgs{});
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
       return fail(KVB_ERR_CUDA, std::string("materialize launch: ") + cudaGetErrorString(e));
@@ -1492,6 +1548,79 @@ extern "C" int kvb_paged_materialize(const KvbPagedPrefillParams* params, void* 
     default:
       return bf ? launch_materialize<__nv_bfloat16, 128>(p, s)
                 : launch_materialize<__half, 128>(p, s);
+  }
+}
+
+extern "C" int64_t kvb_peer_shard_layout(int num_kv_heads, int head_dim, int shard_blocks,
+                                         int zigzag_rows, int64_t* offsets) {
+  if (num_kv_heads < 1 || (head_dim != 64 && head_dim != 96 && head_dim != 128) ||
+      shard_blocks < 1 || zigzag_rows < 0)
+    return -1;
+  const int64_t pool = (int64_t)shard_blocks * 2 * num_kv_heads * 16 * head_dim;
+  const int64_t ks = (int64_t)shard_blocks * num_kv_heads * 16 * 4;
+  const int64_t vs = (int64_t)shard_blocks * num_kv_heads * head_dim * 4;
+  const int64_t sfx = (int64_t)num_kv_heads * 2 * zigzag_rows * head_dim * 2;
+  if (offsets) {
+    offsets[0] = 0;                     // pool
+    offsets[1] = pool;                  // k_scale
+    offsets[2] = pool + ks;             // v_scale
+    offsets[3] = pool + ks + vs;        // suffix K
+    offsets[4] = pool + ks + vs + sfx;  // suffix V
+  }
+  return pool + ks + vs + 2 * sfx;
+}
+
+extern "C" int kvb_paged_materialize_peers(const KvbPagedPrefillParams* params,
+                                           const KvbPeerShards* shards, void* stream) {
+  if (!params || !shards) return fail(KVB_ERR_INVALID, "params and shards must be non-null");
+  const KvbPagedPrefillParams& p = *params;
+  const KvbPeerShards& sh = *shards;
+  if (p.dtype != KVB_DTYPE_BF16 && p.dtype != KVB_DTYPE_FP16)
+    return fail(KVB_ERR_INVALID, "dtype must be KVB_DTYPE_BF16 or KVB_DTYPE_FP16");
+  if (p.batch != 1) return fail(KVB_ERR_UNSUPPORTED, "peer shards hold one sequence (batch 1)");
+  if (sh.world < 1 || sh.world > kMaxPeers)
+    return fail(KVB_ERR_UNSUPPORTED, "world must be in [1, 8]");
+  if (sh.shard_blocks < 1 || p.num_blocks != sh.world * sh.shard_blocks)
+    return fail(KVB_ERR_INVALID, "num_blocks must equal world * shard_blocks");
+  if (p.q_len != 2 * sh.world * sh.zigzag_rows || p.q_len < 0)
+    return fail(KVB_ERR_INVALID, "q_len must equal 2 * world * zigzag_rows");
+  if (p.num_kv_heads < 1 || p.num_kv_heads > 65535 || p.prefix_len < 0)
+    return fail(KVB_ERR_INVALID, "bad num_kv_heads or prefix_len");
+  if (p.block_size != 16) return fail(KVB_ERR_UNSUPPORTED, "block_size must be 16");
+  if (!p.block_tables || (int64_t)p.max_blocks_per_seq * 16 < p.prefix_len)
+    return fail(KVB_ERR_INVALID, "block_tables must be set and cover prefix_len");
+  int64_t off[5];
+  if (kvb_peer_shard_layout(p.num_kv_heads, p.head_dim, sh.shard_blocks, sh.zigzag_rows, off) < 0)
+    return fail(KVB_ERR_INVALID, "head_dim must be one of 64, 96, 128");
+  PeerArgs peer = {};
+  for (int r = 0; r < sh.world; ++r) {
+    if (!sh.base[r] || !aligned16(sh.base[r]))
+      return fail(KVB_ERR_INVALID, "every shard base must be non-null and 16-byte aligned");
+    peer.base[r] = reinterpret_cast<const uint8_t*>(sh.base[r]);
+  }
+  peer.world = sh.world;
+  peer.shard_blocks = sh.shard_blocks;
+  peer.zz_rows = sh.zigzag_rows;
+  peer.kscale_off = off[1];
+  peer.vscale_off = off[2];
+  peer.suffix_off = off[3];
+  peer.suffix_v_off = off[4];
+  const int64_t need = paged_materialize_bytes(p);
+  if (!p.workspace || !aligned16(p.workspace) || p.workspace_bytes < need)
+    return fail(KVB_ERR_INVALID, "workspace must hold " + std::to_string(need) + " bytes");
+  if (p.prefix_len + p.q_len == 0) return KVB_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool bf = p.dtype == KVB_DTYPE_BF16;
+  switch (p.head_dim) {
+    case 64:
+      return bf ? launch_materialize<__nv_bfloat16, 64>(p, s, &peer)
+                : launch_materialize<__half, 64>(p, s, &peer);
+    case 96:
+      return bf ? launch_materialize<__nv_bfloat16, 96>(p, s, &peer)
+                : launch_materialize<__half, 96>(p, s, &peer);
+    default:
+      return bf ? launch_materialize<__nv_bfloat16, 128>(p, s, &peer)
+                : launch_materialize<__half, 128>(p, s, &peer);
   }
 }
 

@@ -89,7 +89,8 @@ def test_ctypes_layouts_match_c_compiler(tmp_path):
     """sizeof/offsetof of both parameter structs as gcc sees the header."""
     from kvboost_b200._build import INCLUDE
     structs = {"KvbPrefillParams": _lib.KvbPrefillParams,
-               "KvbPagedPrefillParams": _lib.KvbPagedPrefillParams}
+               "KvbPagedPrefillParams": _lib.KvbPagedPrefillParams,
+               "KvbPeerShards": _lib.KvbPeerShards}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "kvb_attn.h"', 'int main(){']
     for name, cls in structs.items():
         lines.append(f'printf("{name} %zu\\n", sizeof({name}));')
@@ -124,3 +125,15 @@ def test_paged_strategy_selection():
     p.q_len = 16  # a seam-recompute-sized suffix stays fused (reads int8 once)
     p.num_q_heads = 16
     assert lib.kvb_paged_prefill_workspace_bytes(p) == 0
+
+
+def test_peer_shard_layout(lib):
+    """Region offsets of a context-parallel shard buffer (host-side arithmetic)."""
+    off = (ctypes.c_int64 * 5)()
+    total = lib.kvb_peer_shard_layout(8, 128, 1024, 512, off)
+    pool = 1024 * 2 * 8 * 16 * 128
+    ks, vs, sfx = 1024 * 8 * 16 * 4, 1024 * 8 * 128 * 4, 8 * 1024 * 128 * 2
+    assert list(off) == [0, pool, pool + ks, pool + ks + vs, pool + ks + vs + sfx]
+    assert total == pool + ks + vs + 2 * sfx
+    assert all(o % 16 == 0 for o in off)
+    assert lib.kvb_peer_shard_layout(8, 80, 1024, 512, off) == -1

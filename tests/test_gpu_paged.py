@@ -235,3 +235,51 @@ def test_materialize_matches_oracle_gather():
         assert np.array_equal(Kb[:, Pb:Pb + 40], kn[b].float().cpu().numpy())
         pad_end = (Pb + 40 + 127) // 128 * 128
         assert not Kb[:, Pb + 40:pad_end].any() and not Vb[:, Pb + 40:pad_end].any()
+
+
+def test_context_parallel_peer_shards_emulated():
+    """The fused gather: two ranks' shard buffers (here both in this GPU's memory) read in
+    place by kvb_paged_materialize_peers; each rank's zig-zag rows equal the unsharded
+    paged prefill, and the dense K/V equal the NCCL-path layout bit for bit."""
+    from kvboost_b200 import context_parallel as cp
+    from kvboost_b200.paged import (DeviceBlockAllocator, block_table_tensor,
+                                    paged_materialize, paged_prefill_attention,
+                                    quantize_chunk_int8)
+    world, Hq, Hkv, D, C, Sq = 2, 16, 2, 128, 9, 512
+    P = C * 128
+    g = torch.Generator().manual_seed(23)
+    chunks = []
+    full = DeviceBlockAllocator(1, Hkv, D, C * 8)
+    for c in range(C):
+        k = torch.randn(1, Hkv, 128, D, generator=g).to(torch.bfloat16).half().cuda()
+        v = torch.randn(1, Hkv, 128, D, generator=g).to(torch.bfloat16).half().cuda()
+        qz = quantize_chunk_int8(k, v)
+        chunks.append(qz)
+        full.write_chunk_int8(0, list(range(c * 8, c * 8 + 8)), *qz)
+    q = torch.randn(1, Hq, Sq, D, generator=g).to(torch.bfloat16).cuda()
+    kn = torch.randn(1, Hkv, Sq, D, generator=g).to(torch.bfloat16).cuda()
+    vn = torch.randn(1, Hkv, Sq, D, generator=g).to(torch.bfloat16).cuda()
+    ref, _ = paged_prefill_attention(q, kn, vn, full, 0,
+                                     block_table_tensor([list(range(C * 8))], "cuda"), P)
+    shards = [cp.PeerShardBuffer(C, world, Hkv, D, Sq, torch.bfloat16, "cuda", symmetric=False)
+              for _ in range(world)]
+    for r, sh in enumerate(shards):
+        for slot, c in enumerate(cp.local_chunk_slots(C, world, r)):
+            sh.alloc.write_chunk_int8(0, list(range(slot * 8, slot * 8 + 8)), *chunks[c])
+        rows = torch.cat([torch.arange(s, e) for s, e in cp.zigzag_chunks(Sq, world, r)]).cuda()
+        sh.suffix_k.copy_(kn[0][:, rows])
+        sh.suffix_v.copy_(vn[0][:, rows])
+    bases = [sh.buf.data_ptr() for sh in shards]
+    table = block_table_tensor([cp.gathered_block_table(C, world)], "cuda")
+    K, V = cp.materialize_from_peers(bases, shards[0].shard_blocks, shards[0].zz_rows, Hkv, D,
+                                     torch.bfloat16, table, P, Sq, world * shards[0].shard_blocks)
+    K_ref, V_ref = paged_materialize(full, 0, block_table_tensor([list(range(C * 8))], "cuda"),
+                                     P, kn, vn)
+    torch.cuda.synchronize()
+    assert torch.equal(K, K_ref) and torch.equal(V, V_ref)
+    out = torch.empty_like(q)
+    for r in range(world):
+        rows = torch.cat([torch.arange(s, e) for s, e in cp.zigzag_chunks(Sq, world, r)]).cuda()
+        out[:, :, rows] = cp.zigzag_prefill(q[:, :, rows].contiguous(), K, V, P, Sq, world, r)
+    torch.cuda.synchronize()
+    assert (out.float() - ref.float()).abs().max().item() <= TOL[torch.bfloat16]
