@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define KVB_ABI_VERSION 1
+#define KVB_ABI_VERSION 2
 
 enum {
   KVB_DTYPE_BF16 = 0,
@@ -158,6 +158,11 @@ int kvb_prefill_fwd(const KvbPrefillParams* params, void* stream);
  * has kv_len = prefix_len_b + q_len.  block_size must be 16.  Block ids
  * outside [0, num_blocks) read as zeros and set KVB_STATUS_BAD_BLOCK.
  */
+enum {
+  KVB_POOL_INT8_KIVI = 0,
+  KVB_POOL_COMPUTE = 1
+};
+
 typedef struct KvbPagedPrefillParams {
   int32_t dtype;
   int32_t head_dim;
@@ -189,6 +194,13 @@ typedef struct KvbPagedPrefillParams {
   int32_t* status;
   void* workspace;              /* optional device scratch, see below        */
   int64_t workspace_bytes;
+  /* ABI 2: the pool's element format.  KVB_POOL_INT8_KIVI (0, the default of
+   * a zero-initialised struct): int8 codes with k_scale / v_scale as above.
+   * KVB_POOL_COMPUTE: the pool holds K/V in the compute dtype (the
+   * reference's paged engine pool, block_allocator.py:67-73, with its
+   * float16/bfloat16 dtype); k_scale and v_scale are not used. */
+  int32_t pool_format;
+  int32_t reserved0;
 } KvbPagedPrefillParams;
 
 /*

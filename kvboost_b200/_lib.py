@@ -21,6 +21,7 @@ KVB_ERR_INVALID = 1
 KVB_ERR_UNSUPPORTED = 2
 KVB_ERR_CUDA = -1
 KVB_NOALLOC_SCRATCH_BYTES = 32 << 20
+KVB_POOL_INT8_KIVI, KVB_POOL_COMPUTE = 0, 1
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -69,6 +70,7 @@ class KvbPagedPrefillParams(ctypes.Structure):
         ("block_tables", _vp), ("max_blocks_per_seq", _i32), ("prefix_len", _i32),
         ("prefix_lens", _vp), ("status", _vp),
         ("workspace", _vp), ("workspace_bytes", _i64),
+        ("pool_format", _i32), ("reserved0", _i32),
     ]
 
 

@@ -172,6 +172,7 @@ struct PagedArgs {
   int num_blocks;
   int num_kv_heads;
   int prefix_len;
+  int pool16;             // 1: the pool holds K/V in the compute dtype, no scales
 };
 
 struct SharedCtl {
@@ -426,6 +427,12 @@ __device__ __forceinline__ void gather_kv_tile(uint8_t* dst, const PagedArgs& pa
             bi < pa.max_blocks ? __ldg(pa.block_table + (int64_t)b * pa.max_blocks + bi) : -1;
         if (blk < 0 || blk >= pa.num_blocks) {
           if (status) atomicOr(status, KVB_STATUS_BAD_BLOCK);
+        } else if (pa.pool16) {
+          const uint4* src = reinterpret_cast<const uint4*>(
+              reinterpret_cast<const T*>(pa.pool) +
+              ((((int64_t)blk * 2 + kv) * pa.num_kv_heads + kvh) * 16 + (tok & 15)) * D + ch * 16);
+          w0 = __ldg(src);
+          w1 = __ldg(src + 1);
         } else {
           const int slot = tok & 15;
           const int64_t hb = (int64_t)blk * pa.num_kv_heads + kvh;
@@ -533,6 +540,12 @@ __global__ void __launch_bounds__(256)
           bi < pa.max_blocks ? __ldg(pa.block_table + (int64_t)b * pa.max_blocks + bi) : -1;
       if (blk < 0 || blk >= pa.num_blocks) {
         if (status) atomicOr(status, KVB_STATUS_BAD_BLOCK);
+      } else if (!PEER && pa.pool16) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            reinterpret_cast<const T*>(pa.pool) +
+            ((((int64_t)blk * 2 + kv) * pa.num_kv_heads + kvh) * 16 + (tok & 15)) * D + ch * 16);
+        w0 = __ldg(src);
+        w1 = __ldg(src + 1);
       } else {
         const int slot = tok & 15;
         const int8_t* pool = pa.pool;
@@ -1238,6 +1251,7 @@ static PagedArgs paged_args(const KvbPagedPrefillParams& p) {
   pa.num_blocks = p.num_blocks;
   pa.num_kv_heads = p.num_kv_heads;
   pa.prefix_len = p.prefix_len;
+  pa.pool16 = p.pool_format == KVB_POOL_COMPUTE ? 1 : 0;
   return pa;
 }
 
@@ -1468,11 +1482,15 @@ static int validate_paged(const KvbPagedPrefillParams& p) {
     return fail(KVB_ERR_INVALID, "num_blocks must be positive");
   if ((int64_t)p.max_blocks_per_seq * 16 < p.prefix_len)
     return fail(KVB_ERR_INVALID, "block table too short for prefix_len");
-  if (!p.q || !p.o || !p.kv_pool || !p.k_scale || !p.v_scale || !p.block_tables)
+  if (p.pool_format != KVB_POOL_INT8_KIVI && p.pool_format != KVB_POOL_COMPUTE)
+    return fail(KVB_ERR_INVALID, "pool_format must be KVB_POOL_INT8_KIVI or KVB_POOL_COMPUTE");
+  const bool scales = p.pool_format == KVB_POOL_INT8_KIVI;
+  if (!p.q || !p.o || !p.kv_pool || !p.block_tables || (scales && (!p.k_scale || !p.v_scale)))
     return fail(KVB_ERR_INVALID, "q, o, kv_pool, scales and block_tables must be non-null");
   if (p.q_len > 0 && (!p.k_new || !p.v_new))
     return fail(KVB_ERR_INVALID, "k_new and v_new must be non-null when q_len > 0");
-  if (!aligned16(p.q) || !aligned16(p.o) || !aligned16(p.kv_pool) || !aligned16(p.v_scale) ||
+  if (!aligned16(p.q) || !aligned16(p.o) || !aligned16(p.kv_pool) ||
+      (scales && !aligned16(p.v_scale)) ||
       (p.k_new && !aligned16(p.k_new)) || (p.v_new && !aligned16(p.v_new)))
     return fail(KVB_ERR_INVALID, "q, o, k_new, v_new, kv_pool and v_scale must be 16-byte aligned");
   const int64_t st[] = {p.q_head_stride, p.q_row_stride, p.o_head_stride, p.o_row_stride,
@@ -1520,11 +1538,14 @@ extern "C" int kvb_paged_materialize(const KvbPagedPrefillParams* params, void* 
   if (p.num_blocks < 1 || p.max_blocks_per_seq < 0 ||
       (int64_t)p.max_blocks_per_seq * 16 < p.prefix_len)
     return fail(KVB_ERR_INVALID, "num_blocks must be positive and the table cover prefix_len");
-  if (!p.kv_pool || !p.k_scale || !p.v_scale || !p.block_tables)
+  if (p.pool_format != KVB_POOL_INT8_KIVI && p.pool_format != KVB_POOL_COMPUTE)
+    return fail(KVB_ERR_INVALID, "pool_format must be KVB_POOL_INT8_KIVI or KVB_POOL_COMPUTE");
+  const bool scales = p.pool_format == KVB_POOL_INT8_KIVI;
+  if (!p.kv_pool || !p.block_tables || (scales && (!p.k_scale || !p.v_scale)))
     return fail(KVB_ERR_INVALID, "kv_pool, scales and block_tables must be non-null");
   if (p.q_len > 0 && (!p.k_new || !p.v_new))
     return fail(KVB_ERR_INVALID, "k_new and v_new must be non-null when q_len > 0");
-  if (!aligned16(p.kv_pool) || !aligned16(p.v_scale) || !aligned16(p.workspace) ||
+  if (!aligned16(p.kv_pool) || (scales && !aligned16(p.v_scale)) || !aligned16(p.workspace) ||
       (p.k_new && !aligned16(p.k_new)) || (p.v_new && !aligned16(p.v_new)))
     return fail(KVB_ERR_INVALID, "kv_pool, v_scale, k_new, v_new and workspace must be 16-byte aligned");
   if (p.q_len > 0) {
@@ -1578,6 +1599,8 @@ extern "C" int kvb_paged_materialize_peers(const KvbPagedPrefillParams* params,
   if (p.dtype != KVB_DTYPE_BF16 && p.dtype != KVB_DTYPE_FP16)
     return fail(KVB_ERR_INVALID, "dtype must be KVB_DTYPE_BF16 or KVB_DTYPE_FP16");
   if (p.batch != 1) return fail(KVB_ERR_UNSUPPORTED, "peer shards hold one sequence (batch 1)");
+  if (p.pool_format != KVB_POOL_INT8_KIVI)
+    return fail(KVB_ERR_UNSUPPORTED, "peer shards hold int8 KIVI pools");
   if (sh.world < 1 || sh.world > kMaxPeers)
     return fail(KVB_ERR_UNSUPPORTED, "world must be in [1, 8]");
   if (sh.shard_blocks < 1 || p.num_blocks != sh.world * sh.shard_blocks)

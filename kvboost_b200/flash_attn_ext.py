@@ -268,6 +268,113 @@ def uninstall_flash_attention(model: torch.nn.Module) -> int:
     return restored
 
 
+# ── Paged attention (flash_attn_ext.py:240-453) ───────────────────────────────
+
+_PAGED_ATTR = "_kvboost_paged_layer"
+
+
+def _make_paged_attn_fn(layer_idx: int, state: dict):
+    """Registry attention function reading K/V from the state's block pool.
+
+    Same protocol as the reference's ``sdpa_style`` function
+    (``flash_attn_ext.py:273-328``): the new tokens' K/V (everything past
+    ``state["_write_slot"]`` when HF concatenated a cache, else all of ``key``)
+    are appended to the pool at the write slot, extending ``state["block_table"]``;
+    the queries then attend to the pool.  Here the append is one device scatter,
+    the tokens before the write slot are read from the pool through the block
+    table and the new K/V straight from the call (``kvb_paged_prefill_fwd``), with
+    bottom-right causality; ``state["top_left"] = True`` selects the reference's
+    SDPA ``is_causal`` alignment instead.
+    """
+    from .paged import block_table_tensor, paged_attention_fwd, paged_prefill_attention
+
+    def paged_fn(module, query, key, value, attention_mask=None, dropout=0.0, scaling=None,
+                 is_causal=None, **kwargs):
+        allocator = state["allocator"]
+        write_slot = int(state["_write_slot"])
+        if query.size(0) != 1:
+            raise NotImplementedError("paged attention serves one sequence per forward")
+        if scaling is None:
+            scaling = 1.0 / math.sqrt(query.size(-1))
+        if key.size(2) > write_slot:
+            k_new, v_new = key[:, :, write_slot:], value[:, :, write_slot:]
+        else:
+            k_new, v_new = key, value
+        table, _ = allocator.append_kv(layer_idx, state["block_table"], write_slot,
+                                       k_new[0], v_new[0])
+        state["block_table"] = table
+        if state.get("top_left"):
+            n = write_slot + k_new.size(2)
+            out = paged_attention_fwd(query, allocator, [table], [n], layer_idx,
+                                      causal=query.size(2) > 1, scale=scaling, top_left=True)
+        else:
+            out, _ = paged_prefill_attention(
+                query, k_new.to(query.dtype).contiguous(), v_new.to(query.dtype).contiguous(),
+                allocator, layer_idx, block_table_tensor([table], query.device), write_slot,
+                softmax_scale=scaling, causal=True, return_lse=False)
+        return out.transpose(1, 2), None
+
+    return paged_fn
+
+
+def install_paged_attention(model: torch.nn.Module, state: dict) -> int:
+    """Point every attention module of *model* at the state's block pool
+    (``flash_attn_ext.py:367-440``); returns the number of modules patched.
+
+    ``state``: ``allocator`` (a 16-bit ``DeviceBlockAllocator`` with one pool per
+    layer), ``block_table`` (list of block ids, extended in place), ``_write_slot``
+    (logical slot of the next token, advanced by the caller after each forward).
+    Layers are numbered in module order, as in the reference.
+    """
+    _require_library()
+    patched = 0
+    layer_idx = 0
+    for name, module in model.named_modules():
+        cls_name = type(module).__name__
+        if not any(cls_name.endswith(s) for s in _ATTN_MODULE_SUFFIXES):
+            continue
+        if _PAGED_ATTR in module.__dict__:
+            continue
+        original_forward = module.forward
+        module.__dict__[_PAGED_ATTR] = layer_idx
+        module.__dict__["_paged_original_forward"] = original_forward
+        fn = getattr(original_forward, "__func__", original_forward)
+        registry = _registry_of(fn)
+        if registry is None:
+            raise NotImplementedError("paged attention needs transformers' attention registry")
+        paged_fn = _make_paged_attn_fn(layer_idx, state)
+
+        def paged_forward(self, *args, _fn=paged_fn, _orig=original_forward, **kw):
+            cfg = getattr(self, "config", None)
+            key = getattr(cfg, "_attn_implementation", None) or "sdpa"
+            had = key in registry._local_mapping
+            old = registry._local_mapping.get(key)
+            registry[key] = _fn
+            try:
+                return _orig(*args, **kw)
+            finally:
+                if had:
+                    registry[key] = old
+                else:
+                    del registry[key]
+
+        module.forward = types.MethodType(paged_forward, module)
+        layer_idx += 1
+        patched += 1
+    return patched
+
+
+def uninstall_paged_attention(model: torch.nn.Module) -> int:
+    """Restore the modules ``install_paged_attention`` patched (``flash_attn_ext.py:443-453``)."""
+    restored = 0
+    for module in model.modules():
+        if "_paged_original_forward" in module.__dict__:
+            module.forward = module.__dict__.pop("_paged_original_forward")
+            module.__dict__.pop(_PAGED_ATTR, None)
+            restored += 1
+    return restored
+
+
 # ── Reference injection ───────────────────────────────────────────────────────
 
 def inject_into_reference() -> None:

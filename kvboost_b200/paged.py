@@ -60,17 +60,23 @@ class DeviceBlockAllocator:
     """Block allocator over a GPU int8 KV pool (``BlockAllocator`` semantics)."""
 
     def __init__(self, num_layers: int, num_heads: int, head_dim: int, num_blocks: int = 4096,
-                 block_size: int = BLOCK_SIZE, device="cuda") -> None:
+                 block_size: int = BLOCK_SIZE, device="cuda", dtype=torch.int8) -> None:
+        """``dtype``: ``torch.int8`` for KIVI-quantised chunks (per-block scales), or
+        ``torch.float16`` / ``torch.bfloat16`` for a pool holding K/V as is (the
+        reference's paged engine pool, which tokens are appended to one by one)."""
         if block_size != BLOCK_SIZE:
             raise ValueError("the paged kernels use 16-token blocks")
+        if dtype not in (torch.int8, torch.float16, torch.bfloat16):
+            raise ValueError("pool dtype must be int8, float16 or bfloat16")
         self.num_layers = num_layers
         self.num_heads = num_heads
         self.head_dim = head_dim
         self.num_blocks = num_blocks
         self.block_size = block_size
+        self.dtype = dtype
         self.device = torch.device(device)
         self.pools: List[torch.Tensor] = [
-            torch.zeros(num_blocks, 2, num_heads, block_size, head_dim, dtype=torch.int8,
+            torch.zeros(num_blocks, 2, num_heads, block_size, head_dim, dtype=dtype,
                         device=self.device) for _ in range(num_layers)]
         # float16 scales as the reference stores them, and the float32 copies the kernel reads
         self.k_scale16 = [torch.zeros(num_blocks, num_heads, block_size, dtype=torch.float16,
@@ -170,6 +176,72 @@ class DeviceBlockAllocator:
         self.v_scale16[layer][idx] = vs.unsqueeze(0).expand(n, H, D)
         self.v_scale[layer][idx] = vs.float().unsqueeze(0).expand(n, H, D)
 
+    def write_chunk(self, layer: int, block_ids: List[int], key: torch.Tensor,
+                    val: torch.Tensor) -> None:
+        """Store one chunk's K/V (``[1 or H.., S, D]``) as is in a 16-bit pool: token t
+        goes to ``block_ids[t // 16]``, slot ``t % 16`` (``chunk_to_blocks.py:57-101``)."""
+        if self.dtype == torch.int8:
+            raise RuntimeError("int8 pools store KIVI chunks (write_chunk_int8)")
+        H, D, bs = self.num_heads, self.head_dim, self.block_size
+        k = key.reshape(H, -1, D)
+        S = k.shape[1]
+        n = len(block_ids)
+        if n * bs < S:
+            raise ValueError(f"{n} blocks cannot hold {S} tokens")
+        idx = torch.as_tensor(block_ids, dtype=torch.long, device=self.device)
+        for kv, t in ((0, k), (1, val.reshape(H, -1, D))):
+            pad = torch.zeros(H, n * bs, D, dtype=self.dtype, device=self.device)
+            pad[:, :S] = t.to(self.device, self.dtype)
+            self.pools[layer][idx, kv] = pad.view(H, n, bs, D).permute(1, 0, 2, 3)
+
+    @property
+    def pool_format(self) -> int:
+        return _lib.KVB_POOL_INT8_KIVI if self.dtype == torch.int8 else _lib.KVB_POOL_COMPUTE
+
+    def append_kv(self, layer: int, block_table: List[int], slot_offset: int,
+                  k: torch.Tensor, v: torch.Tensor) -> Tuple[List[int], int]:
+        """``append_kv_to_blocks`` (``cpu_paged/paged_attn_cpu.py:111-163``) for a 16-bit
+        pool: token t of ``k``/``v`` (``[H, n, D]``) goes to logical slot
+        ``slot_offset + t``; blocks are allocated from the free list when the table
+        runs out and shared blocks are copied on write, in the reference's order.  The
+        block bookkeeping stays on the host; the n tokens are written by one device
+        scatter instead of a Python loop of per-token copies.  Returns the updated
+        table and the next slot."""
+        if self.dtype == torch.int8:
+            raise RuntimeError("int8 pools hold whole KIVI chunks (write_chunk_int8)")
+        table = list(block_table)
+        bs = self.block_size
+        n = k.shape[1]
+        blocks, slots = [], []
+        for t in range(n):
+            pos = slot_offset + t
+            bi = pos // bs
+            if bi >= len(table):
+                table.extend(self.allocate(1))
+            bid = self.ensure_writable(table[bi])
+            table[bi] = bid
+            blocks.append(bid)
+            slots.append(pos % bs)
+        if n:
+            bidx = torch.as_tensor(blocks, dtype=torch.long, device=self.device)
+            sidx = torch.as_tensor(slots, dtype=torch.long, device=self.device)
+            pool = self.pools[layer]
+            pool[bidx, 0, :, sidx] = k.permute(1, 0, 2).to(self.device, self.dtype)
+            pool[bidx, 1, :, sidx] = v.permute(1, 0, 2).to(self.device, self.dtype)
+        return table, slot_offset + n
+
+    def read_kv(self, layer: int, block_ids: List[int], seq_len: int):
+        """K/V ``[H, seq_len, D]`` of a 16-bit pool gathered through the table
+        (``block_allocator.py:178-206``); int8 pools: see ``read_dequant``."""
+        if self.dtype == torch.int8:
+            return self.read_dequant(layer, block_ids, seq_len)
+        idx = torch.as_tensor(block_ids, dtype=torch.long, device=self.device)
+        g = self.pools[layer][idx]
+        n, H, bs, D = g.shape[0], self.num_heads, self.block_size, self.head_dim
+        k = g[:, 0].permute(1, 0, 2, 3).reshape(H, n * bs, D)[:, :seq_len]
+        v = g[:, 1].permute(1, 0, 2, 3).reshape(H, n * bs, D)[:, :seq_len]
+        return k, v
+
     def read_dequant(self, layer: int, block_ids: List[int], seq_len: int):
         """float16 K/V ``[H, seq_len, D]`` exactly as the reference's dequantise+gather."""
         idx = torch.as_tensor(block_ids, dtype=torch.long, device=self.device)
@@ -199,10 +271,18 @@ class DeviceChunkMapper:
         with self._lock:
             if chunk_id in self._chunk_blocks:
                 return self.allocator.fork(self._chunk_blocks[chunk_id])
+        bs = self.allocator.block_size
+        if self.allocator.dtype != torch.int8:   # 16-bit pool: the chunk as is
+            S = layers_kv[0][0].shape[-2]
+            block_ids = self.allocator.allocate((S + bs - 1) // bs)
+            for layer, (k, v) in enumerate(layers_kv):
+                self.allocator.write_chunk(layer, block_ids, k, v)
+            with self._lock:
+                self._chunk_blocks[chunk_id] = block_ids
+            return list(block_ids)
         if quantized is None:
             quantized = [quantize_chunk_int8(k, v) for k, v in layers_kv]
         S = quantized[0][0].shape[-2]
-        bs = self.allocator.block_size
         block_ids = self.allocator.allocate((S + bs - 1) // bs)
         for layer, (kq, ks, vq, vs) in enumerate(quantized):
             self.allocator.write_chunk_int8(layer, block_ids, kq, ks, vq, vs)
@@ -300,8 +380,12 @@ def paged_prefill_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.T
     p.k_new_batch_stride, p.k_new_head_stride, p.k_new_row_stride = k_new.stride()[:3]
     p.v_new_batch_stride, p.v_new_head_stride, p.v_new_row_stride = v_new.stride()[:3]
     p.kv_pool = allocator.pools[layer].data_ptr()
-    p.k_scale = allocator.k_scale[layer].data_ptr()
-    p.v_scale = allocator.v_scale[layer].data_ptr()
+    p.pool_format = allocator.pool_format
+    if allocator.dtype == torch.int8:
+        p.k_scale = allocator.k_scale[layer].data_ptr()
+        p.v_scale = allocator.v_scale[layer].data_ptr()
+    elif allocator.dtype != k_new.dtype:
+        raise RuntimeError("a 16-bit pool must hold the compute dtype")
     p.num_blocks, p.block_size = allocator.num_blocks, allocator.block_size
     p.block_tables, p.max_blocks_per_seq = block_tables.data_ptr(), block_tables.shape[1]
     p.prefix_len = int(prefix_len)
@@ -372,8 +456,12 @@ def paged_prefill_attention_noalloc(q: torch.Tensor, k_new: torch.Tensor, v_new:
     p.k_new_batch_stride, p.k_new_head_stride, p.k_new_row_stride = k_new.stride()[:3]
     p.v_new_batch_stride, p.v_new_head_stride, p.v_new_row_stride = v_new.stride()[:3]
     p.kv_pool = allocator.pools[layer].data_ptr()
-    p.k_scale = allocator.k_scale[layer].data_ptr()
-    p.v_scale = allocator.v_scale[layer].data_ptr()
+    p.pool_format = allocator.pool_format
+    if allocator.dtype == torch.int8:
+        p.k_scale = allocator.k_scale[layer].data_ptr()
+        p.v_scale = allocator.v_scale[layer].data_ptr()
+    elif allocator.dtype != k_new.dtype:
+        raise RuntimeError("a 16-bit pool must hold the compute dtype")
     p.num_blocks, p.block_size = allocator.num_blocks, allocator.block_size
     p.block_tables, p.max_blocks_per_seq = block_tables.data_ptr(), block_tables.shape[1]
     p.prefix_len = int(prefix_len)
@@ -423,8 +511,12 @@ def paged_materialize(allocator: DeviceBlockAllocator, layer: int, block_tables:
         p.k_new_batch_stride, p.k_new_head_stride, p.k_new_row_stride = k_new.stride()[:3]
         p.v_new_batch_stride, p.v_new_head_stride, p.v_new_row_stride = v_new.stride()[:3]
     p.kv_pool = allocator.pools[layer].data_ptr()
-    p.k_scale = allocator.k_scale[layer].data_ptr()
-    p.v_scale = allocator.v_scale[layer].data_ptr()
+    p.pool_format = allocator.pool_format
+    if allocator.dtype == torch.int8:
+        p.k_scale = allocator.k_scale[layer].data_ptr()
+        p.v_scale = allocator.v_scale[layer].data_ptr()
+    elif allocator.dtype != k_new.dtype:
+        raise RuntimeError("a 16-bit pool must hold the compute dtype")
     p.num_blocks, p.block_size = allocator.num_blocks, allocator.block_size
     p.block_tables, p.max_blocks_per_seq = block_tables.data_ptr(), block_tables.shape[1]
     p.prefix_len = int(prefix_len)
@@ -436,3 +528,44 @@ def paged_materialize(allocator: DeviceBlockAllocator, layer: int, block_tables:
     _lib.check(rc, "kvb_paged_materialize")
     kv = workspace[:need].view(2, B, Hkv, kv_pad, D)
     return kv[0], kv[1]
+
+
+def paged_attention_fwd(query: torch.Tensor, allocator: DeviceBlockAllocator,
+                        block_tables: Sequence[Sequence[int]], seq_lens: Sequence[int],
+                        layer: int, causal: bool = True, scale: Optional[float] = None,
+                        top_left: bool = False) -> torch.Tensor:
+    """Paged attention over K/V held entirely in the pool (``paged_attention_fwd``,
+    ``cpu_paged/paged_attn_cpu.py:33-108``).
+
+    query ``[B, Hq, Sq, D]``; sequence b attends to the first ``seq_lens[b]`` tokens
+    of its block table (GQA over the pool's heads); an empty history gives zeros.
+    Masking for ``Sq > 1`` with ``causal``: bottom-right (query i sees keys up to
+    ``seq_len - Sq + i``, the queries being the last Sq tokens) by default;
+    ``top_left=True`` reproduces the reference's ``is_causal`` SDPA call
+    (``:100-104``), which aligns the mask to the first key.  One gather pass
+    (dequantising int8 pools) into dense K/V, then the prefill kernel per sequence.
+    Returns ``[B, Hq, Sq, D]`` in the query's dtype.
+    """
+    _check_tensor("query", query, 4)
+    B, Hq, Sq, D = query.shape
+    if len(block_tables) != B or len(seq_lens) != B:
+        raise ValueError("one block table and one seq_len per batch element")
+    if Hq % allocator.num_heads or D != allocator.head_dim:
+        raise RuntimeError("query heads / head_dim do not match the pool")
+    out = torch.zeros_like(query)
+    L = [int(x) for x in seq_lens]
+    if B == 0 or Sq == 0 or max(L) == 0:
+        return out
+    dev = query.device
+    bt = block_table_tensor([list(t) for t in block_tables], dev)
+    plens = torch.tensor(L, dtype=torch.int32, device=dev)
+    empty = torch.empty(B, allocator.num_heads, 0, D, dtype=query.dtype, device=dev)
+    K, V = paged_materialize(allocator, layer, bt, max(L), empty, empty, prefix_lens=plens)
+    from .ops import prefill_attention
+    for b in range(B):
+        if L[b] == 0:
+            continue
+        prefill_attention(query[b:b + 1], K[b:b + 1, :, :L[b]], V[b:b + 1, :, :L[b]], scale,
+                          causal and Sq > 1, out=out[b:b + 1], return_lse=False,
+                          top_left=top_left)
+    return out

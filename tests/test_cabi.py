@@ -36,7 +36,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version(lib):
-    assert lib.kvb_abi_version() == 1
+    assert lib.kvb_abi_version() == 2
 
 
 def test_ctypes_struct_matches_header_size():
