@@ -58,7 +58,7 @@ def parse():
     ap.add_argument("--impl", default="kvboost", choices=["kvboost", "reference"])
     ap.add_argument("--workload", default="reuse_prefill",
                     choices=["reuse_prefill", "causal_op", "varlen_d96", "paged_long",
-                             "ttft_reuse", "paged_long_cp"])
+                             "ttft_reuse", "paged_long_cp", "decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cp-gather", default="peers", choices=["peers", "nccl"],
@@ -170,6 +170,54 @@ class Dense:
         def run():
             attention(q, k, v, 1.0 / math.sqrt(self.D), True, compute_dtype=np.float32)
         return run, fl, f"1 of {self.B} batch elements"
+
+
+class Decode(Dense):
+    """Decode attention of the config-3 model at its 4096-token context: batch 8, 16
+    query heads over 2 KV heads, D 128, bf16, one query row per head
+    (``decode_attention``: GQA heads packed per key tile, keys split over CTAs).
+    HBM-bound: every launch streams the 8 x 2 x 4096 keys and values once."""
+
+    def __init__(self):
+        super().__init__("decode", 8, 16, 2, 1, 4095, 128, "bf16",
+                         "decode attention: B8 Hq16/Hkv2 D128 bf16, 1 query row over 4096 keys")
+        self.bound = "hbm"
+
+    def setup(self, torch, dev, rank, world):
+        from kvboost_b200 import ops
+        self.dt = torch.bfloat16
+        g = torch.Generator(device=dev).manual_seed(4321 + rank)
+        R = max(2, math.ceil(2 * L2_BYTES / self.bytes()))
+        self.sets_desc = f"inputs rotate over {R} sets ({R * self.bytes() / 2**20:.0f} MiB > L2)"
+        sets = []
+        for _ in range(R):
+            q = torch.randn(self.B, self.Hq, self.Sq, self.D, generator=g, device=dev).to(self.dt)
+            k = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(self.dt)
+            v = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(self.dt)
+            sets.append((q, k, v, torch.empty_like(q)))
+        scale = 1.0 / math.sqrt(self.D)
+        # the decode kernel's workspace is allocated on the first call, outside the graph
+        ops.decode_attention(*sets[0][:3], scale, True, out=sets[0][3], return_lse=False)
+
+        def step(i):
+            q, k, v, o = sets[i % R]
+            ops.decode_attention(q, k, v, scale, True, out=o, return_lse=False)
+        return step
+
+    def e2e(self, torch, dev):
+        from kvboost_b200 import ops
+        hq = torch.randn(self.B, self.Hq, self.Sq, self.D).to(self.dt).pin_memory()
+        hk = torch.randn(self.B, self.Hkv, self.kv, self.D).to(self.dt).pin_memory()
+        hv = torch.randn(self.B, self.Hkv, self.kv, self.D).to(self.dt).pin_memory()
+        ho = torch.empty(self.B, self.Hq, self.Sq, self.D, dtype=self.dt).pin_memory()
+        scale = 1.0 / math.sqrt(self.D)
+
+        def step():
+            dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+            o, _ = ops.decode_attention(dq, dk, dv, scale, True, return_lse=False)
+            ho.copy_(o, non_blocking=True)
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+        return step, h2d, ho.numel() * ho.element_size()
 
 
 class Varlen:
@@ -746,6 +794,8 @@ def make_workload(name, small=False):
         return Varlen(small)
     if name == "ttft_reuse":
         return TtftReuse()
+    if name == "decode":
+        return Decode()
     return PagedLong(small)
 
 

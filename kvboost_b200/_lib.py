@@ -110,6 +110,11 @@ def load() -> ctypes.CDLL:
         lib.kvb_peer_shard_layout.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, ctypes.POINTER(ctypes.c_int64)]
         lib.kvb_peer_shard_layout.restype = ctypes.c_int64
+        lib.kvb_decode_fwd.argtypes = [ctypes.POINTER(KvbPrefillParams), ctypes.c_int, _vp,
+                                       ctypes.c_int64, _vp]
+        lib.kvb_decode_fwd.restype = ctypes.c_int
+        lib.kvb_decode_workspace_bytes.argtypes = [ctypes.POINTER(KvbPrefillParams), ctypes.c_int]
+        lib.kvb_decode_workspace_bytes.restype = ctypes.c_int64
         lib.kvb_paged_materialize.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]
         lib.kvb_paged_materialize.restype = ctypes.c_int
         lib.kvb_paged_prefill_fwd_noalloc.argtypes = [ctypes.POINTER(KvbPagedPrefillParams), _vp]

@@ -173,6 +173,15 @@ struct PagedArgs {
   int num_kv_heads;
   int prefix_len;
   int pool16;             // 1: the pool holds K/V in the compute dtype, no scales
+  // Split-key decode (the dense SPLITKV kernels, which read no pool and carry
+  // these here: growing DenseArgs measurably slowed every dense launch): query
+  // rows are a GQA group's heads packed as (head, row) with rows_per_head rows
+  // each; CTA x covers key tiles [x * split_tiles, (x + 1) * split_tiles) and
+  // writes its normalised partial O / LSE at o + x * o_split_stride,
+  // lse + x * lse_split_stride.
+  int rows_per_head;
+  int split_tiles;
+  int64_t o_split_stride, lse_split_stride;
 };
 
 struct SharedCtl {
@@ -618,7 +627,74 @@ __global__ void __launch_bounds__(256)
   reinterpret_cast<uint4*>(dst)[1] = w1;
 }
 
-template <typename T, int D, bool PAGED>
+// Merge the per-split partial results of a split-key decode: for every query
+// row, O = sum_s exp(lse_s - L) O_s and L = log sum_s exp(lse_s).  Partials are
+// packed per KV head as rows r = head_in_group * rows_per_head + i
+// ([splits][batch][num_kv_heads][packed_rows][D], normalised, compute dtype;
+// LSE fp32 [splits][batch][num_kv_heads][packed_rows]).  One thread per 8
+// consecutive features of one row.
+struct CombineArgs {
+  const void* o_part;
+  const float* lse_part;
+  int splits;
+  int64_t o_split_stride, lse_split_stride;
+  int batch, num_kv_heads, group, rows_per_head;
+  void* o;
+  float* lse;
+  int64_t o_bs, o_hs, o_rs, lse_bs, lse_hs;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(256) kvb_split_combine_kernel(CombineArgs c) {
+  constexpr int NCH = D / 8;
+  const int packed = c.group * c.rows_per_head;
+  const int64_t rows = (int64_t)c.batch * c.num_kv_heads * packed;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * NCH) return;
+  const int64_t row = idx / NCH;          // (b, g, r) packed
+  const int ch = (int)(idx - row * NCH);
+  const int r = (int)(row % packed);
+  const int64_t bg = row / packed;
+  const int g = (int)(bg % c.num_kv_heads);
+  const int b = (int)(bg / c.num_kv_heads);
+  float mx = -INFINITY;
+  for (int sp = 0; sp < c.splits; ++sp) mx = fmaxf(mx, c.lse_part[sp * c.lse_split_stride + row]);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float wsum = 0.f;
+  if (mx > -INFINITY) {
+    for (int sp = 0; sp < c.splits; ++sp) {
+      const float w = __expf(c.lse_part[sp * c.lse_split_stride + row] - mx);
+      wsum += w;
+      const uint4 v = *reinterpret_cast<const uint4*>(
+          reinterpret_cast<const T*>(c.o_part) + sp * c.o_split_stride + row * D + ch * 8);
+      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f;
+        if constexpr (std::is_same<T, __half>::value)
+          f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
+        else
+          f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
+        acc[2 * e] += w * f.x;
+        acc[2 * e + 1] += w * f.y;
+      }
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) o[e] = pack2<T>(acc[2 * e] * inv, acc[2 * e + 1] * inv);
+  const int head = g * c.group + r / c.rows_per_head;
+  const int i = r % c.rows_per_head;
+  T* dst = reinterpret_cast<T*>(c.o) + (int64_t)b * c.o_bs + (int64_t)head * c.o_hs +
+           (int64_t)i * c.o_rs + ch * 8;
+  *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+  if (c.lse != nullptr && ch == 0)
+    c.lse[(int64_t)b * c.lse_bs + (int64_t)head * c.lse_hs + i] =
+        wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+}
+
+template <typename T, int D, bool PAGED, bool SPLITKV = false>
 __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     kvb_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -646,7 +722,12 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   // ---- work item: two query tiles sharing one KV head ---------------------
   const int b = blockIdx.z;
   int head[kSlots], mtile[kSlots];
-  if (a.pair_heads) {
+  const int split = SPLITKV ? (int)blockIdx.x : 0;
+  if (SPLITKV) {  // both packed tiles of one KV head's group, one key range
+    head[0] = head[1] = blockIdx.y;
+    mtile[0] = 0;
+    mtile[1] = 1;
+  } else if (a.pair_heads) {
     const int m = gridDim.x - 1 - blockIdx.x;  // heaviest (last) query tiles first
     head[0] = 2 * blockIdx.y;
     head[1] = 2 * blockIdx.y + 1;
@@ -673,15 +754,17 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     tb = 0;
   }
   // causal 1: bottom-right (j <= i + kv_len - q_len); 2: top-left (j <= i)
-  const int off = (a.causal == 2) ? 0 : kv_len - q_len;
+  const int off = (a.causal == 2) ? 0 : kv_len - (SPLITKV ? pa.rows_per_head : q_len);
   int q0[kSlots], q_rows[kSlots], n_t[kSlots];
+  const int jbase = SPLITKV ? split * pa.split_tiles : 0;   // first key tile of this CTA
 #pragma unroll
   for (int sl = 0; sl < kSlots; ++sl) {
     q0[sl] = mtile[sl] * BM;
     q_rows[sl] = max(0, min(BM, q_len - q0[sl]));
-    int kv_end = a.causal ? min(kv_len, q0[sl] + q_rows[sl] + off) : kv_len;
+    int kv_end = (a.causal && !SPLITKV) ? min(kv_len, q0[sl] + q_rows[sl] + off) : kv_len;
     kv_end = max(kv_end, 0);
     n_t[sl] = q_rows[sl] > 0 ? (kv_end + BN - 1) / BN : 0;
+    if (SPLITKV) n_t[sl] = max(0, min(n_t[sl] - jbase, pa.split_tiles));
   }
   if (q_rows[0] == 0 && q_rows[1] == 0) return;  // uniform, before any barrier use
   const int n_max = max(n_t[0], n_t[1]);
@@ -782,7 +865,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       for (int j = 0; j < n_max; ++j) {
         const int st = j % G::NS;
         const uint32_t ph = (j / G::NS) & 1;
-        const int ky = k_base + j * BN;
+        const int ky = k_base + (jbase + j) * BN;
         if (!wait_bar(bar(BAR_K_EMPTY + st), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
           break;
         if (j < 16) KVB_TRACE_AT(16 + j);
@@ -956,9 +1039,12 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       ptx::tc_fence_after();
       if (t == 0 && hf == 0 && j < 16) KVB_TRACE_AT(64 + 96 * sl + j);
 
-      const int kv0 = j * BN;
-      const bool need_mask = (kv0 + BN > kv_len) || (a.causal && kv0 + BN - 1 > q0s + off);
-      const int lim = (a.causal ? min(kv_len - 1, qi + off) : kv_len - 1) - kv0;
+      const int kv0 = (jbase + j) * BN;
+      // split decode: packed row qi is row qi % rows_per_head of its head
+      const int qrow = SPLITKV ? qi % pa.rows_per_head : qi;
+      const bool need_mask =
+          (kv0 + BN > kv_len) || (a.causal && kv0 + BN - 1 > (SPLITKV ? 0 : q0s) + off);
+      const int lim = (a.causal ? min(kv_len - 1, qrow + off) : kv_len - 1) - kv0;
 
       // Stale-maximum softmax.  After the first tile, each tile is
       // exponentiated against the running maximum in one pass with no max
@@ -1044,7 +1130,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     }
     const bool row_valid = t < q_rows[sl];
     const float inv_l = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
-    T* orow = reinterpret_cast<T*>(a.o) + hf * DH +
+    T* orow = reinterpret_cast<T*>(a.o) + hf * DH + (SPLITKV ? split * pa.o_split_stride : 0) +
               (a.cu_q ? (int64_t)(q_base + qi) * a.o_rs + (int64_t)h * a.o_hs
                       : (int64_t)b * a.o_bs + (int64_t)h * a.o_hs + (int64_t)qi * a.o_rs);
 #pragma unroll 1
@@ -1074,7 +1160,8 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       if (a.cu_q)
         a.lse[(int64_t)h * a.lse_hs + q_base + qi] = lse;
       else
-        a.lse[(int64_t)b * a.lse_bs + (int64_t)h * a.lse_hs + qi] = lse;
+        a.lse[(SPLITKV ? split * pa.lse_split_stride : 0) + (int64_t)b * a.lse_bs +
+              (int64_t)h * a.lse_hs + qi] = lse;
     }
   }
 
@@ -1209,6 +1296,102 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
   a.status = p.status;
 
   return launch_dense_core<T, D>(tq, tk, tv, a, p.batch, p.num_q_heads, p.q_len, stream);
+}
+
+// Split-key decode: the workspace holds the partials, then the combine pass.
+static int64_t decode_workspace_bytes(const KvbPrefillParams& p, int splits) {
+  const int64_t rows = (int64_t)p.batch * p.num_q_heads * p.q_len;
+  const int64_t o_bytes = (int64_t)splits * rows * p.head_dim * 2;
+  return (o_bytes + 255) / 256 * 256 + (int64_t)splits * rows * 4;
+}
+
+static int decode_split_tiles(const KvbPrefillParams& p, int splits, int* eff) {
+  const int n_t = (p.kv_len + BN - 1) / BN;
+  const int st = max(1, (n_t + max(splits, 1) - 1) / max(splits, 1));
+  *eff = max(1, (n_t + st - 1) / st);
+  return st;
+}
+
+template <typename T, int D>
+static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cudaStream_t stream) {
+  using G = Geo<D>;
+  const int group = p.num_q_heads / p.num_kv_heads;
+  const int packed = group * p.q_len;
+  int splits = 1;
+  const int split_tiles = decode_split_tiles(p, splits_req, &splits);
+  const int64_t q_rs = p.q_len == 1 ? p.q_head_stride : p.q_row_stride;
+  CUtensorMap tq, tk, tv;
+  std::string err;
+  if (!make_map(&tq, p.q, p.dtype, D, packed, p.num_kv_heads, p.batch, q_rs,
+                (int64_t)group * p.q_head_stride, p.batch > 1 ? p.q_batch_stride : 8, &err) ||
+      !make_map(&tk, p.k, p.dtype, D, std::max(1, p.kv_len), p.num_kv_heads, p.batch,
+                p.k_row_stride, p.k_head_stride, p.batch > 1 ? p.k_batch_stride : 8, &err) ||
+      !make_map(&tv, p.v, p.dtype, D, std::max(1, p.kv_len), p.num_kv_heads, p.batch,
+                p.v_row_stride, p.v_head_stride, p.batch > 1 ? p.v_batch_stride : 8, &err))
+    return fail(KVB_ERR_INVALID, err);
+  const int64_t rows = (int64_t)p.batch * p.num_kv_heads * packed;
+  T* o_part = reinterpret_cast<T*>(ws);
+  const int64_t o_bytes = (int64_t)splits * rows * D * 2;
+  float* lse_part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) +
+                                             (o_bytes + 255) / 256 * 256);
+  DenseArgs a = {};
+  a.o = o_part;
+  a.lse = lse_part;
+  a.o_rs = D;
+  a.o_hs = (int64_t)packed * D;
+  a.o_bs = (int64_t)p.num_kv_heads * packed * D;
+  a.lse_hs = packed;
+  a.lse_bs = (int64_t)p.num_kv_heads * packed;
+  a.q_len = packed;
+  a.kv_len = p.kv_len;
+  a.group = 1;
+  a.pair_heads = 0;
+  a.causal = p.causal;
+  a.scale_log2 = p.softmax_scale * 1.4426950408889634f;
+  a.status = p.status;
+  PagedArgs sp = {};
+  sp.rows_per_head = p.q_len;
+  sp.split_tiles = split_tiles;
+  sp.o_split_stride = rows * D;
+  sp.lse_split_stride = rows;
+  auto kern = kvb_prefill_kernel<T, D, false, true>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         G::SMEM_BYTES);
+    if (e != cudaSuccess)
+      return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    configured_device = dev;
+  }
+  kern<<<dim3(splits, p.num_kv_heads, p.batch), Roles<false>::kThreads, G::SMEM_BYTES, stream>>>(
+      tq, tk, tv, a, sp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(KVB_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
+  CombineArgs c = {};
+  c.o_part = o_part;
+  c.lse_part = lse_part;
+  c.splits = splits;
+  c.o_split_stride = rows * D;
+  c.lse_split_stride = rows;
+  c.batch = p.batch;
+  c.num_kv_heads = p.num_kv_heads;
+  c.group = group;
+  c.rows_per_head = p.q_len;
+  c.o = p.o;
+  c.lse = p.lse;
+  c.o_bs = p.o_batch_stride;
+  c.o_hs = p.o_head_stride;
+  c.o_rs = p.o_row_stride;
+  c.lse_bs = p.lse_batch_stride;
+  c.lse_hs = p.lse_head_stride;
+  const int64_t threads = rows * (D / 8);
+  kvb_split_combine_kernel<T, D><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(c);
+  e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return fail(KVB_ERR_CUDA, std::string("combine launch: ") + cudaGetErrorString(e));
+  return KVB_OK;
 }
 
 // Workspace the paged path uses to dequantise the prefix once instead of in
@@ -1500,6 +1683,58 @@ static int validate_paged(const KvbPagedPrefillParams& p) {
     if (s <= 0 || (s % 8) != 0)
       return fail(KVB_ERR_INVALID, "row and head strides must be positive multiples of 8 elements");
   return KVB_OK;
+}
+
+static int validate_decode(const KvbPrefillParams& p, int splits) {
+  int rc = validate(p);
+  if (rc != KVB_OK) return rc;
+  if (p.cu_seqlens_q) return fail(KVB_ERR_UNSUPPORTED, "split decode takes dense batches");
+  if (splits < 1 || splits > 4096) return fail(KVB_ERR_INVALID, "num_splits must be in [1, 4096]");
+  if (p.q_len < 1 || p.kv_len < p.q_len)
+    return fail(KVB_ERR_INVALID, "split decode needs 1 <= q_len <= kv_len");
+  const int group = p.num_q_heads / p.num_kv_heads;
+  if ((int64_t)group * p.q_len > 2 * BM)
+    return fail(KVB_ERR_UNSUPPORTED, "split decode packs (q heads per KV head) * q_len <= 256 rows");
+  if (p.q_len > 1 && (p.q_head_stride != (int64_t)p.q_len * p.q_row_stride ||
+                      p.o_head_stride != (int64_t)p.q_len * p.o_row_stride))
+    return fail(KVB_ERR_INVALID, "with q_len > 1 the rows of a head must be contiguous "
+                                 "(head stride = q_len * row stride) in q and o");
+  if (p.q_len == 1 && p.o_head_stride % 8)
+    return fail(KVB_ERR_INVALID, "o head stride must be a multiple of 8 elements");
+  return KVB_OK;
+}
+
+extern "C" int64_t kvb_decode_workspace_bytes(const KvbPrefillParams* params, int num_splits) {
+  if (!params || validate_decode(*params, num_splits) != KVB_OK) return -1;
+  int eff = 1;
+  decode_split_tiles(*params, num_splits, &eff);
+  return decode_workspace_bytes(*params, eff);
+}
+
+extern "C" int kvb_decode_fwd(const KvbPrefillParams* params, int num_splits, void* workspace,
+                              int64_t workspace_bytes, void* stream) {
+  if (!params) return fail(KVB_ERR_INVALID, "params is NULL");
+  const KvbPrefillParams& p = *params;
+  int rc = validate_decode(p, num_splits);
+  if (rc != KVB_OK) return rc;
+  int eff = 1;
+  decode_split_tiles(p, num_splits, &eff);
+  const int64_t need = decode_workspace_bytes(p, eff);
+  if (!workspace || !aligned16(workspace) || workspace_bytes < need)
+    return fail(KVB_ERR_INVALID, "workspace must hold " + std::to_string(need) + " bytes");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool bf = p.dtype == KVB_DTYPE_BF16;
+  switch (p.head_dim) {
+    case 64:
+      return bf ? launch_decode<__nv_bfloat16, 64>(p, num_splits, workspace, s)
+                : launch_decode<__half, 64>(p, num_splits, workspace, s);
+    case 96:
+      return bf ? launch_decode<__nv_bfloat16, 96>(p, num_splits, workspace, s)
+                : launch_decode<__half, 96>(p, num_splits, workspace, s);
+    default:
+      return bf ? launch_decode<__nv_bfloat16, 128>(p, num_splits, workspace, s)
+                : launch_decode<__half, 128>(p, num_splits, workspace, s);
+  }
 }
 
 extern "C" int64_t kvb_paged_prefill_workspace_bytes(const KvbPagedPrefillParams* params) {

@@ -171,9 +171,25 @@ def kvboost_attention_forward(module: torch.nn.Module, query: torch.Tensor, key:
     else:
         is_causal = is_causal if is_causal is not None else getattr(module, "is_causal", True)
         causal = bool(is_causal) and q_len > 1
+    group = query.size(1) // key.size(1)
+    if q_len <= DECODE_MAX_Q and q_len * group <= 256 and kv_len >= DECODE_MIN_KV:
+        # decode steps and short seams: GQA heads packed per key tile, keys split
+        from .ops import decode_attention
+        if q_len == 1:   # one row per head: [B, 1, H, D] storage is already head-contiguous
+            out = torch.empty(query.size(0), 1, query.size(1), query.size(3), dtype=query.dtype,
+                              device=query.device).transpose(1, 2)
+        else:            # the packed rows of a head must be contiguous
+            out = None
+        out, _ = decode_attention(query, key, value, float(scaling), causal, out=out,
+                                  return_lse=False)
+        return out.transpose(1, 2), None
     out, _ = prefill_attention(query, key, value, float(scaling), causal, return_lse=False,
                                out_layout="bshd")
     return out, None
+
+
+DECODE_MAX_Q = 16     # query rows per head up to which the split-key decode path is used
+DECODE_MIN_KV = 256   # ... when there are at least this many keys
 
 
 # ── HuggingFace module patching ───────────────────────────────────────────────
@@ -303,10 +319,12 @@ def _make_paged_attn_fn(layer_idx: int, state: dict):
         table, _ = allocator.append_kv(layer_idx, state["block_table"], write_slot,
                                        k_new[0], v_new[0])
         state["block_table"] = table
-        if state.get("top_left"):
-            n = write_slot + k_new.size(2)
+        n = write_slot + k_new.size(2)
+        if state.get("top_left") or query.size(2) <= DECODE_MAX_Q:
+            # decode steps (and the reference's mask alignment): attend over the pool
             out = paged_attention_fwd(query, allocator, [table], [n], layer_idx,
-                                      causal=query.size(2) > 1, scale=scaling, top_left=True)
+                                      causal=query.size(2) > 1, scale=scaling,
+                                      top_left=bool(state.get("top_left")))
         else:
             out, _ = paged_prefill_attention(
                 query, k_new.to(query.dtype).contiguous(), v_new.to(query.dtype).contiguous(),

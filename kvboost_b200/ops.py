@@ -186,3 +186,77 @@ def prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         rc = _lib.load().kvb_prefill_fwd(p, _stream_handle(q.device))
     _lib.check(rc, "kvb_prefill_fwd(varlen)")
     return out, lse
+
+
+_decode_ws = {}
+
+
+def decode_splits(batch: int, num_kv_heads: int, kv_len: int, num_sms: int = 148) -> int:
+    """Key-range splits for one wave of CTAs (one per SM), at least two 128-key tiles
+    per split: a CTA's fixed cost (setup, first tile, epilogue) is several tiles'
+    worth, so a second wave or one-tile splits cost more than they parallelise
+    (measured on B200 for batch 1-32, 2-8 KV heads, 2K-16K keys)."""
+    tiles = (kv_len + 127) // 128
+    return max(1, min(num_sms // max(1, batch * num_kv_heads), tiles // 2))
+
+
+def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                     softmax_scale: Optional[float] = None, causal: bool = True,
+                     out: Optional[torch.Tensor] = None, return_lse: bool = True,
+                     num_splits: Optional[int] = None, top_left: bool = False):
+    """Attention for a few queries per head over many keys (decode, q = 1, and the
+    selective-recompute seams, q <= 16): ``kvb_decode_fwd``.
+
+    Same contract as ``prefill_attention`` (q ``[B, Hq, Sq, D]``, k/v ``[B, Hkv, Skv, D]``,
+    bottom-right causal), restricted to (Hq / Hkv) * Sq <= 256 and Sq <= Skv.  The
+    query heads of a GQA group are packed as rows of one tile so that each key tile
+    is read once per group, and the key range is split over CTAs (one wave); a
+    second pass merges the partial results by their LSE.
+    """
+    _check_tensor("q", q, 4)
+    _check_tensor("k", k, 4)
+    _check_tensor("v", v, 4)
+    if not (q.dtype == k.dtype == v.dtype) or k.shape != v.shape:
+        raise RuntimeError("q, k, v dtypes / k, v shapes must match")
+    B, Hq, Sq, D = q.shape
+    _, Hkv, Skv, _ = k.shape
+    if Hq % Hkv:
+        raise RuntimeError(f"num_q_heads ({Hq}) must be divisible by num_kv_heads ({Hkv})")
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(D)
+    if Sq > 1 and q.stride(1) != Sq * q.stride(2):
+        q = q.contiguous()
+    if out is None:
+        out = torch.empty(B, Hq, Sq, D, dtype=q.dtype, device=q.device)
+    lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device) if return_lse else None
+    if num_splits is None:
+        num_splits = decode_splits(B, Hkv, Skv)
+    p = _lib.KvbPrefillParams()
+    p.dtype = _DTYPES[q.dtype]
+    p.head_dim, p.batch, p.num_q_heads, p.num_kv_heads = D, B, Hq, Hkv
+    p.q_len, p.kv_len, p.causal = Sq, Skv, (2 if top_left else 1) if causal else 0
+    p.softmax_scale = float(softmax_scale)
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    p.lse = lse.data_ptr() if lse is not None else None
+    p.q_batch_stride, p.q_head_stride, p.q_row_stride = q.stride(0), q.stride(1), q.stride(2)
+    p.k_batch_stride, p.k_head_stride, p.k_row_stride = k.stride(0), k.stride(1), k.stride(2)
+    p.v_batch_stride, p.v_head_stride, p.v_row_stride = v.stride(0), v.stride(1), v.stride(2)
+    p.o_batch_stride, p.o_head_stride, p.o_row_stride = out.stride(0), out.stride(1), out.stride(2)
+    if lse is not None:
+        p.lse_batch_stride, p.lse_head_stride = lse.stride(0), lse.stride(1)
+    p.status = status_word(q.device).data_ptr()
+    lib = _lib.load()
+    need = int(lib.kvb_decode_workspace_bytes(p, int(num_splits)))
+    if need < 0:
+        _lib.check(_lib.KVB_ERR_INVALID, "kvb_decode_workspace_bytes: " + (
+            lib.kvb_last_error().decode("utf-8", "replace")))
+    idx = q.device.index if q.device.index is not None else torch.cuda.current_device()
+    ws = _decode_ws.get(idx)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=q.device)
+        _decode_ws[idx] = ws
+    with torch.cuda.device(q.device):
+        rc = lib.kvb_decode_fwd(p, int(num_splits), ws.data_ptr(), ws.numel(),
+                                _stream_handle(q.device))
+    _lib.check(rc, "kvb_decode_fwd")
+    return out, lse

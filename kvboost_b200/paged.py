@@ -561,11 +561,16 @@ def paged_attention_fwd(query: torch.Tensor, allocator: DeviceBlockAllocator,
     plens = torch.tensor(L, dtype=torch.int32, device=dev)
     empty = torch.empty(B, allocator.num_heads, 0, D, dtype=query.dtype, device=dev)
     K, V = paged_materialize(allocator, layer, bt, max(L), empty, empty, prefix_lens=plens)
-    from .ops import prefill_attention
+    from .ops import decode_attention, prefill_attention
+    group = Hq // allocator.num_heads
     for b in range(B):
         if L[b] == 0:
             continue
-        prefill_attention(query[b:b + 1], K[b:b + 1, :, :L[b]], V[b:b + 1, :, :L[b]], scale,
-                          causal and Sq > 1, out=out[b:b + 1], return_lse=False,
-                          top_left=top_left)
+        kb, vb = K[b:b + 1, :, :L[b]], V[b:b + 1, :, :L[b]]
+        if Sq <= 16 and Sq * group <= 256 and Sq <= L[b]:
+            decode_attention(query[b:b + 1], kb, vb, scale, causal and Sq > 1, out=out[b:b + 1],
+                             return_lse=False, top_left=top_left)
+        else:
+            prefill_attention(query[b:b + 1], kb, vb, scale, causal and Sq > 1, out=out[b:b + 1],
+                              return_lse=False, top_left=top_left)
     return out
