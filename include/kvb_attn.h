@@ -134,6 +134,25 @@ typedef struct KvbPrefillParams {
 int kvb_prefill_fwd(const KvbPrefillParams* params, void* stream);
 
 /*
+ * Attention for a few queries per head over many keys: decode steps (q_len 1)
+ * and the selective-recompute seams (q_len <= 16) that reach the SDPA call of
+ * the reference's engine (flash_attn_ext.py:86-103) with a short query.  Same
+ * params and semantics as kvb_prefill_fwd in dense mode, restricted to
+ * (num_q_heads / num_kv_heads) * q_len <= 256 and 1 <= q_len <= kv_len; with
+ * q_len > 1 each head's rows must be contiguous in q and o (head stride =
+ * q_len * row stride).  The query heads sharing a KV head are packed as the
+ * rows of one tile, so every key tile is read once per group, and the key
+ * range is split over num_splits CTAs whose partial outputs are merged by
+ * their LSE in a second pass.  workspace: device memory of at least
+ * kvb_decode_workspace_bytes(params, num_splits) bytes (-1: invalid params,
+ * reason in kvb_last_error).  No counterpart in the reference, whose decode
+ * steps run the same SDPA call as its prefill.
+ */
+int64_t kvb_decode_workspace_bytes(const KvbPrefillParams* params, int num_splits);
+int kvb_decode_fwd(const KvbPrefillParams* params, int num_splits, void* workspace,
+                   int64_t workspace_bytes, void* stream);
+
+/*
  * Reuse prefill over an int8 paged prefix: the suffix's queries attend to
  * the cached prefix (KVBoost's 128-token chunks, KIVI int8, stored in
  * 16-token blocks) followed by the suffix's own fresh K/V, bottom-right
