@@ -759,6 +759,7 @@ def run_ttft(args, torch, dist, rank, world, local, dev):
         "e2e": {"value": e2e, "unit": "ms", "h2d_bytes_per_step": w.B * w.SUFFIX * 8,
                 "d2h_bytes_per_step": w.B * w.NEW * 8, "total_ms": statistics.mean(total),
                 "ttft_ms_sdpa_engine": statistics.mean(sdpa),
+                "ttft_ms_samples": [round(x, 2) for x in ttft],
                 "prompt_tokens_per_s": world * w.B * (w.PREFIX + w.SUFFIX) / (e2e / 1e3)},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "kernel": "suffix-prefill attention (per layer)",
