@@ -21,7 +21,16 @@ reference's metric is defined on; the public datasets are not available):
   tokens, 64 query / 8 KV heads, D 128, bf16.  With N GPUs the KV heads are
   split across ranks (strong scaling; each rank holds its heads' pool shard).
 
-One step = one kernel launch over one batch.  K steps are captured in one
+* ``decode`` -- decode attention of the config-3 model: batch 8, 16 query / 2
+  KV heads, D 128, one query row over 4096 keys (split-key kernel + combine).
+* ``quantize_store`` -- quantise-on-store of the config-3 warm: 24 chunks x
+  128 tokens x 36 layers x 2 KV heads x D 128 bf16 into the int8 block pool
+  (GB/s; one launch per chunk).
+* ``cacheblend`` -- CacheBlend repair of a 3072-position stitched prefix of the
+  config-3 model (deviation over 36 layers, top 15 %, patch; GB/s; 3 launches).
+
+One step = one kernel launch over one batch (the last two: one chunk store per
+chunk, and the repair's three launches).  K steps are captured in one
 CUDA graph and replayed between two events on the launching stream after W
 graph-replayed warm-up steps.  Steps rotate over enough input sets that the
 bytes touched exceed L2 (126 MB).  With N > 1 (torchrun) the elapsed time is
@@ -58,7 +67,8 @@ def parse():
     ap.add_argument("--impl", default="kvboost", choices=["kvboost", "reference"])
     ap.add_argument("--workload", default="reuse_prefill",
                     choices=["reuse_prefill", "causal_op", "varlen_d96", "paged_long",
-                             "ttft_reuse", "paged_long_cp", "decode"])
+                             "ttft_reuse", "paged_long_cp", "decode", "quantize_store",
+                             "cacheblend"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cp-gather", default="peers", choices=["peers", "nccl"],
@@ -182,6 +192,7 @@ class Decode(Dense):
         super().__init__("decode", 8, 16, 2, 1, 4095, 128, "bf16",
                          "decode attention: B8 Hq16/Hkv2 D128 bf16, 1 query row over 4096 keys")
         self.bound = "hbm"
+        self.launches_per_step = 2    # split-key pass + LSE combine
 
     def setup(self, torch, dev, rank, world):
         from kvboost_b200 import ops
@@ -325,6 +336,7 @@ class PagedLong:
         self.scaling = "strong"
         self.bound = "tensor"
         self.world = 1
+        self.launches_per_step = 2    # dequantise-once materialise + attention
 
     def local_heads(self, rank, world):
         if self.Hkv % world:
@@ -427,6 +439,231 @@ class PagedLong:
             V = np.concatenate([v[None], vn], axis=2)
             attention(q, K, V, 1.0 / math.sqrt(self.D), True, compute_dtype=np.float32)
         return run, fl, "1 of 64 query heads (its KV head gathered and dequantised)"
+
+
+class QuantizeStore:
+    """Quantise-on-store of freshly encoded chunks (``kvb_quantize_store``): the config-3
+    model's warm of a 3072-token prefix -- 24 chunks of 128 tokens, 36 layers, 2 KV
+    heads, D 128 -- each chunk's bf16 K/V read as the model's cache holds them
+    ([1, H, S, D] views of [1, S, H, D] projections), KIVI int8 + scales written into
+    its 8 blocks of the int8 pool.  One launch per chunk covers all layers."""
+
+    metric, unit, unit_scale, dtype_name = "quantize-on-store GB/s", "GB/s", 1e9, "bf16->int8"
+
+    def __init__(self):
+        self.name, self.L, self.H, self.S, self.D, self.chunks = "quantize_store", 36, 2, 128, 128, 24
+        self.nblk = self.S // 16
+        self.desc = ("quantise-on-store: 24 chunks x 128 tokens, 36 layers, 2 KV heads, D 128, "
+                     "bf16 model-cache K/V -> KIVI int8 16-token blocks + fp16/fp32 scales")
+        self.scaling, self.bound = "weak", "hbm"
+        self.launches_per_step = self.chunks
+
+    def chunk_bytes(self):
+        L, H, S, D, n = self.L, self.H, self.S, self.D, self.nblk
+        return (L * H * S * D * 2 * 2            # bf16 K and V read
+                + L * H * n * 16 * D * 2         # int8 K and V rows written
+                + L * H * n * 16 * 6             # K scales, fp16 + fp32
+                + n * L * H * D * 6)             # V scales in every block, fp16 + fp32
+
+    def bytes(self):
+        return self.chunks * self.chunk_bytes()
+
+    work = bytes
+
+    def flops(self):
+        return 0
+
+    def tokens(self):
+        return self.chunks * self.S
+
+    def config(self):
+        return {"chunks": self.chunks, "chunk_tokens": self.S, "layers": self.L,
+                "kv_heads": self.H, "head_dim": self.D, "block_size": 16}
+
+    def _chunks(self, torch, dev, g):
+        out = []
+        for _ in range(self.chunks):
+            raw = [torch.randn(2, 1, self.S, self.H, self.D, generator=g, device=dev)
+                   .to(torch.bfloat16) for _ in range(self.L)]
+            out.append(([r[0].transpose(1, 2) for r in raw], [r[1].transpose(1, 2) for r in raw]))
+        return out
+
+    def setup(self, torch, dev, rank, world):
+        from kvboost_b200.paged import DeviceBlockAllocator
+        g = torch.Generator(device=dev).manual_seed(99 + rank)
+        R = max(2, math.ceil(2 * L2_BYTES / self.bytes()))
+        self.alloc = DeviceBlockAllocator(self.L, self.H, self.D, R * self.chunks * self.nblk,
+                                          device=dev)
+        sets = [(self._chunks(torch, dev, g),
+                 [self.alloc.allocate(self.nblk) for _ in range(self.chunks)]) for _ in range(R)]
+        self.sets_desc = f"inputs rotate over {R} sets ({R * self.bytes() / 2**20:.0f} MiB > L2)"
+
+        def step(i):
+            chunks, blocks = sets[i % R]
+            for (ks, vs), b in zip(chunks, blocks):
+                self.alloc.store_chunk_int8(b, ks, vs)
+        return step
+
+    def e2e(self, torch, dev):
+        """Each chunk's K/V from pinned host memory, stored, and its int8 blocks and
+        scales read back to pinned host memory."""
+        g = torch.Generator().manual_seed(5)
+        hk = torch.randn(self.L, self.H, self.S, self.D, generator=g).to(torch.bfloat16).pin_memory()
+        hv = torch.randn(self.L, self.H, self.S, self.D, generator=g).to(torch.bfloat16).pin_memory()
+        blocks = self.alloc.allocate(self.nblk) if self.alloc.free_blocks >= self.nblk else \
+            list(range(self.nblk))
+        idx = torch.tensor(blocks, device=dev)
+        hp = torch.empty(self.L, self.nblk, 2, self.H, 16, self.D, dtype=torch.int8).pin_memory()
+
+        def step():
+            for _ in range(self.chunks):
+                dk, dv = hk.to(dev, non_blocking=True), hv.to(dev, non_blocking=True)
+                self.alloc.store_chunk_int8(blocks, dk, dv)
+                hp.copy_(torch.stack([p[idx] for p in self.alloc.pools]), non_blocking=True)
+        h2d = self.chunks * 2 * hk.numel() * 2
+        return step, h2d, self.chunks * hp.numel()
+
+    def gpu_reference(self, torch, dev):
+        """The reference's store arithmetic as torch ops on this GPU
+        (``_quantize_int8`` per layer, then the block scatter of ``write_chunk_int8``)."""
+        from kvboost_b200.paged import quantize_chunk_int8
+        chunks = self._chunks(torch, dev, torch.Generator(device=dev).manual_seed(3))
+        blocks = list(range(self.nblk))
+
+        def run():
+            for ks, vs in chunks:
+                for layer in range(self.L):
+                    self.alloc.write_chunk_int8(layer, blocks, *quantize_chunk_int8(ks[layer],
+                                                                                    vs[layer]))
+        return run, "torch ops: _quantize_int8 per layer + write_chunk_int8 scatter"
+
+    def cpu_sample(self, np):
+        """One chunk, all layers: the reference's bf16 quantisation arithmetic (numpy)."""
+        from oracle.kv_quant import quantize_int8_model_dtype, round_to_bf16
+        g = np.random.default_rng(0)
+        k = round_to_bf16(g.standard_normal((self.L, self.H, self.S, self.D), dtype=np.float32))
+        v = round_to_bf16(g.standard_normal((self.L, self.H, self.S, self.D), dtype=np.float32))
+
+        def run():
+            for layer in range(self.L):
+                quantize_int8_model_dtype(k[layer], v[layer], "bf16")
+        return run, self.chunk_bytes(), "1 of 24 chunks (all 36 layers)"
+
+
+class CacheBlendRepair:
+    """CacheBlend repair of one config-3 prompt's stitched prefix (``kvb_cacheblend_fwd``):
+    3072 cached positions, 36 layers, 2 KV heads, D 128, bf16; cosine deviation of
+    cached vs full-context K over all layers, top 15 % above 0.01, patch of those
+    positions' K and V.  Cached K/V stacked [L, H, S, D] (the assembled prefix), the
+    full-context K/V as the model's cache holds them."""
+
+    metric, unit, unit_scale, dtype_name = "CacheBlend repair GB/s", "GB/s", 1e9, "bf16"
+
+    def __init__(self):
+        self.name, self.L, self.H, self.S, self.D = "cacheblend", 36, 2, 3072, 128
+        self.k = max(1, int(self.S * 0.15))
+        self.desc = ("CacheBlend repair: 3072 cached positions, 36 layers, 2 KV heads, D 128, "
+                     "bf16, top 15% above 0.01 patched")
+        self.scaling, self.bound = "weak", "hbm"
+        self.launches_per_step = 3
+
+    def bytes(self):
+        L, H, S, D, k = self.L, self.H, self.S, self.D, self.k
+        return (2 * L * H * S * D * 2     # cached K and full-context K read (deviation)
+                + S * 4 * 7               # deviation written, read by the select passes
+                + k * 4                   # chosen positions
+                + 2 * k * L * H * D * 2 * 2)  # K and V rows at k positions: read fresh, write cached
+
+    work = bytes
+
+    def flops(self):
+        return 0
+
+    def tokens(self):
+        return self.S
+
+    def config(self):
+        return {"cached_positions": self.S, "layers": self.L, "kv_heads": self.H,
+                "head_dim": self.D, "recompute_ratio": 0.15, "min_deviation": 0.01,
+                "patched_positions": self.k}
+
+    def _inputs(self, torch, dev, g):
+        ck = torch.randn(self.L, self.H, self.S, self.D, generator=g, device=dev).to(torch.bfloat16)
+        cv = torch.randn(self.L, self.H, self.S, self.D, generator=g, device=dev).to(torch.bfloat16)
+        mags = torch.rand(self.S, generator=g, device=dev).view(1, self.S, 1, 1)
+        raw = [(ck[l].transpose(0, 1)[None] + mags * torch.randn(1, self.S, self.H, self.D,
+               generator=g, device=dev)).to(torch.bfloat16) for l in range(self.L)]
+        fk = [r.transpose(1, 2) for r in raw]
+        fv = [torch.randn(1, self.S, self.H, self.D, generator=g, device=dev).to(torch.bfloat16)
+              .transpose(1, 2) for _ in range(self.L)]
+        return ck, cv, fk, fv
+
+    def setup(self, torch, dev, rank, world):
+        from kvboost_b200.cacheblend import cacheblend_fwd
+        g = torch.Generator(device=dev).manual_seed(17 + rank)
+        R = max(2, math.ceil(2 * L2_BYTES / (4 * self.L * self.H * self.S * self.D * 2)))
+        sets = [self._inputs(torch, dev, g) for _ in range(R)]
+        self.sets_desc = (f"inputs rotate over {R} sets "
+                          f"({R * 4 * self.L * self.H * self.S * self.D * 2 / 2**20:.0f} MiB > L2)")
+        self.e2e_set = sets[0]
+
+        def step(i):
+            cacheblend_fwd(*sets[i % R], 0.15, 0.01, patch=True)
+        return step
+
+    def e2e(self, torch, dev):
+        """Cached and full-context K/V from pinned host memory; the chosen positions
+        and count read back."""
+        from kvboost_b200.cacheblend import cacheblend_fwd
+        ck, cv, fk, fv = self.e2e_set
+        hck, hcv = ck.cpu().pin_memory(), cv.cpu().pin_memory()
+        hfk = torch.stack([t[0] for t in fk]).cpu().pin_memory()
+        hfv = torch.stack([t[0] for t in fv]).cpu().pin_memory()
+        hsel = torch.empty(self.k + 1, dtype=torch.int32).pin_memory()
+
+        def step():
+            d = [t.to(dev, non_blocking=True) for t in (hck, hcv, hfk, hfv)]
+            _, sel, cnt = cacheblend_fwd(*d, 0.15, 0.01, patch=True)
+            hsel[:self.k].copy_(sel, non_blocking=True)
+            hsel[self.k:].copy_(cnt, non_blocking=True)
+        h2d = sum(t.numel() * 2 for t in (hck, hcv, hfk, hfv))
+        return step, h2d, hsel.numel() * 4
+
+    def gpu_reference(self, torch, dev):
+        """The reference's steps as torch ops on this GPU (``cacheblend.py:141-197``)."""
+        import torch.nn.functional as F
+        ck, cv, fk, fv = self._inputs(torch, dev, torch.Generator(device=dev).manual_seed(4))
+
+        def run():
+            devs = []
+            for l in range(self.L):
+                a = ck[l].permute(1, 0, 2).reshape(1, self.S, -1)
+                b = fk[l][0].permute(1, 0, 2).reshape(1, self.S, -1)
+                devs.append(1.0 - F.cosine_similarity(a, b, dim=-1))
+            mean = torch.stack(devs).mean(0).squeeze(0)
+            above = mean > 0.01
+            masked = mean.clone()
+            masked[~above] = -1.0
+            _, top = masked.topk(min(self.k, int(above.sum().item())))
+            idx = top.sort().values
+            for l in range(self.L):
+                ck[l][:, idx] = fk[l][0][:, idx]
+                cv[l][:, idx] = fv[l][0][:, idx]
+        return run, "torch ops: cosine_similarity per layer, mean, topk, index copy"
+
+    def cpu_sample(self, np):
+        """The whole repair through the oracle (numpy; the reference's CPU steps)."""
+        from oracle import cacheblend as ocb
+        g = np.random.default_rng(0)
+        ck = g.standard_normal((self.L, self.H, self.S, self.D), dtype=np.float32)
+        fk = ck + g.standard_normal((self.L, self.H, self.S, self.D), dtype=np.float32) * 0.3
+        cv = g.standard_normal((self.L, self.H, self.S, self.D), dtype=np.float32)
+        fv = g.standard_normal((self.L, self.H, self.S, self.D), dtype=np.float32)
+
+        def run():
+            dev = ocb.deviation(ck, fk)
+            ocb.patch(ck, cv, fk, fv, ocb.select(dev, self.k, 0.01))
+        return run, self.bytes(), "the full repair of one prompt"
 
 
 class TtftReuse:
@@ -619,7 +856,7 @@ def run_cp(args, torch, dist, rank, world, local, dev):
                                     + 4 * local_pool.v_scale[0].numel()
                                     + 2 * 2 * kl.numel())
     line = {
-        "metric": "prefill attention TFLOP/s", "value": value, "unit": "TFLOP/s",
+        "metric": metric, "value": value, "unit": munit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -797,6 +1034,10 @@ def make_workload(name, small=False):
         return TtftReuse()
     if name == "decode":
         return Decode()
+    if name == "quantize_store":
+        return QuantizeStore()
+    if name == "cacheblend":
+        return CacheBlendRepair()
     return PagedLong(small)
 
 
@@ -906,17 +1147,20 @@ def run_reference(args):
         }
         print(json.dumps(line), flush=True)
         return
-    val = fl * args.steps / el / 1e12
+    metric = getattr(w, "metric", "prefill attention TFLOP/s")
+    munit, mscale = getattr(w, "unit", "TFLOP/s"), getattr(w, "unit_scale", 1e12)
+    val = fl * args.steps / el / mscale
     line = {
-        "impl": "reference", "metric": "prefill attention TFLOP/s", "value": val,
-        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "impl": "reference", "metric": metric, "value": val,
+        "unit": munit, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": w.scaling,
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "vs_baseline": None, "dtype": getattr(w, "dtype_name", "f32") if hasattr(w, "work") else "f32",
+        "data": "synthetic",
         "config": {"workload": args.workload, "desc": w.desc, "sample": sample + " per step"},
-        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": sample + " per step, numpy float32 restatement of the "
+        "cpu_baseline": {"value": val, "unit": munit, "cores": cores, "kind": "port",
+                         "sample": sample + " per step, numpy restatement of the "
                                    "reference's CPU path (oracle/)"},
-        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": val, "unit": munit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -983,8 +1227,11 @@ def main():
         ms = float(t.item())
     status = ops.read_status(dev)
     fl = w.flops()                     # per rank per step
+    metric = getattr(w, "metric", "prefill attention TFLOP/s")
+    munit, mscale = getattr(w, "unit", "TFLOP/s"), getattr(w, "unit_scale", 1e12)
+    work = w.work() if hasattr(w, "work") else fl
     per_launch_s = ms / 1e3 / args.steps
-    value = world * fl * args.steps / (ms / 1e3) / 1e12
+    value = world * work * args.steps / (ms / 1e3) / mscale
     units = w.tokens() * (world if w.scaling == "weak" else 1)
     tok_s = units * args.steps / (ms / 1e3)
 
@@ -1006,7 +1253,7 @@ def main():
         t = torch.tensor([ems], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ems = float(t.item())
-    e2e_value = world * fl * args.e2e_steps / (ems / 1e3) / 1e12
+    e2e_value = world * work * args.e2e_steps / (ems / 1e3) / mscale
 
     peak_tf, peak_bw, peak_src = measured_peaks()
     if w.bound == "tensor":
@@ -1021,14 +1268,14 @@ def main():
                            else f"independent batches x{world}") if world > 1 else "single",
            "l2": w.sets_desc, "timing": "CUDA graph of K launches between events"}
     line = {
-        "metric": "prefill attention TFLOP/s", "value": value, "unit": "TFLOP/s",
+        "metric": metric, "value": value, "unit": munit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": w.scaling,
         "vs_baseline": None, "dtype": w.dtype_name, "data": "synthetic", "config": cfg,
         "tokens_per_s": tok_s,
-        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+        "e2e": {"value": e2e_value, "unit": munit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ems / args.e2e_steps},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * getattr(w, "launches_per_step", 1),
         "roofline": {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES.get(w.name),
                      "peak_source": psrc, "algorithmic_flops": fl, "algorithmic_bytes": w.bytes()},
@@ -1052,13 +1299,29 @@ def main():
             "value": fl / (sms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": sms,
             "what": "the reference's torch_flash tier on this GPU: F.scaled_dot_product_attention "
                     "with repeat_interleave'd K/V and the bottom-right bool mask, same shapes"}
+    if hasattr(w, "gpu_reference"):
+        run, what = w.gpu_reference(torch, dev)
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_ref = 5
+        s0.record()
+        for _ in range(n_ref):
+            run()
+        s1.record()
+        torch.cuda.synchronize()
+        rms = s0.elapsed_time(s1) / n_ref
+        line["gpu_reference_torch"] = {"value": work / (rms / 1e3) / mscale, "unit": munit,
+                                       "ms_per_step": rms, "what": "the reference's steps on this GPU: " + what}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import numpy as np
         cores = cpu_threads()
         run, sfl, sample = w.cpu_sample(np)
         v, n, el = time_cpu(run, sfl)
-        line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                                "sample": f"{n} x {sample}, numpy float32 oracle, {el:.1f} s"}
+        v = v * 1e12 / mscale
+        line["cpu_baseline"] = {"value": v, "unit": munit, "cores": cores, "kind": "port",
+                                "sample": f"{n} x {sample}, numpy oracle, {el:.1f} s"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     del gw, gt

@@ -308,6 +308,97 @@ int kvb_paged_materialize_peers(const KvbPagedPrefillParams* params,
  */
 int kvb_paged_prefill_fwd_noalloc(const KvbPagedPrefillParams* params, void* stream);
 
+/* ---- Quantise-on-store: a freshly encoded chunk into the int8 block pool ----
+ *
+ * Replaces, for one encoded chunk, the reference's store path: the K/V taken
+ * out of the model's cache (engine.py:846-850), KIVI int8 quantisation on the
+ * store (cache_manager.py:164-175 -> kv_quantize.py:73-100) and the copy into
+ * 16-token blocks (cpu_paged/chunk_to_blocks.py:57-101).  One launch covers
+ * every layer; the source is read once and nothing goes through the host.
+ *
+ * Arithmetic: the reference's, in the source dtype (torch rounds every step of
+ * kv_quantize.py to the tensor's dtype): K scale per token = round(round(max(
+ * amax_d|k|, 1e-8)) / 127), V scale per channel over the chunk's tokens,
+ * q = clamp(rint(round(x / scale)), -128, 127), 0 where x / scale is NaN
+ * (0 / 0); scales stored as float16 (kv_quantize.py:93-97) and, where the
+ * float32 arrays are given, as the float32 value of that float16.  Token t
+ * goes to block_ids[t / 16], slot t % 16; slots of the last block past the
+ * chunk's end are zeroed (q and K scale); every block of the chunk gets the
+ * chunk's V scales.  Sources must hold finite values.
+ */
+#define KVB_MAX_LAYERS 128
+#define KVB_MAX_CHUNK_BLOCKS 128
+
+typedef struct KvbQuantizeStoreParams {
+  int32_t dtype;              /* source K/V dtype, KVB_DTYPE_*; the arithmetic runs in it */
+  int32_t head_dim;           /* 64, 96 or 128 */
+  int32_t num_layers;         /* 1 .. KVB_MAX_LAYERS */
+  int32_t num_kv_heads;
+  int32_t num_tokens;         /* chunk length S >= 1 */
+  int32_t num_chunk_blocks;   /* ceil(S / 16) .. KVB_MAX_CHUNK_BLOCKS */
+  int32_t block_ids[KVB_MAX_CHUNK_BLOCKS];
+  int64_t num_pool_blocks;    /* every block id must lie in [0, num_pool_blocks) */
+  /* Source, per layer: element (h, t, d) at src_k[l] + h * src_head_stride +
+   * t * src_row_stride + d (elements).  Host arrays of device pointers. */
+  const void* const* src_k;
+  const void* const* src_v;
+  int64_t src_head_stride;
+  int64_t src_row_stride;
+  /* Destination, per layer (host arrays of device pointers): the int8 pool
+   * [num_pool_blocks][2][num_kv_heads][16][head_dim] (K at index 0, V at 1),
+   * float16 scales K [num_pool_blocks][num_kv_heads][16] and V
+   * [num_pool_blocks][num_kv_heads][head_dim], and their float32 copies.
+   * Any of the four scale arrays may be NULL (not written). */
+  void* const* pool;
+  void* const* k_scale16;
+  void* const* v_scale16;
+  void* const* k_scale;
+  void* const* v_scale;
+} KvbQuantizeStoreParams;
+
+int kvb_quantize_store(const KvbQuantizeStoreParams* params, void* stream);
+
+/* ---- CacheBlend: deviation-guided patch of stitched chunk K/V ----
+ *
+ * Replaces CacheBlendRecompute._deviation_recompute after its full-context
+ * forward (cacheblend.py:141-197), device-resident: for each cached position
+ * t, the mean over layers of 1 - cos(cached K_t, fresh K_t), the K vectors of
+ * all KV heads flattened into one (cosine as torch's: x.y / (max(|x|, 1e-8)
+ * max(|y|, 1e-8)), float32 here); positions with deviation > min_deviation
+ * are candidates; the min(num_select, #candidates) largest are chosen (lower
+ * position first among equal deviations; torch's topk leaves that order
+ * unspecified), written ascending to `selected` (-1 after the count) with
+ * their count in *num_selected, and with patch = 1 the fresh K and V rows of
+ * every layer and head are copied over the cached ones there.  No host
+ * synchronisation: the count stays on the device.
+ */
+typedef struct KvbCacheBlendParams {
+  int32_t dtype;              /* KVB_DTYPE_*, all four K/V operands */
+  int32_t head_dim;           /* 64, 96 or 128 */
+  int32_t num_layers;         /* 1 .. KVB_MAX_LAYERS */
+  int32_t num_kv_heads;
+  int32_t num_tokens;         /* S, cached positions compared, >= 1 */
+  int32_t num_select;         /* max(1, int(S * recompute_ratio)) (cacheblend.py:163) */
+  float min_deviation;
+  int32_t patch;              /* 0: deviation and selection only; 1: also patch */
+  /* Per layer (host arrays of device pointers): element (h, t, d) at
+   * ptr[l] + h * head_stride + t * row_stride + d.  Strides in elements, multiples
+   * of 8; pointers 16-byte aligned.  cached_v / fresh_v may be NULL when patch = 0. */
+  void* const* cached_k;
+  void* const* cached_v;
+  const void* const* fresh_k;
+  const void* const* fresh_v;
+  int64_t cached_head_stride;
+  int64_t cached_row_stride;
+  int64_t fresh_head_stride;
+  int64_t fresh_row_stride;
+  float* deviation;           /* device [S], written */
+  int32_t* selected;          /* device [num_select], written */
+  int32_t* num_selected;      /* device [1], written */
+} KvbCacheBlendParams;
+
+int kvb_cacheblend_fwd(const KvbCacheBlendParams* params, void* stream);
+
 /* Human-readable reason for the last non-zero return on this host thread. */
 const char* kvb_last_error(void);
 

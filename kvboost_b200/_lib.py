@@ -78,6 +78,45 @@ _lock = threading.Lock()
 _lib = None
 
 
+KVB_MAX_LAYERS = 128
+KVB_MAX_CHUNK_BLOCKS = 128
+_pp = ctypes.POINTER(ctypes.c_void_p)
+
+
+class KvbQuantizeStoreParams(ctypes.Structure):
+    """Mirror of ``KvbQuantizeStoreParams``."""
+
+    _fields_ = [
+        ("dtype", _i32), ("head_dim", _i32), ("num_layers", _i32), ("num_kv_heads", _i32),
+        ("num_tokens", _i32), ("num_chunk_blocks", _i32),
+        ("block_ids", _i32 * KVB_MAX_CHUNK_BLOCKS),
+        ("num_pool_blocks", _i64),
+        ("src_k", _pp), ("src_v", _pp),
+        ("src_head_stride", _i64), ("src_row_stride", _i64),
+        ("pool", _pp), ("k_scale16", _pp), ("v_scale16", _pp), ("k_scale", _pp), ("v_scale", _pp),
+    ]
+
+
+class KvbCacheBlendParams(ctypes.Structure):
+    """Mirror of ``KvbCacheBlendParams``."""
+
+    _fields_ = [
+        ("dtype", _i32), ("head_dim", _i32), ("num_layers", _i32), ("num_kv_heads", _i32),
+        ("num_tokens", _i32), ("num_select", _i32), ("min_deviation", ctypes.c_float),
+        ("patch", _i32),
+        ("cached_k", _pp), ("cached_v", _pp), ("fresh_k", _pp), ("fresh_v", _pp),
+        ("cached_head_stride", _i64), ("cached_row_stride", _i64),
+        ("fresh_head_stride", _i64), ("fresh_row_stride", _i64),
+        ("deviation", _vp), ("selected", _vp), ("num_selected", _vp),
+    ]
+
+
+def pointer_array(ptrs):
+    """A ctypes ``void*[n]`` of device addresses (keep it alive across the call)."""
+    arr = (ctypes.c_void_p * len(ptrs))(*[int(p) if p else None for p in ptrs])
+    return arr
+
+
 def lib_path() -> str:
     return _build.LIB_PATH
 
@@ -121,6 +160,10 @@ def load() -> ctypes.CDLL:
         lib.kvb_paged_prefill_fwd_noalloc.restype = ctypes.c_int
         lib.kvb_paged_prefill_workspace_bytes.argtypes = [ctypes.POINTER(KvbPagedPrefillParams)]
         lib.kvb_paged_prefill_workspace_bytes.restype = ctypes.c_int64
+        lib.kvb_quantize_store.argtypes = [ctypes.POINTER(KvbQuantizeStoreParams), _vp]
+        lib.kvb_quantize_store.restype = ctypes.c_int
+        lib.kvb_cacheblend_fwd.argtypes = [ctypes.POINTER(KvbCacheBlendParams), _vp]
+        lib.kvb_cacheblend_fwd.restype = ctypes.c_int
         lib.kvb_last_error.argtypes = []
         lib.kvb_last_error.restype = ctypes.c_char_p
         lib.kvb_abi_version.argtypes = []

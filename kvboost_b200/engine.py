@@ -54,6 +54,7 @@ class GenerationMode(str, enum.Enum):
 
 class RecomputeStrategy(str, enum.Enum):
     SELECTIVE = "selective"
+    CACHEBLEND = "cacheblend"
     NONE = "none"
 
 
@@ -139,15 +140,19 @@ class DeviceChunk:
     token_ids: List[int]
     position_start: int
     position_end: int
-    keys: torch.Tensor     # [layers, kv_heads, len, head_dim] on the GPU
-    values: torch.Tensor
+    keys: Optional[torch.Tensor]     # [layers, kv_heads, len, head_dim] on the GPU
+    values: Optional[torch.Tensor]   # (None for a chunk held in the int8 block pool)
     hits: int = 0
+    block_ids: Optional[List[int]] = None   # its blocks in the engine's int8 pool
+    pool_bytes: int = 0
 
     @property
     def length(self) -> int:
         return self.position_end - self.position_start
 
     def nbytes(self) -> int:
+        if self.block_ids is not None:
+            return self.pool_bytes
         return self.keys.numel() * self.keys.element_size() * 2
 
 
@@ -159,11 +164,12 @@ class DeviceChunkStore:
     hash, LRU eviction when the byte budget is exceeded, hit/miss stats.
     """
 
-    def __init__(self, max_bytes: int):
+    def __init__(self, max_bytes: int, on_evict=None):
         self.max_bytes = int(max_bytes)
         self._chunks: "OrderedDict[str, DeviceChunk]" = OrderedDict()
         self.bytes = 0
         self.hits = self.misses = self.evictions = 0
+        self.on_evict = on_evict
 
     def get(self, chunk_id: str) -> Optional[DeviceChunk]:
         c = self._chunks.get(chunk_id)
@@ -180,19 +186,30 @@ class DeviceChunkStore:
             c.hits += 1
         return c
 
-    def store(self, chunk: DeviceChunk) -> bool:
-        size = chunk.nbytes()
+    def make_room(self, size: int) -> bool:
+        """Evict least-recently-used chunks until ``size`` more bytes fit."""
         if size > self.max_bytes:
             return False
         while self.bytes + size > self.max_bytes and self._chunks:
             _, old = self._chunks.popitem(last=False)
             self.bytes -= old.nbytes()
             self.evictions += 1
+            if self.on_evict is not None:
+                self.on_evict(old)
+        return True
+
+    def store(self, chunk: DeviceChunk) -> bool:
+        size = chunk.nbytes()
+        if not self.make_room(size):
+            return False
         self._chunks[chunk.chunk_id] = chunk
         self.bytes += size
         return True
 
     def clear(self) -> None:
+        if self.on_evict is not None:
+            for c in self._chunks.values():
+                self.on_evict(c)
         self._chunks.clear()
         self.bytes = 0
         self.hits = self.misses = self.evictions = 0
@@ -244,7 +261,15 @@ class KVBoost:
                  chunk_size: int = 128, min_chunk_tokens: int = 32,
                  recompute_overlap: int = 16,
                  recompute_strategy: Union[str, RecomputeStrategy] = RecomputeStrategy.SELECTIVE,
-                 device: str = "cuda"):
+                 recompute_ratio: float = 0.15, kv_cache_bits: int = 16,
+                 int8_pool_blocks: Optional[int] = None, device: str = "cuda"):
+        """``kv_cache_bits=8`` keeps cached chunks KIVI-int8 in a device block pool,
+        quantised on store by one kernel per chunk (the reference's
+        ``kv_cache_bits=8`` store, ``cache_manager.py:164-175``), dequantised on
+        assembly by the paged gather kernel; the pool has ``int8_pool_blocks``
+        16-token blocks (default: what ``max_cache_bytes`` buys, at most 8192)."""
+        if kv_cache_bits not in (8, 16):
+            raise ValueError("kv_cache_bits must be 16 or 8")
         self.device = torch.device(device)
         self.model = model.to(self.device).eval()
         self.tokenizer = tokenizer
@@ -252,8 +277,26 @@ class KVBoost:
         self.min_chunk_tokens = min_chunk_tokens
         self.recompute_overlap = recompute_overlap
         self.recompute_strategy = RecomputeStrategy(recompute_strategy)
-        self.store = DeviceChunkStore(max_cache_bytes)
+        self.kv_cache_bits = kv_cache_bits
+        self.pool = None
+        if kv_cache_bits == 8:
+            from .paged import DeviceBlockAllocator
+            cfg = self.model.config
+            L = cfg.num_hidden_layers
+            H = getattr(cfg, "num_key_value_heads", None) or cfg.num_attention_heads
+            D = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+            self._block_bytes = L * (2 * H * 16 * D + H * 16 * 6 + H * D * 6)
+            nblk = int8_pool_blocks or max(1, min(int(max_cache_bytes) // self._block_bytes, 8192))
+            self.pool = DeviceBlockAllocator(L, H, D, nblk, device=self.device)
+            max_cache_bytes = min(int(max_cache_bytes), nblk * self._block_bytes)
+        self.store = DeviceChunkStore(max_cache_bytes, on_evict=self._release_chunk)
+        from .cacheblend import CacheBlendRecompute
+        self.cacheblend_recompute = CacheBlendRecompute(recompute_ratio=recompute_ratio)
         self._flash_attn_patched = install_flash_attention(self.model)
+
+    def _release_chunk(self, chunk: "DeviceChunk") -> None:
+        if chunk.block_ids is not None and self.pool is not None:
+            self.pool.free(chunk.block_ids)
 
     @classmethod
     def from_pretrained(cls, model_name: str, dtype=torch.bfloat16, **kwargs) -> "KVBoost":
@@ -304,14 +347,54 @@ class KVBoost:
             return self.model(input_ids=ids, position_ids=pos, past_key_values=cache,
                               use_cache=True, logits_to_keep=1)
 
-    def _encode_to_kv(self, ids: List[int], position_offset: int):
-        """One chunk on its own at its absolute positions (``engine.py:829-850``)."""
+    def _encode_layers(self, ids: List[int], position_offset: int):
+        """Per-layer ``[1, H, S, D]`` K/V of one chunk encoded on its own at its
+        absolute positions (``engine.py:829-850``), as the model's cache holds them."""
         x = torch.tensor([ids], dtype=torch.long, device=self.device)
         pos = torch.arange(position_offset, position_offset + len(ids), device=self.device)[None]
         from transformers import DynamicCache
         out = self._forward(x, pos, DynamicCache())
-        layers = self._layers(out.past_key_values)
+        return self._layers(out.past_key_values)
+
+    def _encode_to_kv(self, ids: List[int], position_offset: int):
+        layers = self._encode_layers(ids, position_offset)
         return (torch.stack([k[0] for k, _ in layers]), torch.stack([v[0] for _, v in layers]))
+
+    def _store_chunk(self, key: str, ids: List[int], pos: int) -> bool:
+        if self.pool is None:
+            k, v = self._encode_to_kv(ids, pos)
+            return self.store.store(DeviceChunk(key, ids, pos, pos + len(ids), k, v))
+        # int8: the cache tensors go straight into the pool (quantise-on-store kernel)
+        layers = self._encode_layers(ids, pos)
+        nblk = (len(ids) + 15) // 16
+        size = nblk * self._block_bytes
+        if not self.store.make_room(size):
+            return False
+        blocks = self.pool.allocate(nblk)
+        self.pool.store_chunk_int8(blocks, [k for k, _ in layers], [v for _, v in layers])
+        return self.store.store(DeviceChunk(key, ids, pos, pos + len(ids), None, None,
+                                            block_ids=blocks, pool_bytes=size))
+
+    def _chunk_kv(self, chunks: List["DeviceChunk"]):
+        """Stacked ``[L, H, P, D]`` K/V of a run of cached chunks in the model's dtype."""
+        if chunks[0].block_ids is None:
+            return (torch.cat([c.keys for c in chunks], dim=2),
+                    torch.cat([c.values for c in chunks], dim=2))
+        from .paged import block_table_tensor, paged_materialize
+        dt = next(self.model.parameters()).dtype
+        P = sum(c.length for c in chunks)
+        # each chunk starts on a block boundary: gather through a per-token-exact
+        # table (chunks shorter than their blocks leave no gaps in the sequence)
+        if any(c.length % 16 for c in chunks[:-1]):
+            raise RuntimeError("only the last cached chunk may end inside a 16-token block")
+        table = block_table_tensor([[b for c in chunks for b in c.block_ids]], self.device)
+        L, H, D = self.pool.num_layers, self.pool.num_heads, self.pool.head_dim
+        kv_pad = (P + 127) // 128 * 128
+        ws = torch.empty(L, 2, 1, H, kv_pad, D, dtype=dt, device=self.device)
+        empty = torch.empty(1, H, 0, D, dtype=dt, device=self.device)
+        for layer in range(L):
+            paged_materialize(self.pool, layer, table, P, empty, empty, workspace=ws[layer])
+        return ws[:, 0, 0, :, :P], ws[:, 1, 0, :, :P]
 
     def _sample(self, logits: torch.Tensor, temperature: float, do_sample: bool) -> torch.Tensor:
         if do_sample:
@@ -327,8 +410,7 @@ class KVBoost:
         for _, _, ids in fixed_split(token_ids, self.chunk_size, self.min_chunk_tokens):
             key = chained_hash(ids, parent)
             if self.store.get(key) is None:
-                k, v = self._encode_to_kv(ids, pos)
-                if self.store.store(DeviceChunk(key, ids, pos, pos + len(ids), k, v)):
+                if self._store_chunk(key, ids, pos):
                     added += 1
             parent = key
             pos += len(ids)
@@ -354,12 +436,26 @@ class KVBoost:
                                                     self.min_chunk_tokens)
         if not chunks:
             return None, None, 0, boundaries
-        keys = torch.cat([c.keys for c in chunks], dim=2)
-        values = torch.cat([c.values for c in chunks], dim=2)
-        if (repair_seams and self.recompute_strategy == RecomputeStrategy.SELECTIVE
-                and len(boundaries) > 1):
-            keys, values = self._recompute_seams(token_ids, keys, values, boundaries[:-1])
+        keys, values = self._chunk_kv(chunks)
+        if repair_seams and len(boundaries) > 1:
+            if self.recompute_strategy == RecomputeStrategy.SELECTIVE:
+                keys, values = self._recompute_seams(token_ids, keys, values, boundaries[:-1])
+            elif self.recompute_strategy == RecomputeStrategy.CACHEBLEND:
+                keys, values = self._cacheblend(token_ids, keys.contiguous(), values.contiguous(),
+                                                cached_len)
         return keys, values, cached_len, boundaries
+
+    def _cacheblend(self, token_ids, keys, values, cached_len):
+        """``cacheblend.py:103-197``: a full-context forward over the cached tokens,
+        then the deviation / top-k / patch on the device (``kvb_cacheblend_fwd``)."""
+        from transformers import DynamicCache
+        x = torch.tensor([token_ids[:cached_len]], dtype=torch.long, device=self.device)
+        pos = torch.arange(0, cached_len, device=self.device)[None]
+        out = self._forward(x, pos, DynamicCache())
+        layers = self._layers(out.past_key_values)
+        self.cacheblend_recompute.repair(keys, values, [k for k, _ in layers],
+                                         [v for _, v in layers])
+        return keys, values
 
     def _recompute_seams(self, token_ids, keys, values, seams):
         """``selective_recompute.py:99-184``: re-encode the last ``recompute_overlap``

@@ -27,6 +27,7 @@ load stage (``kvb_paged_prefill_fwd``).
 
 from __future__ import annotations
 
+import ctypes
 import math
 import threading
 from typing import Dict, List, Optional, Sequence, Tuple
@@ -54,6 +55,25 @@ def quantize_chunk_int8(key: torch.Tensor, val: torch.Tensor):
     val_scale = val_amax / 127.0
     val_q = (val / val_scale).round().clamp(-128, 127).to(torch.int8)
     return key_q, key_scale.to(torch.float16), val_q, val_scale.to(torch.float16)
+
+
+def _layer_list(x) -> List[torch.Tensor]:
+    """Per-layer ``[H, S, D]`` views of a stacked ``[L, H, S, D]`` tensor or of a
+    sequence of ``[H, S, D]`` / ``[1, H, S, D]`` tensors."""
+    if isinstance(x, torch.Tensor):
+        if x.dim() != 4:
+            raise ValueError("stacked K/V must be [layers, heads, tokens, head_dim]")
+        return list(x.unbind(0))
+    out = []
+    for t in x:
+        if t.dim() == 4:
+            if t.shape[0] != 1:
+                raise ValueError("per-layer K/V must be [H, S, D] or [1, H, S, D]")
+            t = t[0]
+        if t.dim() != 3:
+            raise ValueError("per-layer K/V must be [H, S, D] or [1, H, S, D]")
+        out.append(t)
+    return out
 
 
 class DeviceBlockAllocator:
@@ -175,6 +195,58 @@ class DeviceBlockAllocator:
         vs = val_scale.reshape(H, D).to(torch.float16).to(self.device)
         self.v_scale16[layer][idx] = vs.unsqueeze(0).expand(n, H, D)
         self.v_scale[layer][idx] = vs.float().unsqueeze(0).expand(n, H, D)
+
+    def store_chunk_int8(self, block_ids: List[int], keys, values) -> None:
+        """Quantise one freshly encoded chunk on the device and store it in its blocks,
+        every layer in one launch (``kvb_quantize_store``).
+
+        ``keys`` / ``values``: per layer, the chunk's K/V as ``[H, S, D]`` or
+        ``[1, H, S, D]`` tensors (the model cache's own per-layer tensors, any
+        strides with a contiguous last dimension), or one stacked ``[L, H, S, D]``
+        tensor, in bfloat16 or float16.  Same bytes in the pool and the same scales
+        as quantising with the reference's arithmetic in that dtype
+        (``kv_quantize.py:73-100``) and then ``write_chunk_int8``: token t in
+        ``block_ids[t // 16]``, slot ``t % 16``, zero-padded last block, the chunk's
+        per-channel V scales in every block of the chunk.
+        """
+        if self.dtype != torch.int8:
+            raise RuntimeError("store_chunk_int8 needs an int8 pool")
+        ks, vs = _layer_list(keys), _layer_list(values)
+        L = len(ks)
+        if L != len(vs) or not 1 <= L <= min(self.num_layers, _lib.KVB_MAX_LAYERS):
+            raise ValueError(f"need K and V for 1..{self.num_layers} layers, got {len(ks)} / {len(vs)}")
+        ref = ks[0]
+        if ref.dtype not in _DTYPES:
+            raise TypeError("chunk K/V must be bfloat16 or float16")
+        H, S, D = ref.shape
+        if H != self.num_heads or D != self.head_dim:
+            raise ValueError(f"chunk K/V {tuple(ref.shape)} do not match the pool's heads / head_dim")
+        n = len(block_ids)
+        if n * self.block_size < S or n > _lib.KVB_MAX_CHUNK_BLOCKS:
+            raise ValueError(f"{n} blocks cannot hold {S} tokens (at most "
+                             f"{_lib.KVB_MAX_CHUNK_BLOCKS} blocks per chunk)")
+        for t in ks + vs:
+            if t.shape != ref.shape or t.dtype != ref.dtype or t.device != self.device:
+                raise ValueError("every layer's K and V must share shape, dtype and the pool's device")
+        if any(t.stride() != ref.stride() or t.stride(2) != 1 for t in ks + vs):
+            ks = [t.contiguous() for t in ks]
+            vs = [t.contiguous() for t in vs]
+            ref = ks[0]
+        p = _lib.KvbQuantizeStoreParams()
+        p.dtype, p.head_dim, p.num_layers, p.num_kv_heads = _DTYPES[ref.dtype], D, L, H
+        p.num_tokens, p.num_chunk_blocks = S, n
+        for i, b in enumerate(block_ids):
+            p.block_ids[i] = int(b)
+        p.num_pool_blocks = self.num_blocks
+        arrays = [_lib.pointer_array([t.data_ptr() for t in group]) for group in (
+            ks, vs, self.pools[:L], self.k_scale16[:L], self.v_scale16[:L],
+            self.k_scale[:L], self.v_scale[:L])]
+        (p.src_k, p.src_v, p.pool, p.k_scale16, p.v_scale16, p.k_scale, p.v_scale) = [
+            ctypes.cast(a, _lib._pp) for a in arrays]
+        p.src_head_stride, p.src_row_stride = ref.stride(0), ref.stride(1)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().kvb_quantize_store(ctypes.byref(p), _stream_handle(self.device)),
+                       "kvb_quantize_store")
 
     def write_chunk(self, layer: int, block_ids: List[int], key: torch.Tensor,
                     val: torch.Tensor) -> None:

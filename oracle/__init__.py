@@ -13,7 +13,10 @@ What it restates (each function cites the KVBoost file:line it follows):
   (``src/kvboost/csrc/flash_attn_kernel.cu:184-245``), varlen and paged
   variants (``src/kvboost/cpu_paged/paged_attn_cpu.py:33-108``).
 * ``kv_quant``   -- KIVI int8 quantize / dequantize with the reference's
-  float16 rounding (``src/kvboost/kv_quantize.py:73-109``).
+  float16 rounding (``src/kvboost/kv_quantize.py:73-109``), also on bfloat16
+  K/V as a model hands them to the store.
+* ``cacheblend`` -- CacheBlend's per-position deviation, top-k selection and
+  patch (``src/kvboost/cacheblend.py:103-197``).
 * ``paged``      -- the block allocator's LIFO free list, ref counts,
   copy-on-write, the chunk->block mapper and ``read_kv`` gather
   (``src/kvboost/cpu_paged/block_allocator.py``,

@@ -50,6 +50,46 @@ def _quantize_int8(key, val):
     return key_q, key_scale, val_q, val_scale
 
 
+def _round_to(x: np.ndarray, dtype: str) -> np.ndarray:
+    """float32 values rounded once to ``dtype`` ("f16" or "bf16"), returned as float32."""
+    x = np.asarray(x, dtype=np.float32)
+    if dtype == "f16":
+        return x.astype(np.float16).astype(np.float32)
+    return round_to_bf16(x)
+
+
+def quantize_int8_model_dtype(key: np.ndarray, val: np.ndarray, dtype: str):
+    """``_quantize_int8`` (``kv_quantize.py:73-100``) on K/V held in the model's dtype.
+
+    key/val: float32 arrays holding exact ``dtype`` values (``"bf16"`` or ``"f16"``),
+    ``[..., S, D]``.  Torch runs each elementwise step in float32 and rounds the
+    result to ``dtype``: ``amax`` (exact), ``clamp(min=1e-8)`` (1e-8 rounds to 0 in
+    float16, to 1.0012e-8 in bfloat16), ``/ 127`` (the float32 quotient, rounded;
+    for every finite 16-bit value this equals rounding ``amax * (1/127)``),
+    ``key / key_scale`` (rounded), ``round`` half-to-even, clamp to [-128, 127].
+    ``0 / 0`` (an all-zero row in float16) gives NaN, which the int8 cast turns into
+    0 on the reference's CPU.  The scales are returned cast to float16 as the
+    reference stores them (``kv_quantize.py:93-97``).
+    Returns ``(key_q, key_scale_f16, val_q, val_scale_f16)``.
+    """
+    key = np.asarray(key, dtype=np.float32)
+    val = np.asarray(val, dtype=np.float32)
+
+    def one(x, axis):
+        amax = np.abs(x).max(axis=axis, keepdims=True)
+        amax = _round_to(np.maximum(amax, np.float32(1e-8)), dtype)
+        scale = _round_to(amax / np.float32(127.0), dtype)
+        with np.errstate(invalid="ignore", divide="ignore"):
+            r = _round_to(x / scale, dtype)
+        q = np.clip(np.round(r), -128, 127)
+        q = np.where(np.isnan(q), 0, q).astype(np.int8)
+        return q, scale.astype(np.float16)
+
+    key_q, key_scale = one(key, -1)
+    val_q, val_scale = one(val, -2)
+    return key_q, key_scale, val_q, val_scale
+
+
 def dequantize_int8(q: np.ndarray, scale_f16: np.ndarray) -> np.ndarray:
     """``float16(q * scale)``; ``scale`` broadcasts like the reference's."""
     return _f16(q.astype(np.float32) * np.asarray(scale_f16, dtype=np.float16).astype(np.float32))

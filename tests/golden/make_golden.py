@@ -20,6 +20,11 @@ Reference entry points exercised (file:line in the KVBoost project):
   ``read_kv`` / ``paged_attention_fwd`` (``cpu_paged/``).
 * ``chained_hash`` / ``content_hash_from_tokens`` (``models.py:131-148``) and
   ``ChunkRegistry`` fixed split (``chunk_registry.py:98-110``).
+* ``quantize_kv`` on bfloat16 / float16 model K/V (the quantise-on-store
+  fixtures) and ``CacheBlendRecompute._deviation_recompute``
+  (``cacheblend.py:103-197``) with a preset full-context K/V.
+
+``python tests/golden/make_golden.py blocks`` rewrites only the last two.
 """
 
 from __future__ import annotations
@@ -114,6 +119,120 @@ def quant_cases(kq):
         out[p + "val_scale"] = layer.val_scale.numpy()
         out[p + "key_deq"] = deq[0].numpy()
         out[p + "val_deq"] = deq[1].numpy()
+    return out
+
+
+def quant_bf16_cases(kq):
+    """``quantize_kv`` on the dtypes a model hands it: bfloat16 (the arithmetic then
+    runs in bfloat16 and only the scales are cast to float16) and float16, with
+    all-zero K rows / V columns and magnitudes whose float16 scales are subnormal."""
+    out = {}
+    g = torch.Generator().manual_seed(8)
+    cases = [(torch.bfloat16, 2, 128, 128, 1.0), (torch.bfloat16, 1, 100, 96, 1e-3),
+             (torch.bfloat16, 2, 128, 64, 300.0), (torch.float16, 2, 128, 128, 1e-3),
+             (torch.bfloat16, 1, 16, 128, 1.0)]
+    for i, (dt, H, S, D, mag) in enumerate(cases):
+        key = (torch.randn(1, H, S, D, generator=g) * mag).to(dt)
+        val = (torch.randn(1, H, S, D, generator=g) * mag * 2).to(dt)
+        key[0, 0, 3] = 0
+        val[0, H - 1, :, 5] = 0
+        qkv = kq.quantize_kv(((key, val),), bits=8)
+        layer = qkv.layers[0]
+        deq = kq.dequantize_kv(qkv)[0]
+        p = f"b{i}/"
+        out[p + "dtype"] = np.array(1 if dt == torch.bfloat16 else 2)
+        out[p + "key"] = _store(key)
+        out[p + "val"] = _store(val)
+        out[p + "key_q"] = layer.key_q.numpy()
+        out[p + "key_scale"] = _store(layer.key_scale)
+        out[p + "val_q"] = layer.val_q.numpy()
+        out[p + "val_scale"] = _store(layer.val_scale)
+        out[p + "key_deq"] = _store(deq[0])
+        out[p + "val_deq"] = _store(deq[1])
+    return out
+
+
+class _PresetModel:
+    """Stands in for the model in ``CacheBlendRecompute._deviation_recompute``: its
+    forward returns a preset full-context K/V (the legacy tuple form)."""
+
+    def __init__(self, fresh):
+        self.fresh = fresh
+        self._p = torch.zeros(1)
+
+    def parameters(self):
+        return iter([self._p])
+
+    def __call__(self, input_ids=None, position_ids=None, use_cache=True, **kw):
+        from types import SimpleNamespace
+        assert input_ids.shape[1] == self.fresh[0][0].shape[2]
+        return SimpleNamespace(past_key_values=self.fresh)
+
+
+def cacheblend_cases():
+    """``CacheBlendRecompute._deviation_recompute`` (``cacheblend.py:103-197``) with the
+    full-context forward replaced by a preset K/V, so the deviation / top-k / patch
+    steps run exactly as shipped.  Per-token perturbation magnitudes are spread so
+    the selected set does not hinge on rounding."""
+    from kvboost.cacheblend import CacheBlendRecompute
+    out = {}
+    # name: (dtype, layers, heads, S, D, ratio, min_dev, kind)
+    cases = [("spread_f32", torch.float32, 3, 2, 40, 64, 0.15, 0.01, "spread"),
+             ("none_above_f32", torch.float32, 2, 2, 24, 64, 0.15, 0.01, "tiny"),
+             ("few_above_f32", torch.float32, 2, 1, 50, 128, 0.3, 0.05, "few"),
+             ("gapped_bf16", torch.bfloat16, 3, 2, 64, 128, 0.15, 0.01, "gapped"),
+             ("zero_row_f32", torch.float32, 2, 2, 20, 96, 0.2, 0.01, "zero")]
+    for ci, (name, dt, L, H, S, D, ratio, min_dev, kind) in enumerate(cases):
+        g = torch.Generator().manual_seed(500 + ci)
+        perm = torch.randperm(S, generator=g)
+        if kind == "spread":
+            mag = 0.05 + 0.9 * perm.float() / S
+        elif kind == "tiny":
+            mag = torch.full((S,), 1e-4)
+        elif kind == "few":
+            mag = torch.full((S,), 0.05)
+            mag[perm[:5]] = 1.0 + perm[:5].float() / S
+        elif kind == "gapped":
+            mag = 0.05 + 0.45 * perm.float() / S
+            k = max(1, int(S * ratio))
+            mag[perm[:k]] = 2.0 + 0.5 * torch.arange(k).float()
+        else:
+            mag = 0.05 + 0.9 * perm.float() / S
+        cached, fresh = [], []
+        for l in range(L):
+            ck = torch.randn(1, H, S, D, generator=g)
+            cv = torch.randn(1, H, S, D, generator=g)
+            fk = ck + mag.view(1, 1, S, 1) * torch.randn(1, H, S, D, generator=g)
+            fv = cv + torch.randn(1, H, S, D, generator=g)
+            if kind == "zero" and l == 1:
+                ck[:, :, 4] = 0
+            cached.append((ck.to(dt), cv.to(dt)))
+            fresh.append((fk.to(dt), fv.to(dt)))
+        blend = CacheBlendRecompute(recompute_ratio=ratio, min_deviation=min_dev, device="cpu")
+        patched = blend._deviation_recompute(list(range(S)), tuple(cached), S,
+                                             _PresetModel(tuple(fresh)))
+        # The reference's output, reduced to what it decided: the patched positions
+        # (every other position, and every V, is checked to be an exact copy).
+        pk = torch.stack([k for k, _ in patched])
+        pv = torch.stack([v for _, v in patched])
+        ck = torch.stack([k for k, _ in cached])
+        cv = torch.stack([v for _, v in cached])
+        fk = torch.stack([k for k, _ in fresh])
+        fv = torch.stack([v for _, v in fresh])
+        pos = (pk != ck).flatten(0, 2).any(dim=0).any(dim=-1).nonzero().flatten()
+        keep = torch.ones(S, dtype=torch.bool)
+        keep[pos] = False
+        assert torch.equal(pk[:, :, :, pos], fk[:, :, :, pos])
+        assert torch.equal(pv[:, :, :, pos], fv[:, :, :, pos])
+        assert torch.equal(pk[:, :, :, keep], ck[:, :, :, keep])
+        assert torch.equal(pv[:, :, :, keep], cv[:, :, :, keep])
+        p = f"{name}/"
+        out[p + "meta"] = np.array([L, H, S, D, 1 if dt == torch.bfloat16 else 0])
+        out[p + "ratio"] = np.array(ratio)
+        out[p + "min_dev"] = np.array(min_dev)
+        out[p + "cached_k"] = np.stack([_store(k[0]) for k, _ in cached])
+        out[p + "fresh_k"] = np.stack([_store(k[0]) for k, _ in fresh])
+        out[p + "patched_positions"] = pos.numpy().astype(np.int32)
     return out
 
 
@@ -261,6 +380,20 @@ def main_assembly():
     print("assembly fixture written")
 
 
+def main_blocks():
+    """The quantise-on-store and CacheBlend fixtures."""
+    fae, kq, models, cr, ba, c2b, pac = _ref()
+    np.savez_compressed(os.path.join(HERE, "kv_quant_model_dtypes.npz"), **quant_bf16_cases(kq))
+    np.savez_compressed(os.path.join(HERE, "cacheblend.npz"), **cacheblend_cases())
+    print("quantise-on-store and CacheBlend fixtures written")
+
+
 if __name__ == "__main__":
-    main()
-    main_assembly()
+    # with arguments, only the named groups: core, assembly, blocks
+    groups = sys.argv[1:] or ["core", "assembly", "blocks"]
+    if "core" in groups:
+        main()
+    if "assembly" in groups:
+        main_assembly()
+    if "blocks" in groups:
+        main_blocks()

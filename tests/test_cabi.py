@@ -90,7 +90,9 @@ def test_ctypes_layouts_match_c_compiler(tmp_path):
     from kvboost_b200._build import INCLUDE
     structs = {"KvbPrefillParams": _lib.KvbPrefillParams,
                "KvbPagedPrefillParams": _lib.KvbPagedPrefillParams,
-               "KvbPeerShards": _lib.KvbPeerShards}
+               "KvbPeerShards": _lib.KvbPeerShards,
+               "KvbQuantizeStoreParams": _lib.KvbQuantizeStoreParams,
+               "KvbCacheBlendParams": _lib.KvbCacheBlendParams}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "kvb_attn.h"', 'int main(){']
     for name, cls in structs.items():
         lines.append(f'printf("{name} %zu\\n", sizeof({name}));')
@@ -137,3 +139,82 @@ def test_peer_shard_layout(lib):
     assert total == pool + ks + vs + 2 * sfx
     assert all(o % 16 == 0 for o in off)
     assert lib.kvb_peer_shard_layout(8, 80, 1024, 512, off) == -1
+
+
+def _qstore(**kw):
+    import ctypes as C
+    p = _lib.KvbQuantizeStoreParams()
+    p.dtype, p.head_dim, p.num_layers, p.num_kv_heads = 0, 128, 2, 2
+    p.num_tokens, p.num_chunk_blocks, p.num_pool_blocks = 128, 8, 64
+    for i in range(8):
+        p.block_ids[i] = 63 - i
+    ptrs = _lib.pointer_array([4096, 8192])
+    for f in ("src_k", "src_v", "pool", "k_scale16", "v_scale16", "k_scale", "v_scale"):
+        setattr(p, f, C.cast(ptrs, _lib._pp))
+    p.src_head_stride, p.src_row_stride = 128 * 128, 128
+    for k_, v_ in kw.items():
+        setattr(p, k_, v_)
+    return p, ptrs
+
+
+@pytest.mark.parametrize("field,value,needle", [
+    ("head_dim", 80, "head_dim"),
+    ("dtype", 3, "dtype"),
+    ("num_layers", 0, "num_layers"),
+    ("num_layers", 129, "num_layers"),
+    ("num_tokens", 0, "num_tokens"),
+    ("num_chunk_blocks", 7, "ceil(num_tokens / 16)"),
+    ("num_pool_blocks", 60, "outside the pool"),
+    ("src_row_stride", 0, "src_row_stride"),
+])
+def test_quantize_store_validation(lib, field, value, needle):
+    p, keep = _qstore(**{field: value})
+    assert lib.kvb_quantize_store(ctypes.byref(p), None) == _lib.KVB_ERR_INVALID
+    assert needle in lib.kvb_last_error().decode()
+
+
+def test_quantize_store_rejects_repeated_blocks(lib):
+    p, keep = _qstore()
+    p.block_ids[3] = p.block_ids[0]
+    assert lib.kvb_quantize_store(ctypes.byref(p), None) == _lib.KVB_ERR_INVALID
+    assert b"repeat" in lib.kvb_last_error()
+
+
+def _blend(**kw):
+    import ctypes as C
+    p = _lib.KvbCacheBlendParams()
+    p.dtype, p.head_dim, p.num_layers, p.num_kv_heads = 0, 128, 2, 2
+    p.num_tokens, p.num_select, p.min_deviation, p.patch = 256, 38, 0.01, 1
+    ptrs = _lib.pointer_array([4096, 8192])
+    for f in ("cached_k", "cached_v", "fresh_k", "fresh_v"):
+        setattr(p, f, C.cast(ptrs, _lib._pp))
+    p.cached_head_stride, p.cached_row_stride = 256 * 128, 128
+    p.fresh_head_stride, p.fresh_row_stride = 256 * 128, 128
+    p.deviation = p.selected = p.num_selected = 4096
+    for k_, v_ in kw.items():
+        setattr(p, k_, v_)
+    return p, ptrs
+
+
+@pytest.mark.parametrize("field,value,needle", [
+    ("head_dim", 48, "head_dim"),
+    ("num_select", 0, "num_select"),
+    ("patch", 2, "patch"),
+    ("cached_row_stride", 100, "multiples of 8"),
+    ("fresh_row_stride", 0, "non-zero"),
+    ("cached_v", None, "cached_v"),
+    ("deviation", None, "deviation"),
+])
+def test_cacheblend_validation(lib, field, value, needle):
+    p, keep = _blend(**{field: value})
+    assert lib.kvb_cacheblend_fwd(ctypes.byref(p), None) == _lib.KVB_ERR_INVALID
+    assert needle in lib.kvb_last_error().decode()
+
+
+def test_cacheblend_rejects_unaligned_pointers(lib):
+    import ctypes as C
+    bad = _lib.pointer_array([4096 + 2, 8192])
+    p, keep = _blend()
+    p.fresh_k = C.cast(bad, _lib._pp)
+    assert lib.kvb_cacheblend_fwd(ctypes.byref(p), None) == _lib.KVB_ERR_INVALID
+    assert b"16-byte aligned" in lib.kvb_last_error()

@@ -78,3 +78,20 @@ def test_oversized_chunk_rejected():
     z = torch.zeros(1, 1, 128, 2)
     assert store.store(DeviceChunk("x", [0] * 128, 0, 128, z, z)) is False
     assert len(store) == 0
+
+
+def test_pool_chunks_evicted_release_their_blocks():
+    """Chunks held in the int8 block pool count their pool bytes and hand their
+    blocks back (through ``on_evict``) when LRU eviction or ``clear`` drops them."""
+    freed = []
+    store = DeviceChunkStore(3 * 1000, on_evict=lambda c: freed.extend(c.block_ids))
+    for i in range(4):
+        ids = [i] * 128
+        ok = store.make_room(1000)
+        assert ok
+        assert store.store(DeviceChunk(chained_hash(ids), ids, 0, 128, None, None,
+                                       block_ids=[8 * i + j for j in range(8)], pool_bytes=1000))
+    assert store.bytes == 3000 and freed == list(range(8))
+    assert store.make_room(4000) is False
+    store.clear()
+    assert sorted(freed) == list(range(32)) and store.bytes == 0

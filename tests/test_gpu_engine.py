@@ -108,3 +108,88 @@ def test_store_reuses_generated_prompt_chunks():
     r2 = fast.generate(prompt, max_new_tokens=4)
     assert r2.cached_tokens == 456
     assert fast.stats()["chunks"] == 4
+
+
+def test_cacheblend_strategy_patches_oracle_positions():
+    """recompute_strategy="cacheblend": the assembled prefix after repair equals the
+    oracle's patch of the stitched chunks with the full-context K/V at the
+    positions the oracle's rule picks from the kernel's deviations; greedy tokens
+    equal the same engine on SDPA."""
+    import numpy as np
+    from oracle import cacheblend as ocb
+    fast, slow = _pair("cacheblend")
+    pre, (prompt,) = _prompts(4)
+    for eng in (fast, slow):
+        eng.warm(pre)
+    seen = {}
+    orig = fast.cacheblend_recompute.repair
+
+    def spy(ck, cv, fk, fv):
+        seen["before"] = (ck.float().cpu().numpy().copy(), cv.float().cpu().numpy().copy())
+        seen["fresh"] = (torch.stack([t[0] for t in fk]).float().cpu().numpy(),
+                         torch.stack([t[0] for t in fv]).float().cpu().numpy())
+        out = orig(ck, cv, fk, fv)
+        seen["after"] = (ck.float().cpu().numpy(), cv.float().cpu().numpy())
+        seen["dev"] = out[0].cpu().numpy()
+        seen["n"] = int(out[2].item())
+        return out
+    fast.cacheblend_recompute.repair = spy
+    r_fast = fast.generate(prompt, max_new_tokens=12)
+    r_slow = slow.generate(prompt, max_new_tokens=12)
+    (ck, cv), (fk, fv) = seen["before"], seen["fresh"]
+    S = ck.shape[2]
+    assert S == 384
+    assert np.abs(seen["dev"] - ocb.deviation(ck, fk)).max() <= 1e-5
+    sel = ocb.select(seen["dev"], ocb.num_select(S, 0.15), 0.01)
+    assert seen["n"] == len(sel) == 57
+    pk, pv = ocb.patch(ck, cv, fk, fv, sel)
+    assert np.array_equal(seen["after"][0], pk) and np.array_equal(seen["after"][1], pv)
+    assert r_fast.generated_ids == r_slow.generated_ids
+
+
+def test_int8_store_quantises_on_device_and_generates():
+    """kv_cache_bits=8: each warmed chunk's pool blocks hold the oracle's KIVI int8 of
+    the chunk K/V the model produced (bf16 arithmetic), the assembled prefix is their
+    dequantisation (q * scale rounded once to bf16), and generation over it matches
+    the 16-bit engine given that same prefix."""
+    import numpy as np
+    from kvboost_b200.engine import KVBoost, chained_hash
+    from oracle import kv_quant as oq
+    m = _model()
+    eng8 = KVBoost(m, None, recompute_strategy="none", kv_cache_bits=8, int8_pool_blocks=256)
+    eng16 = KVBoost(copy.deepcopy(m), None, recompute_strategy="none")
+    pre, (prompt,) = _prompts(6)
+    assert eng8.warm(pre).chunks_stored == 3
+    assert eng8.pool.used_blocks == 24
+    parent, want_k, want_v = None, [], []
+    for c in range(3):
+        ids = pre[c * 128:(c + 1) * 128]
+        key = chained_hash(ids, parent)
+        blocks = torch.tensor(eng8.store.get(key).block_ids, device="cuda")
+        k, v = eng8._encode_to_kv(ids, c * 128)          # the encoder output that was stored
+        wk, wv = [], []
+        for layer in range(k.shape[0]):
+            kq, ks, vq, vs = oq.quantize_int8_model_dtype(k[layer].float().cpu().numpy(),
+                                                          v[layer].float().cpu().numpy(), "bf16")
+            pool = eng8.pool.pools[layer][blocks].cpu()
+            H, D = kq.shape[0], kq.shape[2]
+            assert np.array_equal(pool[:, 0].permute(1, 0, 2, 3).reshape(H, 128, D).numpy(), kq)
+            assert np.array_equal(pool[:, 1].permute(1, 0, 2, 3).reshape(H, 128, D).numpy(), vq)
+            wk.append(oq.round_to_bf16(kq.astype(np.float32) * ks.astype(np.float32)))
+            wv.append(oq.round_to_bf16(vq.astype(np.float32) * vs.astype(np.float32)))
+        want_k.append(np.stack(wk))
+        want_v.append(np.stack(wv))
+        parent = key
+    keys, values, cached_len, _ = eng8._assemble(prompt)
+    assert cached_len == 384
+    assert np.array_equal(keys.float().cpu().numpy(), np.concatenate(want_k, axis=2))
+    assert np.array_equal(values.float().cpu().numpy(), np.concatenate(want_v, axis=2))
+    eng16.warm(pre)
+    for c in eng16.store._chunks.values():           # the same prefix in the 16-bit store
+        i = c.position_start
+        c.keys = keys[:, :, i:i + 128].contiguous()
+        c.values = values[:, :, i:i + 128].contiguous()
+    assert eng8.generate(prompt, max_new_tokens=10).generated_ids == \
+        eng16.generate(prompt, max_new_tokens=10).generated_ids
+    eng8.reset_cache()
+    assert eng8.pool.used_blocks == 0

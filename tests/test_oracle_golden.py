@@ -162,3 +162,54 @@ def test_flop_count_config2():
     # 4 * 128 * 32 * 4 * (256*896 + 256*257/2) = 17.19 GFLOP
     f = oattn.attention_flops([256] * 4, [1152] * 4, 32, 128)
     assert f == 4 * 128 * 32 * 4 * (256 * 896 + 256 * 257 // 2)
+
+
+@pytest.mark.parametrize("i", range(5))
+def test_int8_quant_model_dtype_bit_exact(golden_dir, i):
+    """Quantise-on-store arithmetic in the model's dtype (bf16, f16) == the reference."""
+    d = _load(golden_dir, "kv_quant_model_dtypes.npz")
+    p = f"b{i}/"
+    code = int(d[p + "dtype"])
+    name = "bf16" if code == 1 else "f16"
+    key, val = _vals(d[p + "key"], code), _vals(d[p + "val"], code)
+    key_q, key_scale, val_q, val_scale = oq.quantize_int8_model_dtype(key, val, name)
+    assert np.array_equal(key_q, d[p + "key_q"])
+    assert np.array_equal(val_q, d[p + "val_q"])
+    assert np.array_equal(key_scale.view(np.uint16), d[p + "key_scale"])
+    assert np.array_equal(val_scale.view(np.uint16), d[p + "val_scale"])
+    kd = oq.dequantize_int8(key_q, key_scale)
+    vd = oq.dequantize_int8(val_q, val_scale)
+    assert np.array_equal(kd.view(np.uint16), d[p + "key_deq"])
+    assert np.array_equal(vd.view(np.uint16), d[p + "val_deq"])
+
+
+def test_quant_scale_division_single_rounding():
+    """For every finite non-negative 16-bit value a, round(a / 127) == round(a * (1/127))
+    in float32 and the oracle's rounding matches torch's CPU kernel (the one the
+    reference runs)."""
+    import torch
+    for dt, name, top in ((torch.bfloat16, "bf16", 0x7F80), (torch.float16, "f16", 0x7C00)):
+        a = torch.arange(0, top, dtype=torch.int32).to(torch.int16).view(dt)
+        want = (a / 127.0).float().numpy()
+        af = a.float().numpy()
+        got = oq._round_to(af / np.float32(127.0), name)
+        assert np.array_equal(got, want)
+        assert np.array_equal(oq._round_to(af * (np.float32(1) / np.float32(127)), name), want)
+
+
+CB_CASES = ["spread_f32", "none_above_f32", "few_above_f32", "gapped_bf16", "zero_row_f32"]
+
+
+@pytest.mark.parametrize("case", CB_CASES)
+def test_cacheblend_selection_matches_reference(golden_dir, case):
+    from oracle import cacheblend as ocb
+    d = _load(golden_dir, "cacheblend.npz")
+    p = case + "/"
+    L, H, S, D, is_bf16 = d[p + "meta"].tolist()
+    code = 1 if is_bf16 else 0
+    ck, fk = _vals(d[p + "cached_k"], code), _vals(d[p + "fresh_k"], code)
+    assert ck.shape == (L, H, S, D)
+    dev = ocb.deviation(ck, fk)
+    k = ocb.num_select(S, float(d[p + "ratio"]))
+    got = ocb.select(dev, k, float(d[p + "min_dev"]))
+    assert got == d[p + "patched_positions"].tolist()
