@@ -592,7 +592,7 @@ class CacheBlendRepair:
         cv = torch.randn(self.L, self.H, self.S, self.D, generator=g, device=dev).to(torch.bfloat16)
         mags = torch.rand(self.S, generator=g, device=dev).view(1, self.S, 1, 1)
         raw = [(ck[l].transpose(0, 1)[None] + mags * torch.randn(1, self.S, self.H, self.D,
-               generator=g, device=dev)).to(torch.bfloat16) for l in range(self.L)]
+               generator=g, device=dev)).to(torch.bfloat16).contiguous() for l in range(self.L)]
         fk = [r.transpose(1, 2) for r in raw]
         fv = [torch.randn(1, self.S, self.H, self.D, generator=g, device=dev).to(torch.bfloat16)
               .transpose(1, 2) for _ in range(self.L)]

@@ -77,7 +77,10 @@ def cacheblend_fwd(cached_k: LayerKV, cached_v: Optional[LayerKV], fresh_k: Laye
     for t in fk + fv:
         if t.shape != fk[0].shape or t.dtype != dt or t.device != dev:
             raise ValueError("fresh K/V layers must share shape, dtype and device")
-    c_hs, c_rs = _strides(ck + cv, "cached K/V")
+    c_hs, c_rs = _strides(ck + cv, "cached K/V")     # patched in place: must share a layout
+    if any(t.stride() != fk[0].stride() or t.stride(2) != 1 for t in fk + fv):
+        fk = [t.contiguous() for t in fk]             # read only: bring to one layout
+        fv = [t.contiguous() for t in fv]
     f_hs, f_rs = _strides(fk + fv, "fresh K/V")
     k = num_select(S, recompute_ratio)
     deviation = torch.empty(S, dtype=torch.float32, device=dev)

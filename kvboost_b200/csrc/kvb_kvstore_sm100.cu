@@ -89,10 +89,9 @@ struct QStoreArgs {
   int32_t L, H, S, nblk;
 };
 
-constexpr int kQThreads = 256;
-constexpr int kQRowsPerCta = kQThreads / 32;   // K: one warp per (layer, head, token) row
-constexpr int kQColBlock = 32;                 // V: columns per CTA (16 column pairs)
-constexpr int kQPhases = kQThreads / (kQColBlock / 2);   // token phases per V CTA
+constexpr int kQThreads = 1024;
+constexpr int kQWarps = kQThreads / 32;
+constexpr int kQRowsInFlight = 4;   // K rows a warp loads before reducing any of them
 
 __device__ __forceinline__ float2 load_pair(const void* p, bool bf16) {
   const uint32_t u = *static_cast<const uint32_t*>(p);
@@ -102,110 +101,114 @@ __device__ __forceinline__ float2 load_pair(const void* p, bool bf16) {
   return __half22float2(h);
 }
 
-// One launch per chunk, all layers.  CTAs [0, n_k): K rows, one warp per
-// (layer, head, slot) row of the chunk's blocks -- amax over head_dim by
-// shuffles, one scale per token, slots past the chunk's end zeroed.  CTAs
-// [n_k, n_k + n_v): V, one CTA per (layer, head, 32-column block): amax of
-// each column over the chunk's tokens (16 token phases x 16 column pairs,
-// reduced in shared memory), then the quantised rows.  Loads are 4-byte
-// column pairs, coalesced along the row; each thread keeps several rows in
-// flight.
+template <typename T>
+__device__ __forceinline__ uint16_t kivi_q2(float2 x, float sx, float sy) {
+  return static_cast<uint16_t>(static_cast<uint8_t>(kivi_q<T>(x.x, sx)) |
+                               (static_cast<uint32_t>(static_cast<uint8_t>(kivi_q<T>(x.y, sy))) << 8));
+}
+
+// One launch per chunk, all layers: grid (K|V, kv head, layer), one CTA of 1024
+// threads each -- one wave for a 36-layer x 2-head chunk, every CTA's loads in
+// flight at once.  K CTA: each warp takes rows w, w + 32, ... (kQRowsInFlight at a
+// time, loads first), amax over head_dim by shuffles, one scale per token, slots
+// of the last block past the chunk's end zeroed.  V CTA: thread = (column pair,
+// token phase); each column's amax over the chunk's tokens is reduced over the
+// phases in shared memory, then the CTA quantises the rows (re-read from L1).
+// Loads are 4-byte column pairs, coalesced along the row.
 template <typename T, int D>
 __global__ void __launch_bounds__(kQThreads) kvb_quantize_store_kernel(const __grid_constant__ QStoreArgs a) {
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  const int H = a.H, S = a.S, slots = a.nblk * 16;
-  const int n_k = (a.L * H * slots + kQRowsPerCta - 1) / kQRowsPerCta;
-  const int lane = threadIdx.x & 31;
-  if (static_cast<int>(blockIdx.x) < n_k) {
-    const int row = blockIdx.x * kQRowsPerCta + (threadIdx.x >> 5);
-    if (row >= a.L * H * slots) return;
-    const int t = row % slots, h = (row / slots) % H, layer = row / (slots * H);
-    const int blk = a.block_ids[t >> 4], slot = t & 15;
-    int8_t* dst = a.pool[layer] + ((static_cast<int64_t>(blk) * 2 + 0) * H + h) * 16 * D + slot * D;
-    constexpr int kPairs = D / 2, kIters = (kPairs + 31) / 32;
-    float scale = 0.0f;
-    if (t < S) {
-      const T* src = static_cast<const T*>(a.src_k[layer]) + h * a.src_head_stride + t * a.src_row_stride;
-      float2 x[kIters];
-      float amax = 0.0f;
+  constexpr int kPairs = D / 2;
+  const int h = blockIdx.y, layer = blockIdx.z, H = a.H, S = a.S, slots = a.nblk * 16;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int8_t* pool = a.pool[layer];
+  if (blockIdx.x == 0) {
+    constexpr int kIters = (kPairs + 31) / 32;
+    const T* src = static_cast<const T*>(a.src_k[layer]) + h * a.src_head_stride;
+    __half* ks16 = a.ks16[layer];
+    float* ks32 = a.ks32[layer];
+    for (int t0 = warp; t0 < slots; t0 += kQWarps * kQRowsInFlight) {
+      float2 x[kQRowsInFlight][kIters];
 #pragma unroll
-      for (int j = 0; j < kIters; ++j) {
-        const int pr = lane + 32 * j;
-        x[j] = pr < kPairs ? load_pair(src + 2 * pr, kBf16) : make_float2(0.0f, 0.0f);
-        amax = fmaxf(amax, fmaxf(fabsf(x[j].x), fabsf(x[j].y)));
-      }
+      for (int r = 0; r < kQRowsInFlight; ++r) {
+        const int t = t0 + r * kQWarps;
 #pragma unroll
-      for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      scale = kivi_scale<T>(amax);
-#pragma unroll
-      for (int j = 0; j < kIters; ++j) {
-        const int pr = lane + 32 * j;
-        if (pr < kPairs) {
-          const uint32_t lo = static_cast<uint8_t>(kivi_q<T>(x[j].x, scale));
-          const uint32_t hi = static_cast<uint8_t>(kivi_q<T>(x[j].y, scale));
-          *reinterpret_cast<uint16_t*>(dst + 2 * pr) = static_cast<uint16_t>(lo | (hi << 8));
+        for (int j = 0; j < kIters; ++j) {
+          const int pr = lane + 32 * j;
+          x[r][j] = (t < S && pr < kPairs) ? load_pair(src + t * a.src_row_stride + 2 * pr, kBf16)
+                                           : make_float2(0.0f, 0.0f);
         }
       }
-    } else {
 #pragma unroll
-      for (int j = 0; j < kIters; ++j)
-        if (lane + 32 * j < kPairs) *reinterpret_cast<uint16_t*>(dst + 2 * (lane + 32 * j)) = 0;
-    }
-    if (lane == 0) {
-      const __half s16 = __float2half_rn(scale);
-      const int64_t si = (static_cast<int64_t>(blk) * H + h) * 16 + slot;
-      if (a.ks16[layer]) a.ks16[layer][si] = s16;
-      if (a.ks32[layer]) a.ks32[layer][si] = __half2float(s16);
+      for (int r = 0; r < kQRowsInFlight; ++r) {
+        const int t = t0 + r * kQWarps;
+        if (t >= slots) break;
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kIters; ++j) amax = fmaxf(amax, fmaxf(fabsf(x[r][j].x), fabsf(x[r][j].y)));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const bool live = t < S;
+        const float scale = live ? kivi_scale<T>(amax) : 0.0f;
+        const int blk = a.block_ids[t >> 4], slot = t & 15;
+        int8_t* dst = pool + ((static_cast<int64_t>(blk) * 2 + 0) * H + h) * 16 * D + slot * D;
+#pragma unroll
+        for (int j = 0; j < kIters; ++j) {
+          const int pr = lane + 32 * j;
+          if (pr < kPairs)
+            *reinterpret_cast<uint16_t*>(dst + 2 * pr) = live ? kivi_q2<T>(x[r][j], scale, scale) : uint16_t(0);
+        }
+        if (lane == 0) {
+          const __half s16 = __float2half_rn(scale);
+          const int64_t si = (static_cast<int64_t>(blk) * H + h) * 16 + slot;
+          if (ks16) ks16[si] = s16;
+          if (ks32) ks32[si] = __half2float(s16);
+        }
+      }
     }
     return;
   }
   // ---- V ----
-  __shared__ float part[kQPhases][kQColBlock];
-  constexpr int kColBlocks = D / kQColBlock;
-  const int v = blockIdx.x - n_k;
-  const int cb = v % kColBlocks, h = (v / kColBlocks) % H, layer = v / (kColBlocks * H);
-  const int pr = threadIdx.x % (kQColBlock / 2), phase = threadIdx.x / (kQColBlock / 2);
-  const int col = cb * kQColBlock + 2 * pr;
+  constexpr int kPhases = kQThreads / kPairs;   // 32 (D 64), 21 (D 96), 16 (D 128)
+  __shared__ float part[kPhases][D];
+  const int pr = threadIdx.x % kPairs, phase = threadIdx.x / kPairs;
+  const bool active = phase < kPhases;
+  const int col = 2 * pr;
   const T* src = static_cast<const T*>(a.src_v[layer]) + h * a.src_head_stride + col;
-  float ax = 0.0f, ay = 0.0f;
+  if (active) {
+    float ax = 0.0f, ay = 0.0f;
 #pragma unroll 8
-  for (int t = phase; t < S; t += kQPhases) {
-    const float2 x = load_pair(src + t * a.src_row_stride, kBf16);
-    ax = fmaxf(ax, fabsf(x.x));
-    ay = fmaxf(ay, fabsf(x.y));
+    for (int t = phase; t < S; t += kPhases) {
+      const float2 x = load_pair(src + t * a.src_row_stride, kBf16);
+      ax = fmaxf(ax, fabsf(x.x));
+      ay = fmaxf(ay, fabsf(x.y));
+    }
+    part[phase][col] = ax;
+    part[phase][col + 1] = ay;
   }
-  part[phase][2 * pr] = ax;
-  part[phase][2 * pr + 1] = ay;
   __syncthreads();
-  ax = ay = 0.0f;
+  if (!active) return;
+  float ax = 0.0f, ay = 0.0f;
 #pragma unroll
-  for (int ph = 0; ph < kQPhases; ++ph) {
-    ax = fmaxf(ax, part[ph][2 * pr]);
-    ay = fmaxf(ay, part[ph][2 * pr + 1]);
+  for (int ph = 0; ph < kPhases; ++ph) {
+    ax = fmaxf(ax, part[ph][col]);
+    ay = fmaxf(ay, part[ph][col + 1]);
   }
   const float sx = kivi_scale<T>(ax), sy = kivi_scale<T>(ay);
-  int8_t* pool = a.pool[layer];
 #pragma unroll 4
-  for (int t = phase; t < slots; t += kQPhases) {
-    uint16_t w = 0;
-    if (t < S) {
-      const float2 x = load_pair(src + t * a.src_row_stride, kBf16);
-      w = static_cast<uint16_t>(static_cast<uint8_t>(kivi_q<T>(x.x, sx)) |
-                                (static_cast<uint32_t>(static_cast<uint8_t>(kivi_q<T>(x.y, sy))) << 8));
-    }
+  for (int t = phase; t < slots; t += kPhases) {
+    const uint16_t w = t < S ? kivi_q2<T>(load_pair(src + t * a.src_row_stride, kBf16), sx, sy) : uint16_t(0);
     const int blk = a.block_ids[t >> 4], slot = t & 15;
     *reinterpret_cast<uint16_t*>(pool + ((static_cast<int64_t>(blk) * 2 + 1) * H + h) * 16 * D + slot * D + col) = w;
   }
-  if (phase == 0) {
-    const __half2 s16 = __halves2half2(__float2half_rn(sx), __float2half_rn(sy));
-    const float2 s32 = __half22float2(s16);
-    __half* vs16 = a.vs16[layer];
-    float* vs32 = a.vs32[layer];
-    for (int b = 0; b < a.nblk; ++b) {
-      const int64_t si = (static_cast<int64_t>(a.block_ids[b]) * H + h) * D + col;
-      if (vs16) *reinterpret_cast<__half2*>(vs16 + si) = s16;
-      if (vs32) *reinterpret_cast<float2*>(vs32 + si) = s32;
-    }
+  const __half2 s16 = __halves2half2(__float2half_rn(sx), __float2half_rn(sy));
+  const float2 s32 = __half22float2(s16);
+  __half* vs16 = a.vs16[layer];
+  float* vs32 = a.vs32[layer];
+  for (int b = phase; b < a.nblk; b += kPhases) {
+    const int64_t si = (static_cast<int64_t>(a.block_ids[b]) * H + h) * D + col;
+    if (vs16) *reinterpret_cast<__half2*>(vs16 + si) = s16;
+    if (vs32) *reinterpret_cast<float2*>(vs32 + si) = s32;
   }
 }
 
@@ -335,24 +338,59 @@ __global__ void __launch_bounds__(kSelThreads) kvb_blend_select_kernel(const flo
   }
 
   uint32_t prefix = 0, mask = 0, remaining = kk;
+  const int lane = tid & 31;
   for (int shift = 24; shift >= 0; shift -= 8) {
     if (tid < 256) hist[tid] = 0;
     __syncthreads();
-    for (int i = tid; i < S; i += kSelThreads) {
-      const float x = dev[i];
-      const uint32_t key = order_key(x);
-      if (x > min_dev && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    for (int i0 = 0; i0 < S; i0 += kSelThreads) {
+      const int i = i0 + tid;
+      bool in = false;
+      uint32_t bin = 0;
+      if (i < S) {
+        const float x = dev[i];
+        const uint32_t key = order_key(x);
+        in = x > min_dev && (key & mask) == prefix;
+        bin = (key >> shift) & 255u;
+      }
+      // one shared atomic per distinct bin in the warp (deviations cluster in few bins)
+      const uint32_t active = __ballot_sync(0xffffffffu, in);
+      if (in) {
+        const uint32_t peers = __match_any_sync(active, bin);
+        if (lane == __ffs(peers) - 1) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+      }
     }
     __syncthreads();
-    if (tid == 0) {
-      uint32_t rem = remaining;
-      int b = 255;
-      for (; b > 0; --b) {
-        if (hist[b] >= rem) break;
-        rem -= hist[b];
+    if (tid < 32) {
+      // lane l owns bins 255 - 8l .. 248 - 8l; find the bin holding the remaining-th
+      // largest by a suffix scan over lanes from the top bin down
+      uint32_t c[8], sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[255 - 8 * lane - j];
+        sum += c[j];
       }
-      s_prefix = prefix | (static_cast<uint32_t>(b) << shift);
-      s_remaining = rem;
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const uint32_t hit = __ballot_sync(0xffffffffu, incl >= remaining);
+      const int owner = hit ? __ffs(hit) - 1 : 31;
+      if (lane == owner) {
+        uint32_t rem = remaining - (incl - sum);
+        int b = 255 - 8 * lane;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (c[j] >= rem || j == 7) {
+            b = 255 - 8 * lane - j;
+            break;
+          }
+          rem -= c[j];
+        }
+        s_prefix = prefix | (static_cast<uint32_t>(b) << shift);
+        s_remaining = rem;
+      }
     }
     __syncthreads();
     prefix = s_prefix;
@@ -385,7 +423,7 @@ __global__ void __launch_bounds__(kSelThreads) kvb_blend_select_kernel(const flo
   if (tid == 0) *num_selected = static_cast<int32_t>(kk);
 }
 
-constexpr int kPatchSlots = 4;   // chosen positions per CTA
+constexpr int kPatchSlots = 16;  // chosen positions per CTA
 constexpr int kPatchThreads = 256;
 
 // Grid (chosen-position groups, layer): 16-byte copies of the fresh K and V
@@ -417,10 +455,7 @@ bool head_dim_ok(int d) { return d == 64 || d == 96 || d == 128; }
 
 template <typename T, int D>
 cudaError_t launch_qstore(const QStoreArgs& a, int L, cudaStream_t s) {
-  const int64_t rows = static_cast<int64_t>(L) * a.H * a.nblk * 16;
-  const int64_t n_k = (rows + kQRowsPerCta - 1) / kQRowsPerCta;
-  const int64_t n_v = static_cast<int64_t>(L) * a.H * (D / kQColBlock);
-  kvb_quantize_store_kernel<T, D><<<static_cast<unsigned>(n_k + n_v), kQThreads, 0, s>>>(a);
+  kvb_quantize_store_kernel<T, D><<<dim3(2, a.H, L), kQThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -225,8 +225,9 @@ class DeviceBlockAllocator:
         if n * self.block_size < S or n > _lib.KVB_MAX_CHUNK_BLOCKS:
             raise ValueError(f"{n} blocks cannot hold {S} tokens (at most "
                              f"{_lib.KVB_MAX_CHUNK_BLOCKS} blocks per chunk)")
+        pool_dev = self.pools[0].device
         for t in ks + vs:
-            if t.shape != ref.shape or t.dtype != ref.dtype or t.device != self.device:
+            if t.shape != ref.shape or t.dtype != ref.dtype or t.device != pool_dev:
                 raise ValueError("every layer's K and V must share shape, dtype and the pool's device")
         if any(t.stride() != ref.stride() or t.stride(2) != 1 for t in ks + vs):
             ks = [t.contiguous() for t in ks]
@@ -244,8 +245,8 @@ class DeviceBlockAllocator:
         (p.src_k, p.src_v, p.pool, p.k_scale16, p.v_scale16, p.k_scale, p.v_scale) = [
             ctypes.cast(a, _lib._pp) for a in arrays]
         p.src_head_stride, p.src_row_stride = ref.stride(0), ref.stride(1)
-        with torch.cuda.device(self.device):
-            _lib.check(_lib.load().kvb_quantize_store(ctypes.byref(p), _stream_handle(self.device)),
+        with torch.cuda.device(pool_dev):
+            _lib.check(_lib.load().kvb_quantize_store(ctypes.byref(p), _stream_handle(pool_dev)),
                        "kvb_quantize_store")
 
     def write_chunk(self, layer: int, block_ids: List[int], key: torch.Tensor,
