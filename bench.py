@@ -56,7 +56,14 @@ L2_BYTES = 126 * 1024 * 1024
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch from the committed
 # ncu captures (profiles/*.md), per workload.  varlen_d96: the 16-request capture
 # (1 029.9 MB) scaled to the full launch by algorithmic bytes (3 535.4 / 1 004.1 MB).
-NCU_TRAFFIC_BYTES = {"reuse_prefill": 27322880, "varlen_d96": 3626150000}
+NCU_TRAFFIC_BYTES = {"reuse_prefill": 27322880, "varlen_d96": 3626150000,
+                     # per step: 24 launches x 4 753 920 read (pool writes held in L2)
+                     "quantize_store": 24 * 4753920,
+                     # per step: deviation 113 267 968 + 3 780 096, select 47 616,
+                     # patch 16 965 632 + 14 080 (read + write)
+                     "cacheblend": 134075392,
+                     # split-key kernel, 33 647 616 read (the merged partials stay in L2)
+                     "decode": 33647616}
 
 
 def parse():

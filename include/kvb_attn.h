@@ -142,12 +142,18 @@ int kvb_prefill_fwd(const KvbPrefillParams* params, void* stream);
  * q_len > 1 each head's rows must be contiguous in q and o (head stride =
  * q_len * row stride).  The query heads sharing a KV head are packed as the
  * rows of one tile, so every key tile is read once per group, and the key
- * range is split over num_splits CTAs whose partial outputs are merged by
- * their LSE in a second pass.  workspace: device memory of at least
+ * range is split over num_splits CTAs; the last CTA of each (sequence, KV
+ * head) group to finish merges the group's partial outputs by their LSE (one
+ * launch).  workspace: device memory of at least
  * kvb_decode_workspace_bytes(params, num_splits) bytes (-1: invalid params,
- * reason in kvb_last_error).  No counterpart in the reference, whose decode
- * steps run the same SDPA call as its prefill.
+ * reason in kvb_last_error), 16-byte aligned.  Its first
+ * KVB_DECODE_COUNTER_BYTES hold the groups' completion counters: zero them
+ * once before the first call; every call leaves them zero again (so one
+ * workspace serves calls of any shape, in order on one stream).  Needs
+ * batch * num_kv_heads <= KVB_DECODE_COUNTER_BYTES / 4.  No counterpart in the
+ * reference, whose decode steps run the same SDPA call as its prefill.
  */
+#define KVB_DECODE_COUNTER_BYTES (64 * 1024)
 int64_t kvb_decode_workspace_bytes(const KvbPrefillParams* params, int num_splits);
 int kvb_decode_fwd(const KvbPrefillParams* params, int num_splits, void* workspace,
                    int64_t workspace_bytes, void* stream);

@@ -65,14 +65,40 @@ __device__ __forceinline__ float kivi_scale(float amax) {
   return Num<T>::round(__fdiv_rn(m, 127.0f));
 }
 
-// q = clamp(rint(round(x / scale)), -128, 127); NaN (0 / 0 on an all-zero
-// float16 row) becomes 0, as the reference's float-to-int8 cast gives on its CPU.
+// q = clamp(rint(round(x / scale)), -128, 127) for scale > 0 (x finite): the
+// reference's kv_quantize.py:86 / :91 with torch's rounding of the quotient to the
+// tensor's dtype.  Fast path: y = x * (1 / scale) is within 3 float32 ulps of the
+// correctly rounded quotient (two roundings of 2^-24 each against one), i.e.
+// within 6 ulps of y's own binade, and q is a non-decreasing function of the
+// quotient; so when q is the same at |y| -/+ 8 ulps it is q of the quotient.
+// Otherwise (|y| within 8 ulps of a rounding boundary) the quotient is computed
+// exactly.  |y| < 0.25 gives 0 outright (the quotient is below 0.26).
 template <typename T>
-__device__ __forceinline__ int8_t kivi_q(float x, float scale) {
-  const float r = Num<T>::round(__fdiv_rn(x, scale));
-  if (isnan(r)) return 0;
-  const float q = fminf(fmaxf(rintf(r), -128.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(q));
+__device__ __forceinline__ int kivi_qmag(float v) {
+  return __float2int_rn(Num<T>::round(v));   // rint of round-to-T, half to even
+}
+
+template <typename T>
+__device__ __forceinline__ int kivi_q_pos(float x, float scale, float rcp) {
+  const float y = x * rcp;
+  const float a = fabsf(y);
+  int m = 0;
+  if (a >= 0.25f) {
+    const uint32_t u = __float_as_uint(a);
+    m = kivi_qmag<T>(__uint_as_float(u - 8u));
+    if (m != kivi_qmag<T>(__uint_as_float(u + 8u))) m = kivi_qmag<T>(fabsf(__fdiv_rn(x, scale)));
+  }
+  return y < 0.0f ? max(-m, -128) : min(m, 127);
+}
+
+// scale == 0 (an all-zero float16 row, or amax so small that amax / 127 rounds to
+// 0 in float16): x / 0 is +-inf -> 127 / -128, and 0 / 0 is NaN, which the
+// reference's float-to-int8 cast turns into 0 on its CPU.
+__device__ __forceinline__ int kivi_q_zero_scale(float x) { return x > 0.0f ? 127 : (x < 0.0f ? -128 : 0); }
+
+template <typename T>
+__device__ __forceinline__ int kivi_q(float x, float scale, float rcp) {
+  return scale > 0.0f ? kivi_q_pos<T>(x, scale, rcp) : kivi_q_zero_scale(x);
 }
 
 // ---- quantise-on-store ----------------------------------------------------------------
@@ -91,124 +117,149 @@ struct QStoreArgs {
 
 constexpr int kQThreads = 1024;
 constexpr int kQWarps = kQThreads / 32;
-constexpr int kQRowsInFlight = 4;   // K rows a warp loads before reducing any of them
+constexpr int kQLanesPerRow = 8;                 // K: 8 lanes per token row, 4 rows per warp
+constexpr int kQRowsPerWarp = 32 / kQLanesPerRow;
 
-__device__ __forceinline__ float2 load_pair(const void* p, bool bf16) {
-  const uint32_t u = *static_cast<const uint32_t*>(p);
-  if (bf16) return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
-  __half2 h;
-  memcpy(&h, &u, 4);
-  return __half22float2(h);
+template <bool kBf16>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f;
+    if (kBf16) {
+      f = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+    } else {
+      __half2 h;
+      memcpy(&h, &w[i], 4);
+      f = __half22float2(h);
+    }
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
 }
 
-template <typename T>
-__device__ __forceinline__ uint16_t kivi_q2(float2 x, float sx, float sy) {
-  return static_cast<uint16_t>(static_cast<uint8_t>(kivi_q<T>(x.x, sx)) |
-                               (static_cast<uint32_t>(static_cast<uint8_t>(kivi_q<T>(x.y, sy))) << 8));
+// 8 int8 values packed little-endian into two words.
+__device__ __forceinline__ uint2 pack8(const int (&q)[8]) {
+  uint2 r;
+  r.x = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+  r.y = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
+  return r;
 }
 
 // One launch per chunk, all layers: grid (K|V, kv head, layer), one CTA of 1024
-// threads each -- one wave for a 36-layer x 2-head chunk, every CTA's loads in
-// flight at once.  K CTA: each warp takes rows w, w + 32, ... (kQRowsInFlight at a
-// time, loads first), amax over head_dim by shuffles, one scale per token, slots
-// of the last block past the chunk's end zeroed.  V CTA: thread = (column pair,
-// token phase); each column's amax over the chunk's tokens is reduced over the
-// phases in shared memory, then the CTA quantises the rows (re-read from L1).
-// Loads are 4-byte column pairs, coalesced along the row.
+// threads each (one wave for a 36-layer x 2-head chunk).  Sources are read in
+// 16-byte pieces (8 elements), every CTA's loads in flight at once.
+//  K CTA: a token row per 8 lanes, 4 rows per warp: amax over head_dim (3 shuffle
+//    steps), one scale per token, 8 int8 written per lane per piece; slots of the
+//    last block past the chunk's end zeroed.
+//  V CTA: thread = (8-column group, token phase); column amax partials go to
+//    shared memory, one thread per column reduces them and computes the column's
+//    scale and reciprocal once, then every thread quantises its tokens' pieces.
 template <typename T, int D>
 __global__ void __launch_bounds__(kQThreads) kvb_quantize_store_kernel(const __grid_constant__ QStoreArgs a) {
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr int kPairs = D / 2;
+  constexpr int VPR = D / 8;                                   // 16-byte pieces per row
+  constexpr int kPieces = (VPR + kQLanesPerRow - 1) / kQLanesPerRow;
   const int h = blockIdx.y, layer = blockIdx.z, H = a.H, S = a.S, slots = a.nblk * 16;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int8_t* pool = a.pool[layer];
   if (blockIdx.x == 0) {
-    constexpr int kIters = (kPairs + 31) / 32;
     const T* src = static_cast<const T*>(a.src_k[layer]) + h * a.src_head_stride;
     __half* ks16 = a.ks16[layer];
     float* ks32 = a.ks32[layer];
-    for (int t0 = warp; t0 < slots; t0 += kQWarps * kQRowsInFlight) {
-      float2 x[kQRowsInFlight][kIters];
+    const int sub = lane & (kQLanesPerRow - 1);
+    for (int t = warp * kQRowsPerWarp + (lane >> 3); t - (lane >> 3) < slots; t += kQWarps * kQRowsPerWarp) {
+      const bool live = t < S;
+      float x[kPieces][8];
+      float amax = 0.0f;
 #pragma unroll
-      for (int r = 0; r < kQRowsInFlight; ++r) {
-        const int t = t0 + r * kQWarps;
+      for (int c = 0; c < kPieces; ++c) {
+        const int piece = sub + kQLanesPerRow * c;
+        uint4 u = make_uint4(0, 0, 0, 0);
+        if (live && piece < VPR) u = *reinterpret_cast<const uint4*>(src + t * a.src_row_stride + 8 * piece);
+        unpack8<kBf16>(u, x[c]);
 #pragma unroll
-        for (int j = 0; j < kIters; ++j) {
-          const int pr = lane + 32 * j;
-          x[r][j] = (t < S && pr < kPairs) ? load_pair(src + t * a.src_row_stride + 2 * pr, kBf16)
-                                           : make_float2(0.0f, 0.0f);
-        }
+        for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(x[c][e]));
       }
 #pragma unroll
-      for (int r = 0; r < kQRowsInFlight; ++r) {
-        const int t = t0 + r * kQWarps;
-        if (t >= slots) break;
-        float amax = 0.0f;
+      for (int o = 1; o < kQLanesPerRow; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (t >= slots) continue;
+      const float scale = live ? kivi_scale<T>(amax) : 0.0f;
+      const float rcp = __frcp_rn(scale);
+      const int blk = a.block_ids[t >> 4], slot = t & 15;
+      int8_t* dst = pool + ((static_cast<int64_t>(blk) * 2 + 0) * H + h) * 16 * D + slot * D;
 #pragma unroll
-        for (int j = 0; j < kIters; ++j) amax = fmaxf(amax, fmaxf(fabsf(x[r][j].x), fabsf(x[r][j].y)));
+      for (int c = 0; c < kPieces; ++c) {
+        const int piece = sub + kQLanesPerRow * c;
+        if (piece < VPR) {
+          int q[8];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const bool live = t < S;
-        const float scale = live ? kivi_scale<T>(amax) : 0.0f;
-        const int blk = a.block_ids[t >> 4], slot = t & 15;
-        int8_t* dst = pool + ((static_cast<int64_t>(blk) * 2 + 0) * H + h) * 16 * D + slot * D;
-#pragma unroll
-        for (int j = 0; j < kIters; ++j) {
-          const int pr = lane + 32 * j;
-          if (pr < kPairs)
-            *reinterpret_cast<uint16_t*>(dst + 2 * pr) = live ? kivi_q2<T>(x[r][j], scale, scale) : uint16_t(0);
+          for (int e = 0; e < 8; ++e) q[e] = live ? kivi_q<T>(x[c][e], scale, rcp) : 0;
+          *reinterpret_cast<uint2*>(dst + 8 * piece) = pack8(q);
         }
-        if (lane == 0) {
-          const __half s16 = __float2half_rn(scale);
-          const int64_t si = (static_cast<int64_t>(blk) * H + h) * 16 + slot;
-          if (ks16) ks16[si] = s16;
-          if (ks32) ks32[si] = __half2float(s16);
-        }
+      }
+      if (sub == 0) {
+        const __half s16 = __float2half_rn(scale);
+        const int64_t si = (static_cast<int64_t>(blk) * H + h) * 16 + slot;
+        if (ks16) ks16[si] = s16;
+        if (ks32) ks32[si] = __half2float(s16);
       }
     }
     return;
   }
   // ---- V ----
-  constexpr int kPhases = kQThreads / kPairs;   // 32 (D 64), 21 (D 96), 16 (D 128)
-  __shared__ float part[kPhases][D];
-  const int pr = threadIdx.x % kPairs, phase = threadIdx.x / kPairs;
+  constexpr int kPhases = kQThreads / VPR;   // 128 (D 64), 85 (D 96), 64 (D 128)
+  __shared__ float part[kPhases][D + 1];
+  __shared__ float col_scale[D], col_rcp[D];
+  const int g = threadIdx.x % VPR, phase = threadIdx.x / VPR;
   const bool active = phase < kPhases;
-  const int col = 2 * pr;
-  const T* src = static_cast<const T*>(a.src_v[layer]) + h * a.src_head_stride + col;
+  const T* src = static_cast<const T*>(a.src_v[layer]) + h * a.src_head_stride + 8 * g;
   if (active) {
-    float ax = 0.0f, ay = 0.0f;
-#pragma unroll 8
+    float m[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int t = phase; t < S; t += kPhases) {
-      const float2 x = load_pair(src + t * a.src_row_stride, kBf16);
-      ax = fmaxf(ax, fabsf(x.x));
-      ay = fmaxf(ay, fabsf(x.y));
+      float x[8];
+      unpack8<kBf16>(*reinterpret_cast<const uint4*>(src + t * a.src_row_stride), x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m[e] = fmaxf(m[e], fabsf(x[e]));
     }
-    part[phase][col] = ax;
-    part[phase][col + 1] = ay;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part[phase][8 * g + e] = m[e];
+  }
+  __syncthreads();
+  if (threadIdx.x < D) {
+    float m = 0.0f;
+    for (int ph = 0; ph < kPhases; ++ph) m = fmaxf(m, part[ph][threadIdx.x]);
+    const float sc = kivi_scale<T>(m);
+    col_scale[threadIdx.x] = sc;
+    col_rcp[threadIdx.x] = __frcp_rn(sc);
+    const __half s16 = __float2half_rn(sc);
+    __half* vs16 = a.vs16[layer];
+    float* vs32 = a.vs32[layer];
+    for (int b = 0; b < a.nblk; ++b) {
+      const int64_t si = (static_cast<int64_t>(a.block_ids[b]) * H + h) * D + threadIdx.x;
+      if (vs16) vs16[si] = s16;
+      if (vs32) vs32[si] = __half2float(s16);
+    }
   }
   __syncthreads();
   if (!active) return;
-  float ax = 0.0f, ay = 0.0f;
+  float sc[8], rc[8];
 #pragma unroll
-  for (int ph = 0; ph < kPhases; ++ph) {
-    ax = fmaxf(ax, part[ph][col]);
-    ay = fmaxf(ay, part[ph][col + 1]);
+  for (int e = 0; e < 8; ++e) {
+    sc[e] = col_scale[8 * g + e];
+    rc[e] = col_rcp[8 * g + e];
   }
-  const float sx = kivi_scale<T>(ax), sy = kivi_scale<T>(ay);
-#pragma unroll 4
   for (int t = phase; t < slots; t += kPhases) {
-    const uint16_t w = t < S ? kivi_q2<T>(load_pair(src + t * a.src_row_stride, kBf16), sx, sy) : uint16_t(0);
+    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (t < S) {
+      float x[8];
+      unpack8<kBf16>(*reinterpret_cast<const uint4*>(src + t * a.src_row_stride), x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) q[e] = kivi_q<T>(x[e], sc[e], rc[e]);
+    }
     const int blk = a.block_ids[t >> 4], slot = t & 15;
-    *reinterpret_cast<uint16_t*>(pool + ((static_cast<int64_t>(blk) * 2 + 1) * H + h) * 16 * D + slot * D + col) = w;
-  }
-  const __half2 s16 = __halves2half2(__float2half_rn(sx), __float2half_rn(sy));
-  const float2 s32 = __half22float2(s16);
-  __half* vs16 = a.vs16[layer];
-  float* vs32 = a.vs32[layer];
-  for (int b = phase; b < a.nblk; b += kPhases) {
-    const int64_t si = (static_cast<int64_t>(a.block_ids[b]) * H + h) * D + col;
-    if (vs16) *reinterpret_cast<__half2*>(vs16 + si) = s16;
-    if (vs32) *reinterpret_cast<float2*>(vs32 + si) = s32;
+    *reinterpret_cast<uint2*>(pool + ((static_cast<int64_t>(blk) * 2 + 1) * H + h) * 16 * D + slot * D + 8 * g) =
+        pack8(q);
   }
 }
 
@@ -225,59 +276,75 @@ struct BlendArgs {
   int32_t L, H, S, k;
 };
 
-constexpr int kDevWarps = 8;   // positions per CTA in the deviation kernel
-constexpr int kLayerUnroll = 4;
+constexpr int kDevWarps = 8;        // warps per CTA; warp w takes layers w, w + 8, ...
+constexpr int kDevPositions = 8;    // positions per CTA (4 lanes each, in every warp)
+constexpr int kDevVecs = 8;         // 16-byte vectors per lane per operand in flight
 
-// One warp per cached position: for each layer, dot(c, f), |c|^2, |f|^2 over
-// the position's K vectors of every head (16-byte loads, kLayerUnroll layers in
-// flight), reduced across the warp; deviation = mean over layers of 1 - cos.
+// CTA = 8 positions x all layers.  In every warp, lanes 4p..4p+3 own position p
+// and split its per-layer K vector (all heads, 16-byte pieces); the warp walks its
+// share of the layers, reducing dot(c, f), |c|^2, |f|^2 over the 4 lanes (two
+// shuffle steps) and adding 1 - cos per layer; the 8 warps' partial sums are added
+// in warp order in shared memory (a fixed order: same inputs, same bits).
 template <typename T, int D>
 __global__ void __launch_bounds__(kDevWarps * 32) kvb_blend_deviation_kernel(const __grid_constant__ BlendArgs a) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * kDevWarps + warp;
-  if (t >= a.S) return;
+  __shared__ float part[kDevWarps][kDevPositions];
   constexpr int VPH = D / 8;   // 16-byte vectors per head row
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int p = lane >> 2, sub = lane & 3;
+  const int t = blockIdx.x * kDevPositions + p;
+  const bool valid = t < a.S;
+  const int tt = valid ? t : 0;
   const int nvec = a.H * VPH;
-  float dev_sum = 0.0f;
-  for (int l0 = 0; l0 < a.L; l0 += kLayerUnroll) {
-    float dot[kLayerUnroll], nc[kLayerUnroll], nf[kLayerUnroll];
+  float acc = 0.0f;
+  for (int l = warp; l < a.L; l += kDevWarps) {
+    const T* cb = static_cast<const T*>(a.ck[l]) + static_cast<int64_t>(tt) * a.c_rs;
+    const T* fb = static_cast<const T*>(a.fk[l]) + static_cast<int64_t>(tt) * a.f_rs;
+    float dot = 0.0f, nc = 0.0f, nf = 0.0f;
+    for (int v0 = sub; v0 < nvec; v0 += 4 * kDevVecs) {
+      uint4 cu[kDevVecs], fu[kDevVecs];
 #pragma unroll
-    for (int u = 0; u < kLayerUnroll; ++u) dot[u] = nc[u] = nf[u] = 0.0f;
-    for (int v = lane; v < nvec; v += 32) {
-      const int h = v / VPH, dv = (v - h * VPH) * 8;
+      for (int k = 0; k < kDevVecs; ++k) {
+        const int v = v0 + 4 * k;
+        if (valid && v < nvec) {
+          const int h = v / VPH, dv = (v - h * VPH) * 8;
+          cu[k] = *reinterpret_cast<const uint4*>(cb + h * a.c_hs + dv);
+          fu[k] = *reinterpret_cast<const uint4*>(fb + h * a.f_hs + dv);
+        } else {
+          cu[k] = fu[k] = make_uint4(0, 0, 0, 0);
+        }
+      }
 #pragma unroll
-      for (int u = 0; u < kLayerUnroll; ++u) {
-        if (l0 + u < a.L) {
-          const T* c = static_cast<const T*>(a.ck[l0 + u]) + h * a.c_hs + t * a.c_rs + dv;
-          const T* f = static_cast<const T*>(a.fk[l0 + u]) + h * a.f_hs + t * a.f_rs + dv;
-          const uint4 cu = *reinterpret_cast<const uint4*>(c);
-          const uint4 fu = *reinterpret_cast<const uint4*>(f);
-          const uint32_t cw[4] = {cu.x, cu.y, cu.z, cu.w}, fw[4] = {fu.x, fu.y, fu.z, fu.w};
+      for (int k = 0; k < kDevVecs; ++k) {
+        const uint32_t cw[4] = {cu[k].x, cu[k].y, cu[k].z, cu[k].w};
+        const uint32_t fw[4] = {fu[k].x, fu[k].y, fu[k].z, fu[k].w};
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const float2 x = Num<T>::pair(cw[w]), y = Num<T>::pair(fw[w]);
-            dot[u] = fmaf(x.x, y.x, fmaf(x.y, y.y, dot[u]));
-            nc[u] = fmaf(x.x, x.x, fmaf(x.y, x.y, nc[u]));
-            nf[u] = fmaf(y.x, y.x, fmaf(y.y, y.y, nf[u]));
-          }
+        for (int w = 0; w < 4; ++w) {
+          const float2 x = Num<T>::pair(cw[w]), y = Num<T>::pair(fw[w]);
+          dot = fmaf(x.x, y.x, fmaf(x.y, y.y, dot));
+          nc = fmaf(x.x, x.x, fmaf(x.y, x.y, nc));
+          nf = fmaf(y.x, y.x, fmaf(y.y, y.y, nf));
         }
       }
     }
 #pragma unroll
-    for (int u = 0; u < kLayerUnroll; ++u) {
+    for (int o = 1; o < 4; o <<= 1) {
+      dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      nc += __shfl_xor_sync(0xffffffffu, nc, o);
+      nf += __shfl_xor_sync(0xffffffffu, nf, o);
+    }
+    acc += 1.0f - dot / (fmaxf(sqrtf(nc), 1e-8f) * fmaxf(sqrtf(nf), 1e-8f));
+  }
+  if (sub == 0) part[warp][p] = acc;
+  __syncthreads();
+  if (threadIdx.x < kDevPositions) {
+    const int tp = blockIdx.x * kDevPositions + threadIdx.x;
+    if (tp < a.S) {
+      float sum = 0.0f;
 #pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], o);
-        nc[u] += __shfl_xor_sync(0xffffffffu, nc[u], o);
-        nf[u] += __shfl_xor_sync(0xffffffffu, nf[u], o);
-      }
-      if (l0 + u < a.L) {
-        const float cosv = dot[u] / (fmaxf(sqrtf(nc[u]), 1e-8f) * fmaxf(sqrtf(nf[u]), 1e-8f));
-        dev_sum += 1.0f - cosv;
-      }
+      for (int w = 0; w < kDevWarps; ++w) sum += part[w][threadIdx.x];
+      a.deviation[tp] = sum / static_cast<float>(a.L);
     }
   }
-  if (lane == 0) a.deviation[t] = dev_sum / static_cast<float>(a.L);
 }
 
 // Total order on float bit patterns (larger float -> larger key).
@@ -287,6 +354,9 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 }
 
 constexpr int kSelThreads = 1024;
+constexpr int kSelBits = 11;                  // radix digit: passes of 11, 11 and 10 bits
+constexpr int kSelBins = 1 << kSelBits;
+constexpr int kSelCache = 8192;               // deviations kept in shared memory up to this many
 
 // Exclusive prefix sum over the CTA; *total gets the CTA's sum.
 __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_tot, uint32_t* total) {
@@ -315,19 +385,30 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* w
   return excl;
 }
 
-// One CTA: count the candidates (deviation > min_deviation), find the key of the
-// kk-th largest candidate by a 4 x 8-bit radix select, then emit, in position
-// order, every candidate above that key and the first `remaining` equal to it.
-__global__ void __launch_bounds__(kSelThreads) kvb_blend_select_kernel(const float* __restrict__ dev, int S, int k,
+// One CTA.  Candidates are positions with deviation > min_dev; the key of the
+// kk-th largest candidate (kk = min(k, #candidates)) is found by a radix select
+// over the float's order-preserving bit pattern (3 digit passes, shared
+// histogram with warp-aggregated atomics, the bin found by one warp's suffix scan).
+// Then each thread takes a contiguous run of positions: every candidate above that
+// key, and the first `remaining` equal to it in position order (two CTA scans give
+// each run its offsets), written ascending.
+__global__ void __launch_bounds__(kSelThreads) kvb_blend_select_kernel(const float* __restrict__ dev_g, int S, int k,
                                                                         float min_dev, int32_t* selected,
                                                                         int32_t* num_selected) {
-  __shared__ uint32_t hist[256];
+  __shared__ uint32_t hist[kSelBins];
   __shared__ uint32_t warp_tot[32];
   __shared__ uint32_t s_prefix, s_remaining;
-  const int tid = threadIdx.x;
+  extern __shared__ float dev_cache[];   // S floats when S <= kSelCache, else unused
+  const int tid = threadIdx.x, lane = tid & 31;
+  const bool cached = S <= kSelCache;
+  const float* dev = cached ? dev_cache : dev_g;
 
   uint32_t cnt = 0;
-  for (int i = tid; i < S; i += kSelThreads) cnt += dev[i] > min_dev ? 1u : 0u;
+  for (int i = tid; i < S; i += kSelThreads) {
+    const float x = dev_g[i];
+    if (cached) dev_cache[i] = x;
+    cnt += x > min_dev ? 1u : 0u;
+  }
   uint32_t total;
   block_exclusive_scan(cnt, warp_tot, &total);
   const uint32_t kk = min(static_cast<uint32_t>(k), total);
@@ -338,9 +419,11 @@ __global__ void __launch_bounds__(kSelThreads) kvb_blend_select_kernel(const flo
   }
 
   uint32_t prefix = 0, mask = 0, remaining = kk;
-  const int lane = tid & 31;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    if (tid < 256) hist[tid] = 0;
+#pragma unroll 1
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+    const uint32_t dmask = pass == 2 ? 1023u : 2047u;
+    for (int b = tid; b < kSelBins; b += kSelThreads) hist[b] = 0;
     __syncthreads();
     for (int i0 = 0; i0 < S; i0 += kSelThreads) {
       const int i = i0 + tid;
@@ -350,9 +433,8 @@ __global__ void __launch_bounds__(kSelThreads) kvb_blend_select_kernel(const flo
         const float x = dev[i];
         const uint32_t key = order_key(x);
         in = x > min_dev && (key & mask) == prefix;
-        bin = (key >> shift) & 255u;
+        bin = (key >> shift) & dmask;
       }
-      // one shared atomic per distinct bin in the warp (deviations cluster in few bins)
       const uint32_t active = __ballot_sync(0xffffffffu, in);
       if (in) {
         const uint32_t peers = __match_any_sync(active, bin);
@@ -360,91 +442,100 @@ __global__ void __launch_bounds__(kSelThreads) kvb_blend_select_kernel(const flo
       }
     }
     __syncthreads();
-    if (tid < 32) {
-      // lane l owns bins 255 - 8l .. 248 - 8l; find the bin holding the remaining-th
-      // largest by a suffix scan over lanes from the top bin down
-      uint32_t c[8], sum = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = hist[255 - 8 * lane - j];
-        sum += c[j];
-      }
-      uint32_t incl = sum;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const uint32_t hit = __ballot_sync(0xffffffffu, incl >= remaining);
-      const int owner = hit ? __ffs(hit) - 1 : 31;
-      if (lane == owner) {
-        uint32_t rem = remaining - (incl - sum);
-        int b = 255 - 8 * lane;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (c[j] >= rem || j == 7) {
-            b = 255 - 8 * lane - j;
-            break;
-          }
-          rem -= c[j];
-        }
-        s_prefix = prefix | (static_cast<uint32_t>(b) << shift);
-        s_remaining = rem;
+    {
+      // thread t owns bins dmask - 2t and dmask - 2t - 1 (descending); a CTA scan of
+      // the owned counts finds the bin holding the remaining-th largest
+      const int b0 = static_cast<int>(dmask) - 2 * tid;
+      const uint32_t c0 = b0 >= 0 ? hist[b0] : 0u, c1 = b0 >= 1 ? hist[b0 - 1] : 0u;
+      uint32_t tot;
+      const uint32_t before = block_exclusive_scan(c0 + c1, warp_tot, &tot);
+      if (before < remaining && before + c0 + c1 >= remaining) {
+        const uint32_t rem = remaining - before;
+        const bool first = c0 >= rem;
+        s_prefix = prefix | (static_cast<uint32_t>(first ? b0 : b0 - 1) << shift);
+        s_remaining = first ? rem : rem - c0;
       }
     }
     __syncthreads();
     prefix = s_prefix;
     remaining = s_remaining;
-    mask |= 255u << shift;
+    mask |= dmask << shift;
   }
   const uint32_t kth = prefix;   // key of the kk-th largest; `remaining` of its equals are taken
 
-  uint32_t base_sel = 0, base_eq = 0;
-  for (int start = 0; start < S; start += kSelThreads) {
-    const int i = start + tid;
-    bool gt = false, eq = false;
-    if (i < S) {
-      const float x = dev[i];
+  const int per = (S + kSelThreads - 1) / kSelThreads;
+  const int lo = min(tid * per, S), hi = min(lo + per, S);
+  uint32_t gt = 0, eq = 0;
+  for (int i = lo; i < hi; ++i) {
+    const float x = dev[i];
+    if (x > min_dev) {
       const uint32_t key = order_key(x);
-      const bool cand = x > min_dev;
-      gt = cand && key > kth;
-      eq = cand && key == kth;
+      gt += key > kth ? 1u : 0u;
+      eq += key == kth ? 1u : 0u;
     }
-    uint32_t eq_total, sel_total;
-    const uint32_t eq_excl = block_exclusive_scan(eq ? 1u : 0u, warp_tot, &eq_total);
-    const bool take = gt || (eq && base_eq + eq_excl < remaining);
-    const uint32_t sel_excl = block_exclusive_scan(take ? 1u : 0u, warp_tot, &sel_total);
-    const uint32_t out = base_sel + sel_excl;
-    if (take && out < kk) selected[out] = i;
-    base_sel += sel_total;
-    base_eq += eq_total;
+  }
+  uint32_t eq_total, sel_total;
+  const uint32_t eq_before = block_exclusive_scan(eq, warp_tot, &eq_total);
+  const uint32_t take_eq = eq_before >= remaining ? 0u : min(eq, remaining - eq_before);
+  uint32_t out = block_exclusive_scan(gt + take_eq, warp_tot, &sel_total);
+  uint32_t eq_left = take_eq;
+  for (int i = lo; i < hi; ++i) {
+    const float x = dev[i];
+    if (!(x > min_dev)) continue;
+    const uint32_t key = order_key(x);
+    bool take = key > kth;
+    if (key == kth && eq_left > 0) {
+      take = true;
+      --eq_left;
+    }
+    if (take && out < kk) selected[out++] = i;
   }
   for (int j = static_cast<int>(kk) + tid; j < k; j += kSelThreads) selected[j] = -1;
   if (tid == 0) *num_selected = static_cast<int32_t>(kk);
 }
 
-constexpr int kPatchSlots = 16;  // chosen positions per CTA
+constexpr int kPatchSlots = 32;  // chosen positions per CTA (4 per warp)
 constexpr int kPatchThreads = 256;
 
-// Grid (chosen-position groups, layer): 16-byte copies of the fresh K and V
-// rows of every head over the cached ones; groups past *num_selected exit.
+// Grid (chosen-position groups, layer); warp w copies chosen positions 4w .. 4w + 3
+// of its group: for each, the fresh K and V rows of every head over the cached
+// ones in 16-byte pieces (all loads before the stores).  Groups past
+// *num_selected exit.
 template <typename T, int D>
 __global__ void __launch_bounds__(kPatchThreads) kvb_blend_patch_kernel(const __grid_constant__ BlendArgs a) {
-  const int n = *a.num_selected;
-  const int layer = blockIdx.y;
-  if (static_cast<int>(blockIdx.x) * kPatchSlots >= n) return;
   constexpr int VPH = D / 8;
-  const int per_kv = a.H * VPH, per_slot = 2 * per_kv;
-  for (int idx = threadIdx.x; idx < kPatchSlots * per_slot; idx += kPatchThreads) {
-    const int j = blockIdx.x * kPatchSlots + idx / per_slot;
-    if (j >= n) break;
-    const int r = idx % per_slot;
-    const int kv = r / per_kv, hv = r - kv * per_kv;
-    const int h = hv / VPH, dv = (hv - h * VPH) * 8;
-    const int t = a.selected[j];
-    const T* src = static_cast<const T*>(kv ? a.fv[layer] : a.fk[layer]) + h * a.f_hs + t * a.f_rs + dv;
-    T* dst = static_cast<T*>(kv ? a.cv[layer] : a.ck[layer]) + h * a.c_hs + t * a.c_rs + dv;
-    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  constexpr int kPerWarp = kPatchSlots / (kPatchThreads / 32);
+  const int n = *a.num_selected;
+  const int layer = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j0 = blockIdx.x * kPatchSlots + warp * kPerWarp;
+  if (j0 >= n) return;
+  const T* fk = static_cast<const T*>(a.fk[layer]);
+  const T* fv = static_cast<const T*>(a.fv[layer]);
+  T* ck = static_cast<T*>(a.ck[layer]);
+  T* cv = static_cast<T*>(a.cv[layer]);
+  int t[kPerWarp];
+#pragma unroll
+  for (int s = 0; s < kPerWarp; ++s) t[s] = j0 + s < n ? a.selected[j0 + s] : -1;
+  const int nvec = a.H * VPH;
+  for (int e = lane; e < nvec; e += 32) {
+    const int h = e / VPH, dv = (e - h * VPH) * 8;
+    uint4 kx[kPerWarp], vx[kPerWarp];
+#pragma unroll
+    for (int s = 0; s < kPerWarp; ++s) {
+      if (t[s] >= 0) {
+        const int64_t so = h * a.f_hs + static_cast<int64_t>(t[s]) * a.f_rs + dv;
+        kx[s] = *reinterpret_cast<const uint4*>(fk + so);
+        vx[s] = *reinterpret_cast<const uint4*>(fv + so);
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < kPerWarp; ++s) {
+      if (t[s] >= 0) {
+        const int64_t d = h * a.c_hs + static_cast<int64_t>(t[s]) * a.c_rs + dv;
+        *reinterpret_cast<uint4*>(ck + d) = kx[s];
+        *reinterpret_cast<uint4*>(cv + d) = vx[s];
+      }
+    }
   }
 }
 
@@ -470,10 +561,12 @@ cudaError_t launch_qstore_d(const QStoreArgs& a, int L, int D, cudaStream_t s) {
 
 template <typename T, int D>
 cudaError_t launch_blend(const BlendArgs& a, float min_dev, bool patch, cudaStream_t s) {
-  kvb_blend_deviation_kernel<T, D><<<(a.S + kDevWarps - 1) / kDevWarps, kDevWarps * 32, 0, s>>>(a);
+  kvb_blend_deviation_kernel<T, D><<<(a.S + kDevPositions - 1) / kDevPositions, kDevWarps * 32, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  kvb_blend_select_kernel<<<1, kSelThreads, 0, s>>>(a.deviation, a.S, a.k, min_dev, a.selected, a.num_selected);
+  const size_t cache_bytes = a.S <= kSelCache ? static_cast<size_t>(a.S) * sizeof(float) : 0;
+  kvb_blend_select_kernel<<<1, kSelThreads, cache_bytes, s>>>(a.deviation, a.S, a.k, min_dev, a.selected,
+                                                              a.num_selected);
   e = cudaGetLastError();
   if (e != cudaSuccess || !patch) return e;
   kvb_blend_patch_kernel<T, D><<<dim3((a.k + kPatchSlots - 1) / kPatchSlots, a.L), kPatchThreads, 0, s>>>(a);
@@ -508,8 +601,8 @@ extern "C" int kvb_quantize_store(const KvbQuantizeStoreParams* p, void* stream)
   if (p->num_chunk_blocks < need || p->num_chunk_blocks > KVB_MAX_CHUNK_BLOCKS)
     return fail(KVB_ERR_INVALID, "num_chunk_blocks must be in [ceil(num_tokens / 16) = " + std::to_string(need) +
                                      ", " + std::to_string(KVB_MAX_CHUNK_BLOCKS) + "]");
-  if (p->src_row_stride < 1 || p->src_head_stride < 0 || (p->src_row_stride | p->src_head_stride) & 1)
-    return fail(KVB_ERR_INVALID, "src_row_stride must be >= 1, src_head_stride >= 0, both even");
+  if (p->src_row_stride < 1 || p->src_head_stride < 0 || (p->src_row_stride | p->src_head_stride) & 7)
+    return fail(KVB_ERR_INVALID, "src_row_stride must be >= 1, src_head_stride >= 0, both multiples of 8");
   if (!p->src_k || !p->src_v || !p->pool) return fail(KVB_ERR_INVALID, "src_k, src_v and pool must be non-null");
   for (int b = 0; b < p->num_chunk_blocks; ++b) {
     const int id = p->block_ids[b];
@@ -523,8 +616,8 @@ extern "C" int kvb_quantize_store(const KvbQuantizeStoreParams* p, void* stream)
   for (int l = 0; l < p->num_layers; ++l) {
     if (!p->src_k[l] || !p->src_v[l] || !p->pool[l])
       return fail(KVB_ERR_INVALID, "layer " + std::to_string(l) + ": src_k, src_v and pool pointers must be non-null");
-    if ((reinterpret_cast<uintptr_t>(p->src_k[l]) | reinterpret_cast<uintptr_t>(p->src_v[l])) & 3u)
-      return fail(KVB_ERR_INVALID, "layer " + std::to_string(l) + ": source pointers must be 4-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(p->src_k[l]) | reinterpret_cast<uintptr_t>(p->src_v[l])) & 15u)
+      return fail(KVB_ERR_INVALID, "layer " + std::to_string(l) + ": source pointers must be 16-byte aligned");
     a.src_k[l] = p->src_k[l];
     a.src_v[l] = p->src_v[l];
     a.pool[l] = static_cast<int8_t*>(p->pool[l]);

@@ -160,14 +160,25 @@ struct DenseArgs {
 
 // Reused-prefix K/V in the int8 paged pool plus the suffix's own fresh K/V.
 struct PagedArgs {
-  const int8_t* pool;     // [num_blocks, 2, num_kv_heads, 16, D] int8 (K then V)
-  const float* k_scale;   // [num_blocks, num_kv_heads, 16]  per-token K scale
-  const float* v_scale;   // [num_blocks, num_kv_heads, D]   per-channel V scale of the block's chunk
-  const int* block_table; // [batch, max_blocks]
-  const int* prefix_lens; // [batch] cached tokens, or null -> prefix_len
-  const void* k_new;      // suffix K (compute dtype), element (b, h, i, d) at
-  const void* v_new;      //   b*bs + h*hs + i*rs + d
-  int64_t kn_bs, kn_hs, kn_rs, vn_bs, vn_hs, vn_rs;
+  union {
+    struct {                  // paged kernels
+      const int8_t* pool;     // [num_blocks, 2, num_kv_heads, 16, D] int8 (K then V)
+      const float* k_scale;   // [num_blocks, num_kv_heads, 16]  per-token K scale
+      const float* v_scale;   // [num_blocks, num_kv_heads, D]   per-channel V scale of the block's chunk
+      const int* block_table; // [batch, max_blocks]
+      const int* prefix_lens; // [batch] cached tokens, or null -> prefix_len
+      const void* k_new;      // suffix K (compute dtype), element (b, h, i, d) at
+      const void* v_new;      //   b*bs + h*hs + i*rs + d
+      int64_t kn_bs, kn_hs, kn_rs, vn_bs, vn_hs, vn_rs;
+    };
+    struct {                  // split-key decode: the LSE merge done by each group's last CTA
+      int* split_count;       // [batch][num_kv_heads] CTAs of the group done (left 0)
+      void* o_final;          // final O, element (b, head, i, d) at b*bs + head*hs + i*rs + d
+      float* lse_final;       // final LSE (b, head, i) at b*bs + head*hs + i, or null
+      int64_t of_bs, of_hs, of_rs, lf_bs, lf_hs;
+      int group_heads;        // query heads per KV head
+    };
+  };
   int max_blocks;
   int num_blocks;
   int num_kv_heads;
@@ -187,6 +198,7 @@ struct PagedArgs {
 struct SharedCtl {
   uint32_t tmem_base;
   int abort_flag;
+  int last_cta;   // split-key decode: this CTA merges its group's splits
 };
 
 // Bounded wait: spins on try_wait, then checks the CTA abort flag and the
@@ -627,71 +639,58 @@ __global__ void __launch_bounds__(256)
   reinterpret_cast<uint4*>(dst)[1] = w1;
 }
 
-// Merge the per-split partial results of a split-key decode: for every query
-// row, O = sum_s exp(lse_s - L) O_s and L = log sum_s exp(lse_s).  Partials are
-// packed per KV head as rows r = head_in_group * rows_per_head + i
-// ([splits][batch][num_kv_heads][packed_rows][D], normalised, compute dtype;
-// LSE fp32 [splits][batch][num_kv_heads][packed_rows]).  One thread per 8
-// consecutive features of one row.
-struct CombineArgs {
-  const void* o_part;
-  const float* lse_part;
-  int splits;
-  int64_t o_split_stride, lse_split_stride;
-  int batch, num_kv_heads, group, rows_per_head;
-  void* o;
-  float* lse;
-  int64_t o_bs, o_hs, o_rs, lse_bs, lse_hs;
-};
-
+// Merge the per-split partial results of one (sequence, KV head) group of a
+// split-key decode: for each packed query row, O = sum_s exp(lse_s - L) O_s and
+// L = log sum_s exp(lse_s).  Partials are packed as rows
+// r = head_in_group * rows_per_head + i ([splits][batch][num_kv_heads][packed][D],
+// normalised, compute dtype; LSE fp32 [splits][batch][num_kv_heads][packed]) and
+// read through L2 (they were written by other CTAs).  Threads stride over
+// (row, 8-feature chunk) items.
 template <typename T, int D>
-__global__ void __launch_bounds__(256) kvb_split_combine_kernel(CombineArgs c) {
+__device__ __forceinline__ void merge_splits(const DenseArgs& a, const PagedArgs& pa, int b, int g,
+                                             int splits) {
   constexpr int NCH = D / 8;
-  const int packed = c.group * c.rows_per_head;
-  const int64_t rows = (int64_t)c.batch * c.num_kv_heads * packed;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= rows * NCH) return;
-  const int64_t row = idx / NCH;          // (b, g, r) packed
-  const int ch = (int)(idx - row * NCH);
-  const int r = (int)(row % packed);
-  const int64_t bg = row / packed;
-  const int g = (int)(bg % c.num_kv_heads);
-  const int b = (int)(bg / c.num_kv_heads);
-  float mx = -INFINITY;
-  for (int sp = 0; sp < c.splits; ++sp) mx = fmaxf(mx, c.lse_part[sp * c.lse_split_stride + row]);
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  float wsum = 0.f;
-  if (mx > -INFINITY) {
-    for (int sp = 0; sp < c.splits; ++sp) {
-      const float w = __expf(c.lse_part[sp * c.lse_split_stride + row] - mx);
-      wsum += w;
-      const uint4 v = *reinterpret_cast<const uint4*>(
-          reinterpret_cast<const T*>(c.o_part) + sp * c.o_split_stride + row * D + ch * 8);
-      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+  const int packed = a.q_len;
+  const int64_t grow = ((int64_t)b * pa.num_kv_heads + g) * packed;   // first packed row of the group
+  const T* o_part = reinterpret_cast<const T*>(a.o);
+  for (int idx = threadIdx.x; idx < packed * NCH; idx += blockDim.x) {
+    const int r = idx / NCH, ch = idx - r * NCH;
+    const int64_t row = grow + r;
+    float mx = -INFINITY;
+    for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, __ldcg(a.lse + sp * pa.lse_split_stride + row));
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float wsum = 0.f;
+    if (mx > -INFINITY) {
+      for (int sp = 0; sp < splits; ++sp) {
+        const float w = __expf(__ldcg(a.lse + sp * pa.lse_split_stride + row) - mx);
+        wsum += w;
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(o_part + sp * pa.o_split_stride + row * D + ch * 8));
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float2 f;
-        if constexpr (std::is_same<T, __half>::value)
-          f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
-        else
-          f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
-        acc[2 * e] += w * f.x;
-        acc[2 * e + 1] += w * f.y;
+        for (int e = 0; e < 4; ++e) {
+          float2 f;
+          if constexpr (std::is_same<T, __half>::value)
+            f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
+          else
+            f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
+          acc[2 * e] += w * f.x;
+          acc[2 * e + 1] += w * f.y;
+        }
       }
     }
-  }
-  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-  uint32_t o[4];
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    uint32_t o[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) o[e] = pack2<T>(acc[2 * e] * inv, acc[2 * e + 1] * inv);
-  const int head = g * c.group + r / c.rows_per_head;
-  const int i = r % c.rows_per_head;
-  T* dst = reinterpret_cast<T*>(c.o) + (int64_t)b * c.o_bs + (int64_t)head * c.o_hs +
-           (int64_t)i * c.o_rs + ch * 8;
-  *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
-  if (c.lse != nullptr && ch == 0)
-    c.lse[(int64_t)b * c.lse_bs + (int64_t)head * c.lse_hs + i] =
-        wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+    for (int e = 0; e < 4; ++e) o[e] = pack2<T>(acc[2 * e] * inv, acc[2 * e + 1] * inv);
+    const int head = g * pa.group_heads + r / pa.rows_per_head;
+    const int i = r % pa.rows_per_head;
+    T* dst = reinterpret_cast<T*>(pa.o_final) + (int64_t)b * pa.of_bs + (int64_t)head * pa.of_hs +
+             (int64_t)i * pa.of_rs + ch * 8;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+    if (pa.lse_final != nullptr && ch == 0)
+      pa.lse_final[(int64_t)b * pa.lf_bs + (int64_t)head * pa.lf_hs + i] =
+          wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+  }
 }
 
 template <typename T, int D, bool PAGED, bool SPLITKV = false>
@@ -1165,6 +1164,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     }
   }
 
+  if (SPLITKV) __threadfence();   // this CTA's partial O / LSE, before it is counted below
   ptx::tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) KVB_TRACE_AT(3);
@@ -1172,6 +1172,19 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     __syncwarp();
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, G::TMEM_COLS);
+  }
+  if constexpr (SPLITKV) {
+    // The group's last CTA to finish merges all splits' partials and resets the
+    // count.  Every CTA reaches this point exactly once (waits are bounded), so
+    // the count always completes and is left at 0 for the next launch.
+    int* count = pa.split_count + (int64_t)b * pa.num_kv_heads + blockIdx.y;
+    if (threadIdx.x == 0) ctl->last_cta = atomicAdd(count, 1) == (int)gridDim.x - 1;
+    __syncthreads();
+    if (ctl->last_cta) {
+      __threadfence();
+      merge_splits<T, D>(a, pa, b, blockIdx.y, gridDim.x);
+      if (threadIdx.x == 0) *count = 0;
+    }
   }
 }
 
@@ -1299,10 +1312,11 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
 }
 
 // Split-key decode: the workspace holds the partials, then the combine pass.
+// Layout: [KVB_DECODE_COUNTER_BYTES of per-group counters][partial O][partial LSE].
 static int64_t decode_workspace_bytes(const KvbPrefillParams& p, int splits) {
   const int64_t rows = (int64_t)p.batch * p.num_q_heads * p.q_len;
   const int64_t o_bytes = (int64_t)splits * rows * p.head_dim * 2;
-  return (o_bytes + 255) / 256 * 256 + (int64_t)splits * rows * 4;
+  return KVB_DECODE_COUNTER_BYTES + (o_bytes + 255) / 256 * 256 + (int64_t)splits * rows * 4;
 }
 
 static int decode_split_tiles(const KvbPrefillParams& p, int splits, int* eff) {
@@ -1330,9 +1344,10 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
                 p.v_row_stride, p.v_head_stride, p.batch > 1 ? p.v_batch_stride : 8, &err))
     return fail(KVB_ERR_INVALID, err);
   const int64_t rows = (int64_t)p.batch * p.num_kv_heads * packed;
-  T* o_part = reinterpret_cast<T*>(ws);
+  int* counters = reinterpret_cast<int*>(ws);
+  T* o_part = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(ws) + KVB_DECODE_COUNTER_BYTES);
   const int64_t o_bytes = (int64_t)splits * rows * D * 2;
-  float* lse_part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) +
+  float* lse_part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(o_part) +
                                              (o_bytes + 255) / 256 * 256);
   DenseArgs a = {};
   a.o = o_part;
@@ -1354,6 +1369,16 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
   sp.split_tiles = split_tiles;
   sp.o_split_stride = rows * D;
   sp.lse_split_stride = rows;
+  sp.num_kv_heads = p.num_kv_heads;
+  sp.split_count = counters;
+  sp.o_final = p.o;
+  sp.lse_final = p.lse;
+  sp.of_bs = p.o_batch_stride;
+  sp.of_hs = p.o_head_stride;
+  sp.of_rs = p.o_row_stride;
+  sp.lf_bs = p.lse_batch_stride;
+  sp.lf_hs = p.lse_head_stride;
+  sp.group_heads = group;
   auto kern = kvb_prefill_kernel<T, D, false, true>;
   static thread_local int configured_device = -1;
   int dev = 0;
@@ -1369,28 +1394,6 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
       tq, tk, tv, a, sp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(KVB_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
-  CombineArgs c = {};
-  c.o_part = o_part;
-  c.lse_part = lse_part;
-  c.splits = splits;
-  c.o_split_stride = rows * D;
-  c.lse_split_stride = rows;
-  c.batch = p.batch;
-  c.num_kv_heads = p.num_kv_heads;
-  c.group = group;
-  c.rows_per_head = p.q_len;
-  c.o = p.o;
-  c.lse = p.lse;
-  c.o_bs = p.o_batch_stride;
-  c.o_hs = p.o_head_stride;
-  c.o_rs = p.o_row_stride;
-  c.lse_bs = p.lse_batch_stride;
-  c.lse_hs = p.lse_head_stride;
-  const int64_t threads = rows * (D / 8);
-  kvb_split_combine_kernel<T, D><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(c);
-  e = cudaGetLastError();
-  if (e != cudaSuccess)
-    return fail(KVB_ERR_CUDA, std::string("combine launch: ") + cudaGetErrorString(e));
   return KVB_OK;
 }
 
@@ -1701,6 +1704,9 @@ static int validate_decode(const KvbPrefillParams& p, int splits) {
                                  "(head stride = q_len * row stride) in q and o");
   if (p.q_len == 1 && p.o_head_stride % 8)
     return fail(KVB_ERR_INVALID, "o head stride must be a multiple of 8 elements");
+  if ((int64_t)p.batch * p.num_kv_heads > KVB_DECODE_COUNTER_BYTES / 4)
+    return fail(KVB_ERR_UNSUPPORTED, "split decode takes batch * num_kv_heads <= " +
+                                         std::to_string(KVB_DECODE_COUNTER_BYTES / 4));
   return KVB_OK;
 }
 

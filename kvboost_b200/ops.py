@@ -253,7 +253,7 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     idx = q.device.index if q.device.index is not None else torch.cuda.current_device()
     ws = _decode_ws.get(idx)
     if ws is None or ws.numel() < need:
-        ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=q.device)
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=q.device)  # counters start at 0
         _decode_ws[idx] = ws
     with torch.cuda.device(q.device):
         rc = lib.kvb_decode_fwd(p, int(num_splits), ws.data_ptr(), ws.numel(),

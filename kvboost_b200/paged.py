@@ -229,7 +229,8 @@ class DeviceBlockAllocator:
         for t in ks + vs:
             if t.shape != ref.shape or t.dtype != ref.dtype or t.device != pool_dev:
                 raise ValueError("every layer's K and V must share shape, dtype and the pool's device")
-        if any(t.stride() != ref.stride() or t.stride(2) != 1 for t in ks + vs):
+        if any(t.stride() != ref.stride() or t.stride(2) != 1 or t.stride(0) % 8 or t.stride(1) % 8
+               or t.data_ptr() % 16 for t in ks + vs):
             ks = [t.contiguous() for t in ks]
             vs = [t.contiguous() for t in vs]
             ref = ks[0]
