@@ -57,7 +57,8 @@ L2_BYTES = 126 * 1024 * 1024
 # ncu captures (profiles/*.md), per workload.  varlen_d96: the 16-request capture
 # (1 029.9 MB) scaled to the full launch by algorithmic bytes (3 535.4 / 1 004.1 MB).
 NCU_TRAFFIC_BYTES = {"reuse_prefill": 27322880, "varlen_d96": 3626150000,
-                     # per step: 24 launches x 4 753 920 read (pool writes held in L2)
+                     # single-chunk launches: 4 753 920 read per chunk (pool writes held
+                     # in L2); the batched step is 24 chunks
                      "quantize_store": 24 * 4753920,
                      # per step: deviation 113 267 968 + 3 780 096, select 47 616,
                      # patch 16 965 632 + 14 080 (read + write)
@@ -453,7 +454,8 @@ class QuantizeStore:
     model's warm of a 3072-token prefix -- 24 chunks of 128 tokens, 36 layers, 2 KV
     heads, D 128 -- each chunk's bf16 K/V read as the model's cache holds them
     ([1, H, S, D] views of [1, S, H, D] projections), KIVI int8 + scales written into
-    its 8 blocks of the int8 pool.  One launch per chunk covers all layers."""
+    its 8 blocks of the int8 pool.  One launch stores the 24 chunks, all layers
+    (``store_chunks_int8``, as the engine's warm does)."""
 
     metric, unit, unit_scale, dtype_name = "quantize-on-store GB/s", "GB/s", 1e9, "bf16->int8"
 
@@ -463,7 +465,7 @@ class QuantizeStore:
         self.desc = ("quantise-on-store: 24 chunks x 128 tokens, 36 layers, 2 KV heads, D 128, "
                      "bf16 model-cache K/V -> KIVI int8 16-token blocks + fp16/fp32 scales")
         self.scaling, self.bound = "weak", "hbm"
-        self.launches_per_step = self.chunks
+        self.launches_per_step = 1
 
     def chunk_bytes(self):
         L, H, S, D, n = self.L, self.H, self.S, self.D, self.nblk
@@ -501,14 +503,17 @@ class QuantizeStore:
         R = max(2, math.ceil(2 * L2_BYTES / self.bytes()))
         self.alloc = DeviceBlockAllocator(self.L, self.H, self.D, R * self.chunks * self.nblk,
                                           device=dev)
-        sets = [(self._chunks(torch, dev, g),
-                 [self.alloc.allocate(self.nblk) for _ in range(self.chunks)]) for _ in range(R)]
+        sets = []
+        for _ in range(R):
+            chunks = self._chunks(torch, dev, g)
+            blocks = [self.alloc.allocate(self.nblk) for _ in range(self.chunks)]
+            sets.append(self.alloc.prepare_chunks_int8(
+                [(b, ks, vs) for (ks, vs), b in zip(chunks, blocks)]))
+        torch.cuda.synchronize()
         self.sets_desc = f"inputs rotate over {R} sets ({R * self.bytes() / 2**20:.0f} MiB > L2)"
 
         def step(i):
-            chunks, blocks = sets[i % R]
-            for (ks, vs), b in zip(chunks, blocks):
-                self.alloc.store_chunk_int8(b, ks, vs)
+            self.alloc.launch_prepared(sets[i % R])
         return step
 
     def e2e(self, torch, dev):
@@ -529,6 +534,8 @@ class QuantizeStore:
                 hp.copy_(torch.stack([p[idx] for p in self.alloc.pools]), non_blocking=True)
         h2d = self.chunks * 2 * hk.numel() * 2
         return step, h2d, self.chunks * hp.numel()
+    # (e2e: one chunk per call through the public single-chunk store, the
+    # reference's store granularity)
 
     def gpu_reference(self, torch, dev):
         """The reference's store arithmetic as torch ops on this GPU

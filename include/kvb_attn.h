@@ -63,7 +63,8 @@ enum {
   KVB_STATUS_MMA_WAIT = 2,     /* MMA issuer waited too long for operands     */
   KVB_STATUS_SOFTMAX_WAIT = 4, /* softmax warps waited too long for scores    */
   KVB_STATUS_EPILOGUE_WAIT = 8,/* epilogue waited too long for the output     */
-  KVB_STATUS_BAD_BLOCK = 16     /* a block-table entry was outside the pool    */
+  KVB_STATUS_BAD_BLOCK = 16,    /* a block-table entry was outside the pool    */
+  KVB_STATUS_BAD_LENGTH = 32    /* a chunk's token count did not fit its blocks */
 };
 
 /*
@@ -363,6 +364,39 @@ typedef struct KvbQuantizeStoreParams {
 } KvbQuantizeStoreParams;
 
 int kvb_quantize_store(const KvbQuantizeStoreParams* params, void* stream);
+
+/*
+ * The same store for several chunks in one launch (a warm of many chunks):
+ * every pointer below is DEVICE memory, so the tables are built once per call
+ * and copied with the data's stream.  Chunk c has num_tokens[c] tokens (1 ..
+ * 16 * max_chunk_blocks) in blocks block_ids[c][0 .. ceil(num_tokens[c] / 16));
+ * its layer l's K and V are src[(c * num_layers + l) * 2 + 0 / 1], 16-byte
+ * aligned, with the chunk's head and row strides src_strides[c][0 / 1]
+ * (elements, multiples of 8).  tables[k * num_layers + l] for k = 0..4: the
+ * pool, K scale fp16, V scale fp16, K scale fp32, V scale fp32 of layer l (a
+ * NULL scale table entry is not written).  The chunks' blocks must not overlap.
+ * Block ids outside [0, num_pool_blocks) are skipped and set
+ * KVB_STATUS_BAD_BLOCK; a token count out of range, a misaligned source or a
+ * stride that is not a multiple of 8 skips that chunk and sets
+ * KVB_STATUS_BAD_LENGTH, in the optional *status.
+ */
+typedef struct KvbQuantizeStoreBatch {
+  int32_t dtype;
+  int32_t head_dim;
+  int32_t num_layers;
+  int32_t num_kv_heads;
+  int32_t num_chunks;         /* num_chunks * num_layers <= 65535 */
+  int32_t max_chunk_blocks;   /* row length of block_ids, <= KVB_MAX_CHUNK_BLOCKS */
+  int64_t num_pool_blocks;
+  const int32_t* num_tokens;  /* device [num_chunks] */
+  const int32_t* block_ids;   /* device [num_chunks][max_chunk_blocks] */
+  const void* const* src;     /* device [num_chunks][num_layers][2] */
+  const int64_t* src_strides; /* device [num_chunks][2] */
+  void* const* tables;        /* device [5][num_layers] */
+  int32_t* status;
+} KvbQuantizeStoreBatch;
+
+int kvb_quantize_store_batch(const KvbQuantizeStoreBatch* params, void* stream);
 
 /* ---- CacheBlend: deviation-guided patch of stitched chunk K/V ----
  *

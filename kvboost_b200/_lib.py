@@ -22,6 +22,7 @@ KVB_ERR_UNSUPPORTED = 2
 KVB_ERR_CUDA = -1
 KVB_NOALLOC_SCRATCH_BYTES = 32 << 20
 KVB_POOL_INT8_KIVI, KVB_POOL_COMPUTE = 0, 1
+KVB_STATUS_BAD_BLOCK, KVB_STATUS_BAD_LENGTH = 16, 32
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -111,6 +112,17 @@ class KvbCacheBlendParams(ctypes.Structure):
     ]
 
 
+class KvbQuantizeStoreBatch(ctypes.Structure):
+    """Mirror of ``KvbQuantizeStoreBatch``."""
+
+    _fields_ = [
+        ("dtype", _i32), ("head_dim", _i32), ("num_layers", _i32), ("num_kv_heads", _i32),
+        ("num_chunks", _i32), ("max_chunk_blocks", _i32), ("num_pool_blocks", _i64),
+        ("num_tokens", _vp), ("block_ids", _vp), ("src", _vp), ("src_strides", _vp),
+        ("tables", _vp), ("status", _vp),
+    ]
+
+
 def pointer_array(ptrs):
     """A ctypes ``void*[n]`` of device addresses (keep it alive across the call)."""
     arr = (ctypes.c_void_p * len(ptrs))(*[int(p) if p else None for p in ptrs])
@@ -162,6 +174,8 @@ def load() -> ctypes.CDLL:
         lib.kvb_paged_prefill_workspace_bytes.restype = ctypes.c_int64
         lib.kvb_quantize_store.argtypes = [ctypes.POINTER(KvbQuantizeStoreParams), _vp]
         lib.kvb_quantize_store.restype = ctypes.c_int
+        lib.kvb_quantize_store_batch.argtypes = [ctypes.POINTER(KvbQuantizeStoreBatch), _vp]
+        lib.kvb_quantize_store_batch.restype = ctypes.c_int
         lib.kvb_cacheblend_fwd.argtypes = [ctypes.POINTER(KvbCacheBlendParams), _vp]
         lib.kvb_cacheblend_fwd.restype = ctypes.c_int
         lib.kvb_last_error.argtypes = []

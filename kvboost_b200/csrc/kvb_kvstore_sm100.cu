@@ -67,28 +67,47 @@ __device__ __forceinline__ float kivi_scale(float amax) {
 
 // q = clamp(rint(round(x / scale)), -128, 127) for scale > 0 (x finite): the
 // reference's kv_quantize.py:86 / :91 with torch's rounding of the quotient to the
-// tensor's dtype.  Fast path: y = x * (1 / scale) is within 3 float32 ulps of the
-// correctly rounded quotient (two roundings of 2^-24 each against one), i.e.
-// within 6 ulps of y's own binade, and q is a non-decreasing function of the
-// quotient; so when q is the same at |y| -/+ 8 ulps it is q of the quotient.
-// Otherwise (|y| within 8 ulps of a rounding boundary) the quotient is computed
-// exactly.  |y| < 0.25 gives 0 outright (the quotient is below 0.26).
+// tensor's dtype.  Fast path, no conversion instructions: y = x * (1 / scale) is
+// within 3 float32 ulps of the correctly rounded quotient (two roundings of 2^-24
+// each against one), i.e. within 6 ulps of y's own binade.  For |y| >= 0.25 both
+// are normal in bfloat16 and float16, where rounding float32 to T is
+// round-to-nearest-even at bit 16 (bf16) / bit 13 (fp16) of the float32 pattern;
+// when y's dropped bits are more than 8 ulps from the halfway point, the quotient
+// rounds to the same T value as y, computed here with integer operations.  rint of
+// that value (exact in float32, |value| < 2^22) is the low word of value +
+// 1.5 * 2^23.  Near a halfway point the quotient is computed exactly.  |y| < 0.25
+// gives 0 outright (the quotient is below 0.26).
 template <typename T>
-__device__ __forceinline__ int kivi_qmag(float v) {
-  return __float2int_rn(Num<T>::round(v));   // rint of round-to-T, half to even
+struct RoundBits;
+
+template <>
+struct RoundBits<__nv_bfloat16> {
+  static constexpr uint32_t kDrop = 16;
+};
+
+template <>
+struct RoundBits<__half> {
+  static constexpr uint32_t kDrop = 13;
+};
+
+__device__ __forceinline__ int rint_small(float v) {   // round half to even, |v| < 2^22
+  return __float_as_int(v + 12582912.0f) - 0x4B400000;
 }
 
 template <typename T>
 __device__ __forceinline__ int kivi_q_pos(float x, float scale, float rcp) {
+  constexpr uint32_t kDrop = RoundBits<T>::kDrop, kHalf = 1u << (kDrop - 1), kMask = (1u << kDrop) - 1;
   const float y = x * rcp;
-  const float a = fabsf(y);
-  int m = 0;
-  if (a >= 0.25f) {
-    const uint32_t u = __float_as_uint(a);
-    m = kivi_qmag<T>(__uint_as_float(u - 8u));
-    if (m != kivi_qmag<T>(__uint_as_float(u + 8u))) m = kivi_qmag<T>(fabsf(__fdiv_rn(x, scale)));
+  if (fabsf(y) < 0.25f) return 0;
+  const uint32_t u = __float_as_uint(y);
+  int q;
+  if (static_cast<uint32_t>(abs(static_cast<int>(u & kMask) - static_cast<int>(kHalf))) > 8u) {
+    const uint32_t r = (u + (kHalf - 1) + ((u >> kDrop) & 1u)) & ~kMask;   // round to T, nearest even
+    q = rint_small(__uint_as_float(r));
+  } else {
+    q = __float2int_rn(Num<T>::round(__fdiv_rn(x, scale)));
   }
-  return y < 0.0f ? max(-m, -128) : min(m, 127);
+  return min(max(q, -128), 127);
 }
 
 // scale == 0 (an all-zero float16 row, or amax so small that amax / 127 rounds to
@@ -101,6 +120,60 @@ __device__ __forceinline__ int kivi_q(float x, float scale, float rcp) {
   return scale > 0.0f ? kivi_q_pos<T>(x, scale, rcp) : kivi_q_zero_scale(x);
 }
 
+// kivi_q of 8 elements packed as 8 int8 bytes, branch-free on the fast path:
+// each element is rounded to T with integer operations, clamped to [-128, 127]
+// in float (the same as clamping after rint: T values >= 127.5 are the only ones
+// that rint above 127), and t + 1.5 * 2^23 carries rint(t) in its low byte.  If
+// any element's quotient lies within 8 ulps of a halfway point, or a scale is 0
+// (zero_scale), all 8 are redone by kivi_q (rare).  Rounding y of |y| < 0.25 with
+// the float16 rule is inexact in float16's subnormal range, but rint of it is 0
+// either way.
+// 8 int8 values packed little-endian into two words.
+__device__ __forceinline__ uint2 pack8(const int (&q)[8]) {
+  uint2 r;
+  r.x = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+  r.y = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
+  return r;
+}
+
+// The exact path for 8 elements, out of line: it runs rarely and its IEEE
+// divisions would otherwise raise the fast path's register count.
+template <typename T>
+__device__ __noinline__ uint2 kivi_q8_exact(const float4 x0, const float4 x1, const float4 s0, const float4 s1,
+                                            const float4 r0, const float4 r1) {
+  const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+  const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  const float rc[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+  int q[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) q[e] = kivi_q<T>(x[e], sc[e], rc[e]);
+  return pack8(q);
+}
+
+template <typename T>
+__device__ __forceinline__ uint2 kivi_q8(const float (&x)[8], const float (&sc)[8], const float (&rc)[8],
+                                         bool zero_scale) {
+  constexpr uint32_t kDrop = RoundBits<T>::kDrop, kHalf = 1u << (kDrop - 1), kMask = (1u << kDrop) - 1;
+  uint32_t w[8];
+  bool near = zero_scale;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint32_t u = __float_as_uint(x[e] * rc[e]);
+    const uint32_t r = (u + (kHalf - 1) + ((u >> kDrop) & 1u)) & ~kMask;
+    const float t = fminf(fmaxf(__uint_as_float(r), -128.0f), 127.0f);
+    w[e] = __float_as_uint(t + 12582912.0f);
+    near |= static_cast<uint32_t>(abs(static_cast<int>(u & kMask) - static_cast<int>(kHalf))) <= 8u;
+  }
+  if (near)
+    return kivi_q8_exact<T>(make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]),
+                            make_float4(sc[0], sc[1], sc[2], sc[3]), make_float4(sc[4], sc[5], sc[6], sc[7]),
+                            make_float4(rc[0], rc[1], rc[2], rc[3]), make_float4(rc[4], rc[5], rc[6], rc[7]));
+  uint2 p;
+  p.x = __byte_perm(__byte_perm(w[0], w[1], 0x0040), __byte_perm(w[2], w[3], 0x0040), 0x5410);
+  p.y = __byte_perm(__byte_perm(w[4], w[5], 0x0040), __byte_perm(w[6], w[7], 0x0040), 0x5410);
+  return p;
+}
+
 // ---- quantise-on-store ----------------------------------------------------------------
 struct QStoreArgs {
   const void* src_k[KVB_MAX_LAYERS];
@@ -111,14 +184,16 @@ struct QStoreArgs {
   float* ks32[KVB_MAX_LAYERS];
   float* vs32[KVB_MAX_LAYERS];
   int32_t block_ids[KVB_MAX_CHUNK_BLOCKS];
-  int64_t src_head_stride, src_row_stride;
+  int64_t src_head_stride, src_row_stride, num_pool_blocks;
   int32_t L, H, S, nblk;
 };
 
-constexpr int kQThreads = 1024;
+constexpr int kQThreads = 256;                  // several CTAs per SM overlap their chains
 constexpr int kQWarps = kQThreads / 32;
 constexpr int kQLanesPerRow = 8;                 // K: 8 lanes per token row, 4 rows per warp
 constexpr int kQRowsPerWarp = 32 / kQLanesPerRow;
+constexpr int kQRowsPerCta = kQWarps * kQRowsPerWarp;   // K: 32 token rows per CTA
+constexpr int kQVCols = 32;                      // V: 32 columns per CTA (4 pieces x 64 phases)
 
 template <bool kBf16>
 __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
@@ -138,129 +213,225 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
   }
 }
 
-// 8 int8 values packed little-endian into two words.
-__device__ __forceinline__ uint2 pack8(const int (&q)[8]) {
-  uint2 r;
-  r.x = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
-  r.y = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
-  return r;
-}
 
-// One launch per chunk, all layers: grid (K|V, kv head, layer), one CTA of 1024
-// threads each (one wave for a 36-layer x 2-head chunk).  Sources are read in
-// 16-byte pieces (8 elements), every CTA's loads in flight at once.
-//  K CTA: a token row per 8 lanes, 4 rows per warp: amax over head_dim (3 shuffle
+// One CTA of quantise-on-store: either 32 token rows of K or 32 columns of V of one
+// (KV head, layer, chunk).  Sources are read in 16-byte pieces (8 elements).
+//  K: a token row per 8 lanes, 4 rows per warp: amax over head_dim (3 shuffle
 //    steps), one scale per token, 8 int8 written per lane per piece; slots of the
 //    last block past the chunk's end zeroed.
-//  V CTA: thread = (8-column group, token phase); column amax partials go to
-//    shared memory, one thread per column reduces them and computes the column's
-//    scale and reciprocal once, then every thread quantises its tokens' pieces.
+//  V: thread = (8-column piece, token phase); column amax partials go to shared
+//    memory, one thread per column reduces them and computes the column's scale
+//    and reciprocal once, then every thread quantises its tokens' pieces.
+// Block ids outside [0, num_pool_blocks) are skipped and flagged in *status.
+struct QStoreUnit {
+  const void* src;          // this layer's K or V, element (h, t, d) at src + h*hs + t*rs + d
+  int64_t hs, rs;
+  const int32_t* block_ids; // the chunk's blocks
+  int nblk, S, H;
+  int64_t num_pool_blocks;
+  int8_t* pool;
+  __half* s16;              // K: [blocks][H][16]; V: [blocks][H][D]
+  float* s32;
+  int* status;
+};
+
+__device__ __forceinline__ bool block_ok(int blk, const QStoreUnit& u) {
+  if (blk >= 0 && blk < u.num_pool_blocks) return true;
+  if (u.status) atomicOr(u.status, KVB_STATUS_BAD_BLOCK);
+  return false;
+}
+
 template <typename T, int D>
-__global__ void __launch_bounds__(kQThreads) kvb_quantize_store_kernel(const __grid_constant__ QStoreArgs a) {
+__device__ __forceinline__ void quantize_store_k(const QStoreUnit& u, int h, int row0) {
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int VPR = D / 8;                                   // 16-byte pieces per row
   constexpr int kPieces = (VPR + kQLanesPerRow - 1) / kQLanesPerRow;
-  const int h = blockIdx.y, layer = blockIdx.z, H = a.H, S = a.S, slots = a.nblk * 16;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int8_t* pool = a.pool[layer];
-  if (blockIdx.x == 0) {
-    const T* src = static_cast<const T*>(a.src_k[layer]) + h * a.src_head_stride;
-    __half* ks16 = a.ks16[layer];
-    float* ks32 = a.ks32[layer];
-    const int sub = lane & (kQLanesPerRow - 1);
-    for (int t = warp * kQRowsPerWarp + (lane >> 3); t - (lane >> 3) < slots; t += kQWarps * kQRowsPerWarp) {
-      const bool live = t < S;
-      float x[kPieces][8];
-      float amax = 0.0f;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, slots = u.nblk * 16;
+  if (row0 + warp * kQRowsPerWarp >= slots) return;            // warp-uniform
+  const T* src = static_cast<const T*>(u.src) + h * u.hs;
+  const int sub = lane & (kQLanesPerRow - 1);
+  const int t = row0 + warp * kQRowsPerWarp + (lane >> 3);
+  const bool live = t < u.S;
+  float x[kPieces][8];
+  float amax = 0.0f;
 #pragma unroll
-      for (int c = 0; c < kPieces; ++c) {
-        const int piece = sub + kQLanesPerRow * c;
-        uint4 u = make_uint4(0, 0, 0, 0);
-        if (live && piece < VPR) u = *reinterpret_cast<const uint4*>(src + t * a.src_row_stride + 8 * piece);
-        unpack8<kBf16>(u, x[c]);
+  for (int c = 0; c < kPieces; ++c) {
+    const int piece = sub + kQLanesPerRow * c;
+    uint4 w = make_uint4(0, 0, 0, 0);
+    if (live && piece < VPR) w = *reinterpret_cast<const uint4*>(src + t * u.rs + 8 * piece);
+    unpack8<kBf16>(w, x[c]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(x[c][e]));
-      }
-#pragma unroll
-      for (int o = 1; o < kQLanesPerRow; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      if (t >= slots) continue;
-      const float scale = live ? kivi_scale<T>(amax) : 0.0f;
-      const float rcp = __frcp_rn(scale);
-      const int blk = a.block_ids[t >> 4], slot = t & 15;
-      int8_t* dst = pool + ((static_cast<int64_t>(blk) * 2 + 0) * H + h) * 16 * D + slot * D;
-#pragma unroll
-      for (int c = 0; c < kPieces; ++c) {
-        const int piece = sub + kQLanesPerRow * c;
-        if (piece < VPR) {
-          int q[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) q[e] = live ? kivi_q<T>(x[c][e], scale, rcp) : 0;
-          *reinterpret_cast<uint2*>(dst + 8 * piece) = pack8(q);
-        }
-      }
-      if (sub == 0) {
-        const __half s16 = __float2half_rn(scale);
-        const int64_t si = (static_cast<int64_t>(blk) * H + h) * 16 + slot;
-        if (ks16) ks16[si] = s16;
-        if (ks32) ks32[si] = __half2float(s16);
-      }
-    }
-    return;
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(x[c][e]));
   }
-  // ---- V ----
-  constexpr int kPhases = kQThreads / VPR;   // 128 (D 64), 85 (D 96), 64 (D 128)
-  __shared__ float part[kPhases][D + 1];
-  __shared__ float col_scale[D], col_rcp[D];
-  const int g = threadIdx.x % VPR, phase = threadIdx.x / VPR;
-  const bool active = phase < kPhases;
-  const T* src = static_cast<const T*>(a.src_v[layer]) + h * a.src_head_stride + 8 * g;
-  if (active) {
-    float m[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int t = phase; t < S; t += kPhases) {
-      float x[8];
-      unpack8<kBf16>(*reinterpret_cast<const uint4*>(src + t * a.src_row_stride), x);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) m[e] = fmaxf(m[e], fabsf(x[e]));
-    }
+  for (int o = 1; o < kQLanesPerRow; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (t >= slots) return;
+  const int blk = u.block_ids[t >> 4], slot = t & 15;
+  if (!block_ok(blk, u)) return;
+  const float scale = live ? kivi_scale<T>(amax) : 0.0f;
+  const float rcp = __frcp_rn(scale);
+  int8_t* dst = u.pool + ((static_cast<int64_t>(blk) * 2 + 0) * u.H + h) * 16 * D + slot * D;
+  float sc[8], rc[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) part[phase][8 * g + e] = m[e];
+  for (int e = 0; e < 8; ++e) {
+    sc[e] = scale;
+    rc[e] = rcp;
   }
+#pragma unroll
+  for (int c = 0; c < kPieces; ++c) {
+    const int piece = sub + kQLanesPerRow * c;
+    if (piece < VPR)
+      *reinterpret_cast<uint2*>(dst + 8 * piece) =
+          live ? kivi_q8<T>(x[c], sc, rc, !(scale > 0.0f)) : make_uint2(0, 0);
+  }
+  if (sub == 0) {
+    const __half s16 = __float2half_rn(scale);
+    const int64_t si = (static_cast<int64_t>(blk) * u.H + h) * 16 + slot;
+    if (u.s16) u.s16[si] = s16;
+    if (u.s32) u.s32[si] = __half2float(s16);
+  }
+}
+
+template <typename T, int D>
+__device__ __forceinline__ void quantize_store_v(const QStoreUnit& u, int h, int col0) {
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int kG = kQVCols / 8;              // 16-byte pieces per CTA row
+  constexpr int kPhases = kQThreads / kG;      // 64 token phases
+  __shared__ float part[kPhases][kQVCols + 1];
+  __shared__ float col_scale[kQVCols], col_rcp[kQVCols];
+  const int g = threadIdx.x % kG, phase = threadIdx.x / kG, slots = u.nblk * 16;
+  const T* src = static_cast<const T*>(u.src) + h * u.hs + col0 + 8 * g;
+  float m[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int t = phase; t < u.S; t += kPhases) {
+    float x[8];
+    unpack8<kBf16>(*reinterpret_cast<const uint4*>(src + t * u.rs), x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m[e] = fmaxf(m[e], fabsf(x[e]));
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) part[phase][8 * g + e] = m[e];
   __syncthreads();
-  if (threadIdx.x < D) {
-    float m = 0.0f;
-    for (int ph = 0; ph < kPhases; ++ph) m = fmaxf(m, part[ph][threadIdx.x]);
-    const float sc = kivi_scale<T>(m);
+  if (threadIdx.x < kQVCols) {
+    float mx = 0.0f;
+#pragma unroll 8
+    for (int ph = 0; ph < kPhases; ++ph) mx = fmaxf(mx, part[ph][threadIdx.x]);
+    const float sc = kivi_scale<T>(mx);
     col_scale[threadIdx.x] = sc;
     col_rcp[threadIdx.x] = __frcp_rn(sc);
     const __half s16 = __float2half_rn(sc);
-    __half* vs16 = a.vs16[layer];
-    float* vs32 = a.vs32[layer];
-    for (int b = 0; b < a.nblk; ++b) {
-      const int64_t si = (static_cast<int64_t>(a.block_ids[b]) * H + h) * D + threadIdx.x;
-      if (vs16) vs16[si] = s16;
-      if (vs32) vs32[si] = __half2float(s16);
+    for (int b = 0; b < u.nblk; ++b) {
+      const int blk = u.block_ids[b];
+      if (!block_ok(blk, u)) continue;
+      const int64_t si = (static_cast<int64_t>(blk) * u.H + h) * D + col0 + threadIdx.x;
+      if (u.s16) u.s16[si] = s16;
+      if (u.s32) u.s32[si] = __half2float(s16);
     }
   }
   __syncthreads();
-  if (!active) return;
   float sc[8], rc[8];
+  bool zero_scale = false;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     sc[e] = col_scale[8 * g + e];
     rc[e] = col_rcp[8 * g + e];
+    zero_scale |= !(sc[e] > 0.0f);
   }
   for (int t = phase; t < slots; t += kPhases) {
-    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (t < S) {
+    const int blk = u.block_ids[t >> 4], slot = t & 15;
+    if (!block_ok(blk, u)) continue;
+    uint2 q = make_uint2(0, 0);
+    if (t < u.S) {
       float x[8];
-      unpack8<kBf16>(*reinterpret_cast<const uint4*>(src + t * a.src_row_stride), x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) q[e] = kivi_q<T>(x[e], sc[e], rc[e]);
+      unpack8<kBf16>(*reinterpret_cast<const uint4*>(src + t * u.rs), x);
+      q = kivi_q8<T>(x, sc, rc, zero_scale);
     }
-    const int blk = a.block_ids[t >> 4], slot = t & 15;
-    *reinterpret_cast<uint2*>(pool + ((static_cast<int64_t>(blk) * 2 + 1) * H + h) * 16 * D + slot * D + 8 * g) =
-        pack8(q);
+    *reinterpret_cast<uint2*>(u.pool + ((static_cast<int64_t>(blk) * 2 + 1) * u.H + h) * 16 * D + slot * D +
+                              col0 + 8 * g) = q;
   }
+}
+
+// CTA x of a (head, layer[, chunk]): x < n_k -> K rows [32x, 32x + 32), else V
+// columns [32 (x - n_k), +32).
+template <typename T, int D>
+__device__ __forceinline__ void quantize_store_cta(QStoreUnit& u, const void* src_k, const void* src_v,
+                                                   __half* ks16, float* ks32, __half* vs16, float* vs32,
+                                                   int n_k) {
+  const int x = blockIdx.x;
+  if (x < n_k) {
+    u.src = src_k;
+    u.s16 = ks16;
+    u.s32 = ks32;
+    quantize_store_k<T, D>(u, blockIdx.y, x * kQRowsPerCta);
+  } else {
+    u.src = src_v;
+    u.s16 = vs16;
+    u.s32 = vs32;
+    quantize_store_v<T, D>(u, blockIdx.y, (x - n_k) * kQVCols);
+  }
+}
+
+// One chunk, all layers: grid (K row blocks + V column blocks, KV head, layer); the
+// pointer tables travel as kernel parameters (block ids checked on the host).
+template <typename T, int D>
+__global__ void __launch_bounds__(kQThreads) kvb_quantize_store_kernel(const __grid_constant__ QStoreArgs a) {
+  const int layer = blockIdx.z;
+  QStoreUnit u;
+  u.hs = a.src_head_stride;
+  u.rs = a.src_row_stride;
+  u.block_ids = a.block_ids;
+  u.nblk = a.nblk;
+  u.S = a.S;
+  u.H = a.H;
+  u.num_pool_blocks = a.num_pool_blocks;
+  u.pool = a.pool[layer];
+  u.status = nullptr;
+  quantize_store_cta<T, D>(u, a.src_k[layer], a.src_v[layer], a.ks16[layer], a.ks32[layer], a.vs16[layer],
+                           a.vs32[layer], (a.nblk * 16 + kQRowsPerCta - 1) / kQRowsPerCta);
+}
+
+// Several chunks, all layers, in one launch: grid (K row blocks of the longest
+// chunk + V column blocks, KV head, chunk x layer); the per-(chunk, layer) source
+// pointers and strides, the pool's per-layer pointers, token counts and block ids
+// come from small device tables.
+struct QStoreBatchArgs {
+  const void* const* src;        // [chunks][layers][2] (K, V)
+  void* const* tables;           // [5][layers]: pool, K scale16, V scale16, K scale32, V scale32
+  const int32_t* num_tokens;     // [chunks]
+  const int32_t* block_ids;      // [chunks][max_blocks]
+  const int64_t* src_strides;    // [chunks][2]: head, row
+  int64_t num_pool_blocks;
+  int32_t L, H, max_blocks;
+  int* status;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kQThreads) kvb_quantize_store_batch_kernel(const QStoreBatchArgs a) {
+  const int chunk = blockIdx.z / a.L, layer = blockIdx.z - chunk * a.L;
+  const int n_k = (a.max_blocks * 16 + kQRowsPerCta - 1) / kQRowsPerCta;
+  QStoreUnit u;
+  u.S = a.num_tokens[chunk];
+  u.nblk = (u.S + 15) / 16;
+  const int64_t si = (static_cast<int64_t>(chunk) * a.L + layer) * 2;
+  const void* src_k = a.src[si];
+  const void* src_v = a.src[si + 1];
+  u.hs = a.src_strides[2 * chunk];
+  u.rs = a.src_strides[2 * chunk + 1];
+  // checked here: the tables are device memory the host did not validate
+  if (u.S < 1 || u.nblk > a.max_blocks || u.hs < 0 || u.rs < 1 || ((u.hs | u.rs) & 7) ||
+      ((reinterpret_cast<uintptr_t>(src_k) | reinterpret_cast<uintptr_t>(src_v)) & 15)) {
+    if (threadIdx.x == 0 && a.status) atomicOr(a.status, KVB_STATUS_BAD_LENGTH);
+    return;
+  }
+  if ((int)blockIdx.x < n_k && (int)blockIdx.x * kQRowsPerCta >= u.nblk * 16) return;   // shorter chunk
+  u.block_ids = a.block_ids + static_cast<int64_t>(chunk) * a.max_blocks;
+  u.H = a.H;
+  u.num_pool_blocks = a.num_pool_blocks;
+  u.pool = static_cast<int8_t*>(a.tables[layer]);
+  u.status = a.status;
+  quantize_store_cta<T, D>(u, src_k, src_v, static_cast<__half*>(a.tables[a.L + layer]),
+                           static_cast<float*>(a.tables[3 * a.L + layer]),
+                           static_cast<__half*>(a.tables[2 * a.L + layer]),
+                           static_cast<float*>(a.tables[4 * a.L + layer]), n_k);
 }
 
 // ---- CacheBlend -----------------------------------------------------------------------
@@ -277,12 +448,13 @@ struct BlendArgs {
 };
 
 constexpr int kDevWarps = 8;        // warps per CTA; warp w takes layers w, w + 8, ...
-constexpr int kDevPositions = 8;    // positions per CTA (4 lanes each, in every warp)
-constexpr int kDevVecs = 8;         // 16-byte vectors per lane per operand in flight
+constexpr int kDevPositions = 4;    // positions per CTA (8 lanes each, in every warp)
+constexpr int kDevLanes = 32 / kDevPositions;
+constexpr int kDevVecs = 4;         // 16-byte vectors per lane per operand in flight
 
-// CTA = 8 positions x all layers.  In every warp, lanes 4p..4p+3 own position p
+// CTA = 4 positions x all layers.  In every warp, lanes 8p..8p+7 own position p
 // and split its per-layer K vector (all heads, 16-byte pieces); the warp walks its
-// share of the layers, reducing dot(c, f), |c|^2, |f|^2 over the 4 lanes (two
+// share of the layers, reducing dot(c, f), |c|^2, |f|^2 over the 8 lanes (three
 // shuffle steps) and adding 1 - cos per layer; the 8 warps' partial sums are added
 // in warp order in shared memory (a fixed order: same inputs, same bits).
 template <typename T, int D>
@@ -290,7 +462,7 @@ __global__ void __launch_bounds__(kDevWarps * 32) kvb_blend_deviation_kernel(con
   __shared__ float part[kDevWarps][kDevPositions];
   constexpr int VPH = D / 8;   // 16-byte vectors per head row
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int p = lane >> 2, sub = lane & 3;
+  const int p = lane / kDevLanes, sub = lane % kDevLanes;
   const int t = blockIdx.x * kDevPositions + p;
   const bool valid = t < a.S;
   const int tt = valid ? t : 0;
@@ -300,11 +472,11 @@ __global__ void __launch_bounds__(kDevWarps * 32) kvb_blend_deviation_kernel(con
     const T* cb = static_cast<const T*>(a.ck[l]) + static_cast<int64_t>(tt) * a.c_rs;
     const T* fb = static_cast<const T*>(a.fk[l]) + static_cast<int64_t>(tt) * a.f_rs;
     float dot = 0.0f, nc = 0.0f, nf = 0.0f;
-    for (int v0 = sub; v0 < nvec; v0 += 4 * kDevVecs) {
+    for (int v0 = sub; v0 < nvec; v0 += kDevLanes * kDevVecs) {
       uint4 cu[kDevVecs], fu[kDevVecs];
 #pragma unroll
       for (int k = 0; k < kDevVecs; ++k) {
-        const int v = v0 + 4 * k;
+        const int v = v0 + kDevLanes * k;
         if (valid && v < nvec) {
           const int h = v / VPH, dv = (v - h * VPH) * 8;
           cu[k] = *reinterpret_cast<const uint4*>(cb + h * a.c_hs + dv);
@@ -327,7 +499,7 @@ __global__ void __launch_bounds__(kDevWarps * 32) kvb_blend_deviation_kernel(con
       }
     }
 #pragma unroll
-    for (int o = 1; o < 4; o <<= 1) {
+    for (int o = 1; o < kDevLanes; o <<= 1) {
       dot += __shfl_xor_sync(0xffffffffu, dot, o);
       nc += __shfl_xor_sync(0xffffffffu, nc, o);
       nf += __shfl_xor_sync(0xffffffffu, nf, o);
@@ -546,8 +718,25 @@ bool head_dim_ok(int d) { return d == 64 || d == 96 || d == 128; }
 
 template <typename T, int D>
 cudaError_t launch_qstore(const QStoreArgs& a, int L, cudaStream_t s) {
-  kvb_quantize_store_kernel<T, D><<<dim3(2, a.H, L), kQThreads, 0, s>>>(a);
+  const int n_k = (a.nblk * 16 + kQRowsPerCta - 1) / kQRowsPerCta;
+  kvb_quantize_store_kernel<T, D><<<dim3(n_k + D / kQVCols, a.H, L), kQThreads, 0, s>>>(a);
   return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t launch_qstore_batch(const QStoreBatchArgs& a, int chunks, cudaStream_t s) {
+  const int n_k = (a.max_blocks * 16 + kQRowsPerCta - 1) / kQRowsPerCta;
+  kvb_quantize_store_batch_kernel<T, D><<<dim3(n_k + D / kQVCols, a.H, chunks * a.L), kQThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_qstore_batch_d(const QStoreBatchArgs& a, int chunks, int D, cudaStream_t s) {
+  switch (D) {
+    case 64: return launch_qstore_batch<T, 64>(a, chunks, s);
+    case 96: return launch_qstore_batch<T, 96>(a, chunks, s);
+    default: return launch_qstore_batch<T, 128>(a, chunks, s);
+  }
 }
 
 template <typename T>
@@ -629,6 +818,7 @@ extern "C" int kvb_quantize_store(const KvbQuantizeStoreParams* p, void* stream)
   for (int b = 0; b < p->num_chunk_blocks; ++b) a.block_ids[b] = p->block_ids[b];
   a.src_head_stride = p->src_head_stride;
   a.src_row_stride = p->src_row_stride;
+  a.num_pool_blocks = p->num_pool_blocks;
   a.L = p->num_layers;
   a.H = p->num_kv_heads;
   a.S = p->num_tokens;
@@ -637,6 +827,41 @@ extern "C" int kvb_quantize_store(const KvbQuantizeStoreParams* p, void* stream)
   const cudaError_t e = p->dtype == KVB_DTYPE_BF16 ? launch_qstore_d<__nv_bfloat16>(a, p->num_layers, p->head_dim, s)
                                                    : launch_qstore_d<__half>(a, p->num_layers, p->head_dim, s);
   if (e != cudaSuccess) return fail(KVB_ERR_CUDA, std::string("kvb_quantize_store launch: ") + cudaGetErrorString(e));
+  return KVB_OK;
+}
+
+extern "C" int kvb_quantize_store_batch(const KvbQuantizeStoreBatch* p, void* stream) {
+  if (!p) return fail(KVB_ERR_INVALID, "params is NULL");
+  if (p->dtype != KVB_DTYPE_BF16 && p->dtype != KVB_DTYPE_FP16)
+    return fail(KVB_ERR_INVALID, "dtype must be KVB_DTYPE_BF16 or KVB_DTYPE_FP16");
+  if (!head_dim_ok(p->head_dim)) return fail(KVB_ERR_INVALID, "head_dim must be 64, 96 or 128");
+  if (p->num_layers < 1 || p->num_layers > KVB_MAX_LAYERS)
+    return fail(KVB_ERR_INVALID, "num_layers must be in [1, " + std::to_string(KVB_MAX_LAYERS) + "]");
+  if (p->num_kv_heads < 1 || p->num_kv_heads > 65535) return fail(KVB_ERR_INVALID, "num_kv_heads must be in [1, 65535]");
+  if (p->num_chunks < 1 || (int64_t)p->num_chunks * p->num_layers > 65535)
+    return fail(KVB_ERR_INVALID, "num_chunks must be >= 1 with num_chunks * num_layers <= 65535");
+  if (p->max_chunk_blocks < 1 || p->max_chunk_blocks > KVB_MAX_CHUNK_BLOCKS)
+    return fail(KVB_ERR_INVALID, "max_chunk_blocks must be in [1, " + std::to_string(KVB_MAX_CHUNK_BLOCKS) + "]");
+  if (p->num_pool_blocks < 1) return fail(KVB_ERR_INVALID, "num_pool_blocks must be >= 1");
+  if (!p->src || !p->src_strides || !p->tables || !p->num_tokens || !p->block_ids)
+    return fail(KVB_ERR_INVALID, "src, src_strides, tables, num_tokens and block_ids must be non-null device arrays");
+  QStoreBatchArgs a{};
+  a.src = p->src;
+  a.tables = p->tables;
+  a.num_tokens = p->num_tokens;
+  a.block_ids = p->block_ids;
+  a.src_strides = p->src_strides;
+  a.num_pool_blocks = p->num_pool_blocks;
+  a.L = p->num_layers;
+  a.H = p->num_kv_heads;
+  a.max_blocks = p->max_chunk_blocks;
+  a.status = p->status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const cudaError_t e =
+      p->dtype == KVB_DTYPE_BF16 ? launch_qstore_batch_d<__nv_bfloat16>(a, p->num_chunks, p->head_dim, s)
+                                 : launch_qstore_batch_d<__half>(a, p->num_chunks, p->head_dim, s);
+  if (e != cudaSuccess)
+    return fail(KVB_ERR_CUDA, std::string("kvb_quantize_store_batch launch: ") + cudaGetErrorString(e));
   return KVB_OK;
 }
 

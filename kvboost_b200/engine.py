@@ -360,20 +360,38 @@ class KVBoost:
         layers = self._encode_layers(ids, position_offset)
         return (torch.stack([k[0] for k, _ in layers]), torch.stack([v[0] for _, v in layers]))
 
-    def _store_chunk(self, key: str, ids: List[int], pos: int) -> bool:
+    _STORE_BATCH = 32   # encoded chunks held back for one quantise-on-store launch
+
+    def _store_chunk(self, key: str, ids: List[int], pos: int, pending=None) -> bool:
+        """Encode one chunk and cache it.  int8 store: the model cache's tensors are
+        queued in ``pending`` and written by one quantise-on-store launch per batch
+        (``_flush_pending``); the chunk is registered at once (later kernels on the
+        stream see its blocks written)."""
         if self.pool is None:
             k, v = self._encode_to_kv(ids, pos)
             return self.store.store(DeviceChunk(key, ids, pos, pos + len(ids), k, v))
-        # int8: the cache tensors go straight into the pool (quantise-on-store kernel)
         layers = self._encode_layers(ids, pos)
         nblk = (len(ids) + 15) // 16
         size = nblk * self._block_bytes
+        if self.store.bytes + size > self.store.max_bytes:
+            self._flush_pending(pending)      # eviction may hand queued blocks back out
         if not self.store.make_room(size):
             return False
         blocks = self.pool.allocate(nblk)
-        self.pool.store_chunk_int8(blocks, [k for k, _ in layers], [v for _, v in layers])
+        item = (blocks, [k for k, _ in layers], [v for _, v in layers])
+        if pending is None:
+            self.pool.store_chunk_int8(*item)
+        else:
+            pending.append(item)
+            if len(pending) >= self._STORE_BATCH:
+                self._flush_pending(pending)
         return self.store.store(DeviceChunk(key, ids, pos, pos + len(ids), None, None,
                                             block_ids=blocks, pool_bytes=size))
+
+    def _flush_pending(self, pending) -> None:
+        if pending:
+            self.pool.store_chunks_int8(pending)
+            pending.clear()
 
     def _chunk_kv(self, chunks: List["DeviceChunk"]):
         """Stacked ``[L, H, P, D]`` K/V of a run of cached chunks in the model's dtype."""
@@ -407,13 +425,15 @@ class KVBoost:
         """Encode and cache every fixed-size chunk of ``text`` (``engine.py:415-507``)."""
         token_ids = self._encode(text)
         added, pos, parent = 0, position_offset, None
+        pending: list = []
         for _, _, ids in fixed_split(token_ids, self.chunk_size, self.min_chunk_tokens):
             key = chained_hash(ids, parent)
             if self.store.get(key) is None:
-                if self._store_chunk(key, ids, pos):
+                if self._store_chunk(key, ids, pos, pending):
                     added += 1
             parent = key
             pos += len(ids)
+        self._flush_pending(pending)
         n = len(token_ids)
         tail = n % self.chunk_size
         aligned = tail == 0 or tail < self.min_chunk_tokens

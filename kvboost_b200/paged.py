@@ -250,6 +250,84 @@ class DeviceBlockAllocator:
             _lib.check(_lib.load().kvb_quantize_store(ctypes.byref(p), _stream_handle(pool_dev)),
                        "kvb_quantize_store")
 
+    def store_chunks_int8(self, chunks) -> None:
+        """``store_chunk_int8`` for several chunks in one launch
+        (``kvb_quantize_store_batch``): ``chunks`` is a sequence of
+        ``(block_ids, keys, values)`` as ``store_chunk_int8`` takes them, with
+        disjoint blocks.  The pointer tables, token counts and block ids travel to
+        the device in one copy on the current stream."""
+        if chunks:
+            self.launch_prepared(self.prepare_chunks_int8(chunks))
+
+    def launch_prepared(self, prepared) -> None:
+        """Launch a batch built by ``prepare_chunks_int8`` (capturable in a CUDA
+        graph: no host memory is read at launch)."""
+        p, _, _ = prepared
+        dev = self.pools[0].device
+        with torch.cuda.device(dev):
+            _lib.check(_lib.load().kvb_quantize_store_batch(ctypes.byref(p), _stream_handle(dev)),
+                       "kvb_quantize_store_batch")
+
+    def prepare_chunks_int8(self, chunks):
+        """Device tables for ``launch_prepared``: returns ``(params, device tables,
+        sources)``; keep it alive while launches that use it may run."""
+        if self.dtype != torch.int8:
+            raise RuntimeError("store_chunks_int8 needs an int8 pool")
+        if not chunks:
+            raise ValueError("no chunks")
+        items = [(list(b), _layer_list(k), _layer_list(v)) for b, k, v in chunks]
+        L = len(items[0][1])
+        ref = items[0][1][0]
+        if ref.dtype not in _DTYPES:
+            raise TypeError("chunk K/V must be bfloat16 or float16")
+        H, _, D = ref.shape
+        if H != self.num_heads or D != self.head_dim or not 1 <= L <= min(self.num_layers,
+                                                                          _lib.KVB_MAX_LAYERS):
+            raise ValueError("chunk K/V do not match the pool's layers / heads / head_dim")
+        pool_dev = self.pools[0].device
+        seen, fixed = set(), []
+        for blocks, ks, vs in items:
+            if len(ks) != L or len(vs) != L:
+                raise ValueError("every chunk needs K and V for the same layers")
+            S = ks[0].shape[1]
+            if len(blocks) * self.block_size < S or len(blocks) > _lib.KVB_MAX_CHUNK_BLOCKS:
+                raise ValueError(f"{len(blocks)} blocks cannot hold {S} tokens")
+            if seen.intersection(blocks):
+                raise ValueError("the chunks' blocks overlap")
+            seen.update(blocks)
+            st0 = ks[0].stride()
+            for t in ks + vs:
+                if t.shape != (H, S, D) or t.dtype != ref.dtype or t.device != pool_dev:
+                    raise ValueError("chunk K/V must share heads, head_dim, dtype and the pool's device")
+            if any(t.stride() != st0 or st0[2] != 1 or st0[0] % 8 or st0[1] % 8 or t.data_ptr() % 16
+                   for t in ks + vs):   # one layout per chunk: contiguous copies
+                ks, vs = [t.contiguous() for t in ks], [t.contiguous() for t in vs]
+            fixed.append((blocks, ks, vs))
+        items = fixed
+        n, mb = len(items), max(len(b) for b, _, _ in items)
+        src = [p for _, ks, vs in items for k, v in zip(ks, vs) for p in (k.data_ptr(), v.data_ptr())]
+        strides = [x for _, ks, _ in items for x in ks[0].stride()[:2]]
+        tables = [t.data_ptr() for group in (self.pools, self.k_scale16, self.v_scale16,
+                                             self.k_scale, self.v_scale) for t in group[:L]]
+        tokens = [ks[0].shape[1] for _, ks, _ in items]
+        bids = [x for b, _, _ in items for x in (b + [-1] * (mb - len(b)))]
+        n64 = len(src) + len(strides) + len(tables)
+        host = torch.empty(n64 * 8 + (len(tokens) + len(bids)) * 4, dtype=torch.uint8).pin_memory()
+        host[:n64 * 8].view(torch.int64).copy_(torch.tensor(src + strides + tables, dtype=torch.int64))
+        host[n64 * 8:].view(torch.int32).copy_(torch.tensor(tokens + bids, dtype=torch.int32))
+        dev = host.to(pool_dev, non_blocking=True)
+        base = dev.data_ptr()
+        p = _lib.KvbQuantizeStoreBatch()
+        p.dtype, p.head_dim, p.num_layers, p.num_kv_heads = _DTYPES[ref.dtype], D, L, H
+        p.num_chunks, p.max_chunk_blocks, p.num_pool_blocks = n, mb, self.num_blocks
+        p.src = base
+        p.src_strides = base + len(src) * 8
+        p.tables = base + (len(src) + len(strides)) * 8
+        p.num_tokens = base + n64 * 8
+        p.block_ids = base + n64 * 8 + len(tokens) * 4
+        p.status = status_word(pool_dev).data_ptr()
+        return p, dev, items
+
     def write_chunk(self, layer: int, block_ids: List[int], key: torch.Tensor,
                     val: torch.Tensor) -> None:
         """Store one chunk's K/V (``[1 or H.., S, D]``) as is in a 16-bit pool: token t

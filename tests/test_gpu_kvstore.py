@@ -250,3 +250,73 @@ def test_cacheblend_reproduces_reference_fixture(case):
             assert abs(dv[i] - np.sort(dv)[::-1][len(want) - 1]) < 1e-3
         return
     assert sel.cpu().tolist()[:n] == want
+
+
+def test_many_layers_one_launch():
+    """100 layers (the pointer tables near the kernels' 128-layer limit) in one launch
+    each: quantise-on-store bit-exact, CacheBlend equal to the oracle's rule."""
+    from kvboost_b200.cacheblend import cacheblend_fwd
+    from kvboost_b200.paged import DeviceBlockAllocator
+    L, H, S, D = 100, 1, 40, 64
+    g = torch.Generator().manual_seed(100)
+    alloc = DeviceBlockAllocator(L, H, D, 8)
+    blocks = alloc.allocate(3)
+    keys = [torch.randn(1, H, S, D, generator=g).to(torch.bfloat16) for _ in range(L)]
+    vals = [torch.randn(1, H, S, D, generator=g).to(torch.bfloat16) for _ in range(L)]
+    alloc.store_chunk_int8(blocks, [k.cuda() for k in keys], [v.cuda() for v in vals])
+    torch.cuda.synchronize()
+    for layer in (0, 57, 99):
+        _check_layer(alloc, layer, blocks, keys[layer][0], vals[layer][0], "bf16")
+    ck, cv, fk, fv = _blend_inputs(L, H, S, D, torch.bfloat16, 77)
+    gck, gcv = ck.cuda(), cv.cuda()
+    dev, sel, cnt = cacheblend_fwd(gck, gcv, fk.cuda(), fv.cuda(), 0.2, 0.01)
+    dv = dev.cpu().numpy()
+    assert np.abs(dv - ocb.deviation(_f32(ck), _f32(fk))).max() <= 1e-5
+    want = ocb.select(dv, ocb.num_select(S, 0.2), 0.01)
+    assert sel.cpu().tolist()[:int(cnt.item())] == want
+    pk, pv = ocb.patch(_f32(ck), _f32(cv), _f32(fk), _f32(fv), want)
+    assert np.array_equal(_f32(gck), pk) and np.array_equal(_f32(gcv), pv)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_batched_store_matches_oracle(dt):
+    """Several chunks of ragged lengths in one kvb_quantize_store_batch launch."""
+    from kvboost_b200.paged import DeviceBlockAllocator
+    L, H, D = 4, 2, 128
+    g = torch.Generator().manual_seed(21)
+    alloc = DeviceBlockAllocator(L, H, D, 64)
+    alloc.allocate(3)
+    lens = [128, 100, 33, 16, 128]
+    chunks, cpu = [], []
+    for S in lens:
+        blocks = alloc.allocate((S + 15) // 16)
+        ks = [torch.randn(1, H, S, D, generator=g).to(dt) for _ in range(L)]
+        vs = [torch.randn(1, H, S, D, generator=g).to(dt) for _ in range(L)]
+        chunks.append((blocks, [k.cuda() for k in ks], [v.cuda() for v in vs]))
+        cpu.append((blocks, ks, vs))
+    alloc.store_chunks_int8(chunks)
+    torch.cuda.synchronize()
+    name = "bf16" if dt == torch.bfloat16 else "f16"
+    for blocks, ks, vs in cpu:
+        for layer in range(L):
+            _check_layer(alloc, layer, blocks, ks[layer][0], vs[layer][0], name)
+
+
+def test_batched_store_flags_bad_block_and_skips_it():
+    """A block id outside the pool is skipped on the device (never written) and
+    reported in the status word; the chunk's other blocks are still stored."""
+    from kvboost_b200 import _lib, ops
+    from kvboost_b200.paged import DeviceBlockAllocator
+    L, H, S, D = 2, 2, 48, 64
+    g = torch.Generator().manual_seed(22)
+    alloc = DeviceBlockAllocator(L, H, D, 8)
+    ops.read_status(torch.device("cuda"))                     # start from 0
+    ks = [torch.randn(1, H, S, D, generator=g).to(torch.bfloat16) for _ in range(L)]
+    vs = [torch.randn(1, H, S, D, generator=g).to(torch.bfloat16) for _ in range(L)]
+    alloc.store_chunks_int8([([5, 8 + 3, 6], [k.cuda() for k in ks], [v.cuda() for v in vs])])
+    status = ops.read_status(torch.device("cuda"))
+    assert status & _lib.KVB_STATUS_BAD_BLOCK
+    kq, _, _, _ = oq.quantize_int8_model_dtype(_f32(ks[0][0]), _f32(vs[0][0]), "bf16")
+    pool = alloc.pools[0].cpu().numpy()
+    assert np.array_equal(pool[5, 0].reshape(H, 16, D), kq[:, :16])
+    assert np.array_equal(pool[6, 0].reshape(H, 16, D), kq[:, 32:48])
