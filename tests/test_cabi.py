@@ -92,6 +92,7 @@ def test_ctypes_layouts_match_c_compiler(tmp_path):
                "KvbPagedPrefillParams": _lib.KvbPagedPrefillParams,
                "KvbPeerShards": _lib.KvbPeerShards,
                "KvbQuantizeStoreParams": _lib.KvbQuantizeStoreParams,
+               "KvbQuantizeStoreBatch": _lib.KvbQuantizeStoreBatch,
                "KvbCacheBlendParams": _lib.KvbCacheBlendParams}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "kvb_attn.h"', 'int main(){']
     for name, cls in structs.items():
@@ -218,3 +219,21 @@ def test_cacheblend_rejects_unaligned_pointers(lib):
     p.fresh_k = C.cast(bad, _lib._pp)
     assert lib.kvb_cacheblend_fwd(ctypes.byref(p), None) == _lib.KVB_ERR_INVALID
     assert b"16-byte aligned" in lib.kvb_last_error()
+
+
+@pytest.mark.parametrize("field,value,needle", [
+    ("num_chunks", 0, "num_chunks"),
+    ("num_chunks", 2000, "num_chunks"),
+    ("max_chunk_blocks", 129, "max_chunk_blocks"),
+    ("num_pool_blocks", 0, "num_pool_blocks"),
+    ("src", None, "non-null"),
+    ("head_dim", 72, "head_dim"),
+])
+def test_quantize_store_batch_validation(lib, field, value, needle):
+    p = _lib.KvbQuantizeStoreBatch()
+    p.dtype, p.head_dim, p.num_layers, p.num_kv_heads = 0, 128, 36, 2
+    p.num_chunks, p.max_chunk_blocks, p.num_pool_blocks = 24, 8, 1024
+    p.num_tokens = p.block_ids = p.src = p.src_strides = p.tables = 4096
+    setattr(p, field, value)
+    assert lib.kvb_quantize_store_batch(ctypes.byref(p), None) == _lib.KVB_ERR_INVALID
+    assert needle in lib.kvb_last_error().decode()
