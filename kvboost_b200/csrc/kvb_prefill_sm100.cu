@@ -648,22 +648,47 @@ __global__ void __launch_bounds__(256)
 // (row, 8-feature chunk) items.
 template <typename T, int D>
 __device__ __forceinline__ void merge_splits(const DenseArgs& a, const PagedArgs& pa, int b, int g,
-                                             int splits) {
+                                             int splits, float* scratch, int scratch_floats) {
   constexpr int NCH = D / 8;
   const int packed = a.q_len;
   const int64_t grow = ((int64_t)b * pa.num_kv_heads + g) * packed;   // first packed row of the group
   const T* o_part = reinterpret_cast<const T*>(a.o);
+  const bool staged = (int64_t)packed * (splits + 2) <= scratch_floats;
+  float* w = scratch;                               // [splits][packed]: exp(lse_s - max)
+  float* row_mx = scratch + (int64_t)packed * splits;
+  float* row_inv = row_mx + packed;
+  if (staged) {
+    // every partial LSE of the group in one coalesced pass, then per-row weights
+    for (int idx = threadIdx.x; idx < packed * splits; idx += blockDim.x) {
+      const int sp = idx / packed, r = idx - sp * packed;
+      w[idx] = __ldcg(a.lse + sp * pa.lse_split_stride + grow + r);
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < packed; r += blockDim.x) {
+      float mx = -INFINITY;
+      for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, w[sp * packed + r]);
+      float sum = 0.f;
+      for (int sp = 0; sp < splits; ++sp) {
+        const float e = mx > -INFINITY ? __expf(w[sp * packed + r] - mx) : 0.f;
+        w[sp * packed + r] = e;
+        sum += e;
+      }
+      row_mx[r] = mx;
+      row_inv[r] = sum > 0.f ? 1.f / sum : 0.f;
+    }
+    __syncthreads();
+  }
   for (int idx = threadIdx.x; idx < packed * NCH; idx += blockDim.x) {
     const int r = idx / NCH, ch = idx - r * NCH;
     const int64_t row = grow + r;
-    float mx = -INFINITY;
-    for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, __ldcg(a.lse + sp * pa.lse_split_stride + row));
+    float mx, inv;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    float wsum = 0.f;
-    if (mx > -INFINITY) {
+    if (staged) {
+      mx = row_mx[r];
+      inv = row_inv[r];
+#pragma unroll 4
       for (int sp = 0; sp < splits; ++sp) {
-        const float w = __expf(__ldcg(a.lse + sp * pa.lse_split_stride + row) - mx);
-        wsum += w;
+        const float wt = w[sp * packed + r];
         const uint4 v = __ldcg(reinterpret_cast<const uint4*>(o_part + sp * pa.o_split_stride + row * D + ch * 8));
         const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -673,12 +698,34 @@ __device__ __forceinline__ void merge_splits(const DenseArgs& a, const PagedArgs
             f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
           else
             f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
-          acc[2 * e] += w * f.x;
-          acc[2 * e + 1] += w * f.y;
+          acc[2 * e] += wt * f.x;
+          acc[2 * e + 1] += wt * f.y;
         }
       }
+    } else {
+      mx = -INFINITY;
+      for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, __ldcg(a.lse + sp * pa.lse_split_stride + row));
+      float wsum = 0.f;
+      if (mx > -INFINITY) {
+        for (int sp = 0; sp < splits; ++sp) {
+          const float wt = __expf(__ldcg(a.lse + sp * pa.lse_split_stride + row) - mx);
+          wsum += wt;
+          const uint4 v = __ldcg(reinterpret_cast<const uint4*>(o_part + sp * pa.o_split_stride + row * D + ch * 8));
+          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 f;
+            if constexpr (std::is_same<T, __half>::value)
+              f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
+            else
+              f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
+            acc[2 * e] += wt * f.x;
+            acc[2 * e + 1] += wt * f.y;
+          }
+        }
+      }
+      inv = wsum > 0.f ? 1.f / wsum : 0.f;
     }
-    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
     uint32_t o[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[e] = pack2<T>(acc[2 * e] * inv, acc[2 * e + 1] * inv);
@@ -689,7 +736,7 @@ __device__ __forceinline__ void merge_splits(const DenseArgs& a, const PagedArgs
     *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
     if (pa.lse_final != nullptr && ch == 0)
       pa.lse_final[(int64_t)b * pa.lf_bs + (int64_t)head * pa.lf_hs + i] =
-          wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+          inv > 0.f ? mx + __logf(1.f / inv) : -INFINITY;
   }
 }
 
@@ -1182,7 +1229,9 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     __syncthreads();
     if (ctl->last_cta) {
       __threadfence();
-      merge_splits<T, D>(a, pa, b, blockIdx.y, gridDim.x);
+      // the Q and K/V tiles are idle now: scratch for the merge's weights
+      merge_splits<T, D>(a, pa, b, blockIdx.y, gridDim.x, reinterpret_cast<float*>(sQ),
+                         (kSlots + G::NS) * G::TILE_BYTES / 4);
       if (threadIdx.x == 0) *count = 0;
     }
   }
@@ -1326,6 +1375,49 @@ static int decode_split_tiles(const KvbPrefillParams& p, int splits, int* eff) {
   return st;
 }
 
+// Arguments shared by both split-key decode kernels: partials in the workspace
+// after its counter header, merged into params.o / params.lse by each group's
+// last CTA.
+static void decode_args(const KvbPrefillParams& p, int splits, int split_tiles, void* ws, DenseArgs* a,
+                        PagedArgs* sp) {
+  const int group = p.num_q_heads / p.num_kv_heads;
+  const int packed = group * p.q_len;
+  const int D = p.head_dim;
+  const int64_t rows = (int64_t)p.batch * p.num_kv_heads * packed;
+  uint8_t* o_part = reinterpret_cast<uint8_t*>(ws) + KVB_DECODE_COUNTER_BYTES;
+  const int64_t o_bytes = (int64_t)splits * rows * D * 2;
+  *a = DenseArgs{};
+  a->o = o_part;
+  a->lse = reinterpret_cast<float*>(o_part + (o_bytes + 255) / 256 * 256);
+  a->o_rs = D;
+  a->o_hs = (int64_t)packed * D;
+  a->o_bs = (int64_t)p.num_kv_heads * packed * D;
+  a->lse_hs = packed;
+  a->lse_bs = (int64_t)p.num_kv_heads * packed;
+  a->q_len = packed;
+  a->kv_len = p.kv_len;
+  a->group = 1;
+  a->pair_heads = 0;
+  a->causal = p.causal;
+  a->scale_log2 = p.softmax_scale * 1.4426950408889634f;
+  a->status = p.status;
+  *sp = PagedArgs{};
+  sp->rows_per_head = p.q_len;
+  sp->split_tiles = split_tiles;
+  sp->o_split_stride = rows * D;
+  sp->lse_split_stride = rows;
+  sp->num_kv_heads = p.num_kv_heads;
+  sp->split_count = reinterpret_cast<int*>(ws);
+  sp->o_final = p.o;
+  sp->lse_final = p.lse;
+  sp->of_bs = p.o_batch_stride;
+  sp->of_hs = p.o_head_stride;
+  sp->of_rs = p.o_row_stride;
+  sp->lf_bs = p.lse_batch_stride;
+  sp->lf_hs = p.lse_head_stride;
+  sp->group_heads = group;
+}
+
 template <typename T, int D>
 static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cudaStream_t stream) {
   using G = Geo<D>;
@@ -1333,6 +1425,9 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
   const int packed = group * p.q_len;
   int splits = 1;
   const int split_tiles = decode_split_tiles(p, splits_req, &splits);
+  DenseArgs a;
+  PagedArgs sp;
+  decode_args(p, splits, split_tiles, ws, &a, &sp);
   const int64_t q_rs = p.q_len == 1 ? p.q_head_stride : p.q_row_stride;
   CUtensorMap tq, tk, tv;
   std::string err;
@@ -1343,42 +1438,6 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
       !make_map(&tv, p.v, p.dtype, D, std::max(1, p.kv_len), p.num_kv_heads, p.batch,
                 p.v_row_stride, p.v_head_stride, p.batch > 1 ? p.v_batch_stride : 8, &err))
     return fail(KVB_ERR_INVALID, err);
-  const int64_t rows = (int64_t)p.batch * p.num_kv_heads * packed;
-  int* counters = reinterpret_cast<int*>(ws);
-  T* o_part = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(ws) + KVB_DECODE_COUNTER_BYTES);
-  const int64_t o_bytes = (int64_t)splits * rows * D * 2;
-  float* lse_part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(o_part) +
-                                             (o_bytes + 255) / 256 * 256);
-  DenseArgs a = {};
-  a.o = o_part;
-  a.lse = lse_part;
-  a.o_rs = D;
-  a.o_hs = (int64_t)packed * D;
-  a.o_bs = (int64_t)p.num_kv_heads * packed * D;
-  a.lse_hs = packed;
-  a.lse_bs = (int64_t)p.num_kv_heads * packed;
-  a.q_len = packed;
-  a.kv_len = p.kv_len;
-  a.group = 1;
-  a.pair_heads = 0;
-  a.causal = p.causal;
-  a.scale_log2 = p.softmax_scale * 1.4426950408889634f;
-  a.status = p.status;
-  PagedArgs sp = {};
-  sp.rows_per_head = p.q_len;
-  sp.split_tiles = split_tiles;
-  sp.o_split_stride = rows * D;
-  sp.lse_split_stride = rows;
-  sp.num_kv_heads = p.num_kv_heads;
-  sp.split_count = counters;
-  sp.o_final = p.o;
-  sp.lse_final = p.lse;
-  sp.of_bs = p.o_batch_stride;
-  sp.of_hs = p.o_head_stride;
-  sp.of_rs = p.o_row_stride;
-  sp.lf_bs = p.lse_batch_stride;
-  sp.lf_hs = p.lse_head_stride;
-  sp.group_heads = group;
   auto kern = kvb_prefill_kernel<T, D, false, true>;
   static thread_local int configured_device = -1;
   int dev = 0;

@@ -89,3 +89,20 @@ def test_hf_layout_single_query():
                                v.float().cpu().numpy(), 1.0 / math.sqrt(128), True,
                                compute_dtype=np.float32)
     assert np.abs(o.float().cpu().numpy() - o_ref).max() <= 2e-2
+
+
+@pytest.mark.parametrize("Hq,Hkv,Sq,D,dtype", [(4, 2, 6, 64, torch.float16), (32, 2, 1, 96, torch.float16),
+                                                (16, 1, 1, 128, torch.bfloat16), (2, 2, 16, 128, torch.bfloat16)])
+def test_small_groups_masks(Hq, Hkv, Sq, D, dtype):
+    """Packed groups of 1-16 rows per KV head: bottom-right, top-left and no mask."""
+    _case(2, Hq, Hkv, Sq, 777, D, dtype, seed=Hq + Sq)
+    _case(1, Hq, Hkv, Sq, 300, D, dtype, seed=Hq + Sq + 1, top_left=True)
+    _case(1, Hq, Hkv, Sq, 300, D, dtype, seed=Hq + Sq + 2, causal=False)
+
+
+def test_one_query_split_counts_agree():
+    a = _case(2, 16, 2, 1, 3000, 128, torch.bfloat16, seed=15, splits=1)
+    b = _case(2, 16, 2, 1, 3000, 128, torch.bfloat16, seed=15, splits=5)
+    c = _case(2, 16, 2, 1, 3000, 128, torch.bfloat16, seed=15, splits=24)
+    assert (a.float() - b.float()).abs().max().item() <= 2e-2
+    assert (a.float() - c.float()).abs().max().item() <= 2e-2
