@@ -78,6 +78,12 @@ def parse():
                              "ttft_reuse", "paged_long_cp", "decode", "quantize_store",
                              "cacheblend"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kv-bits", type=int, default=16, choices=[16, 8],
+                    help="ttft_reuse: the engine's chunk store (8: KIVI int8 block pool, "
+                         "quantised on store, dequantised on assembly)")
+    ap.add_argument("--recompute", default="selective", choices=["selective", "cacheblend", "none"],
+                    help="ttft_reuse: seam repair of the single-prompt generate() timed "
+                         "beside the batch (generate_batch itself repairs no seams)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cp-gather", default="peers", choices=["peers", "nccl"],
                     help="paged_long_cp: read peers' shards in place over NVLink inside the "
@@ -910,8 +916,8 @@ def run_ttft(args, torch, dist, rank, world, local, dev):
     from kvboost_b200 import _lib, ops
     from kvboost_b200.engine import KVBoost
     w = TtftReuse()
-    eng = KVBoost(w.model(torch, dev), None, recompute_strategy="selective",
-                  max_cache_bytes=48 << 30, device=str(dev))
+    eng = KVBoost(w.model(torch, dev), None, recompute_strategy=args.recompute,
+                  max_cache_bytes=48 << 30, kv_cache_bits=args.kv_bits, device=str(dev))
     prefix, _ = w.prompts(0, rank)
     eng.warm(prefix)
 
@@ -979,6 +985,16 @@ def run_ttft(args, torch, dist, rank, world, local, dev):
             ttft.append(allmax(res[0].ttft_ms))
             total.append(allmax(res[0].total_ms))
     launches = (_lib.calls_ok - c0) // (args.warmup + args.e2e_steps)
+    # one prompt through generate(): the seam repair of --recompute runs here
+    single = []
+    for s in range(args.warmup + args.e2e_steps):
+        _, pr = w.prompts(2000 + s, rank)
+        if world > 1:
+            dist.barrier()
+        r = eng.generate(pr[0], max_new_tokens=1)
+        assert r.cached_tokens == w.PREFIX
+        if s >= args.warmup:
+            single.append(allmax(r.ttft_ms))
     # the same engine on stock SDPA, for the kernel's share of TTFT
     from kvboost_b200.flash_attn_ext import install_flash_attention, uninstall_flash_attention
     uninstall_flash_attention(eng.model)
@@ -1011,6 +1027,8 @@ def run_ttft(args, torch, dist, rank, world, local, dev):
                 "d2h_bytes_per_step": w.B * w.NEW * 8, "total_ms": statistics.mean(total),
                 "ttft_ms_sdpa_engine": statistics.mean(sdpa),
                 "ttft_ms_samples": [round(x, 2) for x in ttft],
+                "ttft_ms_single_prompt_generate": statistics.mean(single),
+                "kv_cache_bits": args.kv_bits, "recompute_single_prompt": args.recompute,
                 "prompt_tokens_per_s": world * w.B * (w.PREFIX + w.SUFFIX) / (e2e / 1e3)},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "kernel": "suffix-prefill attention (per layer)",

@@ -897,15 +897,16 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   } else if (!PAGED && warp == kWarpTma) {
     // ================================================================ TMA
     if (lane == 0 && n_max > 0) {
-#pragma unroll
-      for (int sl = 0; sl < kSlots; ++sl) {
-        if (n_t[sl] == 0) continue;
+      // Q of slot 0, then K0, then Q of slot 1: the first S waits for two tiles, not three
+      auto load_q = [&](int sl) {
+        if (n_t[sl] == 0) return;
         ptx::mbar_arrive_expect_tx(bar(BAR_Q_FULL + sl), G::TILE_BYTES);
 #pragma unroll
         for (int at = 0; at < G::NATOM; ++at)
           ptx::tma_load_4d(ptx::smem_u32(sQ + sl * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_q,
                            at * 64, q_base + q0[sl], head[sl], tb, bar(BAR_Q_FULL + sl));
-      }
+      };
+      load_q(0);
       int issued = 0;
 #pragma unroll 1
       for (int j = 0; j < n_max; ++j) {
@@ -920,6 +921,8 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
         for (int at = 0; at < G::NATOM; ++at)
           ptx::tma_load_4d(ptx::smem_u32(sK + st * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_k,
                            at * 64, ky, kvh, tb, bar(BAR_K_FULL + st));
+        if (j == 0)
+          for (int sl = 1; sl < kSlots; ++sl) load_q(sl);
         if (!wait_bar(bar(BAR_V_EMPTY + st), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
           break;
         if (j < 16) KVB_TRACE_AT(32 + j);
