@@ -43,6 +43,7 @@
 #include <cmath>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "kvb_attn.h"
 #include "kvb_sm100_ptx.cuh"
@@ -542,6 +543,9 @@ __global__ void __launch_bounds__(256)
     kvb_paged_materialize_kernel(PagedArgs pa, T* wk, T* wv, int q_len, int kv_pad, int* status,
                                  PeerArgs peer) {
   constexpr int NCH = D / 16;
+  // The prefill launch that reads this workspace may start its CTAs' setup
+  // now; it waits for this grid before touching memory.
+  ptx::griddep_launch_dependents();
   const int b = blockIdx.z;
   const int kvh = blockIdx.y;
   const int P = pa.prefix_lens ? pa.prefix_lens[b] : pa.prefix_len;
@@ -764,6 +768,38 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   KVB_TRACE_SETUP();
+  auto bar = [&](int i) { return ptx::smem_u32(&bars[i]); };
+
+  // ---- setup that touches no global memory ------------------------------
+  // Runs while the preceding grid in the stream may still be finishing (the
+  // launch allows programmatic dependent launch); everything from the wait
+  // on sees that grid's writes.  TMEM is allocated only after the wait, so a
+  // CTA never holds TMEM while waiting on a grid that may still need some.
+  if (threadIdx.x == 0) {
+    for (int sl = 0; sl < kSlots; ++sl) {
+      ptx::mbar_init(bar(BAR_Q_FULL + sl), 1);
+      ptx::mbar_init(bar(BAR_S_FULL + sl), 1);
+      ptx::mbar_init(bar(BAR_P_FULL + sl), 4 * Roles<PAGED>::kHalves);  // one per softmax warp
+      ptx::mbar_init(bar(BAR_O_FULL + sl), 1);
+    }
+    ptx::mbar_init(bar(BAR_DRAIN), 1);
+    for (int st = 0; st < G::NS; ++st) {
+      ptx::mbar_init(bar(BAR_K_FULL + st), PAGED ? Roles<PAGED>::kConvWarps : 1);
+      ptx::mbar_init(bar(BAR_K_EMPTY + st), 1);
+      ptx::mbar_init(bar(BAR_V_FULL + st), PAGED ? Roles<PAGED>::kConvWarps : 1);
+      ptx::mbar_init(bar(BAR_V_EMPTY + st), 1);
+    }
+    ctl->abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == kWarpTma && lane == 0) {
+    ptx::prefetch_tmap(&tm_q);
+    if (!PAGED) {
+      ptx::prefetch_tmap(&tm_k);
+      ptx::prefetch_tmap(&tm_v);
+    }
+  }
+  ptx::griddep_wait();
 
   // ---- work item: two query tiles sharing one KV head ---------------------
   const int b = blockIdx.z;
@@ -812,36 +848,9 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     n_t[sl] = q_rows[sl] > 0 ? (kv_end + BN - 1) / BN : 0;
     if (SPLITKV) n_t[sl] = max(0, min(n_t[sl] - jbase, pa.split_tiles));
   }
-  if (q_rows[0] == 0 && q_rows[1] == 0) return;  // uniform, before any barrier use
+  if (q_rows[0] == 0 && q_rows[1] == 0) return;  // uniform, before TMEM or any barrier wait
   const int n_max = max(n_t[0], n_t[1]);
 
-  auto bar = [&](int i) { return ptx::smem_u32(&bars[i]); };
-
-  // ---- setup --------------------------------------------------------------
-  if (threadIdx.x == 0) {
-    for (int sl = 0; sl < kSlots; ++sl) {
-      ptx::mbar_init(bar(BAR_Q_FULL + sl), 1);
-      ptx::mbar_init(bar(BAR_S_FULL + sl), 1);
-      ptx::mbar_init(bar(BAR_P_FULL + sl), 4 * Roles<PAGED>::kHalves);  // one per softmax warp
-      ptx::mbar_init(bar(BAR_O_FULL + sl), 1);
-    }
-    ptx::mbar_init(bar(BAR_DRAIN), 1);
-    for (int st = 0; st < G::NS; ++st) {
-      ptx::mbar_init(bar(BAR_K_FULL + st), PAGED ? Roles<PAGED>::kConvWarps : 1);
-      ptx::mbar_init(bar(BAR_K_EMPTY + st), 1);
-      ptx::mbar_init(bar(BAR_V_FULL + st), PAGED ? Roles<PAGED>::kConvWarps : 1);
-      ptx::mbar_init(bar(BAR_V_EMPTY + st), 1);
-    }
-    ctl->abort_flag = 0;
-    ptx::fence_mbar_init();
-  }
-  if (warp == kWarpTma && lane == 0) {
-    ptx::prefetch_tmap(&tm_q);
-    if (!PAGED) {
-      ptx::prefetch_tmap(&tm_k);
-      ptx::prefetch_tmap(&tm_v);
-    }
-  }
   if (warp == kWarpMma) {
     ptx::tmem_alloc(ptx::smem_u32(&ctl->tmem_base), G::TMEM_COLS);
     ptx::tmem_relinquish();
@@ -850,6 +859,9 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
+  // Every CTA of this grid is resident or done once all have passed here: the
+  // next launch may begin its own setup.
+  ptx::griddep_launch_dependents();
   if (threadIdx.x == 0) KVB_TRACE_AT(0);
 
   if (PAGED && warp >= kWarpTma && warp < kWarpTma + Roles<PAGED>::kConvWarps) {
@@ -921,8 +933,13 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
         for (int at = 0; at < G::NATOM; ++at)
           ptx::tma_load_4d(ptx::smem_u32(sK + st * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_k,
                            at * 64, ky, kvh, tb, bar(BAR_K_FULL + st));
-        if (j == 0)
+        if (j == 0) {
           for (int sl = 1; sl < kSlots; ++sl) load_q(sl);
+          // V0 and the next K tiles are needed only after the first softmax:
+          // hold them back until K0 has landed, so that the first S MMAs'
+          // operands do not share DRAM bandwidth with them at launch.
+          if (!wait_bar(bar(BAR_K_FULL), 0, abort_flag, a.status, KVB_STATUS_LOAD_WAIT)) break;
+        }
         if (!wait_bar(bar(BAR_V_EMPTY + st), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
           break;
         if (j < 16) KVB_TRACE_AT(32 + j);
@@ -1179,29 +1196,49 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     }
     const bool row_valid = t < q_rows[sl];
     const float inv_l = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
-    T* orow = reinterpret_cast<T*>(a.o) + hf * DH + (SPLITKV ? split * pa.o_split_stride : 0) +
-              (a.cu_q ? (int64_t)(q_base + qi) * a.o_rs + (int64_t)h * a.o_hs
-                      : (int64_t)b * a.o_bs + (int64_t)h * a.o_hs + (int64_t)qi * a.o_rs);
+    T* obase = reinterpret_cast<T*>(a.o) + hf * DH + (SPLITKV ? split * pa.o_split_stride : 0) +
+               (a.cu_q ? (int64_t)q_base * a.o_rs + (int64_t)h * a.o_hs
+                       : (int64_t)b * a.o_bs + (int64_t)h * a.o_hs);
+    if (have_o) {
+      // The warp's 32 output row segments go through shared memory, so that the
+      // global stores write whole segments (NC lanes per row) instead of one
+      // 16-byte piece of 32 different rows per instruction.  The slot's Q tile
+      // is free: the O_FULL commit follows every MMA that read it.  Pieces are
+      // rotated by row so that neither pass has bank conflicts.
+      constexpr int NC = DH / 8;                   // 16-byte pieces per row segment
+      constexpr int ROT = 8 / (NC % 8 == 0 ? 8 : NC % 4 == 0 ? 4 : 2);
+      uint4* stage = reinterpret_cast<uint4*>(sQ + sl * G::TILE_BYTES) +
+                     (hf * 4 + (warp & 3)) * 32 * NC;
 #pragma unroll 1
-    for (int c = 0; c < DH; c += OCW) {
-      uint32_t r[OCW];
-      if (n_tiles > 0) {
+      for (int c = 0; c < DH; c += OCW) {
+        uint32_t r[OCW];
         tmem_ld_cw<OCW>(tO + c, r);
         ptx::tmem_wait_ld();
-      }
-      if (row_valid) {
         uint32_t pk[OCW / 2];
 #pragma unroll
-        for (int i = 0; i < OCW / 2; ++i) {
-          const float o0 = have_o ? __uint_as_float(r[2 * i]) * inv_l : 0.f;
-          const float o1 = have_o ? __uint_as_float(r[2 * i + 1]) * inv_l : 0.f;
-          pk[i] = pack2<T>(o0, o1);
-        }
-        uint4* dst = reinterpret_cast<uint4*>(orow + c);
+        for (int i = 0; i < OCW / 2; ++i)
+          pk[i] = pack2<T>(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
 #pragma unroll
         for (int i = 0; i < OCW / 8; ++i)
-          dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          stage[lane * NC + (c / 8 + i + lane / ROT) % NC] =
+              make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
+      __syncwarp();
+      constexpr int RPS = 32 / NC;                 // rows per store instruction
+      const int pr = lane / NC, pc = lane % NC;
+      const int wrow = (warp & 3) * 32;            // first row of this warp within the tile
+#pragma unroll 1
+      for (int r0 = 0; r0 < 32; r0 += RPS) {
+        const int rr = r0 + pr;
+        if (pr < RPS && rr < 32 && wrow + rr < q_rows[sl])
+          *reinterpret_cast<uint4*>(obase + (int64_t)(q0s + wrow + rr) * a.o_rs + pc * 8) =
+              stage[rr * NC + (pc + rr / ROT) % NC];
+      }
+    } else if (row_valid) {
+      // no key tiles (or an aborted launch): zeros
+      uint4* dst = reinterpret_cast<uint4*>(obase + (int64_t)qi * a.o_rs);
+#pragma unroll
+      for (int i = 0; i < DH / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
     }
     if (hf == 0 && row_valid && a.lse != nullptr) {
       const float lse = (l_tot > 0.f && have_o) ? (m_run + ptx::lg2(l_tot)) * 0.69314718055994531f
@@ -1294,6 +1331,27 @@ static bool make_map(CUtensorMap* m, const void* base, int dtype, int head_dim, 
   return true;
 }
 
+// Launch with programmatic dependent launch allowed: the kernel's CTAs may
+// start, and run their setup that touches no global memory, while the
+// preceding grid in the stream finishes.  The prefill kernel orders every
+// global access after griddepcontrol.wait, so results are as with plain
+// stream order.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, int threads, int smem,
+                              cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <typename T, int D>
 static int launch_dense_core(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                              const DenseArgs& a, int batch, int num_q_heads, int q_len,
@@ -1314,8 +1372,9 @@ static int launch_dense_core(const CUtensorMap& tq, const CUtensorMap& tk, const
   dim3 grid = a.pair_heads ? dim3(q_tiles, num_q_heads / 2, batch)
                            : dim3((q_tiles + 1) / 2, num_q_heads, batch);
   PagedArgs none = {};
-  kern<<<grid, Roles<false>::kThreads, G::SMEM_BYTES, stream>>>(tq, tk, tv, a, none);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, grid, Roles<false>::kThreads, G::SMEM_BYTES, stream, tq, tk,
+                             tv, a, none);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess)
     return fail(KVB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
   return KVB_OK;
@@ -1452,9 +1511,9 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
       return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured_device = dev;
   }
-  kern<<<dim3(splits, p.num_kv_heads, p.batch), Roles<false>::kThreads, G::SMEM_BYTES, stream>>>(
-      tq, tk, tv, a, sp);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, dim3(splits, p.num_kv_heads, p.batch), Roles<false>::kThreads,
+                             G::SMEM_BYTES, stream, tq, tk, tv, a, sp);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(KVB_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
   return KVB_OK;
 }
@@ -1593,8 +1652,9 @@ static int launch_paged(const KvbPagedPrefillParams& p, cudaStream_t stream,
   const int q_tiles = (p.q_len + BM - 1) / BM;
   dim3 grid = a.pair_heads ? dim3(q_tiles, p.num_q_heads / 2, p.batch)
                            : dim3((q_tiles + 1) / 2, p.num_q_heads, p.batch);
-  kern<<<grid, Roles<true>::kThreads, G::SMEM_BYTES, stream>>>(tq, tq, tq, a, pa);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, grid, Roles<true>::kThreads, G::SMEM_BYTES, stream, tq, tq, tq,
+                             a, pa);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess)
     return fail(KVB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
   return KVB_OK;

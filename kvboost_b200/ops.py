@@ -250,13 +250,18 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if need < 0:
         _lib.check(_lib.KVB_ERR_INVALID, "kvb_decode_workspace_bytes: " + (
             lib.kvb_last_error().decode("utf-8", "replace")))
-    idx = q.device.index if q.device.index is not None else torch.cuda.current_device()
-    ws = _decode_ws.get(idx)
+    # One workspace per (device, stream): its split counters start at zero and every
+    # launch leaves them at zero, so launches queued on one stream can share it, while
+    # launches on another stream (which may overlap) get their own.
+    stream = _stream_handle(q.device)
+    key = (q.device.index if q.device.index is not None else torch.cuda.current_device(), stream)
+    ws = _decode_ws.get(key)
     if ws is None or ws.numel() < need:
+        # (a replaced workspace returns to the caching allocator, whose reuse is
+        # ordered on this same stream)
         ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=q.device)  # counters start at 0
-        _decode_ws[idx] = ws
+        _decode_ws[key] = ws
     with torch.cuda.device(q.device):
-        rc = lib.kvb_decode_fwd(p, int(num_splits), ws.data_ptr(), ws.numel(),
-                                _stream_handle(q.device))
+        rc = lib.kvb_decode_fwd(p, int(num_splits), ws.data_ptr(), ws.numel(), stream)
     _lib.check(rc, "kvb_decode_fwd")
     return out, lse

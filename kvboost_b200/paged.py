@@ -459,17 +459,11 @@ class DeviceChunkMapper:
         return len(self._chunk_blocks)
 
 
-_workspaces: Dict[int, torch.Tensor] = {}
-
-
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Per-device scratch for the materialised-prefix strategy (grown, never shrunk)."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    ws = _workspaces.get(idx)
-    if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{idx}")
-        _workspaces[idx] = ws
-    return ws
+    """Scratch for the materialised-prefix strategy, taken from torch's caching
+    allocator on the current stream for this call only: its reuse is ordered on
+    that stream, so calls on concurrent streams never share a workspace."""
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
 
 
 def block_table_tensor(tables: Sequence[Sequence[int]], device) -> torch.Tensor:
