@@ -135,24 +135,25 @@ typedef struct KvbPrefillParams {
 int kvb_prefill_fwd(const KvbPrefillParams* params, void* stream);
 
 /*
- * Attention for a few queries per head over many keys: decode steps (q_len 1)
- * and the selective-recompute seams (q_len <= 16) that reach the SDPA call of
- * the reference's engine (flash_attn_ext.py:86-103) with a short query.  Same
- * params and semantics as kvb_prefill_fwd in dense mode, restricted to
- * (num_q_heads / num_kv_heads) * q_len <= 256 and 1 <= q_len <= kv_len; with
- * q_len > 1 each head's rows must be contiguous in q and o (head stride =
- * q_len * row stride).  The query heads sharing a KV head are packed as the
- * rows of one tile, so every key tile is read once per group, and the key
- * range is split over num_splits CTAs; the last CTA of each (sequence, KV
- * head) group to finish merges the group's partial outputs by their LSE (one
- * launch).  workspace: device memory of at least
- * kvb_decode_workspace_bytes(params, num_splits) bytes (-1: invalid params,
- * reason in kvb_last_error), 16-byte aligned.  Its first
- * KVB_DECODE_COUNTER_BYTES hold the groups' completion counters: zero them
- * once before the first call; every call leaves them zero again (so one
- * workspace serves calls of any shape, in order on one stream).  Needs
- * batch * num_kv_heads <= KVB_DECODE_COUNTER_BYTES / 4.  No counterpart in the
- * reference, whose decode steps run the same SDPA call as its prefill.
+ * Split-key attention for few queries per head over many keys: decode steps
+ * (q_len 1), the selective-recompute seams (q_len <= 16) and short reuse
+ * suffixes that reach the SDPA call of the reference's engine
+ * (flash_attn_ext.py:86-103).  Same params and semantics as kvb_prefill_fwd in
+ * dense mode, restricted to 1 <= q_len <= kv_len; with q_len > 1 each head's
+ * rows must be contiguous in q (head stride = q_len * row stride).  The query
+ * heads sharing a KV head are packed as rows ((q heads per KV head) * q_len
+ * of them, two 128-row tiles per CTA), so every key tile is read once per
+ * group and tile pair, and the key range is split over num_splits CTAs; the
+ * last CTA of each (sequence, KV head, tile pair) to finish merges the
+ * partial outputs by their LSE (one launch).  workspace: device memory of at
+ * least kvb_decode_workspace_bytes(params, num_splits) bytes (-1: invalid
+ * params, reason in kvb_last_error), 16-byte aligned.  Its first
+ * KVB_DECODE_COUNTER_BYTES hold the completion counters: zero them once
+ * before the first call; every call leaves them zero again (so one workspace
+ * serves calls of any shape, in order on one stream).  Needs batch *
+ * num_kv_heads * ceil(packed rows / 256) <= KVB_DECODE_COUNTER_BYTES / 4.  No
+ * counterpart in the reference, whose decode steps run the same SDPA call as
+ * its prefill.
  */
 #define KVB_DECODE_COUNTER_BYTES (64 * 1024)
 int64_t kvb_decode_workspace_bytes(const KvbPrefillParams* params, int num_splits);

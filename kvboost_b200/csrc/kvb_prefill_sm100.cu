@@ -178,6 +178,7 @@ struct PagedArgs {
       float* lse_final;       // final LSE (b, head, i) at b*bs + head*hs + i, or null
       int64_t of_bs, of_hs, of_rs, lf_bs, lf_hs;
       int group_heads;        // query heads per KV head
+      int tile_pairs;         // 256-row pairs of packed tiles per group (grid x = splits * pairs)
     };
   };
   int max_blocks;
@@ -188,9 +189,9 @@ struct PagedArgs {
   // Split-key decode (the dense SPLITKV kernels, which read no pool and carry
   // these here: growing DenseArgs measurably slowed every dense launch): query
   // rows are a GQA group's heads packed as (head, row) with rows_per_head rows
-  // each; CTA x covers key tiles [x * split_tiles, (x + 1) * split_tiles) and
-  // writes its normalised partial O / LSE at o + x * o_split_stride,
-  // lse + x * lse_split_stride.
+  // each; CTA x takes packed tiles 2p, 2p + 1 (p = x / splits) and key tiles
+  // [s * split_tiles, (s + 1) * split_tiles) (s = x % splits), and writes its
+  // normalised partial O / LSE at o + s * o_split_stride, lse + s * lse_split_stride.
   int rows_per_head;
   int split_tiles;
   int64_t o_split_stride, lse_split_stride;
@@ -643,19 +644,20 @@ __global__ void __launch_bounds__(256)
   reinterpret_cast<uint4*>(dst)[1] = w1;
 }
 
-// Merge the per-split partial results of one (sequence, KV head) group of a
-// split-key decode: for each packed query row, O = sum_s exp(lse_s - L) O_s and
-// L = log sum_s exp(lse_s).  Partials are packed as rows
-// r = head_in_group * rows_per_head + i ([splits][batch][num_kv_heads][packed][D],
-// normalised, compute dtype; LSE fp32 [splits][batch][num_kv_heads][packed]) and
-// read through L2 (they were written by other CTAs).  Threads stride over
-// (row, 8-feature chunk) items.
+// Merge the per-split partial results of packed rows [r0, r0 + packed) of one
+// (sequence, KV head) group of a split-key launch: for each packed query row,
+// O = sum_s exp(lse_s - L) O_s and L = log sum_s exp(lse_s).  Partials are
+// packed as rows r = head_in_group * rows_per_head + i
+// ([splits][batch][num_kv_heads][group rows][D], normalised, compute dtype; LSE
+// fp32 [splits][batch][num_kv_heads][group rows]) and read through L2 (they were
+// written by other CTAs).  Threads stride over (row, 8-feature chunk) items.
 template <typename T, int D>
 __device__ __forceinline__ void merge_splits(const DenseArgs& a, const PagedArgs& pa, int b, int g,
-                                             int splits, float* scratch, int scratch_floats) {
+                                             int splits, int r0, int packed, float* scratch,
+                                             int scratch_floats) {
   constexpr int NCH = D / 8;
-  const int packed = a.q_len;
-  const int64_t grow = ((int64_t)b * pa.num_kv_heads + g) * packed;   // first packed row of the group
+  // first merged row of the group
+  const int64_t grow = ((int64_t)b * pa.num_kv_heads + g) * a.q_len + r0;
   const T* o_part = reinterpret_cast<const T*>(a.o);
   const bool staged = (int64_t)packed * (splits + 2) <= scratch_floats;
   float* w = scratch;                               // [splits][packed]: exp(lse_s - max)
@@ -733,8 +735,8 @@ __device__ __forceinline__ void merge_splits(const DenseArgs& a, const PagedArgs
     uint32_t o[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[e] = pack2<T>(acc[2 * e] * inv, acc[2 * e + 1] * inv);
-    const int head = g * pa.group_heads + r / pa.rows_per_head;
-    const int i = r % pa.rows_per_head;
+    const int head = g * pa.group_heads + (r0 + r) / pa.rows_per_head;
+    const int i = (r0 + r) % pa.rows_per_head;
     T* dst = reinterpret_cast<T*>(pa.o_final) + (int64_t)b * pa.of_bs + (int64_t)head * pa.of_hs +
              (int64_t)i * pa.of_rs + ch * 8;
     *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -804,11 +806,13 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   // ---- work item: two query tiles sharing one KV head ---------------------
   const int b = blockIdx.z;
   int head[kSlots], mtile[kSlots];
-  const int split = SPLITKV ? (int)blockIdx.x : 0;
-  if (SPLITKV) {  // both packed tiles of one KV head's group, one key range
+  const int splits = SPLITKV ? (int)gridDim.x / pa.tile_pairs : 1;
+  const int split = SPLITKV ? (int)blockIdx.x % splits : 0;
+  const int tpair = SPLITKV ? (int)blockIdx.x / splits : 0;
+  if (SPLITKV) {  // two packed tiles of one KV head's group, one key range
     head[0] = head[1] = blockIdx.y;
-    mtile[0] = 0;
-    mtile[1] = 1;
+    mtile[0] = 2 * tpair;
+    mtile[1] = 2 * tpair + 1;
   } else if (a.pair_heads) {
     const int m = gridDim.x - 1 - blockIdx.x;  // heaviest (last) query tiles first
     head[0] = 2 * blockIdx.y;
@@ -1261,17 +1265,20 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     ptx::tmem_dealloc(tmem, G::TMEM_COLS);
   }
   if constexpr (SPLITKV) {
-    // The group's last CTA to finish merges all splits' partials and resets the
-    // count.  Every CTA reaches this point exactly once (waits are bounded), so
-    // the count always completes and is left at 0 for the next launch.
-    int* count = pa.split_count + (int64_t)b * pa.num_kv_heads + blockIdx.y;
-    if (threadIdx.x == 0) ctl->last_cta = atomicAdd(count, 1) == (int)gridDim.x - 1;
+    // The last CTA to finish among the splits of one (sequence, KV head, tile
+    // pair) merges their partials for the pair's rows and resets the count.
+    // Every CTA reaches this point exactly once (waits are bounded), so the
+    // count always completes and is left at 0 for the next launch.
+    int* count = pa.split_count +
+                 ((int64_t)b * pa.num_kv_heads + blockIdx.y) * pa.tile_pairs + tpair;
+    if (threadIdx.x == 0) ctl->last_cta = atomicAdd(count, 1) == splits - 1;
     __syncthreads();
     if (ctl->last_cta) {
       __threadfence();
       // the Q and K/V tiles are idle now: scratch for the merge's weights
-      merge_splits<T, D>(a, pa, b, blockIdx.y, gridDim.x, reinterpret_cast<float*>(sQ),
-                         (kSlots + G::NS) * G::TILE_BYTES / 4);
+      const int r0 = tpair * 2 * BM;
+      merge_splits<T, D>(a, pa, b, blockIdx.y, splits, r0, min(a.q_len, r0 + 2 * BM) - r0,
+                         reinterpret_cast<float*>(sQ), (kSlots + G::NS) * G::TILE_BYTES / 4);
       if (threadIdx.x == 0) *count = 0;
     }
   }
@@ -1478,6 +1485,7 @@ static void decode_args(const KvbPrefillParams& p, int splits, int split_tiles, 
   sp->lf_bs = p.lse_batch_stride;
   sp->lf_hs = p.lse_head_stride;
   sp->group_heads = group;
+  sp->tile_pairs = (packed + 2 * BM - 1) / (2 * BM);
 }
 
 template <typename T, int D>
@@ -1511,8 +1519,8 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
       return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured_device = dev;
   }
-  cudaError_t e = launch_pdl(kern, dim3(splits, p.num_kv_heads, p.batch), Roles<false>::kThreads,
-                             G::SMEM_BYTES, stream, tq, tk, tv, a, sp);
+  cudaError_t e = launch_pdl(kern, dim3(splits * sp.tile_pairs, p.num_kv_heads, p.batch),
+                             Roles<false>::kThreads, G::SMEM_BYTES, stream, tq, tk, tv, a, sp);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(KVB_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
   return KVB_OK;
@@ -1818,17 +1826,18 @@ static int validate_decode(const KvbPrefillParams& p, int splits) {
   if (p.q_len < 1 || p.kv_len < p.q_len)
     return fail(KVB_ERR_INVALID, "split decode needs 1 <= q_len <= kv_len");
   const int group = p.num_q_heads / p.num_kv_heads;
-  if ((int64_t)group * p.q_len > 2 * BM)
-    return fail(KVB_ERR_UNSUPPORTED, "split decode packs (q heads per KV head) * q_len <= 256 rows");
-  if (p.q_len > 1 && (p.q_head_stride != (int64_t)p.q_len * p.q_row_stride ||
-                      p.o_head_stride != (int64_t)p.q_len * p.o_row_stride))
-    return fail(KVB_ERR_INVALID, "with q_len > 1 the rows of a head must be contiguous "
-                                 "(head stride = q_len * row stride) in q and o");
-  if (p.q_len == 1 && p.o_head_stride % 8)
-    return fail(KVB_ERR_INVALID, "o head stride must be a multiple of 8 elements");
-  if ((int64_t)p.batch * p.num_kv_heads > KVB_DECODE_COUNTER_BYTES / 4)
-    return fail(KVB_ERR_UNSUPPORTED, "split decode takes batch * num_kv_heads <= " +
-                                         std::to_string(KVB_DECODE_COUNTER_BYTES / 4));
+  const int64_t packed = (int64_t)group * p.q_len;
+  if (packed > (int64_t)1 << 24)
+    return fail(KVB_ERR_UNSUPPORTED, "split-key attention packs (q heads per KV head) * q_len "
+                                     "<= 2^24 rows");
+  if (p.q_len > 1 && p.q_head_stride != (int64_t)p.q_len * p.q_row_stride)
+    return fail(KVB_ERR_INVALID, "with q_len > 1 the rows of a head must be contiguous in q "
+                                 "(head stride = q_len * row stride)");
+  const int64_t pairs = (packed + 2 * BM - 1) / (2 * BM);
+  if ((int64_t)p.batch * p.num_kv_heads * pairs > KVB_DECODE_COUNTER_BYTES / 4)
+    return fail(KVB_ERR_UNSUPPORTED,
+                "split-key attention takes batch * num_kv_heads * ceil(packed rows / 256) <= " +
+                    std::to_string(KVB_DECODE_COUNTER_BYTES / 4));
   return KVB_OK;
 }
 

@@ -171,25 +171,14 @@ def kvboost_attention_forward(module: torch.nn.Module, query: torch.Tensor, key:
     else:
         is_causal = is_causal if is_causal is not None else getattr(module, "is_causal", True)
         causal = bool(is_causal) and q_len > 1
-    group = query.size(1) // key.size(1)
-    if q_len <= DECODE_MAX_Q and q_len * group <= 256 and kv_len >= DECODE_MIN_KV:
-        # decode steps and short seams: GQA heads packed per key tile, keys split
-        from .ops import decode_attention
-        if q_len == 1:   # one row per head: [B, 1, H, D] storage is already head-contiguous
-            out = torch.empty(query.size(0), 1, query.size(1), query.size(3), dtype=query.dtype,
-                              device=query.device).transpose(1, 2)
-        else:            # the packed rows of a head must be contiguous
-            out = None
-        out, _ = decode_attention(query, key, value, float(scaling), causal, out=out,
-                                  return_lse=False)
-        return out.transpose(1, 2), None
+    # decode steps, seams and short suffixes over long prefixes go to the
+    # split-key kernel inside prefill_attention (ops.split_key_plan)
     out, _ = prefill_attention(query, key, value, float(scaling), causal, return_lse=False,
                                out_layout="bshd")
     return out, None
 
 
-DECODE_MAX_Q = 16     # query rows per head up to which the split-key decode path is used
-DECODE_MIN_KV = 256   # ... when there are at least this many keys
+DECODE_MAX_Q = 16     # paged pools: query rows per step up to which attention reads the pool
 
 
 # ── HuggingFace module patching ───────────────────────────────────────────────

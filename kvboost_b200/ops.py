@@ -108,6 +108,13 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device) if return_lse else None
     if B == 0 or Sq == 0:
         return (out.transpose(1, 2) if out_layout == "bshd" else out), lse
+    use_split, splits = split_key_plan(B, Hq, Hkv, Sq, Skv)
+    if use_split:
+        # few query tiles over many keys: GQA heads packed per key tile, keys
+        # split over CTAs (same results; see split_key_plan)
+        o, l = decode_attention(q, k, v, softmax_scale, causal, out=out, return_lse=return_lse,
+                                num_splits=splits, top_left=top_left)
+        return (o.transpose(1, 2) if out_layout == "bshd" else o), l
 
     p = _lib.KvbPrefillParams()
     p.dtype = _DTYPES[q.dtype]
@@ -191,27 +198,61 @@ def prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 _decode_ws = {}
 
 
-def decode_splits(batch: int, num_kv_heads: int, kv_len: int, num_sms: int = 148) -> int:
+def decode_splits(batch: int, num_kv_heads: int, kv_len: int, num_sms: int = 148,
+                  packed_rows: int = 1) -> int:
     """Key-range splits for one wave of CTAs (one per SM), at least two 128-key tiles
     per split: a CTA's fixed cost (setup, first tile, epilogue) is several tiles'
     worth, so a second wave or one-tile splits cost more than they parallelise
-    (measured on B200 for batch 1-32, 2-8 KV heads, 2K-16K keys)."""
+    (measured on B200 for batch 1-32, 2-8 KV heads, 2K-16K keys).  ``packed_rows``
+    = query heads per KV head x query rows; each 256 of them take one CTA per split."""
     tiles = (kv_len + 127) // 128
-    return max(1, min(num_sms // max(1, batch * num_kv_heads), tiles // 2))
+    pairs = (packed_rows + 255) // 256
+    return max(1, min(num_sms // max(1, batch * num_kv_heads * pairs), tiles // 2))
+
+
+def split_key_plan(B: int, Hq: int, Hkv: int, Sq: int, Skv: int, num_sms: int = 148):
+    """Whether the split-key kernel beats the one-CTA-per-query-tile-pair prefill
+    kernel for this shape, and with how many key splits.
+
+    Cost model in key-tile periods of the slowest wave: the prefill kernel gives
+    each CTA two 128-row query tiles (two heads of a GQA pair, or two tiles of one
+    head) and all their key tiles; the split-key kernel packs the GQA heads' rows
+    (two 128-row tiles per CTA) and splits the keys so that one wave fills the
+    SMs, plus about two periods for the partials' merge.  Short suffixes over long
+    reused prefixes (decode, seams, short reuse prefills) take the split-key
+    kernel; everything with enough query tiles to fill the GPU keeps the prefill
+    kernel."""
+    if Sq > Skv or Sq < 1:
+        return False, 1
+    cdiv = lambda a, b: -(-a // b)
+    kt = cdiv(Skv, 128)
+    group = Hq // Hkv
+    if group % 2 == 0:
+        dense_ctas = B * (Hq // 2) * cdiv(Sq, 128)
+    else:
+        dense_ctas = B * Hq * cdiv(cdiv(Sq, 128), 2)
+    dense = cdiv(dense_ctas, num_sms) * kt
+    per_split = B * Hkv * cdiv(group * Sq, 256)
+    if per_split > 16384:          # completion counters in the workspace header
+        return False, 1
+    splits = decode_splits(B, Hkv, Skv, num_sms, group * Sq)
+    split = cdiv(per_split * splits, num_sms) * cdiv(kt, splits) + 2
+    return split < 0.75 * dense, splits
 
 
 def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                      softmax_scale: Optional[float] = None, causal: bool = True,
                      out: Optional[torch.Tensor] = None, return_lse: bool = True,
                      num_splits: Optional[int] = None, top_left: bool = False):
-    """Attention for a few queries per head over many keys (decode, q = 1, and the
-    selective-recompute seams, q <= 16): ``kvb_decode_fwd``.
+    """Split-key attention for few queries per head over many keys (decode, q = 1,
+    the selective-recompute seams and short reuse suffixes): ``kvb_decode_fwd``.
 
     Same contract as ``prefill_attention`` (q ``[B, Hq, Sq, D]``, k/v ``[B, Hkv, Skv, D]``,
-    bottom-right causal), restricted to (Hq / Hkv) * Sq <= 256 and Sq <= Skv.  The
-    query heads of a GQA group are packed as rows of one tile so that each key tile
-    is read once per group, and the key range is split over CTAs (one wave); a
-    second pass merges the partial results by their LSE.
+    bottom-right causal), restricted to Sq <= Skv.  The query heads of a GQA group
+    are packed as rows (two 128-row tiles per CTA) so that each key tile is read
+    once per group and tile pair, and the key range is split over CTAs (one
+    wave); the last CTA of each group's splits merges the partial results by
+    their LSE in the same launch.
     """
     _check_tensor("q", q, 4)
     _check_tensor("k", k, 4)
@@ -230,7 +271,7 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         out = torch.empty(B, Hq, Sq, D, dtype=q.dtype, device=q.device)
     lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device) if return_lse else None
     if num_splits is None:
-        num_splits = decode_splits(B, Hkv, Skv)
+        num_splits = decode_splits(B, Hkv, Skv, packed_rows=(Hq // Hkv) * Sq)
     p = _lib.KvbPrefillParams()
     p.dtype = _DTYPES[q.dtype]
     p.head_dim, p.batch, p.num_q_heads, p.num_kv_heads = D, B, Hq, Hkv

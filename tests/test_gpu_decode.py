@@ -106,3 +106,42 @@ def test_one_query_split_counts_agree():
     c = _case(2, 16, 2, 1, 3000, 128, torch.bfloat16, seed=15, splits=24)
     assert (a.float() - b.float()).abs().max().item() <= 2e-2
     assert (a.float() - c.float()).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Skv,D,dtype,splits", [
+    (2, 32, 4, 64, 1500, 128, torch.bfloat16, None),   # 512 packed rows: two tile pairs
+    (1, 16, 2, 100, 2000, 128, torch.bfloat16, 3),     # 800 rows: last pair 32 rows
+    (1, 4, 4, 300, 2100, 96, torch.float16, None),     # MHA, 300 rows: 256 + 44
+    (2, 8, 2, 80, 700, 64, torch.float16, 1),          # one split: merge of one partial
+])
+def test_packed_tile_pairs(B, Hq, Hkv, Sq, Skv, D, dtype, splits):
+    """More packed rows than one CTA's two tiles: CTAs per (tile pair, key split),
+    each pair's partials merged by its own last CTA."""
+    _case(B, Hq, Hkv, Sq, Skv, D, dtype, seed=Sq + Skv, splits=splits)
+    _case(1, Hq, Hkv, Sq, Skv, D, dtype, seed=Sq + 1, splits=splits, top_left=True)
+    _case(1, Hq, Hkv, Sq, Skv, D, dtype, seed=Sq + 2, splits=splits, causal=False)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Skv,layout", [
+    (8, 16, 2, 16, 4096, "bhsd"),     # selective-recompute seam shape of the config-3 model
+    (2, 32, 8, 64, 6000, "bshd"),     # short reuse suffix, HF output layout
+    (1, 32, 32, 16, 8192, "bhsd"),    # MHA short suffix (config-4 short requests)
+])
+def test_prefill_routes_short_suffix(B, Hq, Hkv, Sq, Skv, layout):
+    """prefill_attention sends short suffixes over long prefixes to the split-key
+    kernel (split_key_plan); results as the oracle, output in the asked layout."""
+    from kvboost_b200.ops import prefill_attention, split_key_plan
+    assert split_key_plan(B, Hq, Hkv, Sq, Skv)[0]
+    g = torch.Generator().manual_seed(Sq * B)
+    q = torch.randn(B, Hq, Sq, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, Skv, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, Skv, 128, generator=g).to(torch.bfloat16)
+    o, lse = prefill_attention(q.cuda(), k.cuda(), v.cuda(), None, True, out_layout=layout)
+    torch.cuda.synchronize()
+    if layout == "bshd":
+        assert o.shape == (B, Sq, Hq, 128) and o.is_contiguous()
+        o = o.transpose(1, 2)
+    o_ref, lse_ref = oattn.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                     1.0 / math.sqrt(128), True, compute_dtype=np.float32)
+    assert np.abs(o.float().cpu().numpy() - o_ref).max() <= 2e-2
+    assert np.abs(lse.cpu().numpy() - lse_ref).max() <= 2e-3
