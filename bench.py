@@ -22,12 +22,16 @@ reference's metric is defined on; the public datasets are not available):
   split across ranks (strong scaling; each rank holds its heads' pool shard).
 
 * ``decode`` -- decode attention of the config-3 model: batch 8, 16 query / 2
-  KV heads, D 128, one query row over 4096 keys (split-key kernel + combine).
+  KV heads, D 128, one query row over 4096 keys (split-key kernel; each group's
+  last CTA merges the partials in the same launch).
 * ``quantize_store`` -- quantise-on-store of the config-3 warm: 24 chunks x
   128 tokens x 36 layers x 2 KV heads x D 128 bf16 into the int8 block pool
   (GB/s; one launch per chunk).
 * ``cacheblend`` -- CacheBlend repair of a 3072-position stitched prefix of the
   config-3 model (deviation over 36 layers, top 15 %, patch; GB/s; 3 launches).
+* ``short_suffix`` -- reuse-dominated short-suffix prefill: 16 new tokens over a
+  32768-token reused prefix, batch 8, 16 query / 2 KV heads, D 128 (the config-3
+  model's seam shape; split-key kernel through ``prefill_attention``; GB/s).
 
 One step = one kernel launch over one batch (the last two: one chunk store per
 chunk, and the repair's three launches).  K steps are captured in one
@@ -83,7 +87,7 @@ def parse():
     ap.add_argument("--workload", default="reuse_prefill",
                     choices=["reuse_prefill", "causal_op", "varlen_d96", "paged_long",
                              "ttft_reuse", "paged_long_cp", "decode", "quantize_store",
-                             "cacheblend"])
+                             "cacheblend", "short_suffix"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kv-bits", type=int, default=16, choices=[16, 8],
                     help="ttft_reuse: the engine's chunk store (8: KIVI int8 block pool, "
@@ -215,7 +219,7 @@ class Decode(Dense):
         super().__init__("decode", 8, 16, 2, 1, 4095, 128, "bf16",
                          "decode attention: B8 Hq16/Hkv2 D128 bf16, 1 query row over 4096 keys")
         self.bound = "hbm"
-        self.launches_per_step = 2    # split-key pass + LSE combine
+        self.launches_per_step = 1    # split-key kernel; each group's last CTA merges the partials
 
     def setup(self, torch, dev, rank, world):
         from kvboost_b200 import ops
@@ -250,6 +254,65 @@ class Decode(Dense):
         def step(slot=0):
             dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
             o, _ = ops.decode_attention(dq, dk, dv, scale, True, return_lse=False)
+            ho[slot].copy_(o, non_blocking=True)
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+        return step, h2d, ho[0].numel() * ho[0].element_size()
+
+
+class ShortSuffix(Dense):
+    """Reuse-dominated short-suffix prefill: the selective-recompute seam shape of the
+    config-3 model (16 query heads over 2 KV heads, D 128, bf16, 16 new tokens) over a
+    32 768-token reused prefix, batch 8, through ``prefill_attention`` (which takes the
+    split-key kernel for it).  HBM-bound: every launch streams the reused K/V once."""
+
+    def __init__(self):
+        super().__init__("short_suffix", 8, 16, 2, 16, 32768, 128, "bf16",
+                         "short-suffix reuse prefill: B8 Hq16/Hkv2 D128 bf16, 16 new tokens "
+                         "over a 32768-token reused prefix (split-key kernel)")
+        self.bound = "hbm"
+        self.launches_per_step = 2    # split-key kernel + merge of its 128-row partials
+
+    def setup(self, torch, dev, rank, world):
+        from kvboost_b200 import ops
+        self.dt = torch.bfloat16
+        g = torch.Generator(device=dev).manual_seed(99 + rank)
+        R = max(2, math.ceil(2 * L2_BYTES / self.bytes()))
+        self.sets_desc = f"inputs rotate over {R} sets ({R * self.bytes() / 2**20:.0f} MiB > L2)"
+        sets = []
+        for _ in range(R):
+            q = torch.randn(self.B, self.Hq, self.Sq, self.D, generator=g, device=dev).to(self.dt)
+            k = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(self.dt)
+            v = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(self.dt)
+            sets.append((q, k, v, torch.empty_like(q)))
+        scale = 1.0 / math.sqrt(self.D)
+
+        def step(i):
+            q, k, v, o = sets[i % R]
+            ops.prefill_attention(q, k, v, scale, True, out=o, return_lse=False)
+        return step
+
+    def e2e(self, torch, dev):
+        """The reused prefix's K/V is device-resident (the chunk store); each step
+        uploads the suffix's Q and its 16 new K/V rows into the cache tail, runs the
+        public op and reads O back."""
+        from kvboost_b200 import ops
+        g = torch.Generator().manual_seed(17)
+        hq = torch.randn(self.B, self.Hq, self.Sq, self.D, generator=g).to(self.dt).pin_memory()
+        hk = torch.randn(self.B, self.Hkv, self.Sq, self.D, generator=g).to(self.dt).pin_memory()
+        hv = torch.randn(self.B, self.Hkv, self.Sq, self.D, generator=g).to(self.dt).pin_memory()
+        caches = [(torch.randn(self.B, self.Hkv, self.kv, self.D, device=dev).to(self.dt),
+                   torch.randn(self.B, self.Hkv, self.kv, self.D, device=dev).to(self.dt))
+                  for _ in range(2)]   # one per e2e stream slot
+        ho = [torch.empty(self.B, self.Hq, self.Sq, self.D, dtype=self.dt).pin_memory()
+              for _ in range(2)]
+        scale = 1.0 / math.sqrt(self.D)
+
+        def step(slot=0):
+            dk, dv = caches[slot]
+            dk[:, :, self.P:].copy_(hk, non_blocking=True)
+            dv[:, :, self.P:].copy_(hv, non_blocking=True)
+            dq = hq.to(dev, non_blocking=True)
+            o, _ = ops.prefill_attention(dq, dk, dv, scale, True, return_lse=False)
             ho[slot].copy_(o, non_blocking=True)
         h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
         return step, h2d, ho[0].numel() * ho[0].element_size()
@@ -1082,6 +1145,8 @@ def make_workload(name, small=False):
         return QuantizeStore()
     if name == "cacheblend":
         return CacheBlendRepair()
+    if name == "short_suffix":
+        return ShortSuffix()
     return PagedLong(small)
 
 

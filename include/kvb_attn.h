@@ -144,8 +144,9 @@ int kvb_prefill_fwd(const KvbPrefillParams* params, void* stream);
  * heads sharing a KV head are packed as rows ((q heads per KV head) * q_len
  * of them, two 128-row tiles per CTA), so every key tile is read once per
  * group and tile pair, and the key range is split over num_splits CTAs; the
- * last CTA of each (sequence, KV head, tile pair) to finish merges the
- * partial outputs by their LSE (one launch).  workspace: device memory of at
+ * partial outputs are merged by their LSE, for groups of up to 32 packed rows
+ * by the last CTA of each (sequence, KV head, tile pair) to finish (one
+ * launch), else by a second launch.  workspace: device memory of at
  * least kvb_decode_workspace_bytes(params, num_splits) bytes (-1: invalid
  * params, reason in kvb_last_error), 16-byte aligned.  Its first
  * KVB_DECODE_COUNTER_BYTES hold the completion counters: zero them once

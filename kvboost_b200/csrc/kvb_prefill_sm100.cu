@@ -113,6 +113,9 @@ struct Geo {
   static constexpr int ATOM_BYTES = 128 * 128;   // 128 rows x 128 bytes
   static constexpr int TILE_BYTES = NATOM * ATOM_BYTES;
   static constexpr int NS = (D <= 64) ? 4 : 2;   // K/V ring depth
+  // K ring depth of the split-key dual mode: both slots read slot 0's Q tile,
+  // so slot 1's Q buffer is one more K stage when the ring has two.
+  static constexpr int KSD = (NS == 2) ? 3 : NS;
   static constexpr int TMEM_COLS = 512;          // S0 S1 O0 O1, 128 columns each
   static constexpr int QK_STEPS = D / 16;        // K-steps of S = Q K^T
   static constexpr int PV_STEPS = BN / 16;       // K-steps of O += P V
@@ -179,6 +182,8 @@ struct PagedArgs {
       int64_t of_bs, of_hs, of_rs, lf_bs, lf_hs;
       int group_heads;        // query heads per KV head
       int tile_pairs;         // 256-row pairs of packed tiles per group (grid x = splits * pairs)
+      int dual;               // 1: one packed tile; slot s of CTA c takes key split 2c + s
+      int merge_in_kernel;    // 1: each group's last CTA merges; 0: kvb_split_merge_kernel does
     };
   };
   int max_blocks;
@@ -189,9 +194,12 @@ struct PagedArgs {
   // Split-key decode (the dense SPLITKV kernels, which read no pool and carry
   // these here: growing DenseArgs measurably slowed every dense launch): query
   // rows are a GQA group's heads packed as (head, row) with rows_per_head rows
-  // each; CTA x takes packed tiles 2p, 2p + 1 (p = x / splits) and key tiles
-  // [s * split_tiles, (s + 1) * split_tiles) (s = x % splits), and writes its
-  // normalised partial O / LSE at o + s * o_split_stride, lse + s * lse_split_stride.
+  // each; CTA x takes packed tiles 2p, 2p + 1 (p = x / c, c CTAs per tile
+  // pair) and key tiles [s * split_tiles, (s + 1) * split_tiles) (s = x % c),
+  // and writes its normalised partial O / LSE at o + s * o_split_stride,
+  // lse + s * lse_split_stride.  With dual set (all packed rows in one tile),
+  // both slots take that tile and slot t takes key split s = 2 (x % c) + t, so
+  // that one CTA runs two independent key ranges in ping-pong.
   int rows_per_head;
   int split_tiles;
   int64_t o_split_stride, lse_split_stride;
@@ -692,20 +700,32 @@ __device__ __forceinline__ void merge_splits(const DenseArgs& a, const PagedArgs
     if (staged) {
       mx = row_mx[r];
       inv = row_inv[r];
-#pragma unroll 4
-      for (int sp = 0; sp < splits; ++sp) {
-        const float wt = w[sp * packed + r];
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(o_part + sp * pa.o_split_stride + row * D + ch * 8));
-        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+      // Eight partials' loads in flight per thread before any is used: one CTA
+      // merges a whole tile pair, so its L2 latency, not bandwidth, sets the pace.
+      constexpr int MB = 8;
+#pragma unroll 1
+      for (int sp0 = 0; sp0 < splits; sp0 += MB) {
+        uint4 v[MB];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float2 f;
-          if constexpr (std::is_same<T, __half>::value)
-            f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
-          else
-            f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
-          acc[2 * e] += wt * f.x;
-          acc[2 * e + 1] += wt * f.y;
+        for (int u = 0; u < MB; ++u)
+          if (sp0 + u < splits)
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(
+                o_part + (int64_t)(sp0 + u) * pa.o_split_stride + row * D + ch * 8));
+#pragma unroll
+        for (int u = 0; u < MB; ++u) {
+          if (sp0 + u >= splits) break;
+          const float wt = w[(sp0 + u) * packed + r];
+          const uint32_t wv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 f;
+            if constexpr (std::is_same<T, __half>::value)
+              f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
+            else
+              f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
+            acc[2 * e] += wt * f.x;
+            acc[2 * e + 1] += wt * f.y;
+          }
         }
       }
     } else {
@@ -744,6 +764,85 @@ __device__ __forceinline__ void merge_splits(const DenseArgs& a, const PagedArgs
       pa.lse_final[(int64_t)b * pa.lf_bs + (int64_t)head * pa.lf_hs + i] =
           inv > 0.f ? mx + __logf(1.f / inv) : -INFINITY;
   }
+}
+
+// Merge of split-key partials as its own launch, for groups with many packed
+// rows: the in-kernel merge is one CTA per group whose loads pay a dependent
+// L2 round trip per batch of splits.  One thread per (packed row, 8 features)
+// of every group: LSE-weighted sum of the row's partials, online over batches
+// of 16 splits (a running maximum keeps the weights in range), written through
+// the caller's strides; ch == 0 threads also write the merged LSE.  Launched
+// with programmatic dependent launch after the split kernel.
+template <typename T, int D>
+__global__ void __launch_bounds__(256)
+    kvb_split_merge_kernel(const DenseArgs a, const PagedArgs pa, int splits, int64_t rows) {
+  ptx::griddep_wait();
+  constexpr int NCH = D / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * NCH) return;
+  const int64_t row = idx / NCH;                   // [batch][num_kv_heads][packed]
+  const int ch = (int)(idx - row * NCH);
+  const int packed = a.q_len;
+  const int r = (int)(row % packed);
+  const int64_t bg = row / packed;
+  const int g = (int)(bg % pa.num_kv_heads);
+  const int b = (int)(bg / pa.num_kv_heads);
+  const T* o_part = reinterpret_cast<const T*>(a.o);
+  constexpr int MB = 16;
+  float m = -INFINITY, sum = 0.f;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int sp0 = 0; sp0 < splits; sp0 += MB) {
+    float l[MB];
+    uint4 v[MB];
+#pragma unroll
+    for (int u = 0; u < MB; ++u) {
+      l[u] = -INFINITY;
+      if (sp0 + u < splits) {
+        l[u] = __ldcg(a.lse + (int64_t)(sp0 + u) * pa.lse_split_stride + row);
+        v[u] = __ldcg(reinterpret_cast<const uint4*>(
+            o_part + (int64_t)(sp0 + u) * pa.o_split_stride + row * D + ch * 8));
+      }
+    }
+    float bm = m;
+#pragma unroll
+    for (int u = 0; u < MB; ++u) bm = fmaxf(bm, l[u]);
+    if (bm == -INFINITY) continue;                  // no keys in any split so far
+    const float c = __expf(m - bm);                 // 0 when m is still -inf
+    sum *= c;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] *= c;
+    m = bm;
+#pragma unroll
+    for (int u = 0; u < MB; ++u) {
+      if (sp0 + u >= splits || l[u] == -INFINITY) continue;
+      const float wt = __expf(l[u] - m);
+      sum += wt;
+      const uint32_t wv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f;
+        if constexpr (std::is_same<T, __half>::value)
+          f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
+        else
+          f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
+        acc[2 * e] += wt * f.x;
+        acc[2 * e + 1] += wt * f.y;
+      }
+    }
+  }
+  const float inv = sum > 0.f ? 1.f / sum : 0.f;
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) o[e] = pack2<T>(acc[2 * e] * inv, acc[2 * e + 1] * inv);
+  const int head = g * pa.group_heads + r / pa.rows_per_head;
+  const int i = r % pa.rows_per_head;
+  T* dst = reinterpret_cast<T*>(pa.o_final) + (int64_t)b * pa.of_bs + (int64_t)head * pa.of_hs +
+           (int64_t)i * pa.of_rs + ch * 8;
+  *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+  if (pa.lse_final != nullptr && ch == 0)
+    pa.lse_final[(int64_t)b * pa.lf_bs + (int64_t)head * pa.lf_hs + i] =
+        sum > 0.f ? m + __logf(sum) : -INFINITY;
 }
 
 template <typename T, int D, bool PAGED, bool SPLITKV = false>
@@ -785,9 +884,11 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       ptx::mbar_init(bar(BAR_O_FULL + sl), 1);
     }
     ptx::mbar_init(bar(BAR_DRAIN), 1);
-    for (int st = 0; st < G::NS; ++st) {
+    for (int st = 0; st < G::KSD; ++st) {
       ptx::mbar_init(bar(BAR_K_FULL + st), PAGED ? Roles<PAGED>::kConvWarps : 1);
       ptx::mbar_init(bar(BAR_K_EMPTY + st), 1);
+    }
+    for (int st = 0; st < G::NS; ++st) {
       ptx::mbar_init(bar(BAR_V_FULL + st), PAGED ? Roles<PAGED>::kConvWarps : 1);
       ptx::mbar_init(bar(BAR_V_EMPTY + st), 1);
     }
@@ -806,13 +907,18 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   // ---- work item: two query tiles sharing one KV head ---------------------
   const int b = blockIdx.z;
   int head[kSlots], mtile[kSlots];
-  const int splits = SPLITKV ? (int)gridDim.x / pa.tile_pairs : 1;
-  const int split = SPLITKV ? (int)blockIdx.x % splits : 0;
-  const int tpair = SPLITKV ? (int)blockIdx.x / splits : 0;
-  if (SPLITKV) {  // two packed tiles of one KV head's group, one key range
+  const bool dual = SPLITKV && pa.dual;
+  const int ctas = SPLITKV ? (int)gridDim.x / pa.tile_pairs : 1;  // CTAs per tile pair
+  const int csplit = SPLITKV ? (int)blockIdx.x % ctas : 0;
+  const int tpair = SPLITKV ? (int)blockIdx.x / ctas : 0;
+  const int splits = dual ? 2 * ctas : ctas;                      // partial results per row
+  int vsplit[kSlots];                                              // key split of each slot
+  vsplit[0] = dual ? 2 * csplit : csplit;
+  vsplit[1] = dual ? 2 * csplit + 1 : csplit;
+  if (SPLITKV) {  // two packed tiles of one KV head's group (or one tile twice), one key range each
     head[0] = head[1] = blockIdx.y;
-    mtile[0] = 2 * tpair;
-    mtile[1] = 2 * tpair + 1;
+    mtile[0] = dual ? 0 : 2 * tpair;
+    mtile[1] = dual ? 0 : 2 * tpair + 1;
   } else if (a.pair_heads) {
     const int m = gridDim.x - 1 - blockIdx.x;  // heaviest (last) query tiles first
     head[0] = 2 * blockIdx.y;
@@ -841,8 +947,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   }
   // causal 1: bottom-right (j <= i + kv_len - q_len); 2: top-left (j <= i)
   const int off = (a.causal == 2) ? 0 : kv_len - (SPLITKV ? pa.rows_per_head : q_len);
-  int q0[kSlots], q_rows[kSlots], n_t[kSlots];
-  const int jbase = SPLITKV ? split * pa.split_tiles : 0;   // first key tile of this CTA
+  int q0[kSlots], q_rows[kSlots], n_t[kSlots], jbase[kSlots];   // jbase: first key tile
 #pragma unroll
   for (int sl = 0; sl < kSlots; ++sl) {
     q0[sl] = mtile[sl] * BM;
@@ -850,10 +955,19 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     int kv_end = (a.causal && !SPLITKV) ? min(kv_len, q0[sl] + q_rows[sl] + off) : kv_len;
     kv_end = max(kv_end, 0);
     n_t[sl] = q_rows[sl] > 0 ? (kv_end + BN - 1) / BN : 0;
-    if (SPLITKV) n_t[sl] = max(0, min(n_t[sl] - jbase, pa.split_tiles));
+    jbase[sl] = SPLITKV ? vsplit[sl] * pa.split_tiles : 0;
+    if (SPLITKV) n_t[sl] = max(0, min(n_t[sl] - jbase[sl], pa.split_tiles));
   }
   if (q_rows[0] == 0 && q_rows[1] == 0) return;  // uniform, before TMEM or any barrier wait
   const int n_max = max(n_t[0], n_t[1]);
+  // Position of slot s's key tile j in the K/V load sequence: the step j when
+  // both slots read the same tile; in dual mode the loads alternate between
+  // the slots while both have tiles (2j + s), then slot 0's continue in order
+  // (slot 1 never has more tiles than slot 0).  Producer and consumers derive
+  // ring stages and phases from it, so every stage is used in sequence.
+  auto ring_pos = [&](int s, int j) -> int {
+    return !dual ? j : (j < n_t[1] ? 2 * j + s : n_t[1] + j);
+  };
 
   if (warp == kWarpMma) {
     ptx::tmem_alloc(ptx::smem_u32(&ctl->tmem_base), G::TMEM_COLS);
@@ -923,44 +1037,73 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
                            at * 64, q_base + q0[sl], head[sl], tb, bar(BAR_Q_FULL + sl));
       };
       load_q(0);
-      int issued = 0;
+      // Ring position r = ring_pos(slot, j): stage r % depth, phase (r / depth) & 1,
+      // the K ring KSD deep in dual mode (its last stage in slot 1's Q buffer).
+      const int per = dual ? 2 : 1;
+      const int ks = dual ? G::KSD : G::NS;
+      int last_k[4], last_v[4];   // phase of each stage's last issued load
+#pragma unroll
+      for (int i = 0; i < 4; ++i) last_k[i] = last_v[i] = -1;
+      bool go = true;
 #pragma unroll 1
-      for (int j = 0; j < n_max; ++j) {
-        const int st = j % G::NS;
-        const uint32_t ph = (j / G::NS) & 1;
-        const int ky = k_base + (jbase + j) * BN;
-        if (!wait_bar(bar(BAR_K_EMPTY + st), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
-          break;
-        if (j < 16) KVB_TRACE_AT(16 + j);
-        ptx::mbar_arrive_expect_tx(bar(BAR_K_FULL + st), G::TILE_BYTES);
+      for (int j = 0; go && j < n_max; ++j) {
+#pragma unroll 1
+        for (int t = 0; t < per; ++t) {
+          if (dual && j >= n_t[t]) continue;
+          const int r = ring_pos(t, j);
+          const int st = r % ks;
+          const uint32_t ph = (r / ks) & 1;
+          const int ky = k_base + ((dual && t) ? jbase[1] : jbase[0]) * BN + j * BN;
+          if (!wait_bar(bar(BAR_K_EMPTY + st), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT)) {
+            go = false;
+            break;
+          }
+          if (j < 16 && t == 0) KVB_TRACE_AT(16 + j);
+          ptx::mbar_arrive_expect_tx(bar(BAR_K_FULL + st), G::TILE_BYTES);
+          uint8_t* kdst = st < G::NS ? sK + st * G::TILE_BYTES : sQ + G::TILE_BYTES;
 #pragma unroll
-        for (int at = 0; at < G::NATOM; ++at)
-          ptx::tma_load_4d(ptx::smem_u32(sK + st * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_k,
-                           at * 64, ky, kvh, tb, bar(BAR_K_FULL + st));
-        if (j == 0) {
-          for (int sl = 1; sl < kSlots; ++sl) load_q(sl);
-          // V0 and the next K tiles are needed only after the first softmax:
-          // hold them back until K0 has landed, so that the first S MMAs'
-          // operands do not share DRAM bandwidth with them at launch.
-          if (!wait_bar(bar(BAR_K_FULL), 0, abort_flag, a.status, KVB_STATUS_LOAD_WAIT)) break;
+          for (int at = 0; at < G::NATOM; ++at)
+            ptx::tma_load_4d(ptx::smem_u32(kdst + at * G::ATOM_BYTES), &tm_k,
+                             at * 64, ky, kvh, tb, bar(BAR_K_FULL + st));
+          last_k[st] = (int)ph;
+          if (j == 0 && t == 0) {
+            if (!dual)
+              for (int sl = 1; sl < kSlots; ++sl) load_q(sl);
+            // V0 and the next K tiles are needed only after the first softmax:
+            // hold them back until K0 has landed, so that the first S MMAs'
+            // operands do not share DRAM bandwidth with them at launch.
+            if (!dual &&
+                !wait_bar(bar(BAR_K_FULL), 0, abort_flag, a.status, KVB_STATUS_LOAD_WAIT)) {
+              go = false;
+              break;
+            }
+          }
         }
-        if (!wait_bar(bar(BAR_V_EMPTY + st), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT))
-          break;
-        if (j < 16) KVB_TRACE_AT(32 + j);
-        ptx::mbar_arrive_expect_tx(bar(BAR_V_FULL + st), G::TILE_BYTES);
+#pragma unroll 1
+        for (int t = 0; go && t < per; ++t) {
+          if (dual && j >= n_t[t]) continue;
+          const int r = ring_pos(t, j);
+          const int st = r % G::NS;
+          const uint32_t ph = (r / G::NS) & 1;
+          const int ky = k_base + ((dual && t) ? jbase[1] : jbase[0]) * BN + j * BN;
+          if (!wait_bar(bar(BAR_V_EMPTY + st), ph ^ 1, abort_flag, a.status, KVB_STATUS_LOAD_WAIT)) {
+            go = false;
+            break;
+          }
+          if (j < 16 && t == 0) KVB_TRACE_AT(32 + j);
+          ptx::mbar_arrive_expect_tx(bar(BAR_V_FULL + st), G::TILE_BYTES);
 #pragma unroll
-        for (int at = 0; at < G::NATOM; ++at)
-          ptx::tma_load_4d(ptx::smem_u32(sV + st * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_v,
-                           at * 64, ky, kvh, tb, bar(BAR_V_FULL + st));
-        issued = j + 1;
+          for (int at = 0; at < G::NATOM; ++at)
+            ptx::tma_load_4d(ptx::smem_u32(sV + st * G::TILE_BYTES + at * G::ATOM_BYTES), &tm_v,
+                             at * 64, ky, kvh, tb, bar(BAR_V_FULL + st));
+          last_v[st] = (int)ph;
+        }
       }
       if (*abort_flag) {
-        // Drain: wait (bounded) for the loads of the last ring round to land.
-        for (int j = max(0, issued - G::NS); j < issued; ++j) {
-          const int st = j % G::NS;
-          const uint32_t ph = (j / G::NS) & 1;
-          wait_bar(bar(BAR_K_FULL + st), ph, abort_flag, nullptr, 0);
-          wait_bar(bar(BAR_V_FULL + st), ph, abort_flag, nullptr, 0);
+        // Drain: wait (bounded) for each stage's last issued loads to land.
+        for (int st = 0; st < 4; ++st) {
+          if (last_k[st] >= 0) wait_bar(bar(BAR_K_FULL + st), last_k[st], abort_flag, nullptr, 0);
+          if (last_v[st] >= 0) wait_bar(bar(BAR_V_FULL + st), last_v[st], abort_flag, nullptr, 0);
         }
       }
     }
@@ -982,10 +1125,11 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       const uint32_t v_lo = ptx::desc_lo(sVa, G::ATOM_BYTES);
       constexpr uint32_t TILE16 = G::TILE_BYTES >> 4;
 
-      auto issue_s = [&](int sl, int j) {
+      auto issue_s = [&](int sl, int j, int kst) {
         if (j < 16) KVB_TRACE_AT(48 + 96 * sl + j);
-        const uint32_t qa = q_lo + sl * TILE16;
-        const uint32_t kb = k_lo + (j % G::NS) * TILE16;
+        const uint32_t qa = q_lo + (dual ? 0 : sl) * TILE16;
+        // stage NS (dual mode only) is slot 1's Q buffer
+        const uint32_t kb = kst < G::NS ? k_lo + kst * TILE16 : q_lo + TILE16;
         const uint32_t tS = tmem + G::s_col(sl);
 #pragma unroll
         for (int kk = 0; kk < G::QK_STEPS; ++kk) {
@@ -998,9 +1142,9 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       // P of S columns [c, c+16) sits at P column (c / PC) * PC + (c % PC) / 2:
       // each softmax warpgroup packs its PC columns over the start of its own range.
       constexpr int PC = BN / Roles<PAGED>::kHalves;
-      auto issue_pv = [&](int sl, int j) {
+      auto issue_pv = [&](int sl, int j, int vst) {
         if (j < 16) KVB_TRACE_AT(96 + 96 * sl + j);
-        const uint32_t vb = v_lo + (j % G::NS) * TILE16;
+        const uint32_t vb = v_lo + vst * TILE16;
         const uint32_t tP = tmem + G::s_col(sl);
         const uint32_t tO = tmem + G::o_col(sl);
 #pragma unroll
@@ -1010,58 +1154,103 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
         if (sl == 0 && j < 16) KVB_TRACE_AT(240 + j);
       };
 
-      bool ok = wait_bar(bar(BAR_K_FULL), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
+      if (dual) {
+        // Each slot streams its own key range; slot sl's tile j sits at ring
+        // position ring_pos(sl, j) (K stage r % KSD, V stage r % NS).
+        bool ok = true;
 #pragma unroll
-      for (int sl = 0; sl < kSlots && ok; ++sl) {
-        if (n_t[sl] == 0) continue;
-        ok = wait_bar(bar(BAR_Q_FULL + sl), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
-        if (!ok) break;
-        ptx::tc_fence_after();
-        issue_s(sl, 0);
-      }
-      if (ok) ptx::mma_commit(bar(BAR_K_EMPTY));
+        for (int sl = 0; sl < kSlots && ok; ++sl) {
+          if (n_t[sl] == 0) continue;
+          ok = wait_bar(bar(BAR_K_FULL + sl), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT) &&
+               wait_bar(bar(BAR_Q_FULL), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          issue_s(sl, 0, sl);   // ring positions 0 and 1: K stages 0 and 1
+          ptx::mma_commit(bar(BAR_K_EMPTY + sl));
+        }
 #pragma unroll 1
-      for (int j = 0; ok && j < n_max; ++j) {
-        const int st = j % G::NS;
-        const uint32_t ph = (j / G::NS) & 1;
-        const int st1 = (j + 1) % G::NS;
-        const uint32_t ph1 = ((j + 1) / G::NS) & 1;
-        bool v_ready = false, k_next_ready = false;
+        for (int j = 0; ok && j < n_max; ++j) {
 #pragma unroll
-        for (int sl = 0; sl < kSlots; ++sl) {
-          if (j >= n_t[sl]) continue;
-          if (!wait_bar(bar(BAR_P_FULL + sl), j & 1, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) {
-            ok = false;
-            break;
-          }
-          if (sl == 0 && j < 16) KVB_TRACE_AT(112 + j);
-          if (!v_ready) {
-            if (!wait_bar(bar(BAR_V_FULL + st), ph, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) {
+          for (int sl = 0; sl < kSlots; ++sl) {
+            if (j >= n_t[sl]) continue;
+            const int r = ring_pos(sl, j), r1 = ring_pos(sl, j + 1);
+            const int st = r % G::NS, st1 = r1 % G::KSD;
+            const uint32_t ph = (r / G::NS) & 1, ph1 = (r1 / G::KSD) & 1;
+            if (!wait_bar(bar(BAR_P_FULL + sl), j & 1, abort_flag, a.status, KVB_STATUS_MMA_WAIT) ||
+                !wait_bar(bar(BAR_V_FULL + st), ph, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) {
               ok = false;
               break;
             }
-            v_ready = true;
-          }
-          if (sl == 0 && j < 16) KVB_TRACE_AT(128 + j);
-          ptx::tc_fence_after();
-          issue_pv(sl, j);
-          if (j + 1 < n_t[sl]) {
-            if (!k_next_ready) {
-              if (!wait_bar(bar(BAR_K_FULL + st1), ph1, abort_flag, a.status,
-                            KVB_STATUS_MMA_WAIT)) {
+            if (sl == 0 && j < 16) KVB_TRACE_AT(128 + j);
+            ptx::tc_fence_after();
+            issue_pv(sl, j, st);
+            ptx::mma_commit(bar(BAR_V_EMPTY + st));
+            if (j + 1 < n_t[sl]) {
+              if (!wait_bar(bar(BAR_K_FULL + st1), ph1, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) {
                 ok = false;
                 break;
               }
-              k_next_ready = true;
+              issue_s(sl, j + 1, st1);
+              ptx::mma_commit(bar(BAR_K_EMPTY + st1));
+            } else {
+              ptx::mma_commit(bar(BAR_O_FULL + sl));  // this slot's last PV
             }
-            issue_s(sl, j + 1);
-          } else {
-            ptx::mma_commit(bar(BAR_O_FULL + sl));  // this slot's last PV
           }
         }
-        if (!ok) break;
-        ptx::mma_commit(bar(BAR_V_EMPTY + st));
-        if (k_next_ready) ptx::mma_commit(bar(BAR_K_EMPTY + st1));
+      } else {
+        bool ok = wait_bar(bar(BAR_K_FULL), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
+#pragma unroll
+        for (int sl = 0; sl < kSlots && ok; ++sl) {
+          if (n_t[sl] == 0) continue;
+          ok = wait_bar(bar(BAR_Q_FULL + sl), 0, abort_flag, a.status, KVB_STATUS_MMA_WAIT);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          issue_s(sl, 0, 0);
+        }
+        if (ok) ptx::mma_commit(bar(BAR_K_EMPTY));
+#pragma unroll 1
+        for (int j = 0; ok && j < n_max; ++j) {
+          const int st = j % G::NS;
+          const uint32_t ph = (j / G::NS) & 1;
+          const int st1 = (j + 1) % G::NS;
+          const uint32_t ph1 = ((j + 1) / G::NS) & 1;
+          bool v_ready = false, k_next_ready = false;
+#pragma unroll
+          for (int sl = 0; sl < kSlots; ++sl) {
+            if (j >= n_t[sl]) continue;
+            if (!wait_bar(bar(BAR_P_FULL + sl), j & 1, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) {
+              ok = false;
+              break;
+            }
+            if (sl == 0 && j < 16) KVB_TRACE_AT(112 + j);
+            if (!v_ready) {
+              if (!wait_bar(bar(BAR_V_FULL + st), ph, abort_flag, a.status, KVB_STATUS_MMA_WAIT)) {
+                ok = false;
+                break;
+              }
+              v_ready = true;
+            }
+            if (sl == 0 && j < 16) KVB_TRACE_AT(128 + j);
+            ptx::tc_fence_after();
+            issue_pv(sl, j, st);
+            if (j + 1 < n_t[sl]) {
+              if (!k_next_ready) {
+                if (!wait_bar(bar(BAR_K_FULL + st1), ph1, abort_flag, a.status,
+                              KVB_STATUS_MMA_WAIT)) {
+                  ok = false;
+                  break;
+                }
+                k_next_ready = true;
+              }
+              issue_s(sl, j + 1, st1);
+            } else {
+              ptx::mma_commit(bar(BAR_O_FULL + sl));  // this slot's last PV
+            }
+          }
+          if (!ok) break;
+          ptx::mma_commit(bar(BAR_V_EMPTY + st));
+          if (k_next_ready) ptx::mma_commit(bar(BAR_K_EMPTY + st1));
+        }
       }
       // Drain: every MMA issued above completes before TMEM can be freed.
       ptx::mma_commit(bar(BAR_DRAIN));
@@ -1096,6 +1285,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     const int h = head[sl];
     const int q0s = q0[sl];
     const int n_tiles = n_t[sl];
+    const int jb = SPLITKV ? jbase[sl] : 0;
     const int qi = q0s + t;
     const float sl2 = a.scale_log2;
     constexpr float kSumLimit = std::is_same<T, __half>::value ? 32768.f : 1.0995116e12f;
@@ -1109,7 +1299,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       ptx::tc_fence_after();
       if (t == 0 && hf == 0 && j < 16) KVB_TRACE_AT(64 + 96 * sl + j);
 
-      const int kv0 = (jbase + j) * BN;
+      const int kv0 = (jb + j) * BN;
       // split decode: packed row qi is row qi % rows_per_head of its head
       const int qrow = SPLITKV ? qi % pa.rows_per_head : qi;
       const bool need_mask =
@@ -1200,10 +1390,31 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     }
     const bool row_valid = t < q_rows[sl];
     const float inv_l = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
-    T* obase = reinterpret_cast<T*>(a.o) + hf * DH + (SPLITKV ? split * pa.o_split_stride : 0) +
+    T* obase = reinterpret_cast<T*>(a.o) + hf * DH + (SPLITKV ? vsplit[sl] * pa.o_split_stride : 0) +
                (a.cu_q ? (int64_t)q_base * a.o_rs + (int64_t)h * a.o_hs
                        : (int64_t)b * a.o_bs + (int64_t)h * a.o_hs);
-    if (have_o) {
+    if (have_o && dual) {
+      // dual split-key mode: the Q tile and slot 1's Q buffer may still be read
+      // by the other slot's MMAs, so each thread stores its own row segment
+      T* orow = obase + (int64_t)qi * a.o_rs;
+#pragma unroll 1
+      for (int c = 0; c < DH; c += OCW) {
+        uint32_t r[OCW];
+        tmem_ld_cw<OCW>(tO + c, r);
+        ptx::tmem_wait_ld();
+        if (row_valid) {
+          uint32_t pk[OCW / 2];
+#pragma unroll
+          for (int i = 0; i < OCW / 2; ++i)
+            pk[i] = pack2<T>(__uint_as_float(r[2 * i]) * inv_l,
+                             __uint_as_float(r[2 * i + 1]) * inv_l);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+          for (int i = 0; i < OCW / 8; ++i)
+            dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+    } else if (have_o) {
       // The warp's 32 output row segments go through shared memory, so that the
       // global stores write whole segments (NC lanes per row) instead of one
       // 16-byte piece of 32 different rows per instruction.  The slot's Q tile
@@ -1250,7 +1461,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       if (a.cu_q)
         a.lse[(int64_t)h * a.lse_hs + q_base + qi] = lse;
       else
-        a.lse[(SPLITKV ? split * pa.lse_split_stride : 0) + (int64_t)b * a.lse_bs +
+        a.lse[(SPLITKV ? vsplit[sl] * pa.lse_split_stride : 0) + (int64_t)b * a.lse_bs +
               (int64_t)h * a.lse_hs + qi] = lse;
     }
   }
@@ -1264,14 +1475,14 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, G::TMEM_COLS);
   }
-  if constexpr (SPLITKV) {
+  if (SPLITKV && pa.merge_in_kernel) {
     // The last CTA to finish among the splits of one (sequence, KV head, tile
     // pair) merges their partials for the pair's rows and resets the count.
     // Every CTA reaches this point exactly once (waits are bounded), so the
     // count always completes and is left at 0 for the next launch.
     int* count = pa.split_count +
                  ((int64_t)b * pa.num_kv_heads + blockIdx.y) * pa.tile_pairs + tpair;
-    if (threadIdx.x == 0) ctl->last_cta = atomicAdd(count, 1) == splits - 1;
+    if (threadIdx.x == 0) ctl->last_cta = atomicAdd(count, 1) == ctas - 1;
     __syncthreads();
     if (ctl->last_cta) {
       __threadfence();
@@ -1444,6 +1655,18 @@ static int decode_split_tiles(const KvbPrefillParams& p, int splits, int* eff) {
   return st;
 }
 
+// Dual mode: all packed rows of a group fit one 128-row tile, so each CTA runs
+// two key splits, one per slot, in ping-pong (the second slot would be idle).
+static bool decode_dual(const KvbPrefillParams& p, int eff_splits) {
+  return (int64_t)(p.num_q_heads / p.num_kv_heads) * p.q_len <= BM && eff_splits >= 2;
+}
+
+// Partial results per packed row: one per key split, rounded up to even in dual
+// mode (a last CTA with one split left writes an empty second partial).
+static int decode_partials(const KvbPrefillParams& p, int eff_splits) {
+  return decode_dual(p, eff_splits) ? (eff_splits + 1) / 2 * 2 : eff_splits;
+}
+
 // Arguments shared by both split-key decode kernels: partials in the workspace
 // after its counter header, merged into params.o / params.lse by each group's
 // last CTA.
@@ -1488,6 +1711,10 @@ static void decode_args(const KvbPrefillParams& p, int splits, int split_tiles, 
   sp->tile_pairs = (packed + 2 * BM - 1) / (2 * BM);
 }
 
+// Packed rows per group up to which the split kernel's last CTA merges the
+// partials itself (decode steps); larger groups merge in kvb_split_merge_kernel.
+constexpr int kMergeInKernelRows = 32;
+
 template <typename T, int D>
 static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cudaStream_t stream) {
   using G = Geo<D>;
@@ -1495,9 +1722,15 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
   const int packed = group * p.q_len;
   int splits = 1;
   const int split_tiles = decode_split_tiles(p, splits_req, &splits);
+  const bool dual = decode_dual(p, splits);
+  const int parts = decode_partials(p, splits);
   DenseArgs a;
   PagedArgs sp;
-  decode_args(p, splits, split_tiles, ws, &a, &sp);
+  decode_args(p, parts, split_tiles, ws, &a, &sp);
+  sp.dual = dual ? 1 : 0;
+  const int packed_rows = (p.num_q_heads / p.num_kv_heads) * p.q_len;
+  sp.merge_in_kernel = packed_rows <= kMergeInKernelRows ? 1 : 0;
+  const int ctas = dual ? parts / 2 : splits;   // CTAs per (sequence, KV head, tile pair)
   const int64_t q_rs = p.q_len == 1 ? p.q_head_stride : p.q_row_stride;
   CUtensorMap tq, tk, tv;
   std::string err;
@@ -1519,8 +1752,14 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
       return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured_device = dev;
   }
-  cudaError_t e = launch_pdl(kern, dim3(splits * sp.tile_pairs, p.num_kv_heads, p.batch),
+  cudaError_t e = launch_pdl(kern, dim3(ctas * sp.tile_pairs, p.num_kv_heads, p.batch),
                              Roles<false>::kThreads, G::SMEM_BYTES, stream, tq, tk, tv, a, sp);
+  if (e == cudaSuccess && !sp.merge_in_kernel) {
+    const int64_t rows = (int64_t)p.batch * p.num_kv_heads * packed_rows;
+    const int64_t items = rows * (D / 8);
+    e = launch_pdl(kvb_split_merge_kernel<T, D>, dim3((unsigned)((items + 255) / 256)), 256, 0,
+                   stream, a, sp, parts, rows);
+  }
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(KVB_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
   return KVB_OK;
@@ -1845,7 +2084,7 @@ extern "C" int64_t kvb_decode_workspace_bytes(const KvbPrefillParams* params, in
   if (!params || validate_decode(*params, num_splits) != KVB_OK) return -1;
   int eff = 1;
   decode_split_tiles(*params, num_splits, &eff);
-  return decode_workspace_bytes(*params, eff);
+  return decode_workspace_bytes(*params, decode_partials(*params, eff));
 }
 
 extern "C" int kvb_decode_fwd(const KvbPrefillParams* params, int num_splits, void* workspace,
@@ -1856,7 +2095,7 @@ extern "C" int kvb_decode_fwd(const KvbPrefillParams* params, int num_splits, vo
   if (rc != KVB_OK) return rc;
   int eff = 1;
   decode_split_tiles(p, num_splits, &eff);
-  const int64_t need = decode_workspace_bytes(p, eff);
+  const int64_t need = decode_workspace_bytes(p, decode_partials(p, eff));
   if (!workspace || !aligned16(workspace) || workspace_bytes < need)
     return fail(KVB_ERR_INVALID, "workspace must hold " + std::to_string(need) + " bytes");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

@@ -204,10 +204,12 @@ def decode_splits(batch: int, num_kv_heads: int, kv_len: int, num_sms: int = 148
     per split: a CTA's fixed cost (setup, first tile, epilogue) is several tiles'
     worth, so a second wave or one-tile splits cost more than they parallelise
     (measured on B200 for batch 1-32, 2-8 KV heads, 2K-16K keys).  ``packed_rows``
-    = query heads per KV head x query rows; each 256 of them take one CTA per split."""
+    = query heads per KV head x query rows; each 256 of them take one CTA per split,
+    and when they fit one 128-row tile each CTA runs two splits (one per slot)."""
     tiles = (kv_len + 127) // 128
     pairs = (packed_rows + 255) // 256
-    return max(1, min(num_sms // max(1, batch * num_kv_heads * pairs), tiles // 2))
+    per_cta = 2 if packed_rows <= 128 else 1
+    return max(1, min(per_cta * (num_sms // max(1, batch * num_kv_heads * pairs)), tiles // 2))
 
 
 def split_key_plan(B: int, Hq: int, Hkv: int, Sq: int, Skv: int, num_sms: int = 148):
@@ -218,7 +220,8 @@ def split_key_plan(B: int, Hq: int, Hkv: int, Sq: int, Skv: int, num_sms: int = 
     each CTA two 128-row query tiles (two heads of a GQA pair, or two tiles of one
     head) and all their key tiles; the split-key kernel packs the GQA heads' rows
     (two 128-row tiles per CTA) and splits the keys so that one wave fills the
-    SMs, plus about two periods for the partials' merge.  Short suffixes over long
+    SMs (two key ranges per CTA when the packed rows fit one tile), plus about
+    two periods for the partials' merge.  Short suffixes over long
     reused prefixes (decode, seams, short reuse prefills) take the split-key
     kernel; everything with enough query tiles to fill the GPU keeps the prefill
     kernel."""
@@ -236,7 +239,8 @@ def split_key_plan(B: int, Hq: int, Hkv: int, Sq: int, Skv: int, num_sms: int = 
     if per_split > 16384:          # completion counters in the workspace header
         return False, 1
     splits = decode_splits(B, Hkv, Skv, num_sms, group * Sq)
-    split = cdiv(per_split * splits, num_sms) * cdiv(kt, splits) + 2
+    ctas = per_split * (cdiv(splits, 2) if group * Sq <= 128 and splits > 1 else splits)
+    split = cdiv(ctas, num_sms) * cdiv(kt, splits) + 2
     return split < 0.75 * dense, splits
 
 
@@ -251,8 +255,8 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     bottom-right causal), restricted to Sq <= Skv.  The query heads of a GQA group
     are packed as rows (two 128-row tiles per CTA) so that each key tile is read
     once per group and tile pair, and the key range is split over CTAs (one
-    wave); the last CTA of each group's splits merges the partial results by
-    their LSE in the same launch.
+    wave); the partial results are merged by their LSE, by the last CTA of each
+    group's splits (groups of up to 32 packed rows) or by a second launch.
     """
     _check_tensor("q", q, 4)
     _check_tensor("k", k, 4)

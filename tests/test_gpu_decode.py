@@ -145,3 +145,16 @@ def test_prefill_routes_short_suffix(B, Hq, Hkv, Sq, Skv, layout):
                                      1.0 / math.sqrt(128), True, compute_dtype=np.float32)
     assert np.abs(o.float().cpu().numpy() - o_ref).max() <= 2e-2
     assert np.abs(lse.cpu().numpy() - lse_ref).max() <= 2e-3
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Skv,D,dtype,splits", [
+    (2, 8, 2, 3, 5000, 64, torch.float16, 5),      # ring of 4: two stages per slot
+    (1, 4, 1, 16, 3333, 96, torch.bfloat16, 3),    # odd split count: last CTA's second slot empty
+    (3, 16, 2, 8, 2600, 128, torch.bfloat16, 2),   # one CTA per group, both slots busy
+    (1, 8, 1, 4, 891, 128, torch.bfloat16, 4),     # 7 tiles: last CTA's slots take 2 and 1
+    (2, 8, 2, 1, 4097, 96, torch.bfloat16, 16),    # 11 splits: last CTA's second slot empty
+])
+def test_dual_key_ranges(B, Hq, Hkv, Sq, Skv, D, dtype, splits):
+    """Packed rows within one tile: each CTA's two slots stream two key splits."""
+    _case(B, Hq, Hkv, Sq, Skv, D, dtype, seed=Skv, splits=splits)
+    _case(1, Hq, Hkv, Sq, Skv, D, dtype, seed=Skv + 1, splits=splits, causal=False)

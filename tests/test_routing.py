@@ -12,8 +12,8 @@ def test_dense_configs_keep_prefill_kernel():
 
 
 def test_short_suffixes_take_split_key():
-    use, splits = split_key_plan(8, 16, 2, 1, 4096)      # decode step
-    assert use and splits == 9
+    use, splits = split_key_plan(8, 16, 2, 1, 4096)      # decode step: 9 CTAs x 2 ranges per group
+    assert use and splits == 16
     assert split_key_plan(8, 16, 2, 16, 32784)[0]         # seam over a 32K prefix
     assert split_key_plan(1, 32, 32, 16, 8208)[0]         # MHA short suffix
     assert split_key_plan(1, 64, 8, 64, 32832)[0]         # short suffix, 64/8 heads
@@ -25,8 +25,11 @@ def test_not_for_queries_longer_than_keys_or_tiny_kv():
 
 
 def test_splits_fill_one_wave():
-    # one CTA per split per (sequence, KV head, 256 packed rows), at least two key tiles each
-    assert decode_splits(8, 2, 4096) == 9
+    # one CTA per split per (sequence, KV head, 256 packed rows), at least two key tiles
+    # each; two splits per CTA when a group's packed rows fit one 128-row tile
+    assert decode_splits(8, 2, 4096) == 16
+    assert decode_splits(8, 2, 32768, packed_rows=128) == 18
+    assert decode_splits(8, 2, 32768, packed_rows=129) == 9
     assert decode_splits(1, 8, 32768, packed_rows=8 * 64) == 9
     assert decode_splits(1, 2, 300) == 1
     assert decode_splits(200, 2, 4096) == 1
