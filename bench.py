@@ -75,7 +75,9 @@ NCU_TRAFFIC_BYTES = {"reuse_prefill": 27322880, "varlen_d96": 3626150000,
                      # patch 16 965 632 + 14 080 (read + write)
                      "cacheblend": 134075392,
                      # split-key kernel, 33 647 616 read (the merged partials stay in L2)
-                     "decode": 33647616}
+                     "decode": 33647616,
+                     # split-key kernel: 270 195 200 read + 11 918 592 partials written
+                     "short_suffix": 282113792}
 
 
 def parse():
