@@ -22,8 +22,7 @@ reference's metric is defined on; the public datasets are not available):
   split across ranks (strong scaling; each rank holds its heads' pool shard).
 
 * ``decode`` -- decode attention of the config-3 model: batch 8, 16 query / 2
-  KV heads, D 128, one query row over 4096 keys (split-key kernel; each group's
-  last CTA merges the partials in the same launch).
+  KV heads, D 128, one query row over 4096 keys (split-key kernel + merge launch).
 * ``quantize_store`` -- quantise-on-store of the config-3 warm: 24 chunks x
   128 tokens x 36 layers x 2 KV heads x D 128 bf16 into the int8 block pool
   (GB/s; one launch per chunk).
@@ -221,7 +220,7 @@ class Decode(Dense):
         super().__init__("decode", 8, 16, 2, 1, 4095, 128, "bf16",
                          "decode attention: B8 Hq16/Hkv2 D128 bf16, 1 query row over 4096 keys")
         self.bound = "hbm"
-        self.launches_per_step = 1    # split-key kernel; each group's last CTA merges the partials
+        self.launches_per_step = 2    # split-key kernel + merge of its partials
 
     def setup(self, torch, dev, rank, world):
         from kvboost_b200 import ops
@@ -236,7 +235,6 @@ class Decode(Dense):
             v = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(self.dt)
             sets.append((q, k, v, torch.empty_like(q)))
         scale = 1.0 / math.sqrt(self.D)
-        # the decode kernel's workspace is allocated on the first call, outside the graph
         ops.decode_attention(*sets[0][:3], scale, True, out=sets[0][3], return_lse=False)
 
         def step(i):

@@ -143,18 +143,14 @@ int kvb_prefill_fwd(const KvbPrefillParams* params, void* stream);
  * rows must be contiguous in q (head stride = q_len * row stride).  The query
  * heads sharing a KV head are packed as rows ((q heads per KV head) * q_len
  * of them, two 128-row tiles per CTA), so every key tile is read once per
- * group and tile pair, and the key range is split over num_splits CTAs; the
- * partial outputs are merged by their LSE, for groups of up to 32 packed rows
- * by the last CTA of each (sequence, KV head, tile pair) to finish (one
- * launch), else by a second launch.  workspace: device memory of at
- * least kvb_decode_workspace_bytes(params, num_splits) bytes (-1: invalid
- * params, reason in kvb_last_error), 16-byte aligned.  Its first
- * KVB_DECODE_COUNTER_BYTES hold the completion counters: zero them once
- * before the first call; every call leaves them zero again (so one workspace
- * serves calls of any shape, in order on one stream).  Needs batch *
- * num_kv_heads * ceil(packed rows / 256) <= KVB_DECODE_COUNTER_BYTES / 4.  No
- * counterpart in the reference, whose decode steps run the same SDPA call as
- * its prefill.
+ * group and tile pair, and the key range is split over num_splits CTAs; a
+ * second launch merges the partial outputs by their LSE.  workspace: device
+ * memory of at least kvb_decode_workspace_bytes(params, num_splits) bytes (-1:
+ * invalid params, reason in kvb_last_error), 16-byte aligned, holding the
+ * partials after a reserved header of KVB_DECODE_COUNTER_BYTES (no
+ * initialisation needed); calls that overlap on the GPU must not share one.
+ * No counterpart in the reference, whose decode steps run the same SDPA call
+ * as its prefill.
  */
 #define KVB_DECODE_COUNTER_BYTES (64 * 1024)
 int64_t kvb_decode_workspace_bytes(const KvbPrefillParams* params, int num_splits);

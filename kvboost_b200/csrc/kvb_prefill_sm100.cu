@@ -175,15 +175,13 @@ struct PagedArgs {
       const void* v_new;      //   b*bs + h*hs + i*rs + d
       int64_t kn_bs, kn_hs, kn_rs, vn_bs, vn_hs, vn_rs;
     };
-    struct {                  // split-key decode: the LSE merge done by each group's last CTA
-      int* split_count;       // [batch][num_kv_heads] CTAs of the group done (left 0)
+    struct {                  // split-key attention: where kvb_split_merge_kernel writes
       void* o_final;          // final O, element (b, head, i, d) at b*bs + head*hs + i*rs + d
       float* lse_final;       // final LSE (b, head, i) at b*bs + head*hs + i, or null
       int64_t of_bs, of_hs, of_rs, lf_bs, lf_hs;
       int group_heads;        // query heads per KV head
       int tile_pairs;         // 256-row pairs of packed tiles per group (grid x = splits * pairs)
       int dual;               // 1: one packed tile; slot s of CTA c takes key split 2c + s
-      int merge_in_kernel;    // 1: each group's last CTA merges; 0: kvb_split_merge_kernel does
     };
   };
   int max_blocks;
@@ -208,7 +206,6 @@ struct PagedArgs {
 struct SharedCtl {
   uint32_t tmem_base;
   int abort_flag;
-  int last_cta;   // split-key decode: this CTA merges its group's splits
 };
 
 // Bounded wait: spins on try_wait, then checks the CTA abort flag and the
@@ -652,127 +649,16 @@ __global__ void __launch_bounds__(256)
   reinterpret_cast<uint4*>(dst)[1] = w1;
 }
 
-// Merge the per-split partial results of packed rows [r0, r0 + packed) of one
-// (sequence, KV head) group of a split-key launch: for each packed query row,
-// O = sum_s exp(lse_s - L) O_s and L = log sum_s exp(lse_s).  Partials are
-// packed as rows r = head_in_group * rows_per_head + i
-// ([splits][batch][num_kv_heads][group rows][D], normalised, compute dtype; LSE
-// fp32 [splits][batch][num_kv_heads][group rows]) and read through L2 (they were
-// written by other CTAs).  Threads stride over (row, 8-feature chunk) items.
-template <typename T, int D>
-__device__ __forceinline__ void merge_splits(const DenseArgs& a, const PagedArgs& pa, int b, int g,
-                                             int splits, int r0, int packed, float* scratch,
-                                             int scratch_floats) {
-  constexpr int NCH = D / 8;
-  // first merged row of the group
-  const int64_t grow = ((int64_t)b * pa.num_kv_heads + g) * a.q_len + r0;
-  const T* o_part = reinterpret_cast<const T*>(a.o);
-  const bool staged = (int64_t)packed * (splits + 2) <= scratch_floats;
-  float* w = scratch;                               // [splits][packed]: exp(lse_s - max)
-  float* row_mx = scratch + (int64_t)packed * splits;
-  float* row_inv = row_mx + packed;
-  if (staged) {
-    // every partial LSE of the group in one coalesced pass, then per-row weights
-    for (int idx = threadIdx.x; idx < packed * splits; idx += blockDim.x) {
-      const int sp = idx / packed, r = idx - sp * packed;
-      w[idx] = __ldcg(a.lse + sp * pa.lse_split_stride + grow + r);
-    }
-    __syncthreads();
-    for (int r = threadIdx.x; r < packed; r += blockDim.x) {
-      float mx = -INFINITY;
-      for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, w[sp * packed + r]);
-      float sum = 0.f;
-      for (int sp = 0; sp < splits; ++sp) {
-        const float e = mx > -INFINITY ? __expf(w[sp * packed + r] - mx) : 0.f;
-        w[sp * packed + r] = e;
-        sum += e;
-      }
-      row_mx[r] = mx;
-      row_inv[r] = sum > 0.f ? 1.f / sum : 0.f;
-    }
-    __syncthreads();
-  }
-  for (int idx = threadIdx.x; idx < packed * NCH; idx += blockDim.x) {
-    const int r = idx / NCH, ch = idx - r * NCH;
-    const int64_t row = grow + r;
-    float mx, inv;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (staged) {
-      mx = row_mx[r];
-      inv = row_inv[r];
-      // Eight partials' loads in flight per thread before any is used: one CTA
-      // merges a whole tile pair, so its L2 latency, not bandwidth, sets the pace.
-      constexpr int MB = 8;
-#pragma unroll 1
-      for (int sp0 = 0; sp0 < splits; sp0 += MB) {
-        uint4 v[MB];
-#pragma unroll
-        for (int u = 0; u < MB; ++u)
-          if (sp0 + u < splits)
-            v[u] = __ldcg(reinterpret_cast<const uint4*>(
-                o_part + (int64_t)(sp0 + u) * pa.o_split_stride + row * D + ch * 8));
-#pragma unroll
-        for (int u = 0; u < MB; ++u) {
-          if (sp0 + u >= splits) break;
-          const float wt = w[(sp0 + u) * packed + r];
-          const uint32_t wv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float2 f;
-            if constexpr (std::is_same<T, __half>::value)
-              f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
-            else
-              f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
-            acc[2 * e] += wt * f.x;
-            acc[2 * e + 1] += wt * f.y;
-          }
-        }
-      }
-    } else {
-      mx = -INFINITY;
-      for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, __ldcg(a.lse + sp * pa.lse_split_stride + row));
-      float wsum = 0.f;
-      if (mx > -INFINITY) {
-        for (int sp = 0; sp < splits; ++sp) {
-          const float wt = __expf(__ldcg(a.lse + sp * pa.lse_split_stride + row) - mx);
-          wsum += wt;
-          const uint4 v = __ldcg(reinterpret_cast<const uint4*>(o_part + sp * pa.o_split_stride + row * D + ch * 8));
-          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float2 f;
-            if constexpr (std::is_same<T, __half>::value)
-              f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
-            else
-              f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
-            acc[2 * e] += wt * f.x;
-            acc[2 * e + 1] += wt * f.y;
-          }
-        }
-      }
-      inv = wsum > 0.f ? 1.f / wsum : 0.f;
-    }
-    uint32_t o[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[e] = pack2<T>(acc[2 * e] * inv, acc[2 * e + 1] * inv);
-    const int head = g * pa.group_heads + (r0 + r) / pa.rows_per_head;
-    const int i = (r0 + r) % pa.rows_per_head;
-    T* dst = reinterpret_cast<T*>(pa.o_final) + (int64_t)b * pa.of_bs + (int64_t)head * pa.of_hs +
-             (int64_t)i * pa.of_rs + ch * 8;
-    *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
-    if (pa.lse_final != nullptr && ch == 0)
-      pa.lse_final[(int64_t)b * pa.lf_bs + (int64_t)head * pa.lf_hs + i] =
-          inv > 0.f ? mx + __logf(1.f / inv) : -INFINITY;
-  }
-}
-
-// Merge of split-key partials as its own launch, for groups with many packed
-// rows: the in-kernel merge is one CTA per group whose loads pay a dependent
-// L2 round trip per batch of splits.  One thread per (packed row, 8 features)
-// of every group: LSE-weighted sum of the row's partials, online over batches
-// of 16 splits (a running maximum keeps the weights in range), written through
-// the caller's strides; ch == 0 threads also write the merged LSE.  Launched
-// with programmatic dependent launch after the split kernel.
+// Merge of split-key partials, the second launch of a split-key call.  One
+// thread per (packed row, 8 features) of every group: LSE-weighted sum of the
+// row's partials ([splits][batch][num_kv_heads][group rows][D], normalised,
+// compute dtype; LSE fp32 [splits][batch][num_kv_heads][group rows]), online over
+// batches of 16 splits whose loads are all in flight at once (a running maximum
+// keeps the weights in range), written through the caller's strides; ch == 0
+// threads also write the merged LSE.  Launched with programmatic dependent launch
+// after the split kernel, so its CTAs are resident when that grid completes.
+// (Merging in each group's last split CTA instead was slower at every measured
+// shape: one CTA's loads pay a dependent L2 round trip per batch of splits.)
 template <typename T, int D>
 __global__ void __launch_bounds__(256)
     kvb_split_merge_kernel(const DenseArgs a, const PagedArgs pa, int splits, int64_t rows) {
@@ -911,7 +797,6 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   const int ctas = SPLITKV ? (int)gridDim.x / pa.tile_pairs : 1;  // CTAs per tile pair
   const int csplit = SPLITKV ? (int)blockIdx.x % ctas : 0;
   const int tpair = SPLITKV ? (int)blockIdx.x / ctas : 0;
-  const int splits = dual ? 2 * ctas : ctas;                      // partial results per row
   int vsplit[kSlots];                                              // key split of each slot
   vsplit[0] = dual ? 2 * csplit : csplit;
   vsplit[1] = dual ? 2 * csplit + 1 : csplit;
@@ -1466,7 +1351,6 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     }
   }
 
-  if (SPLITKV) __threadfence();   // this CTA's partial O / LSE, before it is counted below
   ptx::tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) KVB_TRACE_AT(3);
@@ -1474,24 +1358,6 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     __syncwarp();
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, G::TMEM_COLS);
-  }
-  if (SPLITKV && pa.merge_in_kernel) {
-    // The last CTA to finish among the splits of one (sequence, KV head, tile
-    // pair) merges their partials for the pair's rows and resets the count.
-    // Every CTA reaches this point exactly once (waits are bounded), so the
-    // count always completes and is left at 0 for the next launch.
-    int* count = pa.split_count +
-                 ((int64_t)b * pa.num_kv_heads + blockIdx.y) * pa.tile_pairs + tpair;
-    if (threadIdx.x == 0) ctl->last_cta = atomicAdd(count, 1) == ctas - 1;
-    __syncthreads();
-    if (ctl->last_cta) {
-      __threadfence();
-      // the Q and K/V tiles are idle now: scratch for the merge's weights
-      const int r0 = tpair * 2 * BM;
-      merge_splits<T, D>(a, pa, b, blockIdx.y, splits, r0, min(a.q_len, r0 + 2 * BM) - r0,
-                         reinterpret_cast<float*>(sQ), (kSlots + G::NS) * G::TILE_BYTES / 4);
-      if (threadIdx.x == 0) *count = 0;
-    }
   }
 }
 
@@ -1640,8 +1506,8 @@ static int launch_dense(const KvbPrefillParams& p, cudaStream_t stream) {
   return launch_dense_core<T, D>(tq, tk, tv, a, p.batch, p.num_q_heads, p.q_len, stream);
 }
 
-// Split-key decode: the workspace holds the partials, then the combine pass.
-// Layout: [KVB_DECODE_COUNTER_BYTES of per-group counters][partial O][partial LSE].
+// Split-key attention: the workspace holds the partials the merge launch reads.
+// Layout: [KVB_DECODE_COUNTER_BYTES reserved][partial O][partial LSE].
 static int64_t decode_workspace_bytes(const KvbPrefillParams& p, int splits) {
   const int64_t rows = (int64_t)p.batch * p.num_q_heads * p.q_len;
   const int64_t o_bytes = (int64_t)splits * rows * p.head_dim * 2;
@@ -1699,7 +1565,6 @@ static void decode_args(const KvbPrefillParams& p, int splits, int split_tiles, 
   sp->o_split_stride = rows * D;
   sp->lse_split_stride = rows;
   sp->num_kv_heads = p.num_kv_heads;
-  sp->split_count = reinterpret_cast<int*>(ws);
   sp->o_final = p.o;
   sp->lse_final = p.lse;
   sp->of_bs = p.o_batch_stride;
@@ -1711,9 +1576,6 @@ static void decode_args(const KvbPrefillParams& p, int splits, int split_tiles, 
   sp->tile_pairs = (packed + 2 * BM - 1) / (2 * BM);
 }
 
-// Packed rows per group up to which the split kernel's last CTA merges the
-// partials itself (decode steps); larger groups merge in kvb_split_merge_kernel.
-constexpr int kMergeInKernelRows = 32;
 
 template <typename T, int D>
 static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cudaStream_t stream) {
@@ -1729,7 +1591,6 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
   decode_args(p, parts, split_tiles, ws, &a, &sp);
   sp.dual = dual ? 1 : 0;
   const int packed_rows = (p.num_q_heads / p.num_kv_heads) * p.q_len;
-  sp.merge_in_kernel = packed_rows <= kMergeInKernelRows ? 1 : 0;
   const int ctas = dual ? parts / 2 : splits;   // CTAs per (sequence, KV head, tile pair)
   const int64_t q_rs = p.q_len == 1 ? p.q_head_stride : p.q_row_stride;
   CUtensorMap tq, tk, tv;
@@ -1754,7 +1615,7 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
   }
   cudaError_t e = launch_pdl(kern, dim3(ctas * sp.tile_pairs, p.num_kv_heads, p.batch),
                              Roles<false>::kThreads, G::SMEM_BYTES, stream, tq, tk, tv, a, sp);
-  if (e == cudaSuccess && !sp.merge_in_kernel) {
+  if (e == cudaSuccess) {
     const int64_t rows = (int64_t)p.batch * p.num_kv_heads * packed_rows;
     const int64_t items = rows * (D / 8);
     e = launch_pdl(kvb_split_merge_kernel<T, D>, dim3((unsigned)((items + 255) / 256)), 256, 0,
@@ -2072,11 +1933,6 @@ static int validate_decode(const KvbPrefillParams& p, int splits) {
   if (p.q_len > 1 && p.q_head_stride != (int64_t)p.q_len * p.q_row_stride)
     return fail(KVB_ERR_INVALID, "with q_len > 1 the rows of a head must be contiguous in q "
                                  "(head stride = q_len * row stride)");
-  const int64_t pairs = (packed + 2 * BM - 1) / (2 * BM);
-  if ((int64_t)p.batch * p.num_kv_heads * pairs > KVB_DECODE_COUNTER_BYTES / 4)
-    return fail(KVB_ERR_UNSUPPORTED,
-                "split-key attention takes batch * num_kv_heads * ceil(packed rows / 256) <= " +
-                    std::to_string(KVB_DECODE_COUNTER_BYTES / 4));
   return KVB_OK;
 }
 

@@ -195,9 +195,6 @@ def prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return out, lse
 
 
-_decode_ws = {}
-
-
 def decode_splits(batch: int, num_kv_heads: int, kv_len: int, num_sms: int = 148,
                   packed_rows: int = 1) -> int:
     """Key-range splits for one wave of CTAs (one per SM), at least two 128-key tiles
@@ -236,8 +233,6 @@ def split_key_plan(B: int, Hq: int, Hkv: int, Sq: int, Skv: int, num_sms: int = 
         dense_ctas = B * Hq * cdiv(cdiv(Sq, 128), 2)
     dense = cdiv(dense_ctas, num_sms) * kt
     per_split = B * Hkv * cdiv(group * Sq, 256)
-    if per_split > 16384:          # completion counters in the workspace header
-        return False, 1
     splits = decode_splits(B, Hkv, Skv, num_sms, group * Sq)
     ctas = per_split * (cdiv(splits, 2) if group * Sq <= 128 and splits > 1 else splits)
     split = cdiv(ctas, num_sms) * cdiv(kt, splits) + 2
@@ -255,8 +250,7 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     bottom-right causal), restricted to Sq <= Skv.  The query heads of a GQA group
     are packed as rows (two 128-row tiles per CTA) so that each key tile is read
     once per group and tile pair, and the key range is split over CTAs (one
-    wave); the partial results are merged by their LSE, by the last CTA of each
-    group's splits (groups of up to 32 packed rows) or by a second launch.
+    wave); a second launch merges the partial results by their LSE.
     """
     _check_tensor("q", q, 4)
     _check_tensor("k", k, 4)
@@ -295,17 +289,11 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if need < 0:
         _lib.check(_lib.KVB_ERR_INVALID, "kvb_decode_workspace_bytes: " + (
             lib.kvb_last_error().decode("utf-8", "replace")))
-    # One workspace per (device, stream): its split counters start at zero and every
-    # launch leaves them at zero, so launches queued on one stream can share it, while
-    # launches on another stream (which may overlap) get their own.
+    # The partials' workspace comes from torch's caching allocator for this call:
+    # its reuse is ordered on the current stream, so calls on concurrent streams
+    # never share one.
+    ws = torch.empty(need, dtype=torch.uint8, device=q.device)
     stream = _stream_handle(q.device)
-    key = (q.device.index if q.device.index is not None else torch.cuda.current_device(), stream)
-    ws = _decode_ws.get(key)
-    if ws is None or ws.numel() < need:
-        # (a replaced workspace returns to the caching allocator, whose reuse is
-        # ordered on this same stream)
-        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=q.device)  # counters start at 0
-        _decode_ws[key] = ws
     with torch.cuda.device(q.device):
         rc = lib.kvb_decode_fwd(p, int(num_splits), ws.data_ptr(), ws.numel(), stream)
     _lib.check(rc, "kvb_decode_fwd")
