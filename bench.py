@@ -951,7 +951,7 @@ def run_cp(args, torch, dist, rank, world, local, dev):
                                     + 4 * local_pool.v_scale[0].numel()
                                     + 2 * 2 * kl.numel())
     line = {
-        "metric": metric, "value": value, "unit": munit,
+        "metric": "prefill attention TFLOP/s", "value": value, "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
