@@ -206,7 +206,7 @@ def decode_splits(batch: int, num_kv_heads: int, kv_len: int, num_sms: int = 148
     tiles = (kv_len + 127) // 128
     pairs = (packed_rows + 255) // 256
     per_cta = 2 if packed_rows <= 128 else 1
-    return max(1, min(per_cta * (num_sms // max(1, batch * num_kv_heads * pairs)), tiles // 2))
+    return max(1, min(per_cta * max(1, num_sms // max(1, batch * num_kv_heads * pairs)), tiles // 2))
 
 
 def split_key_plan(B: int, Hq: int, Hkv: int, Sq: int, Skv: int, num_sms: int = 148):

@@ -32,4 +32,5 @@ def test_splits_fill_one_wave():
     assert decode_splits(8, 2, 32768, packed_rows=129) == 9
     assert decode_splits(1, 8, 32768, packed_rows=8 * 64) == 9
     assert decode_splits(1, 2, 300) == 1
-    assert decode_splits(200, 2, 4096) == 1
+    assert decode_splits(200, 2, 4096) == 2      # more groups than SMs: still both slots busy
+    assert decode_splits(200, 2, 4096, packed_rows=129) == 1
