@@ -731,7 +731,11 @@ __global__ void __launch_bounds__(256)
         sum > 0.f ? m + __logf(sum) : -INFINITY;
 }
 
-template <typename T, int D, bool PAGED, bool SPLITKV = false>
+// DUALOK (dense launches only): a CTA whose second query tile has no rows (a
+// varlen sequence's last odd tile, a single-tile sequence) gives slot 1 the
+// same tile and the second half of the key range, so its two slots still run
+// two chains in ping-pong; slot 0 merges the two halves in the epilogue.
+template <typename T, int D, bool PAGED, bool SPLITKV = false, bool DUALOK = false>
 __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     kvb_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -793,17 +797,17 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   // ---- work item: two query tiles sharing one KV head ---------------------
   const int b = blockIdx.z;
   int head[kSlots], mtile[kSlots];
-  const bool dual = SPLITKV && pa.dual;
+  const bool dual_split = SPLITKV && pa.dual;
   const int ctas = SPLITKV ? (int)gridDim.x / pa.tile_pairs : 1;  // CTAs per tile pair
   const int csplit = SPLITKV ? (int)blockIdx.x % ctas : 0;
   const int tpair = SPLITKV ? (int)blockIdx.x / ctas : 0;
   int vsplit[kSlots];                                              // key split of each slot
-  vsplit[0] = dual ? 2 * csplit : csplit;
-  vsplit[1] = dual ? 2 * csplit + 1 : csplit;
+  vsplit[0] = dual_split ? 2 * csplit : csplit;
+  vsplit[1] = dual_split ? 2 * csplit + 1 : csplit;
   if (SPLITKV) {  // two packed tiles of one KV head's group (or one tile twice), one key range each
     head[0] = head[1] = blockIdx.y;
-    mtile[0] = dual ? 0 : 2 * tpair;
-    mtile[1] = dual ? 0 : 2 * tpair + 1;
+    mtile[0] = dual_split ? 0 : 2 * tpair;
+    mtile[1] = dual_split ? 0 : 2 * tpair + 1;
   } else if (a.pair_heads) {
     const int m = gridDim.x - 1 - blockIdx.x;  // heaviest (last) query tiles first
     head[0] = 2 * blockIdx.y;
@@ -844,6 +848,19 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     if (SPLITKV) n_t[sl] = max(0, min(n_t[sl] - jbase[sl], pa.split_tiles));
   }
   if (q_rows[0] == 0 && q_rows[1] == 0) return;  // uniform, before TMEM or any barrier wait
+  bool dual_dense = false;
+  if (DUALOK && !SPLITKV && !PAGED && q_rows[1] == 0 && n_t[0] >= 4) {
+    // slot 1 takes slot 0's rows and the second half of its key tiles
+    dual_dense = true;
+    head[1] = head[0];
+    q0[1] = q0[0];
+    q_rows[1] = q_rows[0];
+    const int half = (n_t[0] + 1) / 2;
+    jbase[1] = half;
+    n_t[1] = n_t[0] - half;
+    n_t[0] = half;
+  }
+  const bool dual = dual_split || dual_dense;
   const int n_max = max(n_t[0], n_t[1]);
   // Position of slot s's key tile j in the K/V load sequence: the step j when
   // both slots read the same tile; in dual mode the loads alternate between
@@ -1170,7 +1187,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     const int h = head[sl];
     const int q0s = q0[sl];
     const int n_tiles = n_t[sl];
-    const int jb = SPLITKV ? jbase[sl] : 0;
+    const int jb = (SPLITKV || DUALOK) ? jbase[sl] : 0;
     const int qi = q0s + t;
     const float sl2 = a.scale_log2;
     constexpr float kSumLimit = std::is_same<T, __half>::value ? 32768.f : 1.0995116e12f;
@@ -1278,7 +1295,70 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     T* obase = reinterpret_cast<T*>(a.o) + hf * DH + (SPLITKV ? vsplit[sl] * pa.o_split_stride : 0) +
                (a.cu_q ? (int64_t)q_base * a.o_rs + (int64_t)h * a.o_hs
                        : (int64_t)b * a.o_bs + (int64_t)h * a.o_hs);
-    if (have_o && dual) {
+    constexpr int NC = DH / 8;                   // 16-byte pieces per row segment
+    constexpr int ROT = 8 / (NC % 8 == 0 ? 8 : NC % 4 == 0 ? 4 : 2);
+    constexpr int RPS = 32 / NC;                 // rows per store instruction
+    const int wrow = (warp & 3) * 32;            // first row of this warp within the tile
+    if (DUALOK && dual_dense) {
+      // Two key halves of one query tile: slot 1 hands each row's maximum and sum
+      // to slot 0 (through the exact path's exchange slots, idle now), and slot 0
+      // writes O = (O0 2^(m0-m) + O1 2^(m1-m)) / (l0 2^(m0-m) + l1 2^(m1-m)).
+      if (sl == 1 && hf == 0) {
+        xmax[256 + t] = have_o ? m_run : -INFINITY;
+        xmax[384 + t] = have_o ? l_tot : 0.f;
+      }
+      ptx::bar_sync(9, 4 * kSlots * H * 32);     // every softmax warp, once
+      if (sl == 0) {
+        bool have_o1 = wait_bar(bar(BAR_O_FULL + 1), 0, abort_flag, a.status,
+                                KVB_STATUS_EPILOGUE_WAIT);
+        have_o1 = __all_sync(0xffffffffu, have_o1);
+        ptx::tc_fence_after();
+        const float m1 = xmax[256 + t], l1 = xmax[384 + t];
+        const float m0 = have_o ? m_run : -INFINITY, l0 = have_o ? l_tot : 0.f;
+        const float mm = fmaxf(m0, m1);
+        const float a0 = (m0 == -INFINITY) ? 0.f : ptx::ex2(m0 - mm);
+        const float a1 = (m1 == -INFINITY || !have_o1) ? 0.f : ptx::ex2(m1 - mm);
+        const float L = l0 * a0 + l1 * a1;
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        const float w0 = a0 * inv, w1 = a1 * inv;
+        const uint32_t tO1 = tmem + lane_base + G::o_col(1) + hf * DH;
+        // every MMA has completed (both O_FULL commits): the Q tile is free
+        uint4* stage = reinterpret_cast<uint4*>(sQ) + (hf * 4 + (warp & 3)) * 32 * NC;
+#pragma unroll 1
+        for (int c = 0; c < DH; c += OCW) {
+          uint32_t r0[OCW], r1[OCW];
+          tmem_ld_cw<OCW>(tO + c, r0);
+          tmem_ld_cw<OCW>(tO1 + c, r1);
+          ptx::tmem_wait_ld();
+          uint32_t pk[OCW / 2];
+#pragma unroll
+          for (int i = 0; i < OCW / 2; ++i)
+            pk[i] = pack2<T>(__uint_as_float(r0[2 * i]) * w0 + __uint_as_float(r1[2 * i]) * w1,
+                             __uint_as_float(r0[2 * i + 1]) * w0 +
+                                 __uint_as_float(r1[2 * i + 1]) * w1);
+#pragma unroll
+          for (int i = 0; i < OCW / 8; ++i)
+            stage[lane * NC + (c / 8 + i + lane / ROT) % NC] =
+                make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+        __syncwarp();
+        const int pr = lane / NC, pc = lane % NC;
+#pragma unroll 1
+        for (int r0_ = 0; r0_ < 32; r0_ += RPS) {
+          const int rr = r0_ + pr;
+          if (pr < RPS && rr < 32 && wrow + rr < q_rows[0])
+            *reinterpret_cast<uint4*>(obase + (int64_t)(q0s + wrow + rr) * a.o_rs + pc * 8) =
+                stage[rr * NC + (pc + rr / ROT) % NC];
+        }
+        if (hf == 0 && row_valid && a.lse != nullptr) {
+          const float lse = L > 0.f ? (mm + ptx::lg2(L)) * 0.69314718055994531f : -INFINITY;
+          if (a.cu_q)
+            a.lse[(int64_t)h * a.lse_hs + q_base + qi] = lse;
+          else
+            a.lse[(int64_t)b * a.lse_bs + (int64_t)h * a.lse_hs + qi] = lse;
+        }
+      }
+    } else if (have_o && dual) {
       // dual split-key mode: the Q tile and slot 1's Q buffer may still be read
       // by the other slot's MMAs, so each thread stores its own row segment
       T* orow = obase + (int64_t)qi * a.o_rs;
@@ -1305,8 +1385,6 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       // 16-byte piece of 32 different rows per instruction.  The slot's Q tile
       // is free: the O_FULL commit follows every MMA that read it.  Pieces are
       // rotated by row so that neither pass has bank conflicts.
-      constexpr int NC = DH / 8;                   // 16-byte pieces per row segment
-      constexpr int ROT = 8 / (NC % 8 == 0 ? 8 : NC % 4 == 0 ? 4 : 2);
       uint4* stage = reinterpret_cast<uint4*>(sQ + sl * G::TILE_BYTES) +
                      (hf * 4 + (warp & 3)) * 32 * NC;
 #pragma unroll 1
@@ -1324,9 +1402,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
               make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
       __syncwarp();
-      constexpr int RPS = 32 / NC;                 // rows per store instruction
       const int pr = lane / NC, pc = lane % NC;
-      const int wrow = (warp & 3) * 32;            // first row of this warp within the tile
 #pragma unroll 1
       for (int r0 = 0; r0 < 32; r0 += RPS) {
         const int rr = r0 + pr;
@@ -1340,7 +1416,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
 #pragma unroll
       for (int i = 0; i < DH / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
     }
-    if (hf == 0 && row_valid && a.lse != nullptr) {
+    if (!(DUALOK && dual_dense) && hf == 0 && row_valid && a.lse != nullptr) {
       const float lse = (l_tot > 0.f && have_o) ? (m_run + ptx::lg2(l_tot)) * 0.69314718055994531f
                                                 : -INFINITY;
       if (a.cu_q)
@@ -1441,18 +1517,23 @@ static int launch_dense_core(const CUtensorMap& tq, const CUtensorMap& tk, const
                              const DenseArgs& a, int batch, int num_q_heads, int q_len,
                              cudaStream_t stream) {
   using G = Geo<D>;
-  auto kern = kvb_prefill_kernel<T, D, false>;
-  static thread_local int configured_device = -1;
+  const int q_tiles = (q_len + BM - 1) / BM;
+  // Launches that can have a CTA whose second query tile is empty (varlen, or an
+  // odd tile count of one head) take the DUALOK instantiation; the others keep
+  // the plain kernel.
+  const bool dualok = !a.pair_heads && (a.cu_q != nullptr || q_tiles % 2 == 1);
+  auto kern = dualok ? kvb_prefill_kernel<T, D, false, false, true>
+                     : kvb_prefill_kernel<T, D, false>;
+  static thread_local int configured_device[2] = {-1, -1};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured_device != dev) {
+  if (configured_device[dualok] != dev) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          G::SMEM_BYTES);
     if (e != cudaSuccess)
       return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    configured_device = dev;
+    configured_device[dualok] = dev;
   }
-  const int q_tiles = (q_len + BM - 1) / BM;
   dim3 grid = a.pair_heads ? dim3(q_tiles, num_q_heads / 2, batch)
                            : dim3((q_tiles + 1) / 2, num_q_heads, batch);
   PagedArgs none = {};

@@ -70,6 +70,7 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                       softmax_scale: Optional[float] = None, causal: bool = True,
                       out: Optional[torch.Tensor] = None, return_lse: bool = True,
                       out_layout: str = "bhsd", top_left: bool = False,
+                      kernel: str = "auto",
                       ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """Bottom-right causal (or full) attention with GQA.
 
@@ -80,6 +81,7 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     Returns ``(o, lse)``: o in q's dtype, ``[B, Hq, Sq, D]`` (``out_layout="bhsd"``)
     or ``[B, Sq, Hq, D]`` (``"bshd"``, what HF attention functions return);
     lse float32 ``[B, Hq, Sq]`` (natural log) or None.
+    ``kernel``: "auto" (``split_key_plan`` decides), "prefill" or "split" to force one.
     """
     _check_tensor("q", q, 4)
     _check_tensor("k", k, 4)
@@ -108,7 +110,12 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device) if return_lse else None
     if B == 0 or Sq == 0:
         return (out.transpose(1, 2) if out_layout == "bshd" else out), lse
+    if kernel not in ("auto", "prefill", "split"):
+        raise RuntimeError(f"kernel must be 'auto', 'prefill' or 'split', got {kernel!r}")
     use_split, splits = split_key_plan(B, Hq, Hkv, Sq, Skv)
+    if kernel != "auto":
+        use_split = kernel == "split"
+        splits = decode_splits(B, Hkv, Skv, packed_rows=(Hq // Hkv) * Sq)
     if use_split:
         # few query tiles over many keys: GQA heads packed per key tile, keys
         # split over CTAs (same results; see split_key_plan)

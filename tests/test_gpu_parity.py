@@ -270,3 +270,50 @@ def test_running_max_raises_late(dtype):
     o, lse = prefill_attention(q.cuda(), k.cuda(), v.cuda(), 1.0 / math.sqrt(D), True)
     torch.cuda.synchronize()
     _check(o, lse, q, k, v, 1.0 / math.sqrt(D), True, dtype)
+
+
+def _varlen_case(sq, pre, H, D, dtype, causal, seed):
+    from kvboost_b200.ops import prefill_attention_varlen
+    g = torch.Generator().manual_seed(seed)
+    skv = [a + b for a, b in zip(sq, pre)]
+    cu_q = np.concatenate([[0], np.cumsum(sq)]).astype(np.int32)
+    cu_k = np.concatenate([[0], np.cumsum(skv)]).astype(np.int32)
+    q = _rand((int(cu_q[-1]), H, D), dtype, g)
+    k = _rand((int(cu_k[-1]), H, D), dtype, g)
+    v = _rand((int(cu_k[-1]), H, D), dtype, g)
+    o, lse = prefill_attention_varlen(q.cuda(), k.cuda(), v.cuda(),
+                                      torch.from_numpy(cu_q).cuda(), torch.from_numpy(cu_k).cuda(),
+                                      max(sq), max(skv), 1.0 / math.sqrt(D), causal)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = oattn.attention_varlen(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                            cu_q, cu_k, 1.0 / math.sqrt(D), causal,
+                                            compute_dtype=np.float32)
+    assert np.max(np.abs(o.float().cpu().numpy() - o_ref)) <= TOL[dtype]
+    assert np.max(np.abs(lse.cpu().numpy() - lse_ref)) <= LSE_TOL
+
+
+@pytest.mark.parametrize("D,dtype", [(96, torch.float16), (128, torch.bfloat16), (64, torch.float16)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_varlen_lone_tiles_split_keys(D, dtype, causal):
+    """Varlen MHA sequences whose last CTA holds one query tile over many key tiles:
+    the CTA's two slots take the two halves of the key range and slot 0 merges them
+    (single-tile sequences, the third tile of three, short key ranges that stay whole)."""
+    sq = [16, 128, 1, 300, 100, 64, 40]
+    pre = [2048, 1024, 3000, 1280, 256, 0, 640]
+    _varlen_case(sq, pre, 4, D, dtype, causal, seed=D + int(causal))
+
+
+@pytest.mark.parametrize("causal,top_left", [(True, False), (False, False), (True, True)])
+def test_dense_odd_tiles_split_keys(causal, top_left):
+    """Dense MHA with an odd query-tile count, through the prefill kernel: the last
+    tile's CTA splits its keys over both slots."""
+    from kvboost_b200.ops import prefill_attention
+    g = torch.Generator().manual_seed(31)
+    B, H, Sq, Skv, D = 2, 3, 300, 2100, 128
+    q = _rand((B, H, Sq, D), torch.bfloat16, g)
+    k = _rand((B, H, Skv, D), torch.bfloat16, g)
+    v = _rand((B, H, Skv, D), torch.bfloat16, g)
+    o, lse = prefill_attention(q.cuda(), k.cuda(), v.cuda(), 1.0 / math.sqrt(D), causal,
+                               top_left=top_left, kernel="prefill")
+    torch.cuda.synchronize()
+    _check(o, lse, q, k, v, 1.0 / math.sqrt(D), causal, torch.bfloat16, top_left)
