@@ -663,6 +663,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(256)
     kvb_split_merge_kernel(const DenseArgs a, const PagedArgs pa, int splits, int64_t rows) {
   ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
   constexpr int NCH = D / 8;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows * NCH) return;
@@ -764,8 +765,10 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   // ---- setup that touches no global memory ------------------------------
   // Runs while the preceding grid in the stream may still be finishing (the
   // launch allows programmatic dependent launch); everything from the wait
-  // on sees that grid's writes.  TMEM is allocated only after the wait, so a
-  // CTA never holds TMEM while waiting on a grid that may still need some.
+  // on sees that grid's writes.  TMEM is allocated here too: a dependent
+  // launch only starts once every CTA of the preceding grid has signalled
+  // (these kernels signal after their own allocation) or exited, so no CTA of
+  // that grid can still be waiting to allocate on this SM.
   if (threadIdx.x == 0) {
     for (int sl = 0; sl < kSlots; ++sl) {
       ptx::mbar_init(bar(BAR_Q_FULL + sl), 1);
@@ -792,6 +795,14 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       ptx::prefetch_tmap(&tm_v);
     }
   }
+  if (warp == kWarpMma) {
+    ptx::tmem_alloc(ptx::smem_u32(&ctl->tmem_base), G::TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
   ptx::griddep_wait();
 
   // ---- work item: two query tiles sharing one KV head ---------------------
@@ -847,7 +858,10 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     jbase[sl] = SPLITKV ? vsplit[sl] * pa.split_tiles : 0;
     if (SPLITKV) n_t[sl] = max(0, min(n_t[sl] - jbase[sl], pa.split_tiles));
   }
-  if (q_rows[0] == 0 && q_rows[1] == 0) return;  // uniform, before TMEM or any barrier wait
+  if (q_rows[0] == 0 && q_rows[1] == 0) {        // uniform, before any barrier wait
+    if (warp == kWarpMma) ptx::tmem_dealloc(tmem, G::TMEM_COLS);
+    return;
+  }
   bool dual_dense = false;
   if (DUALOK && !SPLITKV && !PAGED && q_rows[1] == 0 && n_t[0] >= 4) {
     // slot 1 takes slot 0's rows and the second half of its key tiles
@@ -871,14 +885,6 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     return !dual ? j : (j < n_t[1] ? 2 * j + s : n_t[1] + j);
   };
 
-  if (warp == kWarpMma) {
-    ptx::tmem_alloc(ptx::smem_u32(&ctl->tmem_base), G::TMEM_COLS);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem = ctl->tmem_base;
   // Every CTA of this grid is resident or done once all have passed here: the
   // next launch may begin its own setup.
   ptx::griddep_launch_dependents();
