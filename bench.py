@@ -21,15 +21,15 @@ reference's metric is defined on; the public datasets are not available):
   tokens, 64 query / 8 KV heads, D 128, bf16.  With N GPUs the KV heads are
   split across ranks (strong scaling; each rank holds its heads' pool shard).
 
-* ``decode`` -- decode attention of the config-3 model: batch 8, 16 query / 2
+* ``decode`` -- decode attention of the Qwen2.5-3B-architecture model: batch 8, 16 query / 2
   KV heads, D 128, one query row over 4096 keys (split-key kernel + merge launch).
-* ``quantize_store`` -- quantise-on-store of the config-3 warm: 24 chunks x
+* ``quantize_store`` -- quantise-on-store of the Qwen2.5-3B-architecture warm: 24 chunks x
   128 tokens x 36 layers x 2 KV heads x D 128 bf16 into the int8 block pool
   (GB/s; one launch per chunk).
 * ``cacheblend`` -- CacheBlend repair of a 3072-position stitched prefix of the
-  config-3 model (deviation over 36 layers, top 15 %, patch; GB/s; 3 launches).
+  Qwen2.5-3B-architecture model (deviation over 36 layers, top 15 %, patch; GB/s; 3 launches).
 * ``short_suffix`` -- reuse-dominated short-suffix prefill: 16 new tokens over a
-  32768-token reused prefix, batch 8, 16 query / 2 KV heads, D 128 (the config-3
+  32768-token reused prefix, batch 8, 16 query / 2 KV heads, D 128 (the Qwen2.5-3B-architecture
   model's seam shape; split-key kernel through ``prefill_attention``; GB/s).
 
 One step = one kernel launch over one batch (the last two: one chunk store per
@@ -211,7 +211,7 @@ class Dense:
 
 
 class Decode(Dense):
-    """Decode attention of the config-3 model at its 4096-token context: batch 8, 16
+    """Decode attention of the Qwen2.5-3B-architecture model at its 4096-token context: batch 8, 16
     query heads over 2 KV heads, D 128, bf16, one query row per head
     (``decode_attention``: GQA heads packed per key tile, keys split over CTAs).
     HBM-bound: every launch streams the 8 x 2 x 4096 keys and values once."""
@@ -261,7 +261,7 @@ class Decode(Dense):
 
 class ShortSuffix(Dense):
     """Reuse-dominated short-suffix prefill: the selective-recompute seam shape of the
-    config-3 model (16 query heads over 2 KV heads, D 128, bf16, 16 new tokens) over a
+    Qwen2.5-3B-architecture model (16 query heads over 2 KV heads, D 128, bf16, 16 new tokens) over a
     32 768-token reused prefix, batch 8, through ``prefill_attention`` (which takes the
     split-key kernel for it).  HBM-bound: every launch streams the reused K/V once."""
 
@@ -319,7 +319,7 @@ class ShortSuffix(Dense):
 
 
 class Varlen:
-    """Config 4: packed varlen, 32 heads MHA, head_dim 96, fp16."""
+    """Packed varlen reuse prefill: 64 requests, 32 heads MHA, head_dim 96, fp16."""
 
     def __init__(self, small=False):
         import torch
@@ -410,7 +410,7 @@ class Varlen:
 
 
 class PagedLong:
-    """Config 5: int8 paged 32K prefix + 2048 new tokens, heads split over ranks."""
+    """Paged int8 reuse: 32K-token prefix + 2048 new tokens, KV heads split over ranks."""
 
     def __init__(self, small=False):
         self.name = "paged_long"
@@ -531,7 +531,7 @@ class PagedLong:
 
 
 class QuantizeStore:
-    """Quantise-on-store of freshly encoded chunks (``kvb_quantize_store``): the config-3
+    """Quantise-on-store of freshly encoded chunks (``kvb_quantize_store``): the Qwen2.5-3B-architecture
     model's warm of a 3072-token prefix -- 24 chunks of 128 tokens, 36 layers, 2 KV
     heads, D 128 -- each chunk's bf16 K/V read as the model's cache holds them
     ([1, H, S, D] views of [1, S, H, D] projections), KIVI int8 + scales written into
@@ -646,7 +646,7 @@ class QuantizeStore:
 
 
 class CacheBlendRepair:
-    """CacheBlend repair of one config-3 prompt's stitched prefix (``kvb_cacheblend_fwd``):
+    """CacheBlend repair of one Qwen2.5-3B-architecture prompt's stitched prefix (``kvb_cacheblend_fwd``):
     3072 cached positions, 36 layers, 2 KV heads, D 128, bf16; cosine deviation of
     cached vs full-context K over all layers, top 15 % above 0.01, patch of those
     positions' K and V.  Cached K/V stacked [L, H, S, D] (the assembled prefix), the
@@ -762,7 +762,7 @@ class CacheBlendRepair:
 
 
 class TtftReuse:
-    """Config 3: TTFT at 75% prefix reuse through the engine on a random-init
+    """TTFT at 75% prefix reuse through the engine on a random-init
     Qwen2.5-3B-architecture decoder (36 layers, hidden 2048, 16 q / 2 KV heads,
     D 128, MLP 11008, vocab 151936, bf16).  8 prompts x 4096 seeded token ids share
     a 3072-token prefix (24 chunks) warmed first; each step is one
@@ -842,7 +842,7 @@ class TtftReuse:
 
 
 def run_cp(args, torch, dist, rank, world, local, dev):
-    """Config 5 with the prefix chunks placed round-robin across the ranks (chunk c on
+    """The paged int8 32K-prefix workload with the prefix chunks placed round-robin across the ranks (chunk c on
     rank c % N): every step all-gathers the int8 pool shards and the suffix K/V
     (NCCL over NVLink), dequantises prefix + suffix once, and runs this rank's
     zig-zag query chunks over all 64 query heads.  Strong scaling: the work of one
@@ -986,7 +986,7 @@ def run_cp(args, torch, dist, rank, world, local, dev):
 
 
 def run_ttft(args, torch, dist, rank, world, local, dev):
-    """Config 3 through the engine: TTFT (ms, lower is better)."""
+    """TTFT at 75% reuse through the engine (ms, lower is better)."""
     import numpy as np
     from kvboost_b200 import _lib, ops
     from kvboost_b200.engine import KVBoost

@@ -123,9 +123,9 @@ def test_packed_tile_pairs(B, Hq, Hkv, Sq, Skv, D, dtype, splits):
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,Sq,Skv,layout", [
-    (8, 16, 2, 16, 4096, "bhsd"),     # selective-recompute seam shape of the config-3 model
+    (8, 16, 2, 16, 4096, "bhsd"),     # selective-recompute seam shape of the Qwen2.5-3B architecture
     (2, 32, 8, 64, 6000, "bshd"),     # short reuse suffix, HF output layout
-    (1, 32, 32, 16, 8192, "bhsd"),    # MHA short suffix (config-4 short requests)
+    (1, 32, 32, 16, 8192, "bhsd"),    # MHA short suffix (short varlen requests)
 ])
 def test_prefill_routes_short_suffix(B, Hq, Hkv, Sq, Skv, layout):
     """prefill_attention sends short suffixes over long prefixes to the split-key

@@ -1,4 +1,4 @@
-"""GPU parity of the int8 paged reuse prefill (config-5 semantics).
+"""GPU parity of the int8 paged reuse prefill (KIVI int8 prefix in 16-token blocks).
 
 The cached prefix is KIVI-int8 quantised per 128-token chunk, stored in
 16-token blocks of a device pool at a seeded random permutation of block ids,
@@ -138,7 +138,7 @@ def test_paged_suffix_shorter_than_tile_mha():
 
 @pytest.mark.parametrize("fused_only", STRATEGIES)
 def test_paged_config5_full_size_last_rows(fused_only):
-    """Full config 5 on one GPU: P=32768 int8 prefix in an 8192-block pool, 2048 new
+    """The full 32K-prefix paged workload on one GPU: P=32768 int8 prefix in an 8192-block pool, 2048 new
     tokens, Hq 64 / Hkv 8, D 128; the last 64 query rows of every head are checked."""
     _run_case(1, 64, 8, 128, [[128] * 256], 2048, torch.bfloat16, seed=50, num_blocks=8192,
               rows=64, fused_only=fused_only)
