@@ -28,6 +28,8 @@ reference's metric is defined on; the public datasets are not available):
   (GB/s; one launch per chunk).
 * ``cacheblend`` -- CacheBlend repair of a 3072-position stitched prefix of the
   Qwen2.5-3B-architecture model (deviation over 36 layers, top 15 %, patch; GB/s; 3 launches).
+* ``long_causal`` -- long causal prefill (KV encoding of a 16384-token prompt): batch 1,
+  32 query / 8 KV heads, D 128, bf16, q = kv = 16384.
 * ``short_suffix`` -- reuse-dominated short-suffix prefill: 16 new tokens over a
   32768-token reused prefix, batch 8, 16 query / 2 KV heads, D 128 (the Qwen2.5-3B-architecture
   model's seam shape; split-key kernel through ``prefill_attention``; GB/s).
@@ -88,7 +90,7 @@ def parse():
     ap.add_argument("--workload", default="reuse_prefill",
                     choices=["reuse_prefill", "causal_op", "varlen_d96", "paged_long",
                              "ttft_reuse", "paged_long_cp", "decode", "quantize_store",
-                             "cacheblend", "short_suffix"])
+                             "cacheblend", "short_suffix", "long_causal"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kv-bits", type=int, default=16, choices=[16, 8],
                     help="ttft_reuse: the engine's chunk store (8: KIVI int8 block pool, "
@@ -257,6 +259,46 @@ class Decode(Dense):
             ho[slot].copy_(o, non_blocking=True)
         h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
         return step, h2d, ho[0].numel() * ho[0].element_size()
+
+
+class LongCausal(Dense):
+    """Long causal prefill: the KV encoding of one 16384-token prompt (q = kv), 32 query
+    heads over 8 KV heads, D 128, bf16.  Tensor-bound; many waves of query-tile pairs."""
+
+    def __init__(self):
+        super().__init__("long_causal", 1, 32, 8, 16384, 0, 128, "bf16",
+                         "long causal prefill: B1 Hq32/Hkv8 D128 bf16, q = kv = 16384")
+
+    def gpu_sdpa(self, torch, dev):
+        """The reference's torch tier for q == kv without a mask
+        (``flash_attn_ext.py:86-95``): SDPA with ``is_causal`` over K/V repeated to the
+        query heads."""
+        import torch.nn.functional as F
+        g = torch.Generator(device=dev).manual_seed(77)
+        q = torch.randn(self.B, self.Hq, self.Sq, self.D, generator=g, device=dev).to(self.dt)
+        k = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(self.dt)
+        v = torch.randn(self.B, self.Hkv, self.kv, self.D, generator=g, device=dev).to(self.dt)
+        rep = self.Hq // self.Hkv
+
+        def run():
+            F.scaled_dot_product_attention(q, k.repeat_interleave(rep, 1), v.repeat_interleave(rep, 1),
+                                           is_causal=True, scale=1.0 / math.sqrt(self.D))
+        return run
+
+    def cpu_sample(self, np):
+        """The last 256 query rows of one query head against all 16384 keys (the oracle
+        on the full launch would take hours on the host)."""
+        from oracle.attention import attention, attention_flops
+        g = np.random.default_rng(0)
+        n = 256
+        q = g.standard_normal((1, 1, n, self.D), dtype=np.float32)
+        k = g.standard_normal((1, 1, self.kv, self.D), dtype=np.float32)
+        v = g.standard_normal((1, 1, self.kv, self.D), dtype=np.float32)
+        fl = attention_flops([n], [self.kv], 1, self.D)
+
+        def run():
+            attention(q, k, v, 1.0 / math.sqrt(self.D), True, compute_dtype=np.float32)
+        return run, fl, f"the last {n} query rows of 1 of {self.Hq} heads"
 
 
 class ShortSuffix(Dense):
@@ -1147,6 +1189,8 @@ def make_workload(name, small=False):
         return CacheBlendRepair()
     if name == "short_suffix":
         return ShortSuffix()
+    if name == "long_causal":
+        return LongCausal()
     return PagedLong(small)
 
 
