@@ -48,11 +48,15 @@
 #include "kvb_attn.h"
 #include "kvb_sm100_ptx.cuh"
 
-// Share of exponent pairs computed on the FMA pipe: pair i of each 32-column
-// chunk uses the polynomial when (i % 8) < KVB_POLY_PAIRS_OF_8.
-#ifndef KVB_POLY_PAIRS_OF_8
-#define KVB_POLY_PAIRS_OF_8 0
-#endif
+// Share of exponent pairs computed on the FMA pipe instead of MUFU: pair i of
+// each chunk uses the polynomial when (i % 8) < the pairs-of-8 count.  At
+// D = 64 a tile's two MMAs take half the cycles of its exponentials, so moving
+// a quarter of them to the FMA pipe pays (+4-5 % measured); at D >= 96 the
+// MMAs already match the exponentials and it costs 3-5 %.
+template <int D>
+__host__ __device__ constexpr int poly_pairs_of_8() {
+  return D <= 64 ? 2 : 0;
+}
 // 1: pack bf16 probabilities with integer round-half-up + byte permute
 // instead of the cvt.rn.bf16x2.f32 conversion.
 #ifndef KVB_PACK_INT
@@ -358,7 +362,7 @@ __device__ __forceinline__ float cols_row_max(uint32_t tS, int c0, int lim) {
 
 // Softmax work on one chunk of CW columns already in registers (tile column
 // c): P pairs packed into pk, partial sums updated.
-template <typename T, bool MASK, int CW>
+template <typename T, bool MASK, int CW, int POLY>
 __device__ __forceinline__ void chunk_exp(const uint32_t (&r)[CW], int c, int lim, uint64_t sc2,
                                           uint64_t nm2, uint64_t& acc0, uint64_t& acc1,
                                           uint32_t (&pk)[CW / 2]) {
@@ -372,7 +376,7 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&r)[CW], int c, int li
     }
     const uint64_t a = ffma2(f2pack(x0, x1), sc2, nm2);
     float p0, p1;
-    if (!MASK && (i & 7) < KVB_POLY_PAIRS_OF_8) {
+    if (!MASK && (i & 7) < POLY) {
       ex2_poly_pair(a, p0, p1);
     } else {
       p0 = ptx::ex2(f2lo(a));
@@ -392,7 +396,7 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&r)[CW], int c, int li
 // chunk k+1 is in flight while chunk k is exponentiated.  S in TMEM is left
 // intact (the caller stores P only once the row sums pass the range check).
 // Returns the row sum of P over these columns (fp32, before rounding).
-template <typename T, bool MASK, int NCH, int CW>
+template <typename T, bool MASK, int NCH, int CW, int POLY>
 __device__ __forceinline__ float cols_exp(uint32_t tS, int c0, float sl2, float m_use, int lim,
                                           uint32_t (&pk)[NCH * CW / 2]) {
   const uint64_t sc2 = f2pack(sl2, sl2);
@@ -404,7 +408,7 @@ __device__ __forceinline__ float cols_exp(uint32_t tS, int c0, float sl2, float 
 #pragma unroll
   for (int k = 0; k < NCH; ++k) {
     if (k + 1 < NCH) tmem_ld_cw<CW>(tS + (k + 1) * CW, (k & 1) ? ra : rb);
-    chunk_exp<T, MASK, CW>((k & 1) ? rb : ra, c0 + k * CW, lim, sc2, nm2, acc0, acc1,
+    chunk_exp<T, MASK, CW, POLY>((k & 1) ? rb : ra, c0 + k * CW, lim, sc2, nm2, acc0, acc1,
                            *reinterpret_cast<uint32_t(*)[CW / 2]>(&pk[k * CW / 2]));
     if (k + 1 < NCH) ptx::tmem_wait_ld();
   }
@@ -1174,6 +1178,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     constexpr int COLS = BN / H;                  // S columns per thread
     constexpr int CW = (H == 1) ? 32 : 16;        // TMEM load width
     constexpr int NCH = COLS / CW;
+    constexpr int kPoly = poly_pairs_of_8<D>();
     constexpr int DH = D / H;                     // O columns per thread
     constexpr int OCW = (DH % 32 == 0) ? 32 : 16;
     const int grp = warp >> 2;
@@ -1229,8 +1234,8 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       uint32_t pk[COLS / 2];
       bool need = !ok || m_run == -INFINITY;
       if (!__any_sync(0xffffffffu, need)) {
-        sum = need_mask ? cols_exp<T, true, NCH, CW>(tS, hf * COLS, sl2, m_run, lim, pk)
-                        : cols_exp<T, false, NCH, CW>(tS, hf * COLS, sl2, m_run, lim, pk);
+        sum = need_mask ? cols_exp<T, true, NCH, CW, kPoly>(tS, hf * COLS, sl2, m_run, lim, pk)
+                        : cols_exp<T, false, NCH, CW, kPoly>(tS, hf * COLS, sl2, m_run, lim, pk);
         need = !(sum <= kSumLimit);  // also catches inf / NaN
       }
       if (pair_any(need)) {
@@ -1269,8 +1274,8 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
           }
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        sum = need_mask ? cols_exp<T, true, NCH, CW>(tS, hf * COLS, sl2, m_use, lim, pk)
-                        : cols_exp<T, false, NCH, CW>(tS, hf * COLS, sl2, m_use, lim, pk);
+        sum = need_mask ? cols_exp<T, true, NCH, CW, kPoly>(tS, hf * COLS, sl2, m_use, lim, pk)
+                        : cols_exp<T, false, NCH, CW, kPoly>(tS, hf * COLS, sl2, m_use, lim, pk);
       }
       store_p<COLS / 2>(tS, pk);
       l_run = l_run * alpha + sum;
