@@ -1,31 +1,37 @@
 // Offset-causal prefill attention for B200 (sm_100a).
 //
-// One CTA computes one 128-row query tile of one query head against the
-// visible part of its KV head:
+// One CTA (one per SM: 202 KB of shared memory, all 512 TMEM columns) runs two
+// 128-row query tiles ("slots") that share a KV head — two query heads of a
+// GQA pair, two consecutive tiles of one head, or (split-key mode) packed GQA
+// rows — in ping-pong against the visible part of that KV head:
 //
-//   warps 0-3  softmax / correction / epilogue.  Thread t owns query row t,
-//              which is TMEM lane t, so scores and the output row are read
-//              and written with 32x32b tcgen05.ld/st and no shuffles.
-//   warp 4     TMA producer: Q once, then K_j / V_j tiles (128 x D, 128-byte
-//              swizzle) into an NS-deep shared-memory ring.
-//   warp 5     MMA issuer (one thread) and TMEM owner:
-//                S_j  = Q K_j^T        tcgen05.mma SS, fp32 accumulator in TMEM
-//                O   += P_j V_j        tcgen05.mma TS, P read from TMEM
+//   warps 0-15  softmax / epilogue, two warpgroups per slot.  Thread t of a
+//               warpgroup owns query row t = TMEM lane t and one half of the
+//               key columns; the two threads of a row agree on the running
+//               maximum through 64-thread named-barrier reductions.
+//   warp 16     TMA producer: Q once per slot, then K_j / V_j tiles (128 x D,
+//               128-byte swizzle) into NS-deep shared-memory rings.
+//   warp 17     MMA issuer (one thread) and TMEM owner:
+//                 S_j  = Q K_j^T   tcgen05.mma SS, fp32 accumulator in TMEM
+//                 O   += P_j V_j   tcgen05.mma TS, P read from TMEM
+//               issued PV0(j), S0(j+1), PV1(j), S1(j+1), so one slot's MMAs
+//               overlap the other slot's softmax.
+//   (paged kernels: one softmax warpgroup per slot, three converter warps that
+//   gather int8 blocks through the block table and dequantise into the ring.)
 //
-// TMEM (256 columns): S at [0,128); P is written back over S as packed
-// 16-bit pairs in [0,64); O at [128, 128+DP).  256 columns and <=97 KB of
-// shared memory let two CTAs share an SM, so one CTA's MMAs overlap the
-// other's softmax.
+// TMEM: S0, S1, O0, O1 at columns 0/128/256/384; each warpgroup writes its P
+// as packed 16-bit pairs over the start of its own S columns.
 //
-// Online softmax runs in the log2 domain on scaled scores.  The running row
-// maximum is only raised when it grows by more than 8 (a factor of 256), so
-// most tiles skip the O rescale; the final normalisation uses the same
-// maximum, so this is exact up to rounding.
+// Online softmax runs in the log2 domain against a stale running maximum: a
+// tile is exponentiated in one pass, and the maximum is raised (tile maximum,
+// O rescale, redo) only when a thread's probability sum shows one could leave
+// the P operand's range; the final normalisation uses the same maximum, so
+// this is exact up to rounding.
 //
 // Causality is bottom-right (key j visible to query i iff
-// j <= i + kv_len - q_len) or, on request, top-left (j <= i); key tiles entirely above the diagonal are never
-// loaded, and only the tiles crossing the diagonal or the end of the keys
-// are masked element by element.
+// j <= i + kv_len - q_len) or, on request, top-left (j <= i); key tiles
+// entirely above the diagonal are never loaded, and only the tiles crossing
+// the diagonal or the end of the keys are masked element by element.
 //
 // Every mbarrier wait is bounded (KVB_WAIT_NS); a wait that gives up sets a
 // CTA-wide abort flag and ORs a code into the caller's status word, after
