@@ -1631,9 +1631,8 @@ static int decode_partials(const KvbPrefillParams& p, int eff_splits) {
   return decode_dual(p, eff_splits) ? (eff_splits + 1) / 2 * 2 : eff_splits;
 }
 
-// Arguments shared by both split-key decode kernels: partials in the workspace
-// after its counter header, merged into params.o / params.lse by each group's
-// last CTA.
+// Arguments of a split-key launch: partials in the workspace after its reserved
+// header, merged into params.o / params.lse by kvb_split_merge_kernel.
 static void decode_args(const KvbPrefillParams& p, int splits, int split_tiles, void* ws, DenseArgs* a,
                         PagedArgs* sp) {
   const int group = p.num_q_heads / p.num_kv_heads;

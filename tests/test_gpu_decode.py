@@ -116,7 +116,7 @@ def test_one_query_split_counts_agree():
 ])
 def test_packed_tile_pairs(B, Hq, Hkv, Sq, Skv, D, dtype, splits):
     """More packed rows than one CTA's two tiles: CTAs per (tile pair, key split),
-    each pair's partials merged by its own last CTA."""
+    every row's partials merged by the merge launch."""
     _case(B, Hq, Hkv, Sq, Skv, D, dtype, seed=Sq + Skv, splits=splits)
     _case(1, Hq, Hkv, Sq, Skv, D, dtype, seed=Sq + 1, splits=splits, top_left=True)
     _case(1, Hq, Hkv, Sq, Skv, D, dtype, seed=Sq + 2, splits=splits, causal=False)
