@@ -92,6 +92,10 @@ def parse():
                              "ttft_reuse", "paged_long_cp", "decode", "quantize_store",
                              "cacheblend", "short_suffix", "long_causal"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--varlen-split", default="replicate", choices=["replicate", "lpt"],
+                    help="varlen_d96 with N > 1: every rank runs the whole batch (weak "
+                         "scaling) or the 64 requests are placed longest-first over the "
+                         "ranks (strong scaling, no collective)")
     ap.add_argument("--kv-bits", type=int, default=16, choices=[16, 8],
                     help="ttft_reuse: the engine's chunk store (8: KIVI int8 block pool, "
                          "quantised on store, dequantised on assembly)")
@@ -388,7 +392,26 @@ class Varlen:
         return 2 * self.D * (2 * self.Hq * sum(self.sq) + 2 * self.Hkv * sum(self.skv))
 
     def tokens(self):
-        return sum(self.sq)
+        return getattr(self, "all_tokens", sum(self.sq))
+
+    def work(self):
+        """Per-rank share of the job's FLOPs (the value line multiplies by N)."""
+        return getattr(self, "all_flops", None) or self.flops()
+
+    def shard(self, rank, world):
+        """Keep this rank's requests of a longest-processing-time-first placement of
+        the batch over ``world`` ranks (every rank computes the same placement)."""
+        from kvboost_b200.sharding import lpt_partition, request_cost
+        from oracle.attention import attention_flops
+        self.all_flops = attention_flops(self.sq, self.skv, self.Hq, self.D) / world
+        self.all_tokens = sum(self.sq)
+        costs = [request_cost(a, b, self.Hq, self.Hkv, self.D) for a, b in zip(self.sq, self.skv)]
+        mine = lpt_partition(costs, world)[rank]
+        self.sq = [self.sq[i] for i in mine]
+        self.pre = [self.pre[i] for i in mine]
+        self.skv = [self.skv[i] for i in mine]
+        self.scaling = "strong"
+        self.desc += f"; requests placed longest-first over {world} ranks"
 
     def config(self):
         return {"requests": len(self.sq), "q_heads": self.Hq, "kv_heads": self.Hkv, "head_dim": self.D,
@@ -1347,6 +1370,8 @@ def main():
         return
 
     w = make_workload(args.workload, args.small)
+    if args.workload == "varlen_d96" and args.varlen_split == "lpt" and world > 1:
+        w.shard(rank, world)
     step = w.setup(torch, dev, rank, world)
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
@@ -1447,7 +1472,9 @@ def main():
         psrc = f"{peak_src} HBM copy"
     cfg = {"workload": w.name + (" (small profiling case)" if args.small else ""),
            "desc": w.desc, **w.config(),
-           "parallelism": (f"KV heads split over {world} ranks" if w.scaling == "strong"
+           "parallelism": ((f"requests placed longest-first over {world} ranks"
+                            if hasattr(w, "all_flops") else f"KV heads split over {world} ranks")
+                           if w.scaling == "strong"
                            else f"independent batches x{world}") if world > 1 else "single",
            "l2": w.sets_desc,
            "timing": f"CUDA graph of K launches between events, after {PREWARM_S} s of untimed replays"}

@@ -131,3 +131,42 @@ def test_zigzag_chunks_cover_and_balance():
         assert max(work) == min(work)
         idx = cp.zigzag_token_index(q_len, world)
         assert sorted(idx.tolist()) == list(range(q_len))
+
+
+def test_lpt_partition_covers_and_balances():
+    from kvboost_b200.sharding import lpt_partition, request_cost
+    import bench
+    w = bench.make_workload("varlen_d96")
+    costs = [request_cost(a, b, w.Hq, w.Hkv, w.D) for a, b in zip(w.sq, w.skv)]
+    for world in (1, 2, 4, 8):
+        parts = lpt_partition(costs, world)
+        assert sorted(i for p in parts for i in p) == list(range(len(costs)))
+        loads = [sum(costs[i] for i in p) for p in parts]
+        # longest-first placement: the slowest rank within 4/3 of the average share,
+        # or held up by one request alone
+        assert max(loads) <= max(sum(costs) / world * 4 / 3, max(costs)) + 1e-12
+    assert lpt_partition([3.0, 1.0, 2.0], 2) == [[0], [1, 2]]
+    assert lpt_partition([1.0, 1.0], 4) == [[0], [1], [], []]
+
+
+def _varlen_shard_rank(rank, world, out):
+    import bench
+    w = bench.make_workload("varlen_d96")
+    total = w.flops()
+    w.shard(rank, world)
+    out[rank] = (w.sq, w.skv, w.flops(), w.work(), total, w.scaling, w.tokens())
+
+
+def test_varlen_shards_agree_across_ranks():
+    """Each rank derives its share on its own; together they are the batch."""
+    import bench
+    full = bench.make_workload("varlen_d96")
+    out = {}
+    for r in range(4):
+        _varlen_shard_rank(r, 4, out)
+    pairs = sorted((a, b) for r in range(4) for a, b in zip(out[r][0], out[r][1]))
+    assert pairs == sorted(zip(full.sq, full.skv))
+    assert abs(sum(out[r][2] for r in range(4)) - full.flops()) < 1e-3 * full.flops()
+    for r in range(4):
+        assert abs(out[r][3] * 4 - full.flops()) < 1e-6 * full.flops()
+        assert out[r][5] == "strong" and out[r][6] == sum(full.sq)
