@@ -60,6 +60,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
+# what the CPU legs run, per workload family
+TORCH_PATH = ("the reference's CPU dispatch restated as its own torch calls (oracle/sdpa_ref.py, "
+              "bit-identical to its outputs): SDPA in the inputs' dtype")
+NUMPY_PATH = "the reference's arithmetic restated in numpy (oracle/)"
 # Untimed replays of the warm-up graph before the timed region, so that the
 # timed steps run at the clocks the GPU holds under load rather than during
 # its ramp from idle.
@@ -202,18 +206,34 @@ class Dense:
             F.scaled_dot_product_attention(q, kk, vv, attn_mask=mask, scale=1.0 / math.sqrt(self.D))
         return run
 
+    # the CPU sample: this many batch elements and query heads of one step
+    cpu_batch = None
+    cpu_heads = None
+
     def cpu_sample(self, np):
-        """One batch element through the oracle (numpy float32)."""
-        from oracle.attention import attention, attention_flops
-        g = np.random.default_rng(0)
-        q = g.standard_normal((1, self.Hq, self.Sq, self.D), dtype=np.float32)
-        k = g.standard_normal((1, self.Hkv, self.kv, self.D), dtype=np.float32)
-        v = g.standard_normal((1, self.Hkv, self.kv, self.D), dtype=np.float32)
-        fl = attention_flops([self.Sq], [self.kv], self.Hq, self.D)
+        """The reference's CPU path (``oracle.sdpa_ref``: torch SDPA in the inputs' dtype,
+        K/V expanded to the query heads, HF's bottom-right mask) on ``cpu_batch``
+        batch elements x ``cpu_heads`` query heads (with their KV heads) of one step."""
+        import torch
+        from oracle import sdpa_ref
+        from oracle.attention import attention_flops
+        nb = self.cpu_batch or self.B
+        nh = self.cpu_heads or self.Hq
+        group = self.Hq // self.Hkv
+        nkv = max(1, nh // group)
+        dt = torch.bfloat16 if self.dtype_name == "bf16" else torch.float16
+        g = torch.Generator().manual_seed(0)
+        q = torch.randn(nb, nh, self.Sq, self.D, generator=g).to(dt)
+        k = torch.randn(nb, nkv, self.kv, self.D, generator=g).to(dt)
+        v = torch.randn(nb, nkv, self.kv, self.D, generator=g).to(dt)
+        fl = attention_flops([self.Sq] * nb, [self.kv] * nb, nh, self.D)
+        scale = 1.0 / math.sqrt(self.D)
 
         def run():
-            attention(q, k, v, 1.0 / math.sqrt(self.D), True, compute_dtype=np.float32)
-        return run, fl, f"1 of {self.B} batch elements"
+            sdpa_ref.reuse_prefill(q, k, v, scale)
+        what = ("the whole step" if (nb, nh) == (self.B, self.Hq)
+                else f"{nb} of {self.B} batch elements x {nh} of {self.Hq} query heads")
+        return run, fl, what
 
 
 class Decode(Dense):
@@ -289,20 +309,7 @@ class LongCausal(Dense):
                                            is_causal=True, scale=1.0 / math.sqrt(self.D))
         return run
 
-    def cpu_sample(self, np):
-        """The last 256 query rows of one query head against all 16384 keys (the oracle
-        on the full launch would take hours on the host)."""
-        from oracle.attention import attention, attention_flops
-        g = np.random.default_rng(0)
-        n = 256
-        q = g.standard_normal((1, 1, n, self.D), dtype=np.float32)
-        k = g.standard_normal((1, 1, self.kv, self.D), dtype=np.float32)
-        v = g.standard_normal((1, 1, self.kv, self.D), dtype=np.float32)
-        fl = attention_flops([n], [self.kv], 1, self.D)
-
-        def run():
-            attention(q, k, v, 1.0 / math.sqrt(self.D), True, compute_dtype=np.float32)
-        return run, fl, f"the last {n} query rows of 1 of {self.Hq} heads"
+    cpu_heads = 1      # one query head of the full causal square: ~0.2 s on the host
 
 
 class ShortSuffix(Dense):
@@ -317,6 +324,7 @@ class ShortSuffix(Dense):
                          "over a 32768-token reused prefix (split-key kernel)")
         self.bound = "hbm"
         self.launches_per_step = 2    # split-key kernel + merge of its 128-row partials
+        self.cpu_batch = 1
 
     def setup(self, torch, dev, rank, world):
         from kvboost_b200 import ops
@@ -457,21 +465,22 @@ class Varlen:
         return step, h2d, ho[0].numel() * ho[0].element_size()
 
     def cpu_sample(self, np):
-        from oracle.attention import attention_varlen, attention_flops
-        n = 3  # the first 3 requests
-        g = np.random.default_rng(0)
+        """The reference's CPU path per request (``oracle.sdpa_ref``: fp16 SDPA with the
+        request's bottom-right mask, MHA) on the first 8 of the 64 requests."""
+        import torch
+        from oracle import sdpa_ref
+        from oracle.attention import attention_flops
+        n = 8
         sq, skv = self.sq[:n], self.skv[:n]
-        q = g.standard_normal((sum(sq), self.Hq, self.D), dtype=np.float32)
-        k = g.standard_normal((sum(skv), self.Hkv, self.D), dtype=np.float32)
-        v = g.standard_normal((sum(skv), self.Hkv, self.D), dtype=np.float32)
-        cq = np.concatenate([[0], np.cumsum(sq)])
-        ck = np.concatenate([[0], np.cumsum(skv)])
+        g = torch.Generator().manual_seed(0)
+        reqs = [tuple(torch.randn(1, self.Hq, m, self.D, generator=g).half() for m in (a, b, b))
+                for a, b in zip(sq, skv)]
         fl = attention_flops(sq, skv, self.Hq, self.D)
 
         def run():
-            attention_varlen(q, k, v, cq, ck, 1.0 / math.sqrt(self.D), True,
-                             compute_dtype=np.float32)
-        return run, fl, f"the first {n} of 64 requests"
+            for q, k, v in reqs:
+                sdpa_ref.reuse_prefill(q, k, v, 1.0 / math.sqrt(self.D))
+        return run, fl, f"the first {n} of {len(self.sq)} requests"
 
 
 class PagedLong:
@@ -569,30 +578,34 @@ class PagedLong:
         return step, h2d, ho[0].numel() * ho[0].element_size()
 
     def cpu_sample(self, np):
-        """One query head of the full workload with its KV head: dequantise + gather by
-        the block table + attention, the reference's host path (numpy float32)."""
-        from oracle.attention import attention, attention_flops
-        from oracle.kv_quant import dequantize_int8
-        g = np.random.default_rng(0)
-        nblk = self.P // 16
-        kq = g.integers(-127, 128, size=(1, self.P, self.D), dtype=np.int8)
-        vq = g.integers(-127, 128, size=(1, self.P, self.D), dtype=np.int8)
-        ks = (np.abs(g.standard_normal((1, self.P, 1))) / 40 + 1e-3).astype(np.float16)
-        vs = (np.abs(g.standard_normal((1, self.P // 128, self.D))) / 40 + 1e-3).astype(np.float16)
-        perm = g.permutation(nblk)
-        q = g.standard_normal((1, 1, self.Sq, self.D), dtype=np.float32)
-        kn = g.standard_normal((1, 1, self.Sq, self.D), dtype=np.float32)
-        vn = g.standard_normal((1, 1, self.Sq, self.D), dtype=np.float32)
-        fl = attention_flops([self.Sq], [self.P + self.Sq], 1, self.D)
+        """One KV-head group (1 KV head, its 8 query heads) of the full step through the
+        reference's host path (``oracle.sdpa_ref``): ``dequantize_kv`` of the int8
+        chunks (float16 product), ``read_kv`` through the block table, the suffix
+        appended, K/V expanded to the query heads, SDPA with the bottom-right mask."""
+        import torch
+        from oracle import sdpa_ref
+        from oracle.attention import attention_flops
+        g = torch.Generator().manual_seed(0)
+        nblk, grp = self.P // 16, self.Hq // self.Hkv
+        pool_q = torch.randint(-127, 128, (self.num_blocks, 2, 1, 16, self.D), generator=g,
+                               dtype=torch.int8)
+        k_scale = (torch.rand(self.num_blocks, 1, 16, 1, generator=g) / 40 + 1e-3).half()
+        v_scale = (torch.rand(self.num_blocks, 1, 1, self.D, generator=g) / 40 + 1e-3).half()
+        table = torch.randperm(self.num_blocks, generator=g)[:nblk].tolist()
+        q = torch.randn(1, grp, self.Sq, self.D, generator=g).bfloat16()
+        kn = torch.randn(1, 1, self.Sq, self.D, generator=g).bfloat16()
+        vn = torch.randn(1, 1, self.Sq, self.D, generator=g).bfloat16()
+        fl = attention_flops([self.Sq], [self.P + self.Sq], grp, self.D)
 
         def run():
-            tok = (perm[np.arange(self.P) // 16] * 16 + np.arange(self.P) % 16) % self.P
-            k = dequantize_int8(kq[:, tok], ks[:, tok]).astype(np.float32)
-            v = dequantize_int8(vq[:, tok], np.repeat(vs, 128, axis=1)[:, tok]).astype(np.float32)
-            K = np.concatenate([k[None], kn], axis=2)
-            V = np.concatenate([v[None], vn], axis=2)
-            attention(q, K, V, 1.0 / math.sqrt(self.D), True, compute_dtype=np.float32)
-        return run, fl, "1 of 64 query heads (its KV head gathered and dequantised)"
+            used = pool_q[table]      # the reused chunks' blocks, dequantised, in table order
+            pool = torch.stack([sdpa_ref.dequantize_int8(used[:, 0], k_scale[table]),
+                                sdpa_ref.dequantize_int8(used[:, 1], v_scale[table])], 1)
+            k, v = sdpa_ref.read_kv(pool.bfloat16(), range(nblk), self.P)
+            K = torch.cat([k[None], kn], dim=2)
+            V = torch.cat([v[None], vn], dim=2)
+            sdpa_ref.reuse_prefill(q, K, V, 1.0 / math.sqrt(self.D))
+        return run, fl, f"1 of {self.Hkv} KV-head groups ({grp} query heads)"
 
 
 class QuantizeStore:
@@ -696,6 +709,8 @@ class QuantizeStore:
                     self.alloc.write_chunk_int8(layer, blocks, *quantize_chunk_int8(ks[layer],
                                                                                     vs[layer]))
         return run, "torch ops: _quantize_int8 per layer + write_chunk_int8 scatter"
+
+    cpu_path = NUMPY_PATH
 
     def cpu_sample(self, np):
         """One chunk, all layers: the reference's bf16 quantisation arithmetic (numpy)."""
@@ -811,6 +826,8 @@ class CacheBlendRepair:
                 cv[l][:, idx] = fv[l][0][:, idx]
         return run, "torch ops: cosine_similarity per layer, mean, topk, index copy"
 
+    cpu_path = NUMPY_PATH
+
     def cpu_sample(self, np):
         """The whole repair through the oracle (numpy; the reference's CPU steps)."""
         from oracle import cacheblend as ocb
@@ -858,18 +875,21 @@ class TtftReuse:
 
     def cpu_sample(self, np):
         """Attention of the suffix prefill for one prompt, one layer and one KV-head
-        group (8 query heads over 1 KV head) through the oracle; the projection to
-        the whole batch multiplies by prompts x layers x KV heads."""
-        from oracle.attention import attention, attention_flops
-        g = np.random.default_rng(0)
+        group (8 query heads over 1 KV head) through the reference's CPU dispatch
+        (``oracle.sdpa_ref``, bf16); the projection to the whole batch multiplies by
+        prompts x layers x KV heads."""
+        import torch
+        from oracle import sdpa_ref
+        from oracle.attention import attention_flops
+        g = torch.Generator().manual_seed(0)
         grp = self.HQ // self.HKV
-        q = g.standard_normal((1, grp, self.SUFFIX, self.D), dtype=np.float32)
-        k = g.standard_normal((1, 1, self.PREFIX + self.SUFFIX, self.D), dtype=np.float32)
-        v = g.standard_normal((1, 1, self.PREFIX + self.SUFFIX, self.D), dtype=np.float32)
+        q = torch.randn(1, grp, self.SUFFIX, self.D, generator=g).bfloat16()
+        k = torch.randn(1, 1, self.PREFIX + self.SUFFIX, self.D, generator=g).bfloat16()
+        v = torch.randn(1, 1, self.PREFIX + self.SUFFIX, self.D, generator=g).bfloat16()
         fl = attention_flops([self.SUFFIX], [self.PREFIX + self.SUFFIX], grp, self.D)
 
         def run():
-            attention(q, k, v, 1.0 / math.sqrt(self.D), True, compute_dtype=np.float32)
+            sdpa_ref.reuse_prefill(q, k, v, 1.0 / math.sqrt(self.D))
         return run, fl, "suffix-prefill attention of 1 prompt x 1 layer x 1 KV-head group"
 
     def projection(self):
@@ -1186,8 +1206,8 @@ def run_ttft(args, torch, dist, rank, world, local, dev):
         _, n, el = time_cpu(run, sfl)
         line["cpu_baseline"] = {
             "value": el / n * w.projection() * 1e3, "unit": "ms (suffix-prefill attention only)",
-            "cores": cores, "kind": "port",
-            "sample": f"{n} x {sample}, numpy float32 oracle, {el:.1f} s; projected x"
+            "cores": cores, "kind": "port", "cpu": cpu_model(),
+            "sample": f"{n} x {sample}, {TORCH_PATH}, {el:.1f} s; projected x"
                       f"{w.projection()} (prompts x layers x KV heads)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -1285,16 +1305,34 @@ def time_cpu(run, fl, budget_s=10.0, max_iters=100000):
 
 
 def cpu_threads():
+    """All host threads for the CPU legs (torch intra-op and BLAS pools)."""
+    n = os.cpu_count()
     try:
         from threadpoolctl import threadpool_limits
-        threadpool_limits(limits=os.cpu_count())
+        threadpool_limits(limits=n)
     except Exception:  # pragma: no cover
         pass
-    return os.cpu_count()
+    import torch
+    torch.set_num_threads(n)
+    return n
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
 
 
 def run_reference(args):
-    """--impl reference: the reference's CPU path (restated: numpy, all host threads)."""
+    """--impl reference: the reference's CPU path on all host threads (its own torch
+    calls for attention, ``oracle/sdpa_ref.py``; numpy restatements for the store and
+    CacheBlend workloads)."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
     import numpy as np
@@ -1314,12 +1352,12 @@ def run_reference(args):
             "impl": "reference", "metric": "TTFT at 75% prefix reuse", "value": val,
             "unit": "ms", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": val, "higher_is_better": False, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": args.workload, "desc": w.desc,
                        "sample": sample + " per step; attention of the suffix prefill only"},
             "cpu_baseline": {"value": val, "unit": "ms (suffix-prefill attention only)",
-                             "cores": cores, "kind": "port",
-                             "sample": sample + ", numpy float32 restatement (oracle/)"},
+                             "cores": cores, "kind": "port", "cpu": cpu_model(),
+                             "sample": sample + ", " + TORCH_PATH},
             "e2e": {"value": val, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
         print(json.dumps(line), flush=True)
@@ -1331,12 +1369,14 @@ def run_reference(args):
         "impl": "reference", "metric": metric, "value": val,
         "unit": munit, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": w.scaling,
-        "vs_baseline": None, "dtype": getattr(w, "dtype_name", "f32") if hasattr(w, "work") else "f32",
+        "vs_baseline": None,
+        "dtype": getattr(w, "dtype_name", "f32") if getattr(w, "cpu_path", TORCH_PATH) == TORCH_PATH
+        else "f32",
         "data": "synthetic",
         "config": {"workload": args.workload, "desc": w.desc, "sample": sample + " per step"},
         "cpu_baseline": {"value": val, "unit": munit, "cores": cores, "kind": "port",
-                         "sample": sample + " per step, numpy restatement of the "
-                                   "reference's CPU path (oracle/)"},
+                         "cpu": cpu_model(),
+                         "sample": sample + " per step, " + getattr(w, "cpu_path", TORCH_PATH)},
         "e2e": {"value": val, "unit": munit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -1533,7 +1573,9 @@ def main():
         v, n, el = time_cpu(run, sfl)
         v = v * 1e12 / mscale
         line["cpu_baseline"] = {"value": v, "unit": munit, "cores": cores, "kind": "port",
-                                "sample": f"{n} x {sample}, numpy oracle, {el:.1f} s"}
+                                "cpu": cpu_model(),
+                                "sample": f"{n} x {sample}, {getattr(w, 'cpu_path', TORCH_PATH)}, "
+                                          f"{el:.1f} s"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     del gw, gt

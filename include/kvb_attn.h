@@ -307,9 +307,14 @@ int kvb_paged_materialize_peers(const KvbPagedPrefillParams* params,
  * the materialise kernel writes every row the attention kernel reads.
  *
  * The first call on a device looks up the scratch's address (which loads the
- * library's module on that device); make it before any stream capture.  Calls
- * share one scratch per device: two calls that overlap in time (different
- * streams or host threads) race on it.
+ * library's module on that device); make it before any stream capture.  The
+ * address is looked up again after a context teardown (cudaDeviceReset), so
+ * the first call after one should also precede any capture.  Under lazy module
+ * loading (the default since CUDA 12.2) only processes that use the library's
+ * kernels on a device hold the 32 MiB there; with CUDA_MODULE_LOADING=EAGER
+ * every process that loads the library holds it on each device it uses.
+ * Calls share one scratch per device: two calls that overlap in time
+ * (different streams or host threads) race on it.
  */
 int kvb_paged_prefill_fwd_noalloc(const KvbPagedPrefillParams* params, void* stream);
 

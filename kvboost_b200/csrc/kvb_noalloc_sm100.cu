@@ -8,13 +8,20 @@
 // reservation and its release, where a new allocation would grow the pool.
 // Nothing here calls cudaMalloc/cudaFree or an allocating library routine.
 //
-// The array lives in this translation unit (its own module), so processes that
-// never call this entry point do not reserve it.  The first call on a device
-// looks up its address with cudaGetSymbolAddress, which loads the module on
-// that device; make that call before any stream capture.  Every call on a
-// device shares the one array: calls that overlap in time (different streams
-// or host threads) race on it.
+// The array lives in this library's module.  Under lazy module loading (the
+// default since CUDA 12.2, CUDA_MODULE_LOADING=LAZY) a process reserves it on
+// a device only once something in the module runs or is looked up there; with
+// CUDA_MODULE_LOADING=EAGER every process that loads the library reserves the
+// 32 MiB on each device it uses.  The first call on a device looks up its
+// address with cudaGetSymbolAddress, which loads the module on that device;
+// make that call before any stream capture.  The address is kept per device
+// together with the context it belongs to: after a context teardown
+// (cudaDeviceReset) the next call looks it up again in the new context, so,
+// like the first call, it should come before any stream capture.  Every call
+// on a device shares the one array: calls that overlap in time (different
+// streams or host threads) race on it.
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -36,9 +43,26 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 
-// Address of this device's copy of the scratch; looked up once per device,
-// with that device current.
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+
+// cuCtxGetCurrent through the runtime's driver entry point (no link to libcuda).
+CtxGetCurrent ctx_get_current() {
+  static CtxGetCurrent fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrent>(p);
+  });
+  return fn;
+}
+
+// Address of this device's copy of the scratch, looked up with that device
+// current once per device and context.
 int scratch_for_current_device(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
@@ -47,14 +71,19 @@ int scratch_for_current_device(void** out) {
   if (dev < 0 || dev >= kMaxDevices)
     return kvb_detail_fail(KVB_ERR_UNSUPPORTED, "device ordinal " + std::to_string(dev) +
                                                     " is beyond the scratch table");
+  CtxGetCurrent get_ctx = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (get_ctx == nullptr || get_ctx(&ctx) != CUDA_SUCCESS)
+    return kvb_detail_fail(KVB_ERR_CUDA, "cuCtxGetCurrent is not available");
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
+  if (g_scratch_ptr[dev] == nullptr || g_scratch_ctx[dev] != ctx) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess || ptr == nullptr)
       return kvb_detail_fail(KVB_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") +
                                                cudaGetErrorString(e));
     g_scratch_ptr[dev] = ptr;
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_ptr[dev];
   return KVB_OK;

@@ -3,7 +3,7 @@
 Run from the repository root in a checkout that has the reference source
 (``KVBOOST_REF_SRC`` points at its ``src`` directory)::
 
-    KVBOOST_REF_SRC=/root/reference/src python tests/golden/make_golden.py
+    KVBOOST_REF_SRC=<reference checkout>/src python tests/golden/make_golden.py
 
 Writes ``tests/golden/*.npz`` / ``*.json``.  The fixtures are small (well
 under 2 MB together) and are what ``tests/test_oracle_golden.py`` pins the
@@ -24,7 +24,9 @@ Reference entry points exercised (file:line in the KVBoost project):
   fixtures) and ``CacheBlendRecompute._deviation_recompute``
   (``cacheblend.py:103-197``) with a preset full-context K/V.
 
-``python tests/golden/make_golden.py blocks`` rewrites only the last two.
+``python tests/golden/make_golden.py blocks`` rewrites only the last two;
+``engine`` writes ``engine.json`` (the reference engine's greedy choices on the
+random-init Qwen2.5-3B-architecture decoder, ``engine_model.py``).
 """
 
 from __future__ import annotations
@@ -369,6 +371,12 @@ def assembly_cases(models, cr):
     groups = [[base[:512] + [1] * 40, base[:512] + [2] * 40], [base[:300], base[:200] + [5] * 100],
               [base[:128] * 2, base[:256]]]
     out["common_prefix"] = [{"ids": g, "common": kb.find_common_chunk_prefix(g, 128)} for g in groups]
+    # group_by_prefix (batch.py:86-104): prompts keyed by their first three chunks
+    tail = lambda n: rng.integers(0, 50000, size=n).tolist()
+    many = [base[:400] + tail(30), other[:200], base[:384] + tail(5), base[:383] + tail(90),
+            [], base[:500], other[:200] + [9], tail(100)]
+    out["group_by_prefix"] = {"ids": many, "groups": list(
+        kb.group_by_prefix([""] * len(many), many, 128).values())}
     out["stored"] = {"base": base[:640], "other": other}
     return out
 
@@ -380,6 +388,109 @@ def main_assembly():
     print("assembly fixture written")
 
 
+class _TopK:
+    """Records the top candidates of every greedy choice the reference engine makes
+    (``InferenceEngine._sample``, ``engine.py:982-988``), in call order."""
+
+    K = 8
+
+    def __init__(self, engine_cls):
+        self.cls = engine_cls
+        self.orig = engine_cls.__dict__["_sample"].__func__
+        self.calls = []
+
+    def __enter__(self):
+        orig, calls, k = self.orig, self.calls, self.K
+
+        def recording(logits, temperature, do_sample):
+            top = logits.float().reshape(-1).topk(k)
+            chosen = orig(logits, temperature, do_sample)
+            calls.append((top.indices.tolist(), top.values.tolist(), int(chosen)))
+            return chosen
+        self.cls._sample = staticmethod(recording)
+        return self
+
+    def __exit__(self, *exc):
+        self.cls._sample = staticmethod(self.orig)
+
+    def take(self):
+        out, self.calls[:] = list(self.calls), []
+        return out
+
+
+def engine_cases():
+    """The reference's ``InferenceEngine`` in CHUNK_KV_REUSE mode on the CPU
+    (``engine.py:207-365``, ``:415-507``, ``:592-753``) on the random-init
+    Qwen2.5-3B-architecture decoder of ``engine_model.py``, one engine, one
+    scripted sequence of calls:
+
+    1. ``warm`` of a 3072-token prefix (24 chunks of 128);
+    2. ``generate`` of prefix + 1024 new tokens, ``recompute_strategy`` "none",
+       32 new tokens;
+    3. ``generate`` of another 1024-token suffix with "selective" (23 seams),
+       32 new tokens;
+    4. ``generate_batch`` of 8 prompts of 3072 + 1024 tokens (the TTFT workload's
+       shape), 16 new tokens;
+    5. ``generate_batch`` of 3 prompts with ragged suffixes (1024 / 700 / 333
+       tokens; the reference right-pads them and passes no mask), 16 new tokens.
+
+    Stored per call: the generated ids, ``cached_tokens``, ``prompt_tokens``,
+    ``kv_reuse_ratio``, the top-8 candidates (ids and logits) of every greedy
+    choice; at the end the prefix-chained keys of every cached chunk."""
+    sys.path.insert(0, HERE)
+    import engine_model as em
+    from kvboost.engine import InferenceEngine, RecomputeStrategy
+    model = em.build_model(0)
+    tok = em.IntTokenizer()
+    eng = InferenceEngine(model, tok, max_cache_bytes=64 << 30,
+                          recompute_strategy=RecomputeStrategy.NONE, device="cpu")
+    prefix, singles, batch, ragged = em.prompts()
+    out = {"weights": em.weight_checksum(model), "calls": []}
+    with _TopK(InferenceEngine) as rec:
+        w = eng.warm(em.text(prefix))
+        out["warm"] = {"chunks_stored": w.chunks_stored, "token_count": w.token_count,
+                       "aligned": w.chunk_boundary_aligned}
+
+        def one(kind, strategy, prompts, new):
+            eng.recompute_strategy = RecomputeStrategy(strategy)
+            if kind == "generate":
+                rs = [eng.generate(em.text(prompts[0]), max_new_tokens=new)]
+            else:
+                rs = eng.generate_batch([em.text(p) for p in prompts], max_new_tokens=new)
+            calls = rec.take()
+            B = len(rs)
+            gen = [[int(t) for t in r.output_text.split()] for r in rs]
+            assert all(len(g) == new for g in gen), "an end-of-sequence id was generated"
+            # call order: single prompt = steps; batch = step-major over the prompts
+            tops = [[calls[s * B + b] for s in range(new)] for b in range(B)]
+            for b in range(B):    # (the top-k order of tied logits is arbitrary)
+                assert [t[2] for t in tops[b]] == gen[b]
+            out["calls"].append({
+                "kind": kind, "strategy": strategy, "new_tokens": new,
+                "prompts": [list(p) for p in prompts],
+                "generated": gen,
+                "cached_tokens": [r.cached_tokens for r in rs],
+                "prompt_tokens": [r.prompt_tokens for r in rs],
+                "kv_reuse_ratio": [r.kv_reuse_ratio for r in rs],
+                "top_ids": [[t[0] for t in tb] for tb in tops],
+                "top_logits": [[t[1] for t in tb] for tb in tops]})
+            print(kind, strategy, "done", [g[:4] for g in gen], flush=True)
+
+        one("generate", "none", singles[:1], 32)
+        one("generate", "selective", singles[1:], 32)
+        one("batch", "none", batch, 16)
+        one("batch", "none", ragged, 16)
+    out["chunk_keys"] = sorted(eng.cache_manager._hot.keys())
+    return out
+
+
+def main_engine():
+    _ref()
+    with open(os.path.join(HERE, "engine.json"), "w") as f:
+        json.dump(engine_cases(), f)
+    print("engine fixture written")
+
+
 def main_blocks():
     """The quantise-on-store and CacheBlend fixtures."""
     fae, kq, models, cr, ba, c2b, pac = _ref()
@@ -389,11 +500,14 @@ def main_blocks():
 
 
 if __name__ == "__main__":
-    # with arguments, only the named groups: core, assembly, blocks
-    groups = sys.argv[1:] or ["core", "assembly", "blocks"]
+    # with arguments, only the named groups: core, assembly, blocks, engine
+    # (engine runs a 3B-parameter model on the CPU: about ten minutes)
+    groups = sys.argv[1:] or ["core", "assembly", "blocks", "engine"]
     if "core" in groups:
         main()
     if "assembly" in groups:
         main_assembly()
     if "blocks" in groups:
         main_blocks()
+    if "engine" in groups:
+        main_engine()

@@ -65,7 +65,8 @@ def test_cpu_samples_are_bounded():
     for name in ("reuse_prefill", "long_causal", "short_suffix"):
         run, fl, sample = bench.make_workload(name).cpu_sample(np)
         assert fl > 0 and sample
-        assert fl < 5e9     # a sample the host finishes in well under a second
+        # torch SDPA runs at >= 0.3 TFLOP/s on 8 host cores: well under a second
+        assert fl < 1e11
 
 
 def test_reference_arm_prints_one_line():

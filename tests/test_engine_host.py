@@ -15,7 +15,7 @@ import torch
 
 from kvboost_b200.engine import (DeviceChunk, DeviceChunkStore, chained_hash,
                                  content_hash_from_tokens, find_common_chunk_prefix, fixed_split,
-                                 plan_reuse)
+                                 group_by_prefix, plan_reuse)
 from oracle import hashing as ohash
 
 
@@ -58,6 +58,38 @@ def test_reuse_plan_matches_reference_assembler(assembly, name):
 def test_common_chunk_prefix_matches_reference(assembly):
     for g in assembly["common_prefix"]:
         assert find_common_chunk_prefix(g["ids"], 128) == g["common"]
+
+
+def test_common_chunk_prefix_chunkwise():
+    """The same answer as comparing whole chunks from the start (``batch.py:31-54``)
+    on random prompt sets that diverge at random places."""
+    import random
+    rnd = random.Random(3)
+
+    def chunkwise(all_ids, c):
+        if len(all_ids) < 2:
+            return len(all_ids[0]) if all_ids else 0
+        n, common = min(len(x) for x in all_ids), 0
+        for i in range(0, n - c + 1, c):
+            if any(x[i:i + c] != all_ids[0][i:i + c] for x in all_ids[1:]):
+                break
+            common = i + c
+        return common
+
+    for _ in range(300):
+        base = [rnd.randrange(50) for _ in range(rnd.randrange(0, 700))]
+        group = []
+        for _ in range(rnd.randrange(1, 5)):
+            cut = rnd.randrange(0, len(base) + 1)
+            group.append(base[:cut] + [rnd.randrange(50) for _ in range(rnd.randrange(0, 300))])
+        for c in (16, 128):
+            assert find_common_chunk_prefix(group, c) == chunkwise(group, c)
+    assert find_common_chunk_prefix([], 128) == 0
+
+
+def test_group_by_prefix_matches_reference(assembly):
+    case = assembly["group_by_prefix"]
+    assert list(group_by_prefix(case["ids"], 128).values()) == case["groups"]
 
 
 def test_store_lru_eviction_by_bytes():

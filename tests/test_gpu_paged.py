@@ -53,7 +53,7 @@ def _oracle_prefix(alloc, tbl, P):
 
 
 def _run_case(B, Hq, Hkv, D, chunk_sets, Sq, dtype, seed, num_blocks=512, rows=None,
-              fused_only=False):
+              fused_only=False, heads=None):
     from kvboost_b200.paged import (DeviceBlockAllocator, block_table_tensor,
                                     paged_prefill_attention, quantize_chunk_int8)
     g = torch.Generator().manual_seed(seed + 1)
@@ -100,6 +100,12 @@ def _run_case(B, Hq, Hkv, D, chunk_sets, Sq, dtype, seed, num_blocks=512, rows=N
         lb = lse[b:b + 1].cpu().numpy()
         if rows is not None:  # the last `rows` queries only (same bottom-right offsets)
             qb, ob, lb = qb[:, :, -rows:], ob[:, :, -rows:], lb[:, :, -rows:]
+        if heads is not None:  # whole GQA groups [h0, h1) of query heads, every row
+            h0, h1 = heads
+            g = Hq // Hkv
+            assert h0 % g == 0 and h1 % g == 0
+            qb, ob, lb = qb[:, h0:h1], ob[:, h0:h1], lb[:, h0:h1]
+            k_all, v_all = k_all[:, h0 // g:h1 // g], v_all[:, h0 // g:h1 // g]
         o_ref, l_ref = oattn.attention(qb, k_all, v_all, 1.0 / math.sqrt(D), True,
                                        compute_dtype=np.float32)
         err = np.abs(ob - o_ref).max()
@@ -142,6 +148,15 @@ def test_paged_config5_full_size_last_rows(fused_only):
     tokens, Hq 64 / Hkv 8, D 128; the last 64 query rows of every head are checked."""
     _run_case(1, 64, 8, 128, [[128] * 256], 2048, torch.bfloat16, seed=50, num_blocks=8192,
               rows=64, fused_only=fused_only)
+
+
+@pytest.mark.parametrize("fused_only", STRATEGIES)
+def test_paged_config5_full_size_whole_group(fused_only):
+    """The full 32K-prefix paged workload (P 32768 int8 in an 8192-block pool at a seeded
+    permutation, 2048 new tokens, Hq 64 / Hkv 8, D 128, bf16): every one of the 2048 query
+    rows of one whole GQA group (8 query heads over KV head 5) against the oracle."""
+    _run_case(1, 64, 8, 128, [[128] * 256], 2048, torch.bfloat16, seed=51, num_blocks=8192,
+              heads=(40, 48), fused_only=fused_only)
 
 
 @pytest.mark.parametrize("fused_only", STRATEGIES)

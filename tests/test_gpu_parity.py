@@ -196,6 +196,32 @@ def test_varlen_config4_shape():
     assert np.max(np.abs(lse.cpu().numpy() - lse_ref)) <= LSE_TOL
 
 
+def test_varlen_config4_full_size():
+    """The whole varlen D96 batch as the bench draws it: 64 requests, suffixes U{16..512},
+    prefixes 128 * U{0..64} (up to 8192 tokens), 32 heads MHA, fp16; every row of every
+    head of every request against the oracle."""
+    import bench
+    from kvboost_b200.ops import prefill_attention_varlen
+    w = bench.make_workload("varlen_d96")
+    sq, skv, H, D = w.sq, w.skv, w.Hq, w.D
+    assert len(sq) == 64 and max(w.pre) > 4096
+    g = torch.Generator().manual_seed(404)
+    cu_q = np.concatenate([[0], np.cumsum(sq)]).astype(np.int32)
+    cu_k = np.concatenate([[0], np.cumsum(skv)]).astype(np.int32)
+    q = _rand((int(cu_q[-1]), H, D), torch.float16, g)
+    k = _rand((int(cu_k[-1]), H, D), torch.float16, g)
+    v = _rand((int(cu_k[-1]), H, D), torch.float16, g)
+    o, lse = prefill_attention_varlen(q.cuda(), k.cuda(), v.cuda(),
+                                      torch.from_numpy(cu_q).cuda(), torch.from_numpy(cu_k).cuda(),
+                                      max(sq), max(skv), 1.0 / math.sqrt(D), True)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = oattn.attention_varlen(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                            cu_q, cu_k, 1.0 / math.sqrt(D), True,
+                                            compute_dtype=np.float32)
+    assert np.max(np.abs(o.float().cpu().numpy() - o_ref)) <= TOL[torch.float16]
+    assert np.max(np.abs(lse.cpu().numpy() - lse_ref)) <= LSE_TOL
+
+
 def test_golden_vectors_through_gpu(golden_dir):
     """The reference's own outputs (SDPA) on its own inputs, rerun on the GPU path."""
     from kvboost_b200.ops import prefill_attention

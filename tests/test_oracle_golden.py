@@ -213,3 +213,31 @@ def test_cacheblend_selection_matches_reference(golden_dir, case):
     k = ocb.num_select(S, float(d[p + "ratio"]))
     got = ocb.select(dev, k, float(d[p + "min_dev"]))
     assert got == d[p + "patched_positions"].tolist()
+
+
+def _torch_vals(arr, dtype_code):
+    import torch
+    if dtype_code == 0:
+        return torch.from_numpy(arr.astype(np.float32))
+    t = torch.from_numpy(arr.astype(np.uint16).view(np.int16).copy())
+    return t.view(torch.bfloat16 if dtype_code == 1 else torch.float16)
+
+
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_timed_cpu_path_reproduces_reference_bits(golden_dir, case):
+    """``oracle.sdpa_ref`` (what the CPU baseline and the reference arm of the bench
+    time) reproduces the reference dispatcher's outputs bit for bit."""
+    import torch
+    from oracle import sdpa_ref
+    d = _load(golden_dir, "attention.npz")
+    B, Hq, Hkv, Sq, Skv, D, causal, dt = d[case + "/meta"].tolist()
+    q, k, v = (_torch_vals(d[f"{case}/{n}"], dt) for n in "qkv")
+    if causal:
+        o = sdpa_ref.reuse_prefill(q, k, v, 1.0 / math.sqrt(D))
+    else:
+        rep = Hq // Hkv
+        o = sdpa_ref.kvboost_flash_attn_cpu(q, k.repeat_interleave(rep, 1),
+                                            v.repeat_interleave(rep, 1), 1.0 / math.sqrt(D),
+                                            False)
+    ref = _torch_vals(d[case + "/o"], dt)
+    assert o.dtype == ref.dtype and torch.equal(o, ref)

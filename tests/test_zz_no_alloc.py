@@ -1,13 +1,19 @@
-"""GPU: ``kvb_paged_prefill_fwd_noalloc`` against ``kvb_paged_prefill_fwd``.
+"""GPU: ``kvb_paged_prefill_fwd_noalloc`` against ``kvb_paged_prefill_fwd`` and the oracle.
 
 The no-allocation entry point keeps the dequantised prefix in the library's
 static per-device scratch instead of a workspace the caller allocates.  On two
 calls in a row (the second reuses the scratch the first wrote) it must agree
-with the existing entry point within the paged tests' tolerance, allocate no
-device memory after its first call, and reject requests larger than the
-scratch.  The file name sorts last so it also runs after every other test.
+with the existing entry point and with the oracle (the reference's host path:
+dequantise, gather by the block table, bottom-right causal attention) within
+the paged tests' tolerance; a small ragged call after a large one must not see
+the large call's rows left in the scratch; it must allocate no device memory
+after its first call, and reject requests larger than the scratch.  The file
+name sorts last so it also runs after every other test.
 """
 
+import math
+
+import numpy as np
 import pytest
 import torch
 
@@ -49,7 +55,31 @@ def _case(B, Hq, Hkv, D, prefixes, Sq, dtype, seed, num_blocks=512):
     bt = block_table_tensor(tables, "cuda")
     plens = (torch.tensor(prefixes, dtype=torch.int32, device="cuda")
              if len(set(prefixes)) > 1 else None)
-    return q, kn, vn, alloc, bt, max(prefixes), plens
+    return q, kn, vn, alloc, bt, max(prefixes), plens, tables
+
+
+def _oracle(q, kn, vn, alloc, tables, prefixes, dtype):
+    """O and LSE of the reference's host path for every sequence (float32)."""
+    from oracle import attention as oattn
+    from oracle import paged as opaged
+    pool = alloc.pools[0].cpu().numpy()
+    ks = alloc.k_scale16[0].cpu().numpy()
+    vs = alloc.v_scale16[0].cpu().numpy()
+    D = q.shape[-1]
+    outs, lses = [], []
+    for b, P in enumerate(prefixes):
+        H = kn.shape[1]
+        kp, vp = (opaged.dequant_gather(pool, ks, vs, tables[b], P, 16) if P else   # float16
+                  (np.zeros((H, 0, D), np.float16), np.zeros((H, 0, D), np.float16)))  # [H, P, D]
+        kp = torch.from_numpy(kp).to(dtype).float().numpy()              # to the model dtype
+        vp = torch.from_numpy(vp).to(dtype).float().numpy()
+        k_all = np.concatenate([kp, kn[b].float().cpu().numpy()], axis=1)[None]
+        v_all = np.concatenate([vp, vn[b].float().cpu().numpy()], axis=1)[None]
+        o, l = oattn.attention(q[b:b + 1].float().cpu().numpy(), k_all, v_all,
+                               1.0 / math.sqrt(D), True, compute_dtype=np.float32)
+        outs.append(o[0])
+        lses.append(l[0])
+    return np.stack(outs), np.stack(lses)
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,D,prefixes,Sq,dtype", [
@@ -60,7 +90,8 @@ def _case(B, Hq, Hkv, D, prefixes, Sq, dtype, seed, num_blocks=512):
 def test_noalloc_matches_existing_entry_point(B, Hq, Hkv, D, prefixes, Sq, dtype):
     from kvboost_b200.ops import status_word
     from kvboost_b200.paged import paged_prefill_attention, paged_prefill_attention_noalloc
-    q, kn, vn, alloc, bt, P, plens = _case(B, Hq, Hkv, D, prefixes, Sq, dtype, seed=B * 100 + D)
+    q, kn, vn, alloc, bt, P, plens, tables = _case(B, Hq, Hkv, D, prefixes, Sq, dtype,
+                                                   seed=B * 100 + D)
     ref, ref_lse = paged_prefill_attention(q, kn, vn, alloc, 0, bt, P, prefix_lens=plens)
     st = status_word(q.device)
     outs = [torch.full_like(q, float("nan")) for _ in range(2)]
@@ -69,15 +100,44 @@ def test_noalloc_matches_existing_entry_point(B, Hq, Hkv, D, prefixes, Sq, dtype
         paged_prefill_attention_noalloc(q, kn, vn, alloc, 0, bt, P, o, lse=l, prefix_lens=plens,
                                         status=st)
     torch.cuda.synchronize()
+    o_or, l_or = _oracle(q, kn, vn, alloc, tables, prefixes, dtype)
     for o, l in zip(outs, lses):
         assert torch.isfinite(o).all()
         assert (o.float() - ref.float()).abs().max().item() <= TOL[dtype]
         assert (l - ref_lse).abs().max().item() <= 2e-3
+        assert np.abs(o.float().cpu().numpy() - o_or).max() <= TOL[dtype]
+        assert np.abs(l.cpu().numpy() - l_or).max() <= 2e-3
+
+
+def test_noalloc_small_ragged_call_after_large_call():
+    """The scratch keeps the last call's rows.  A large call (B 4, long prefixes)
+    fills most of it; a smaller call with ragged prefixes that follows must read
+    only what it wrote itself: equal to the existing entry point and the oracle."""
+    from kvboost_b200.ops import status_word
+    from kvboost_b200.paged import paged_prefill_attention, paged_prefill_attention_noalloc
+    big = _case(4, 16, 4, 128, [3072, 2944, 3072, 2000], 256, torch.bfloat16, seed=11,
+                num_blocks=1024)
+    q, kn, vn, alloc, bt, P, plens, _ = big
+    out = torch.empty_like(q)
+    st = status_word(q.device)
+    paged_prefill_attention_noalloc(q, kn, vn, alloc, 0, bt, P, out, prefix_lens=plens, status=st)
+    prefixes = [300, 0, 1100]
+    q, kn, vn, alloc, bt, P, plens, tables = _case(3, 8, 2, 128, prefixes, 77, torch.bfloat16,
+                                                   seed=12)
+    small = torch.full_like(q, float("nan"))
+    paged_prefill_attention_noalloc(q, kn, vn, alloc, 0, bt, P, small, prefix_lens=plens,
+                                    status=st)
+    ref, _ = paged_prefill_attention(q, kn, vn, alloc, 0, bt, P, prefix_lens=plens)
+    torch.cuda.synchronize()
+    assert torch.isfinite(small).all()
+    assert (small.float() - ref.float()).abs().max().item() <= TOL[torch.bfloat16]
+    o_or, _ = _oracle(q, kn, vn, alloc, tables, prefixes, torch.bfloat16)
+    assert np.abs(small.float().cpu().numpy() - o_or).max() <= TOL[torch.bfloat16]
 
 
 def test_noalloc_allocates_nothing_after_setup():
     from kvboost_b200.paged import paged_prefill_attention_noalloc
-    q, kn, vn, alloc, bt, P, plens = _case(1, 8, 2, 128, [1024], 512, torch.bfloat16, seed=7)
+    q, kn, vn, alloc, bt, P, plens, _ = _case(1, 8, 2, 128, [1024], 512, torch.bfloat16, seed=7)
     out = torch.empty_like(q)
     paged_prefill_attention_noalloc(q, kn, vn, alloc, 0, bt, P, out)   # first call: setup
     torch.cuda.synchronize()
