@@ -477,10 +477,16 @@ class KVBoost:
 
     # ── assembly and seam repair ─────────────────────────────────────────────
     def _assemble(self, token_ids: TokenIds, repair_seams: bool = True):
+        """Stacked ``[L, H, P, D]`` K/V of the reused run (seams repaired per the
+        strategy), its length and its chunk boundaries."""
+        return self._assemble_run(token_ids, repair_seams)[:4]
+
+    def _assemble_run(self, token_ids: TokenIds, repair_seams: bool = True):
+        """``_assemble`` plus the list of reused chunks."""
         chunks, cached_len, boundaries = plan_reuse(token_ids, self.store, self.chunk_size,
                                                     self.min_chunk_tokens)
         if not chunks:
-            return None, None, 0, boundaries
+            return None, None, 0, boundaries, chunks
         keys, values = self._chunk_kv(chunks)
         if repair_seams and len(boundaries) > 1:
             if self.recompute_strategy == RecomputeStrategy.SELECTIVE:
@@ -488,7 +494,7 @@ class KVBoost:
             elif self.recompute_strategy == RecomputeStrategy.CACHEBLEND:
                 keys, values = self._cacheblend(token_ids, keys.contiguous(), values.contiguous(),
                                                 cached_len)
-        return keys, values, cached_len, boundaries
+        return keys, values, cached_len, boundaries, chunks
 
     def _cacheblend(self, token_ids, keys, values, cached_len):
         """``cacheblend.py:103-197``: a full-context forward over the cached tokens,

@@ -215,6 +215,10 @@ def _patch_module(module: torch.nn.Module) -> bool:
     registry = _registry_of(fn)
 
     def patched_forward(self, *args, **kwargs):
+        if _PAGED_ATTR in self.__dict__:
+            # a paged interceptor wraps this forward and has put its own function in
+            # the registry for this call: leave it there
+            return original_forward(*args, **kwargs)
         g = fn.__globals__ if hasattr(fn, "__globals__") else {}
         old_sdpa = g.get(_LEGACY_SDPA_NAME, None)
         had_sdpa = _LEGACY_SDPA_NAME in g

@@ -458,6 +458,10 @@ class DeviceChunkMapper:
     def loaded_chunks(self) -> int:
         return len(self._chunk_blocks)
 
+    def blocks_used_by_chunks(self) -> int:
+        with self._lock:
+            return sum(len(v) for v in self._chunk_blocks.values())
+
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """Scratch for the materialised-prefix strategy, taken from torch's caching

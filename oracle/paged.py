@@ -13,6 +13,8 @@ TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).
   ``build_block_table`` / ``on_evict`` (``chunk_to_blocks.py:57-139``):
   ``ceil(len/bs)`` fresh blocks per new chunk, a fork of the same ids on a
   repeat load, and concatenation in chunk order.
+* ``append_slots`` restates the block bookkeeping of ``append_kv_to_blocks``
+  (``cpu_paged/paged_attn_cpu.py:111-163``).
 * ``gather`` restates ``BlockAllocator.read_kv`` (``block_allocator.py:178-206``):
   logical token ``t`` lives at ``(table[t // bs], t % bs)``.
 """
@@ -89,6 +91,21 @@ class MapperModel:
         ids = self.chunk_blocks.pop(chunk_id, None)
         if ids is not None:
             self.alloc.free(ids)
+
+
+def append_slots(alloc: AllocatorModel, table: List[int], slot_offset: int, n: int,
+                 block_size: int):
+    """Block bookkeeping of ``append_kv_to_blocks`` (``cpu_paged/paged_attn_cpu.py:111-163``)
+    for ``n`` tokens from logical slot ``slot_offset``: a block is allocated when the
+    table runs out, and every touched block is made writable (copy-on-write) in
+    token order.  Returns ``(table, slot_offset + n)``."""
+    table = list(table)
+    for t in range(n):
+        bi = (slot_offset + t) // block_size
+        if bi >= len(table):
+            table.extend(alloc.allocate(1))
+        table[bi] = alloc.ensure_writable(table[bi])
+    return table, slot_offset + n
 
 
 def gather(pool_kv: np.ndarray, table: List[int], seq_len: int):

@@ -109,13 +109,8 @@ def test_block_tables_bit_exact(golden_dir):
     shared = a.fork(t["load_c1"][:2])
     assert a.ensure_writable(shared[0]) == t["cow_first"]
     # append 20 tokens at slot 128 of c1's table: one new block, CoW on shared ids
-    table = list(t["load_c1"])
-    for slot in range(128, 148):
-        bi = slot // 16
-        if bi >= len(table):
-            table.extend(a.allocate(1))
-        table[bi] = a.ensure_writable(table[bi])
-    assert table == t["append_20_after_128"]
+    table, off = opaged.append_slots(a, list(t["load_c1"]), 128, 20, 16)
+    assert table == t["append_20_after_128"] and off == t["append_new_offset"]
     assert len(a.free_list) == t["free_blocks_end"]
     assert a.free_list == t["free_list_end"]
 
