@@ -96,6 +96,9 @@ def parse():
                              "ttft_reuse", "paged_long_cp", "decode", "quantize_store",
                              "cacheblend", "short_suffix", "long_causal"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the long paged prefill sharded over the ranks that the "
+                         "default workload's line carries beside its own number")
     ap.add_argument("--varlen-split", default="replicate", choices=["replicate", "lpt"],
                     help="varlen_d96 with N > 1: every rank runs the whole batch (weak "
                          "scaling) or the 64 requests are placed longest-first over the "
@@ -413,6 +416,9 @@ class Varlen:
         from oracle.attention import attention_flops
         self.all_flops = attention_flops(self.sq, self.skv, self.Hq, self.D) / world
         self.all_tokens = sum(self.sq)
+        if world > len(self.sq):
+            raise SystemExit(f"varlen_d96 --varlen-split lpt: {len(self.sq)} requests cannot "
+                             f"give each of {world} ranks one")
         costs = [request_cost(a, b, self.Hq, self.Hkv, self.D) for a, b in zip(self.sq, self.skv)]
         mine = lpt_partition(costs, world)[rank]
         self.sq = [self.sq[i] for i in mine]
@@ -1382,6 +1388,85 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def time_graph_steps(torch, dist, step, steps, warmup, dev, world, stream, prewarm_s=0.2):
+    """K steps captured in one CUDA graph, replayed between two events on ``stream``
+    after untimed replays and the W warm-up steps; returns the max over ranks of
+    the elapsed milliseconds."""
+    with torch.cuda.stream(stream):
+        step(0)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        gw, gt = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gw, stream=stream):
+            for i in range(warmup):
+                step(i)
+        with torch.cuda.graph(gt, stream=stream):
+            for i in range(steps):
+                step(i)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        t_end = time.time() + prewarm_s
+        while time.time() < t_end:
+            gt.replay()
+            gw.replay()
+            stream.synchronize()
+        gw.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        gt.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del gw, gt
+    return ms
+
+
+def sharded_paged_line(torch, dist, rank, world, dev, steps=20, warmup=3):
+    """The long paged int8 reuse prefill (32K-token prefix, 2048 new tokens, 64/8 heads)
+    sharded over the job's ranks by KV head (each rank holds its heads' pool shard;
+    no collective), beside the headline line: per-step time (max over ranks), the
+    whole job's TFLOP/s, and the same prefill on one GPU (rank 0 alone, all 8 KV
+    heads) for the speed-up and the strong-scaling efficiency."""
+    from oracle.attention import attention_flops
+    full = PagedLong()
+    fl_all = attention_flops([full.Sq], [full.P + full.Sq], full.Hq, full.D)
+    stream = torch.cuda.Stream(device=dev)
+    w = PagedLong()
+    ms_n = time_graph_steps(torch, dist, w.setup(torch, dev, rank, world), steps, warmup, dev,
+                            world, stream) / steps
+    del w
+    torch.cuda.empty_cache()
+    ms_1 = None
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        w1 = PagedLong()
+        ms_1 = time_graph_steps(torch, dist, w1.setup(torch, dev, 0, 1), steps, warmup, dev, 1,
+                                stream) / steps
+        del w1
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+    out = {"workload": "paged_long (" + full.desc + ")",
+           "parallelism": f"KV heads split over {world} ranks, no collective",
+           "scaling": "strong", "n_gpus": world, "ms_per_step": ms_n,
+           "value": fl_all / (ms_n / 1e3) / 1e12, "unit": "TFLOP/s",
+           "prefill_tokens_per_s": full.Sq / (ms_n / 1e3)}
+    if ms_1 is not None:
+        out["one_gpu_ms_per_step"] = ms_1
+        out["speedup_vs_one_gpu"] = ms_1 / ms_n
+        out["strong_scaling_efficiency"] = ms_1 / ms_n / world
+    return out
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1576,9 +1661,12 @@ def main():
                                 "cpu": cpu_model(),
                                 "sample": f"{n} x {sample}, {getattr(w, 'cpu_path', TORCH_PATH)}, "
                                           f"{el:.1f} s"}
+    del gw, gt
+    if args.workload == "reuse_prefill" and not args.no_sharded and not args.small \
+            and 8 % world == 0:
+        line["sharded_paged_long"] = sharded_paged_line(torch, dist, rank, world, dev)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del gw, gt
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -64,7 +64,8 @@ enum {
   KVB_STATUS_SOFTMAX_WAIT = 4, /* softmax warps waited too long for scores    */
   KVB_STATUS_EPILOGUE_WAIT = 8,/* epilogue waited too long for the output     */
   KVB_STATUS_BAD_BLOCK = 16,    /* a block-table entry was outside the pool    */
-  KVB_STATUS_BAD_LENGTH = 32    /* a chunk's token count did not fit its blocks */
+  KVB_STATUS_BAD_LENGTH = 32,   /* a chunk's token count did not fit its blocks */
+  KVB_STATUS_PEER_WAIT = 64     /* a cross-GPU barrier waited too long for a peer */
 };
 
 /*
@@ -288,6 +289,26 @@ int64_t kvb_peer_shard_layout(int num_kv_heads, int head_dim, int shard_blocks,
  * pool is one host process's memory. */
 int kvb_paged_materialize_peers(const KvbPagedPrefillParams* params,
                                 const KvbPeerShards* shards, void* stream);
+
+/* Signal words of a bounded cross-GPU barrier.  slot[r] is rank r's array of
+ * `world` uint32 words (zero before the first barrier) as mapped in the calling
+ * process (peer-mapped memory, e.g. symmetric memory over NVLink). */
+typedef struct KvbPeerSignals {
+  uint32_t* slot[8];
+  int32_t world;
+  int32_t rank;
+} KvbPeerSignals;
+
+/* Barrier of the context-parallel group before kvb_paged_materialize_peers:
+ * enqueued on `stream`, it stores `epoch` into word `rank` of every rank's
+ * array, then waits until every word of this rank's array has reached `epoch`
+ * (epochs grow by one per barrier, starting at 1).  Every write this GPU made
+ * before the launch is visible to a peer once it sees the word.  A wait still
+ * unsatisfied after timeout_ns ORs KVB_STATUS_PEER_WAIT into *status and the
+ * kernel returns (no trap, the context stays usable).  Plain peer stores and
+ * loads only.  No counterpart in the reference, which runs on one host. */
+int kvb_peer_barrier(const KvbPeerSignals* signals, uint32_t epoch, int64_t timeout_ns,
+                     int* status, void* stream);
 
 /* Size of the static device scratch of kvb_paged_prefill_fwd_noalloc: 32 MiB. */
 #define KVB_NOALLOC_SCRATCH_BYTES (32ll << 20)

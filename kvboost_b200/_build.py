@@ -19,7 +19,8 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB_NAME = "_kvb_attn.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
-SOURCES = ["kvb_prefill_sm100.cu", "kvb_noalloc_sm100.cu", "kvb_kvstore_sm100.cu"]
+SOURCES = ["kvb_prefill_sm100.cu", "kvb_noalloc_sm100.cu", "kvb_kvstore_sm100.cu",
+           "kvb_peer_sm100.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -22,7 +22,7 @@ KVB_ERR_UNSUPPORTED = 2
 KVB_ERR_CUDA = -1
 KVB_NOALLOC_SCRATCH_BYTES = 32 << 20
 KVB_POOL_INT8_KIVI, KVB_POOL_COMPUTE = 0, 1
-KVB_STATUS_BAD_BLOCK, KVB_STATUS_BAD_LENGTH = 16, 32
+KVB_STATUS_BAD_BLOCK, KVB_STATUS_BAD_LENGTH, KVB_STATUS_PEER_WAIT = 16, 32, 64
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -50,6 +50,12 @@ class KvbPeerShards(ctypes.Structure):
 
     _fields_ = [("base", _vp * 8), ("world", _i32), ("shard_blocks", _i32),
                 ("zigzag_rows", _i32), ("reserved0", _i32)]
+
+
+class KvbPeerSignals(ctypes.Structure):
+    """Mirror of ``KvbPeerSignals``."""
+
+    _fields_ = [("slot", _vp * 8), ("world", _i32), ("rank", _i32)]
 
 
 class KvbPagedPrefillParams(ctypes.Structure):
@@ -158,6 +164,9 @@ def load() -> ctypes.CDLL:
         lib.kvb_paged_materialize_peers.argtypes = [ctypes.POINTER(KvbPagedPrefillParams),
                                                     ctypes.POINTER(KvbPeerShards), _vp]
         lib.kvb_paged_materialize_peers.restype = ctypes.c_int
+        lib.kvb_peer_barrier.argtypes = [ctypes.POINTER(KvbPeerSignals), ctypes.c_uint32,
+                                         ctypes.c_int64, _vp, _vp]
+        lib.kvb_peer_barrier.restype = ctypes.c_int
         lib.kvb_peer_shard_layout.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, ctypes.POINTER(ctypes.c_int64)]
         lib.kvb_peer_shard_layout.restype = ctypes.c_int64

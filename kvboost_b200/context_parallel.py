@@ -163,6 +163,27 @@ def zigzag_prefill(q_local: torch.Tensor, K: torch.Tensor, V: torch.Tensor, pref
     return out
 
 
+BARRIER_TIMEOUT_NS = 2_000_000_000
+
+
+def peer_barrier(signal_slots: Sequence[int], rank: int, epoch: int, device,
+                 timeout_ns: int = BARRIER_TIMEOUT_NS,
+                 status: Optional[torch.Tensor] = None) -> None:
+    """``kvb_peer_barrier`` on the current stream of ``device``: ``signal_slots[r]`` is
+    rank r's signal array (``world`` int32 words) as mapped here.  A wait that runs
+    out ORs ``KVB_STATUS_PEER_WAIT`` into the status word (read it with
+    ``ops.read_status``); the call itself never blocks the host."""
+    sig = _lib.KvbPeerSignals()
+    for r, ptr in enumerate(signal_slots):
+        sig.slot[r] = ptr
+    sig.world, sig.rank = len(signal_slots), rank
+    st = status if status is not None else status_word(torch.device(device))
+    with torch.cuda.device(device):
+        rc = _lib.load().kvb_peer_barrier(sig, epoch, timeout_ns, st.data_ptr(),
+                                          _stream_handle(torch.device(device)))
+    _lib.check(rc, "kvb_peer_barrier")
+
+
 class PeerShardBuffer:
     """This rank's shard of a context-parallel prompt, in memory the other ranks
     read directly over NVLink.
@@ -194,6 +215,7 @@ class PeerShardBuffer:
             raise ValueError("unsupported shard geometry")
         self.offsets = list(off)
         self.handle = None
+        self.epoch = 0
         if symmetric:
             import torch.distributed as dist
             import torch.distributed._symmetric_memory as symm_mem
@@ -201,6 +223,14 @@ class PeerShardBuffer:
             grp = group if group is not None else dist.group.WORLD
             self.handle = symm_mem.rendezvous(self.buf, grp)
             self.bases = [int(p) for p in self.handle.buffer_ptrs]
+            # the barrier's signal words: one int32 per rank, zero before the first use
+            self.sig = symm_mem.empty(8, dtype=torch.int32, device=device)
+            self.sig.zero_()
+            self.sig_handle = symm_mem.rendezvous(self.sig, grp)
+            self.sig_slots = [int(p) for p in self.sig_handle.buffer_ptrs]
+            self.rank = dist.get_rank(grp)
+            torch.cuda.synchronize(device)
+            dist.barrier(group=grp)
         else:
             self.buf = torch.zeros(total, dtype=torch.uint8, device=device)
             self.bases = [self.buf.data_ptr()]
@@ -214,10 +244,15 @@ class PeerShardBuffer:
         self.suffix_v = b[off[4]:total].view(dtype).view(H, r2, D)
 
     def barrier(self, timeout_ms: int = 2000) -> None:
-        """Every rank's writes to its shard buffer are visible to the others after this
-        (a device-side barrier over the peers' signal pads, bounded by the timeout)."""
+        """Every rank's writes to its shard buffer are visible to the others after this:
+        ``kvb_peer_barrier`` over the ranks' signal words, enqueued on the current
+        stream.  A rank that does not arrive within the timeout makes the others'
+        barrier kernels give up and set ``KVB_STATUS_PEER_WAIT`` in their status
+        words instead of hanging."""
         if self.handle is not None:
-            self.handle.barrier(channel=0, timeout_ms=timeout_ms)
+            self.epoch += 1
+            peer_barrier(self.sig_slots, self.rank, self.epoch, self.buf.device,
+                         timeout_ns=int(timeout_ms) * 1_000_000)
 
 
 def materialize_from_peers(bases: Sequence[int], shard_blocks: int, zz_rows: int,

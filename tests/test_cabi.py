@@ -91,6 +91,7 @@ def test_ctypes_layouts_match_c_compiler(tmp_path):
     structs = {"KvbPrefillParams": _lib.KvbPrefillParams,
                "KvbPagedPrefillParams": _lib.KvbPagedPrefillParams,
                "KvbPeerShards": _lib.KvbPeerShards,
+               "KvbPeerSignals": _lib.KvbPeerSignals,
                "KvbQuantizeStoreParams": _lib.KvbQuantizeStoreParams,
                "KvbQuantizeStoreBatch": _lib.KvbQuantizeStoreBatch,
                "KvbCacheBlendParams": _lib.KvbCacheBlendParams}
@@ -237,3 +238,30 @@ def test_quantize_store_batch_validation(lib, field, value, needle):
     setattr(p, field, value)
     assert lib.kvb_quantize_store_batch(ctypes.byref(p), None) == _lib.KVB_ERR_INVALID
     assert needle in lib.kvb_last_error().decode()
+
+
+@pytest.mark.parametrize("field,value,needle", [
+    ("world", 0, "world must be in"), ("world", 9, "world must be in"),
+    ("rank", 2, "rank must be in"), ("slot", None, "non-null and 4-byte"),
+])
+def test_peer_barrier_validation(lib, field, value, needle):
+    """Argument errors come back before anything launches (no device needed)."""
+    sig = _lib.KvbPeerSignals()
+    sig.world, sig.rank = 2, 0
+    sig.slot[0], sig.slot[1] = 4096, 8192
+    if field == "slot":
+        sig.slot[1] = value
+    else:
+        setattr(sig, field, value)
+    rc = lib.kvb_peer_barrier(ctypes.byref(sig), 1, 1_000_000, None, None)
+    assert rc == _lib.KVB_ERR_INVALID or rc == _lib.KVB_ERR_UNSUPPORTED
+    assert needle in lib.kvb_last_error().decode()
+
+
+def test_peer_barrier_rejects_epoch_zero_and_bad_timeouts(lib):
+    sig = _lib.KvbPeerSignals()
+    sig.world, sig.rank, sig.slot[0] = 1, 0, 4096
+    assert lib.kvb_peer_barrier(ctypes.byref(sig), 0, 1_000_000, None, None) == _lib.KVB_ERR_INVALID
+    assert lib.kvb_peer_barrier(ctypes.byref(sig), 1, 0, None, None) == _lib.KVB_ERR_INVALID
+    assert lib.kvb_peer_barrier(ctypes.byref(sig), 1, 61 * 10**9, None, None) == \
+        _lib.KVB_ERR_INVALID

@@ -5,7 +5,9 @@ shard of a 1152-token int8 paged prefix and the suffix K/V of its zig-zag
 query rows; both gather paths (NCCL all-gather, and the dequantise kernel
 reading the peers' symmetric-memory shards over NVLink) must give every rank's
 rows the result of the unsharded paged prefill, which each rank can compute
-because all shards are generated from one seed.
+because all shards are generated from one seed.  The peers path orders the
+shard writes with ``kvb_peer_barrier``; a barrier one rank skips makes the
+other's give up within its limit and report ``KVB_STATUS_PEER_WAIT``.
 """
 
 import os
@@ -70,11 +72,23 @@ def _worker(rank, world, port, q):
         o_nccl = cp.cp_reuse_prefill(ql, kl, vl, local, gathered, P, Sq)
         torch.cuda.synchronize()
         want = ref[:, :, rows]
+        from kvboost_b200 import _lib, ops
+        status = ops.read_status(dev)            # the peer barrier passed on every rank
         err = torch.tensor([(o_peer.float() - want.float()).abs().max().item(),
-                            (o_nccl.float() - want.float()).abs().max().item()], device=dev)
+                            (o_nccl.float() - want.float()).abs().max().item(), float(status)],
+                           device=dev)
         dist.all_reduce(err, op=dist.ReduceOp.MAX)
+        # A rank that does not come to a barrier (a failure made on the host, between
+        # steps, with nothing of its own in flight): the other rank's barrier kernel
+        # gives up after its limit and reports it in the status word.
+        missed = 0
         if rank == 0:
-            q.put(err.tolist())
+            shards.barrier(timeout_ms=100)
+            torch.cuda.synchronize()
+            missed = ops.read_status(dev) & _lib.KVB_STATUS_PEER_WAIT
+        dist.barrier()
+        if rank == 0:
+            q.put(err.tolist() + [missed])
         dist.barrier()
     except Exception as e:  # report, then let the group time out the peer if it waits
         q.put(repr(e))
@@ -97,5 +111,7 @@ def test_context_parallel_two_gpus():
     for p in procs:
         p.join(timeout=120)
     assert isinstance(res, list), res
-    assert max(res) <= 2e-2, res
+    assert max(res[:2]) <= 2e-2, res
+    assert res[2] == 0, res          # no barrier gave up while both ranks took part
+    assert res[3] != 0, res          # the lone rank's barrier reported the missing peer
     assert all(p.exitcode == 0 for p in procs)
