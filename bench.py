@@ -1444,10 +1444,10 @@ def sharded_paged_line(torch, dist, rank, world, dev, steps=20, warmup=3):
                             world, stream) / steps
     del w
     torch.cuda.empty_cache()
-    ms_1 = None
+    ms_1 = ms_n if world == 1 else None
     if world > 1:
         dist.barrier()
-    if rank == 0:
+    if rank == 0 and world > 1:
         w1 = PagedLong()
         ms_1 = time_graph_steps(torch, dist, w1.setup(torch, dev, 0, 1), steps, warmup, dev, 1,
                                 stream) / steps

@@ -813,7 +813,6 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  ptx::griddep_wait();
 
   // ---- work item: two query tiles sharing one KV head ---------------------
   const int b = blockIdx.z;
@@ -841,6 +840,26 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     mtile[1] = 2 * x + 1;
   }
   const int kvh = head[0] / a.group;
+  if (!PAGED && !SPLITKV && warp == kWarpTma && lane == 0 && a.cu_q == nullptr &&
+      a.kv_prefix == nullptr) {
+    // While the preceding grid finishes, pull this CTA's query tiles and first
+    // key / value tiles into L2 (plain dense layout only: the coordinates come
+    // from the kernel's parameters, no global read).  L2 is where every write
+    // of that grid lands, so the loads after the wait below still see them;
+    // the prefetch only moves the first HBM reads ahead.
+#pragma unroll
+    for (int sl = 0; sl < kSlots; ++sl)
+      if (mtile[sl] * BM < a.q_len)
+#pragma unroll
+        for (int at = 0; at < G::NATOM; ++at)
+          ptx::tma_prefetch_l2_4d(&tm_q, at * 64, mtile[sl] * BM, head[sl], b);
+#pragma unroll
+    for (int at = 0; at < G::NATOM; ++at) {
+      ptx::tma_prefetch_l2_4d(&tm_k, at * 64, 0, kvh, b);
+      ptx::tma_prefetch_l2_4d(&tm_v, at * 64, 0, kvh, b);
+    }
+  }
+  ptx::griddep_wait();
   int q_len = a.q_len, kv_len = a.kv_len, q_base = 0, k_base = 0, tb = b;
   int P = 0;  // paged: cached-prefix tokens of this sequence
   if (PAGED) {

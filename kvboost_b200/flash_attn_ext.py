@@ -349,7 +349,10 @@ def install_paged_attention(model: torch.nn.Module, state: dict) -> int:
         original_forward = module.forward
         module.__dict__[_PAGED_ATTR] = layer_idx
         module.__dict__["_paged_original_forward"] = original_forward
-        fn = getattr(original_forward, "__func__", original_forward)
+        # a module already routed by install_flash_attention keeps the model's own
+        # forward under _original_forward: the registry is found through that
+        base = module.__dict__.get("_original_forward", original_forward)
+        fn = getattr(base, "__func__", base)
         registry = _registry_of(fn)
         if registry is None:
             raise NotImplementedError("paged attention needs transformers' attention registry")
