@@ -162,7 +162,7 @@ __device__ __forceinline__ uint2 kivi_q8(const float (&x)[8], const float (&sc)[
     const uint32_t r = (u + (kHalf - 1) + ((u >> kDrop) & 1u)) & ~kMask;
     const float t = fminf(fmaxf(__uint_as_float(r), -128.0f), 127.0f);
     w[e] = __float_as_uint(t + 12582912.0f);
-    near |= static_cast<uint32_t>(abs(static_cast<int>(u & kMask) - static_cast<int>(kHalf))) <= 8u;
+    near |= ((u - (kHalf - 8u)) & kMask) <= 16u;     // low bits within 8 of the halfway point
   }
   if (near)
     return kivi_q8_exact<T>(make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]),
@@ -297,24 +297,53 @@ __device__ __forceinline__ void quantize_store_v(const QStoreUnit& u, int h, int
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int kG = kQVCols / 8;              // 16-byte pieces per CTA row
   constexpr int kPhases = kQThreads / kG;      // 64 token phases
-  __shared__ float part[kPhases][kQVCols + 1];
+  constexpr int kWarpsV = kQThreads / 32;
+  __shared__ float part[kWarpsV][kQVCols];
   __shared__ float col_scale[kQVCols], col_rcp[kQVCols];
   const int g = threadIdx.x % kG, phase = threadIdx.x / kG, slots = u.nblk * 16;
   const T* src = static_cast<const T*>(u.src) + h * u.hs + col0 + 8 * g;
   float m[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int t = phase; t < u.S; t += kPhases) {
-    float x[8];
-    unpack8<kBf16>(*reinterpret_cast<const uint4*>(src + t * u.rs), x);
+  // A chunk of up to 2 * kPhases tokens (the 128-token chunks) stays in registers
+  // between the two passes: both of a thread's pieces are loaded before either is
+  // reduced, and the quantise pass reads no memory.
+  constexpr int kHeld = 2;
+  const bool held = u.S <= kHeld * kPhases;
+  uint4 keep[kHeld];
+  if (held) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) m[e] = fmaxf(m[e], fabsf(x[e]));
+    for (int i = 0; i < kHeld; ++i) {
+      const int t = phase + i * kPhases;
+      keep[i] = t < u.S ? *reinterpret_cast<const uint4*>(src + t * u.rs) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < kHeld; ++i) {
+      float x[8];
+      unpack8<kBf16>(keep[i], x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m[e] = fmaxf(m[e], fabsf(x[e]));
+    }
+  } else {
+    for (int t = phase; t < u.S; t += kPhases) {
+      float x[8];
+      unpack8<kBf16>(*reinterpret_cast<const uint4*>(src + t * u.rs), x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m[e] = fmaxf(m[e], fabsf(x[e]));
+    }
   }
+  // column maxima: over the warp's 8 token phases (lanes g, g + 4, ...) by
+  // shuffles, then over the 8 warps through shared memory
 #pragma unroll
-  for (int e = 0; e < 8; ++e) part[phase][8 * g + e] = m[e];
+  for (int o = kG; o < 32; o <<= 1)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m[e] = fmaxf(m[e], __shfl_xor_sync(0xffffffffu, m[e], o));
+  if ((threadIdx.x & 31) < kG)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part[threadIdx.x >> 5][8 * g + e] = m[e];
   __syncthreads();
   if (threadIdx.x < kQVCols) {
     float mx = 0.0f;
-#pragma unroll 8
-    for (int ph = 0; ph < kPhases; ++ph) mx = fmaxf(mx, part[ph][threadIdx.x]);
+#pragma unroll
+    for (int w = 0; w < kWarpsV; ++w) mx = fmaxf(mx, part[w][threadIdx.x]);
     const float sc = kivi_scale<T>(mx);
     col_scale[threadIdx.x] = sc;
     col_rcp[threadIdx.x] = __frcp_rn(sc);
@@ -335,6 +364,24 @@ __device__ __forceinline__ void quantize_store_v(const QStoreUnit& u, int h, int
     sc[e] = col_scale[8 * g + e];
     rc[e] = col_rcp[8 * g + e];
     zero_scale |= !(sc[e] > 0.0f);
+  }
+  if (held) {
+#pragma unroll
+    for (int i = 0; i < kHeld; ++i) {
+      const int t = phase + i * kPhases;
+      if (t >= slots) break;
+      const int blk = u.block_ids[t >> 4], slot = t & 15;
+      if (!block_ok(blk, u)) continue;
+      uint2 q = make_uint2(0, 0);
+      if (t < u.S) {
+        float x[8];
+        unpack8<kBf16>(keep[i], x);
+        q = kivi_q8<T>(x, sc, rc, zero_scale);
+      }
+      *reinterpret_cast<uint2*>(u.pool + ((static_cast<int64_t>(blk) * 2 + 1) * u.H + h) * 16 * D +
+                                slot * D + col0 + 8 * g) = q;
+    }
+    return;
   }
   for (int t = phase; t < slots; t += kPhases) {
     const int blk = u.block_ids[t >> 4], slot = t & 15;
