@@ -192,7 +192,8 @@ constexpr int kQThreads = 256;                  // several CTAs per SM overlap t
 constexpr int kQWarps = kQThreads / 32;
 constexpr int kQLanesPerRow = 8;                 // K: 8 lanes per token row, 4 rows per warp
 constexpr int kQRowsPerWarp = 32 / kQLanesPerRow;
-constexpr int kQRowsPerCta = kQWarps * kQRowsPerWarp;   // K: 32 token rows per CTA
+constexpr int kQKRows = 2;                       // K: token rows per thread, all loaded first
+constexpr int kQRowsPerCta = kQWarps * kQRowsPerWarp * kQKRows;   // K: 128 token rows per CTA
 constexpr int kQVCols = 32;                      // V: 32 columns per CTA (4 pieces x 64 phases)
 
 template <bool kBf16>
@@ -246,49 +247,74 @@ __device__ __forceinline__ void quantize_store_k(const QStoreUnit& u, int h, int
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int VPR = D / 8;                                   // 16-byte pieces per row
   constexpr int kPieces = (VPR + kQLanesPerRow - 1) / kQLanesPerRow;
+  constexpr int kStride = kQWarps * kQRowsPerWarp;             // 32 rows between a thread's rows
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, slots = u.nblk * 16;
   if (row0 + warp * kQRowsPerWarp >= slots) return;            // warp-uniform
   const T* src = static_cast<const T*>(u.src) + h * u.hs;
   const int sub = lane & (kQLanesPerRow - 1);
-  const int t = row0 + warp * kQRowsPerWarp + (lane >> 3);
-  const bool live = t < u.S;
-  float x[kPieces][8];
-  float amax = 0.0f;
+  const int tr = row0 + warp * kQRowsPerWarp + (lane >> 3);   // this thread's first row
+  // every row's pieces are requested before any is reduced
+  uint4 w[kQKRows][kPieces];
 #pragma unroll
-  for (int c = 0; c < kPieces; ++c) {
-    const int piece = sub + kQLanesPerRow * c;
-    uint4 w = make_uint4(0, 0, 0, 0);
-    if (live && piece < VPR) w = *reinterpret_cast<const uint4*>(src + t * u.rs + 8 * piece);
-    unpack8<kBf16>(w, x[c]);
+  for (int r = 0; r < kQKRows; ++r) {
+    const int t = tr + r * kStride;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(x[c][e]));
+    for (int c = 0; c < kPieces; ++c) {
+      const int piece = sub + kQLanesPerRow * c;
+      w[r][c] = (t < u.S && piece < VPR)
+                    ? *reinterpret_cast<const uint4*>(src + t * u.rs + 8 * piece)
+                    : make_uint4(0, 0, 0, 0);
+    }
+  }
+  float amax[kQKRows];
+#pragma unroll
+  for (int r = 0; r < kQKRows; ++r) {
+    amax[r] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kPieces; ++c) {
+      float x[8];
+      unpack8<kBf16>(w[r][c], x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax[r] = fmaxf(amax[r], fabsf(x[e]));
+    }
   }
 #pragma unroll
-  for (int o = 1; o < kQLanesPerRow; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if (t >= slots) return;
-  const int blk = u.block_ids[t >> 4], slot = t & 15;
-  if (!block_ok(blk, u)) return;
-  const float scale = live ? kivi_scale<T>(amax) : 0.0f;
-  const float rcp = __frcp_rn(scale);
-  int8_t* dst = u.pool + ((static_cast<int64_t>(blk) * 2 + 0) * u.H + h) * 16 * D + slot * D;
-  float sc[8], rc[8];
+  for (int o = 1; o < kQLanesPerRow; o <<= 1)
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    sc[e] = scale;
-    rc[e] = rcp;
-  }
+    for (int r = 0; r < kQKRows; ++r)
+      amax[r] = fmaxf(amax[r], __shfl_xor_sync(0xffffffffu, amax[r], o));
 #pragma unroll
-  for (int c = 0; c < kPieces; ++c) {
-    const int piece = sub + kQLanesPerRow * c;
-    if (piece < VPR)
-      *reinterpret_cast<uint2*>(dst + 8 * piece) =
-          live ? kivi_q8<T>(x[c], sc, rc, !(scale > 0.0f)) : make_uint2(0, 0);
-  }
-  if (sub == 0) {
-    const __half s16 = __float2half_rn(scale);
-    const int64_t si = (static_cast<int64_t>(blk) * u.H + h) * 16 + slot;
-    if (u.s16) u.s16[si] = s16;
-    if (u.s32) u.s32[si] = __half2float(s16);
+  for (int r = 0; r < kQKRows; ++r) {
+    const int t = tr + r * kStride;
+    if (t >= slots) break;                                     // rows only grow with r
+    const bool live = t < u.S;
+    const int blk = u.block_ids[t >> 4], slot = t & 15;
+    if (!block_ok(blk, u)) continue;
+    const float scale = live ? kivi_scale<T>(amax[r]) : 0.0f;
+    const float rcp = __frcp_rn(scale);
+    int8_t* dst = u.pool + ((static_cast<int64_t>(blk) * 2 + 0) * u.H + h) * 16 * D + slot * D;
+    float sc[8], rc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      sc[e] = scale;
+      rc[e] = rcp;
+    }
+#pragma unroll
+    for (int c = 0; c < kPieces; ++c) {
+      const int piece = sub + kQLanesPerRow * c;
+      if (piece < VPR) {
+        float x[8];
+        unpack8<kBf16>(w[r][c], x);
+        *reinterpret_cast<uint2*>(dst + 8 * piece) =
+            live ? kivi_q8<T>(x, sc, rc, !(scale > 0.0f)) : make_uint2(0, 0);
+      }
+    }
+    if (sub == 0) {
+      const __half s16 = __float2half_rn(scale);
+      const int64_t si = (static_cast<int64_t>(blk) * u.H + h) * 16 + slot;
+      if (u.s16) u.s16[si] = s16;
+      if (u.s32) u.s32[si] = __half2float(s16);
+    }
   }
 }
 
