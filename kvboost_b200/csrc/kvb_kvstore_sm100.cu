@@ -192,7 +192,10 @@ constexpr int kQThreads = 256;                  // several CTAs per SM overlap t
 constexpr int kQWarps = kQThreads / 32;
 constexpr int kQLanesPerRow = 8;                 // K: 8 lanes per token row, 4 rows per warp
 constexpr int kQRowsPerWarp = 32 / kQLanesPerRow;
-constexpr int kQKRows = 2;                       // K: token rows per thread, all loaded first
+// K: token rows per thread (all loaded before any is reduced).  One row keeps
+// the kernel at 58 registers and 4 CTAs per SM; 2 and 4 rows (74 and 116
+// registers) measured 9 % and 36 % slower on the 24-chunk store.
+constexpr int kQKRows = 1;
 constexpr int kQRowsPerCta = kQWarps * kQRowsPerWarp * kQKRows;   // K: 128 token rows per CTA
 constexpr int kQVCols = 32;                      // V: 32 columns per CTA (4 pieces x 64 phases)
 
