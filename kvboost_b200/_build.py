@@ -68,6 +68,19 @@ def build(force: bool = False, verbose: bool = True) -> str:
     return LIB_PATH
 
 
+def build_traced(out_path: str) -> str:
+    """A copy of the library with the kernels' phase timestamps compiled in
+    (``-DKVB_TRACE``; clock64 and global-timer stamps per CTA into a buffer set with
+    ``kvb_debug_set_trace``), for pipeline studies only (``kvboost_b200._trace``)."""
+    flags = [f for f in NVCC_FLAGS if f not in ("-Xptxas", "-v")]
+    cmd = [nvcc_path(), *flags, "-DKVB_TRACE", "-I", INCLUDE, "-I", CSRC, "-o", out_path,
+           *sources()]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
+    return out_path
+
+
 if __name__ == "__main__":
     build(force="--force" in sys.argv)
     print(LIB_PATH)

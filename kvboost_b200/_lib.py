@@ -136,7 +136,9 @@ def pointer_array(ptrs):
 
 
 def lib_path() -> str:
-    return _build.LIB_PATH
+    """The in-tree library, or the build named by ``KVB_LIB`` (the traced build that
+    ``kvboost_b200._trace`` loads)."""
+    return os.environ.get("KVB_LIB") or _build.LIB_PATH
 
 
 def load() -> ctypes.CDLL:
