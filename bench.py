@@ -72,10 +72,10 @@ PREWARM_S = 0.5
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch from the committed
 # ncu captures (profiles/*.md), per workload.  varlen_d96: the 16-request capture
 # (1 029.9 MB) scaled to the full launch by algorithmic bytes (3 535.4 / 1 004.1 MB).
-NCU_TRAFFIC_BYTES = {"reuse_prefill": 27322880, "varlen_d96": 3626150000,
-                     # single-chunk launches: 4 753 920 read per chunk (pool writes held
-                     # in L2); the batched step is 24 chunks
-                     "quantize_store": 24 * 4753920,
+NCU_TRAFFIC_BYTES = {"reuse_prefill": 27328000, "varlen_d96": 3626150000,
+                     # the batched 24-chunk launch: 113.3 MB read + 40.4 MB written
+                     # (the rest of the pool writes still in L2 at the end)
+                     "quantize_store": 113305088 + 40395520,
                      # per step: deviation 113 267 968 + 3 780 096, select 47 616,
                      # patch 16 965 632 + 14 080 (read + write)
                      "cacheblend": 134075392,
