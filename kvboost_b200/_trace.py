@@ -71,6 +71,12 @@ def steady_chain(torch, lib, shape):
                  & (rows[:, 64 + j + 1] > 0)]
         if len(r) == 0:
             continue
+        if j == 4:   # every softmax warp of slot 0 stamps its P arrival at tile 4
+            last = r[:, 8:16].max(1).values
+            out["tile 4 arrivals"] = {
+                "first_to_last_warp": med(last - r[:, 8:16].min(1).values),
+                "last_warp_to_mma_awake": med(r[:, 112 + j] - last),
+                "last_warp_to_pv_issued": med(r[:, 96 + j] - last)}
         out[j] = {"softmax": med(r[:, 80 + j] - r[:, 64 + j]),
                   "p_to_mma_awake": med(r[:, 112 + j] - r[:, 80 + j]),
                   "p_to_pv_issued": med(r[:, 96 + j] - r[:, 80 + j]),
@@ -119,16 +125,20 @@ def launch_timeline(torch, lib, shape, launches=20):
             for i in range(launches):
                 ops.prefill_attention(*sets[i % 8], 1 / math.sqrt(D), True, out=outs[i % 8],
                                       return_lse=False)
-    for _ in range(3):
+    with torch.cuda.stream(st):
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
         graph.replay()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    graph.replay()
-    e1.record(st)
+        e1.record(st)
     torch.cuda.synchronize()
     per_launch_us = e0.elapsed_time(e1) / launches * 1000
-    rows = _traced_rows(torch, lib, lambda: (graph.replay(), torch.cuda.synchronize()))
+    def replay():
+        with torch.cuda.stream(st):
+            graph.replay()
+    rows = _traced_rows(torch, lib, replay)
     rel = rows[:, 5].min()
     us = lambda x: [round(float(v) / 1000, 2) for v in (x.min(), x.double().median(), x.max())]
     out = {"us_per_launch": round(per_launch_us, 2), "ctas": len(rows),

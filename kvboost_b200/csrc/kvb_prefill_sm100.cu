@@ -88,7 +88,15 @@ __device__ long long* g_kvb_trace;
       g_kvb_trace ? g_kvb_trace + 256ull * (blockIdx.x +                                       \
                                             gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) \
                   : nullptr
+// global-timer stamps (ns, comparable across SMs) for launch-level timelines
+#define KVB_TRACE_GT(slot)                                                                 \
+  do {                                                                                     \
+    if (kvb_trace_row) kvb_trace_row[(slot)] = static_cast<long long>(ptx::globaltimer_ns()); \
+  } while (0)
 #else
+#define KVB_TRACE_GT(slot) \
+  do {                     \
+  } while (0)
 #define KVB_TRACE_SETUP() \
   do {                    \
   } while (0)
@@ -770,6 +778,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   KVB_TRACE_SETUP();
+  if (threadIdx.x == 0) KVB_TRACE_GT(4);
   auto bar = [&](int i) { return ptx::smem_u32(&bars[i]); };
 
   // ---- setup that touches no global memory ------------------------------
@@ -860,6 +869,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     }
   }
   ptx::griddep_wait();
+  if (threadIdx.x == 0) KVB_TRACE_GT(5);
   int q_len = a.q_len, kv_len = a.kv_len, q_base = 0, k_base = 0, tb = b;
   int P = 0;  // paged: cached-prefix tokens of this sequence
   if (PAGED) {
@@ -1227,6 +1237,8 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     const int qi = q0s + t;
     const float sl2 = a.scale_log2;
     constexpr float kSumLimit = std::is_same<T, __half>::value ? 32768.f : 1.0995116e12f;
+    constexpr bool kGuessMax = SPLITKV && std::is_same<T, __nv_bfloat16>::value;
+    constexpr float kSumFloor = 5.42101086e-20f;   // 2^-64
     float m_run = -INFINITY;
     float l_run = 0.f;   // row sum over this thread's columns
     bool ok = true;
@@ -1254,16 +1266,31 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       // half), and rows without a maximum yet, take the exact path: tile
       // maximum, O rescale, redo.  The final normalisation uses the same
       // maximum as the exponentials, so the result is exact up to rounding.
+      //
+      // Split-key launches in bf16: a row's first tile tries the maximum 0
+      // (log2 domain) before it has one; bf16 P keeps float32's exponent range,
+      // so any sum in [2^-64, 2^40] over the thread's columns leaves every
+      // probability that matters normal and finite, and the rounding of P is
+      // the same relative to any maximum.  Rows outside that range (and fp16,
+      // whose P range is narrow) take the exact path as before.  A split of a
+      // few key tiles saves the first tile's maximum pass (16 new tokens over
+      // 32 K keys: 60.4 -> 59.5 us); the prefill launches keep the exact first
+      // tile (no gain on the reuse prefill, 2.4 % slower on long causal prefill).
       float alpha = 1.f;
       float sum = 0.f;
       uint32_t pk[COLS / 2];
-      bool need = !ok || m_run == -INFINITY;
+      const bool first = m_run == -INFINITY;
+      bool need = !ok || (!kGuessMax && first);
       if (!__any_sync(0xffffffffu, need)) {
-        sum = need_mask ? cols_exp<T, true, NCH, CW, kPoly>(tS, hf * COLS, sl2, m_run, lim, pk)
-                        : cols_exp<T, false, NCH, CW, kPoly>(tS, hf * COLS, sl2, m_run, lim, pk);
-        need = !(sum <= kSumLimit);  // also catches inf / NaN
+        const float m_try = (kGuessMax && first) ? 0.f : m_run;
+        sum = need_mask ? cols_exp<T, true, NCH, CW, kPoly>(tS, hf * COLS, sl2, m_try, lim, pk)
+                        : cols_exp<T, false, NCH, CW, kPoly>(tS, hf * COLS, sl2, m_try, lim, pk);
+        need = !(sum <= kSumLimit) ||   // also catches inf / NaN
+               (kGuessMax && first && !(sum >= kSumFloor));
       }
-      if (pair_any(need)) {
+      const bool redo = pair_any(need);
+      if (kGuessMax && !redo && first) m_run = 0.f;   // both threads of the row took the guess
+      if (redo) {
         if (pair_any(!ok)) {
           ok = false;
           break;
@@ -1309,6 +1336,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(BAR_P_FULL + sl));
       if (lane == 0 && warp == 3 && j < 16) KVB_TRACE_AT(208 + j);
+      if (lane == 0 && sl == 0 && j == 4) KVB_TRACE_AT(8 + (warp & 7));   // every warp, tile 4
       if (t == 0 && hf == 0 && j < 16) KVB_TRACE_AT(80 + 96 * sl + j);
     }
 
@@ -1466,6 +1494,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   ptx::tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) KVB_TRACE_AT(3);
+  if (threadIdx.x == 0) KVB_TRACE_GT(6);
   if (warp == kWarpMma) {
     __syncwarp();
     ptx::tc_fence_after();
