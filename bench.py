@@ -1673,7 +1673,13 @@ def main():
     del gw, gt
     if args.workload == "reuse_prefill" and not args.no_sharded and not args.small \
             and 8 % world == 0:
-        line["sharded_paged_long"] = sharded_paged_line(torch, dist, rank, world, dev)
+        try:   # every rank takes the same steps; a failure here must not cost the line
+            line["sharded_paged_long"] = sharded_paged_line(torch, dist, rank, world, dev)
+        except Exception as e:  # pragma: no cover - reported in the line
+            line["sharded_paged_long"] = {"error": repr(e)[:300]}
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
