@@ -104,7 +104,8 @@ int kvb_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, flo
  * lse + h*lse_head_stride + row.
  *
  * Requirements: innermost stride 1; row/head/batch strides multiples of 8
- * elements; base pointers 16-byte aligned.
+ * elements; base pointers 16-byte aligned; batch, num_q_heads <= 65535 and
+ * q_len <= 65535 * 128 (KVB_ERR_UNSUPPORTED otherwise).
  */
 typedef struct KvbPrefillParams {
   int32_t dtype;

@@ -3,7 +3,7 @@
     python -m kvboost_b200._trace            # on an sm_100a device, nvcc on PATH
 
 Builds a copy of the library with ``-DKVB_TRACE`` (per-CTA clock64 stamps at each
-phase of the first 16 key tiles, and global-timer stamps at CTA entry, after the
+phase of the first 16 key tiles, softmax sub-phases included, and global-timer stamps at CTA entry, after the
 dependent-launch wait and at CTA end), loads it instead of the shipped library,
 and prints:
 
@@ -47,12 +47,12 @@ def _inputs(torch, B, Hq, Hkv, Sq, Skv, D, n=1, seed=0):
 
 
 def _traced_rows(torch, lib, launch):
-    buf = torch.zeros(4096 * 256, dtype=torch.int64, device="cuda")
+    buf = torch.zeros(4096 * 512, dtype=torch.int64, device="cuda")
     lib.kvb_debug_set_trace(buf.data_ptr())
     launch()
     torch.cuda.synchronize()
     lib.kvb_debug_set_trace(None)
-    t = buf.view(4096, 256).cpu()
+    t = buf.view(4096, 512).cpu()
     return t[t[:, 0] != 0]
 
 
@@ -77,6 +77,15 @@ def steady_chain(torch, lib, shape):
                 "first_to_last_warp": med(last - r[:, 8:16].min(1).values),
                 "last_warp_to_mma_awake": med(r[:, 112 + j] - last),
                 "last_warp_to_pv_issued": med(r[:, 96 + j] - last)}
+        if (r[:, 256 + j] > 0).all() and (r[:, 320 + j] > 0).all():
+            # softmax sub-phases of row 0 (both column halves), from S visible
+            out[f"{j} softmax phases"] = {
+                "exp_done_h0": med(r[:, 256 + j] - r[:, 64 + j]),
+                "exp_done_h1": med(r[:, 304 + j] - r[:, 64 + j]),
+                "pair_decided": med(r[:, 272 + j] - r[:, 64 + j]),
+                "p_stored_h0": med(r[:, 288 + j] - r[:, 64 + j]),
+                "p_stored_h1": med(r[:, 320 + j] - r[:, 64 + j]),
+                "arrived_w0": med(r[:, 80 + j] - r[:, 64 + j])}
         out[j] = {"softmax": med(r[:, 80 + j] - r[:, 64 + j]),
                   "p_to_mma_awake": med(r[:, 112 + j] - r[:, 80 + j]),
                   "p_to_pv_issued": med(r[:, 96 + j] - r[:, 80 + j]),

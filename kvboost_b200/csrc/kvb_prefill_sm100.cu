@@ -85,7 +85,7 @@ __device__ long long* g_kvb_trace;
   } while (0)
 #define KVB_TRACE_SETUP()                                                                      \
   long long* kvb_trace_row =                                                                   \
-      g_kvb_trace ? g_kvb_trace + 256ull * (blockIdx.x +                                       \
+      g_kvb_trace ? g_kvb_trace + 512ull * (blockIdx.x +                                       \
                                             gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) \
                   : nullptr
 // global-timer stamps (ns, comparable across SMs) for launch-level timelines
@@ -838,13 +838,15 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     mtile[0] = dual_split ? 0 : 2 * tpair;
     mtile[1] = dual_split ? 0 : 2 * tpair + 1;
   } else if (a.pair_heads) {
-    const int m = gridDim.x - 1 - blockIdx.x;  // heaviest (last) query tiles first
-    head[0] = 2 * blockIdx.y;
-    head[1] = 2 * blockIdx.y + 1;
+    // grid (head pairs, query tiles, batch): blocks go out head-fastest, so every
+    // head's heaviest (last) query tile is dispatched before any lighter one
+    const int m = gridDim.y - 1 - blockIdx.y;
+    head[0] = 2 * blockIdx.x;
+    head[1] = 2 * blockIdx.x + 1;
     mtile[0] = mtile[1] = m;
   } else {
-    const int x = gridDim.x - 1 - blockIdx.x;
-    head[0] = head[1] = blockIdx.y;
+    const int x = gridDim.y - 1 - blockIdx.y;  // grid (heads, tile pairs, batch)
+    head[0] = head[1] = blockIdx.x;
     mtile[0] = 2 * x;
     mtile[1] = 2 * x + 1;
   }
@@ -1288,7 +1290,9 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
         need = !(sum <= kSumLimit) ||   // also catches inf / NaN
                (kGuessMax && first && !(sum >= kSumFloor));
       }
+      if (t == 0 && sl == 0 && j < 16) KVB_TRACE_AT(256 + 48 * hf + j);
       const bool redo = pair_any(need);
+      if (t == 0 && sl == 0 && hf == 0 && j < 16) KVB_TRACE_AT(272 + j);
       if (kGuessMax && !redo && first) m_run = 0.f;   // both threads of the row took the guess
       if (redo) {
         if (pair_any(!ok)) {
@@ -1332,6 +1336,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       store_p<COLS / 2>(tS, pk);
       l_run = l_run * alpha + sum;
       ptx::tmem_wait_st();
+      if (t == 0 && sl == 0 && j < 16) KVB_TRACE_AT(288 + 32 * hf + j);
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(BAR_P_FULL + sl));
@@ -1599,8 +1604,9 @@ static int launch_dense_core(const CUtensorMap& tq, const CUtensorMap& tk, const
       return fail(KVB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured_device[dualok] = dev;
   }
-  dim3 grid = a.pair_heads ? dim3(q_tiles, num_q_heads / 2, batch)
-                           : dim3((q_tiles + 1) / 2, num_q_heads, batch);
+  // head-fastest grids: each head's (pair's) heaviest query tiles go out first
+  dim3 grid = a.pair_heads ? dim3(num_q_heads / 2, q_tiles, batch)
+                           : dim3(num_q_heads, (q_tiles + 1) / 2, batch);
   PagedArgs none = {};
   cudaError_t e = launch_pdl(kern, grid, Roles<false>::kThreads, G::SMEM_BYTES, stream, tq, tk,
                              tv, a, none);
@@ -1903,8 +1909,8 @@ static int launch_paged(const KvbPagedPrefillParams& p, cudaStream_t stream,
     configured_device = dev;
   }
   const int q_tiles = (p.q_len + BM - 1) / BM;
-  dim3 grid = a.pair_heads ? dim3(q_tiles, p.num_q_heads / 2, p.batch)
-                           : dim3((q_tiles + 1) / 2, p.num_q_heads, p.batch);
+  dim3 grid = a.pair_heads ? dim3(p.num_q_heads / 2, q_tiles, p.batch)
+                           : dim3(p.num_q_heads, (q_tiles + 1) / 2, p.batch);
   cudaError_t e = launch_pdl(kern, grid, Roles<true>::kThreads, G::SMEM_BYTES, stream, tq, tq, tq,
                              a, pa);
   if (e == cudaSuccess) e = cudaGetLastError();
@@ -1933,6 +1939,8 @@ static int validate(const KvbPrefillParams& p) {
     return fail(KVB_ERR_INVALID, "causal must be 0 (none), 1 (bottom-right) or 2 (top-left)");
   if (p.q_len < 0 || p.kv_len < 0)
     return fail(KVB_ERR_INVALID, "sequence lengths must be non-negative");
+  if (p.q_len > 65535 * BM)  // query tiles are the grid's y dimension
+    return fail(KVB_ERR_UNSUPPORTED, "q_len must be <= " + std::to_string(65535 * BM));
   const bool varlen = p.cu_seqlens_q != nullptr;
   // An empty key side may come with null k/v (an empty tensor's data pointer).
   const bool no_keys = varlen ? p.total_k == 0 : p.kv_len == 0;
@@ -2037,6 +2045,8 @@ static int validate_paged(const KvbPagedPrefillParams& p) {
     return fail(KVB_ERR_INVALID, "causal must be 0 (none), 1 (bottom-right) or 2 (top-left)");
   if (p.q_len < 0 || p.prefix_len < 0)
     return fail(KVB_ERR_INVALID, "q_len and prefix_len must be non-negative");
+  if (p.q_len > 65535 * BM)  // query tiles are the grid's y dimension
+    return fail(KVB_ERR_UNSUPPORTED, "q_len must be <= " + std::to_string(65535 * BM));
   if (p.block_size != 16)
     return fail(KVB_ERR_UNSUPPORTED, "block_size must be 16");
   if (p.num_blocks < 1 || p.max_blocks_per_seq < 0)

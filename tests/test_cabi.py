@@ -75,6 +75,13 @@ def test_host_validation_rejects_before_launch(lib, field, value, needle):
     assert needle in lib.kvb_last_error().decode()
 
 
+def test_query_tile_count_limit(lib):
+    # query tiles are the grid's y dimension: at most 65535 tiles of 128 rows
+    p = _params(q_len=65535 * 128 + 1, kv_len=65535 * 128 + 1)
+    assert lib.kvb_prefill_fwd(ctypes.byref(p), None) == _lib.KVB_ERR_UNSUPPORTED
+    assert "q_len must be <=" in lib.kvb_last_error().decode()
+
+
 def test_null_params_rejected(lib):
     assert lib.kvb_prefill_fwd(None, None) == _lib.KVB_ERR_INVALID
 
