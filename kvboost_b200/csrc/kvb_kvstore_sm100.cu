@@ -156,13 +156,33 @@ __device__ __forceinline__ uint2 kivi_q8(const float (&x)[8], const float (&sc)[
   constexpr uint32_t kDrop = RoundBits<T>::kDrop, kHalf = 1u << (kDrop - 1), kMask = (1u << kDrop) - 1;
   uint32_t w[8];
   bool near = zero_scale;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    // bfloat16: the rounding of y to T by the conversion unit (round to nearest
+    // even, as the integer rule above), two at a time; only the upper clamp,
+    // since |y| <= 127.3 (scale = amax / 127 rounded to 8 bits, y within 3
+    // float32 ulps of the quotient), so rint(T(y)) >= -128.  The halfway test
+    // looks at the dropped 16 bits as the top half of (u - (kHalf - 8)) << 16.
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const uint32_t u = __float_as_uint(x[e] * rc[e]);
-    const uint32_t r = (u + (kHalf - 1) + ((u >> kDrop) & 1u)) & ~kMask;
-    const float t = fminf(fmaxf(__uint_as_float(r), -128.0f), 127.0f);
-    w[e] = __float_as_uint(t + 12582912.0f);
-    near |= ((u - (kHalf - 8u)) & kMask) <= 16u;     // low bits within 8 of the halfway point
+    for (int e = 0; e < 8; e += 2) {
+      const float y0 = x[e] * rc[e], y1 = x[e + 1] * rc[e + 1];
+      uint32_t p;
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(y1), "f"(y0));
+      const float t0 = fminf(__uint_as_float(p << 16), 127.0f);
+      const float t1 = fminf(__uint_as_float(p & 0xffff0000u), 127.0f);
+      w[e] = __float_as_uint(t0 + 12582912.0f);
+      w[e + 1] = __float_as_uint(t1 + 12582912.0f);
+      near |= ((__float_as_uint(y0) - (kHalf - 8u)) << 16) <= (16u << 16 | 0xffffu);
+      near |= ((__float_as_uint(y1) - (kHalf - 8u)) << 16) <= (16u << 16 | 0xffffu);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t u = __float_as_uint(x[e] * rc[e]);
+      const uint32_t r = (u + (kHalf - 1) + ((u >> kDrop) & 1u)) & ~kMask;
+      const float t = fminf(fmaxf(__uint_as_float(r), -128.0f), 127.0f);
+      w[e] = __float_as_uint(t + 12582912.0f);
+      near |= ((u - (kHalf - 8u)) & kMask) <= 16u;     // low bits within 8 of the halfway point
+    }
   }
   if (near)
     return kivi_q8_exact<T>(make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]),
@@ -510,6 +530,252 @@ __global__ void __launch_bounds__(kQThreads) kvb_quantize_store_batch_kernel(con
                            static_cast<float*>(a.tables[4 * a.L + layer]), n_k);
 }
 
+// ---- quantise-on-store, staged: one CTA per (chunk, layer, KV head) --------------------
+// For chunks of up to 128 tokens at head_dim 128 (the engine's chunks): the CTA
+// copies the chunk's K and V tiles of one head (128 rows x 256 bytes each) into
+// shared memory with cp.async (zero-filled past the chunk's tokens; K and V in
+// two commit groups, so the K pass starts while V is still arriving), then
+//  K: 8 lanes per token row, 16 elements each, 4 rows per warp and pass, 4 passes;
+//  V: thread = (8-column group cg, token phase tb): tokens tb, tb + 16, ...; the
+//     column maxima reduce over the 16 phases of a half-warp by shuffles, and
+//     lanes tb < 8 compute column cg * 8 + tb's scale once.
+// Row t's 16-byte piece p sits at t * 256 + ((p ^ (t & 15)) << 4): the copies,
+// the K reads (one row per 8 lanes) and the V reads (16 rows, one per lane, per
+// column group) all spread over the 32 banks.  Maxima are taken on packed pairs
+// with the sign bits cleared.  Output bytes and scales are those of
+// quantize_store_k / quantize_store_v.
+constexpr int kSTileRows = 128;
+constexpr int kSRowBytes = 256;                         // head_dim 128, 16-bit
+constexpr int kSTileBytes = kSTileRows * kSRowBytes;    // 32 KB per operand
+constexpr int kSThreads = 256;
+constexpr int kSSmem = 2 * kSTileBytes;
+
+__device__ __forceinline__ uint32_t s_piece(int t, int p) {
+  return static_cast<uint32_t>(t * kSRowBytes + ((p ^ (t & 15)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool live) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(live ? 16 : 0)
+               : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t max_abs2(uint32_t m, uint32_t w) {
+  uint32_t a = w & 0x7fff7fffu, r;
+  if (std::is_same<T, __nv_bfloat16>::value)
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(a));
+  else
+    asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(a));
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  return Num<T>::pair(w);
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8s(const uint4& u, float (&x)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack2<T>(w[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const void* src_k,
+                                                     const void* src_v, __half* ks16, float* ks32,
+                                                     __half* vs16, float* vs32, int h) {
+  constexpr int D = 128;
+  extern __shared__ __align__(128) uint8_t s_tile[];
+  const uint32_t sK = static_cast<uint32_t>(__cvta_generic_to_shared(s_tile));
+  const uint32_t sV = sK + kSTileBytes;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int S = u0.S, slots = u0.nblk * 16;
+  // ---- stage: 2048 pieces per operand, 8 per thread each --------------------------------
+#pragma unroll
+  for (int kv = 0; kv < 2; ++kv) {
+    const T* src = static_cast<const T*>(kv ? src_v : src_k) + h * u0.hs;
+#pragma unroll
+    for (int k = 0; k < kSTileBytes / 16 / kSThreads; ++k) {
+      const int i = tid + kSThreads * k;
+      const int t = i >> 4, pc = i & 15;
+      const bool live = t < S;
+      cp_async16((kv ? sV : sK) + s_piece(t, pc), live ? src + t * u0.rs + 8 * pc : src, live);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  // ---- K: per-token scales ------------------------------------------------------------
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+  __syncthreads();
+  {
+    const int sub = lane & 7;
+#pragma unroll 1
+    for (int pass = 0; pass < 4; ++pass) {
+      const int t = pass * 32 + warp * 4 + (lane >> 3);
+      if (t >= slots) break;                          // 4-row groups: warp-uniform
+      uint4 w0, w1;
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w0.x), "=r"(w0.y), "=r"(w0.z), "=r"(w0.w)
+                   : "r"(sK + s_piece(t, sub)));
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
+                   : "r"(sK + s_piece(t, sub + 8)));
+      uint32_t m2 = 0;
+      m2 = max_abs2<T>(m2, w0.x); m2 = max_abs2<T>(m2, w0.y);
+      m2 = max_abs2<T>(m2, w0.z); m2 = max_abs2<T>(m2, w0.w);
+      m2 = max_abs2<T>(m2, w1.x); m2 = max_abs2<T>(m2, w1.y);
+      m2 = max_abs2<T>(m2, w1.z); m2 = max_abs2<T>(m2, w1.w);
+      const float2 mf = unpack2<T>(m2);
+      float amax = fmaxf(mf.x, mf.y);
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const int blk = u0.block_ids[t >> 4], slot = t & 15;
+      if (!block_ok(blk, u0)) continue;
+      const bool live = t < S;
+      const float scale = live ? kivi_scale<T>(amax) : 0.0f;
+      const float rcp = __frcp_rn(scale);
+      float sc[8], rc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        sc[e] = scale;
+        rc[e] = rcp;
+      }
+      int8_t* dst = u0.pool + ((static_cast<int64_t>(blk) * 2 + 0) * u0.H + h) * 16 * D + slot * D;
+      uint2 q0 = make_uint2(0, 0), q1 = make_uint2(0, 0);
+      if (live) {
+        float x[8];
+        unpack8s<T>(w0, x);
+        q0 = kivi_q8<T>(x, sc, rc, !(scale > 0.0f));
+        unpack8s<T>(w1, x);
+        q1 = kivi_q8<T>(x, sc, rc, !(scale > 0.0f));
+      }
+      *reinterpret_cast<uint2*>(dst + 8 * sub) = q0;
+      *reinterpret_cast<uint2*>(dst + 8 * (sub + 8)) = q1;
+      if (sub == 0) {
+        const __half s16 = __float2half_rn(scale);
+        const int64_t si = (static_cast<int64_t>(blk) * u0.H + h) * 16 + slot;
+        if (ks16) ks16[si] = s16;
+        if (ks32) ks32[si] = __half2float(s16);
+      }
+    }
+  }
+  // ---- V: per-channel scales over the chunk ---------------------------------------------
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  {
+    const int cg = warp * 2 + (lane >> 4), tb = lane & 15;
+    uint32_t m2[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {   // rows past the chunk are zero-filled
+      uint4 w;
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                   : "r"(sV + s_piece(tb + 16 * i, cg)));
+      m2[0] = max_abs2<T>(m2[0], w.x);
+      m2[1] = max_abs2<T>(m2[1], w.y);
+      m2[2] = max_abs2<T>(m2[2], w.z);
+      m2[3] = max_abs2<T>(m2[3], w.w);
+    }
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) m2[k] = max_abs2<T>(m2[k], __shfl_xor_sync(0xffffffffu, m2[k], o));
+    // lane tb < 8 owns column cg * 8 + tb
+    const uint32_t mine = (tb & 4) ? ((tb & 2) ? m2[3] : m2[2]) : ((tb & 2) ? m2[1] : m2[0]);
+    const float2 mf = unpack2<T>(mine);
+    const float my_sc = kivi_scale<T>((tb & 1) ? mf.y : mf.x);
+    const float my_rc = __frcp_rn(my_sc);
+    if (tb < 8) {
+      const __half s16 = __float2half_rn(my_sc);
+      for (int b = 0; b < u0.nblk; ++b) {
+        const int blk = u0.block_ids[b];
+        if (blk < 0 || blk >= u0.num_pool_blocks) continue;   // flagged by the row writes below
+        const int64_t si = (static_cast<int64_t>(blk) * u0.H + h) * D + cg * 8 + tb;
+        if (vs16) vs16[si] = s16;
+        if (vs32) vs32[si] = __half2float(s16);
+      }
+    }
+    float sc[8], rc[8];
+    bool zero_scale = false;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      sc[e] = __shfl_sync(0xffffffffu, my_sc, (lane & 16) + e);
+      rc[e] = __shfl_sync(0xffffffffu, my_rc, (lane & 16) + e);
+      zero_scale |= !(sc[e] > 0.0f);
+    }
+#pragma unroll 1
+    for (int i = 0; i < u0.nblk; ++i) {          // token tb + 16 i sits in block i, slot tb
+      const int t = tb + 16 * i;
+      const int blk = u0.block_ids[i];
+      if (!block_ok(blk, u0)) continue;
+      uint2 q = make_uint2(0, 0);
+      if (t < S) {
+        uint4 w;
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                     : "r"(sV + s_piece(t, cg)));
+        float x[8];
+        unpack8s<T>(w, x);
+        q = kivi_q8<T>(x, sc, rc, zero_scale);
+      }
+      *reinterpret_cast<uint2*>(u0.pool + ((static_cast<int64_t>(blk) * 2 + 1) * u0.H + h) * 16 * D +
+                                tb * D + cg * 8) = q;
+    }
+  }
+}
+
+// One chunk (<= 128 tokens), all layers, head_dim 128: grid (KV head, layer).
+template <typename T>
+__global__ void __launch_bounds__(kSThreads) kvb_quantize_store_staged_kernel(const __grid_constant__ QStoreArgs a) {
+  const int layer = blockIdx.y;
+  QStoreUnit u;
+  u.hs = a.src_head_stride;
+  u.rs = a.src_row_stride;
+  u.block_ids = a.block_ids;
+  u.nblk = a.nblk;
+  u.S = a.S;
+  u.H = a.H;
+  u.num_pool_blocks = a.num_pool_blocks;
+  u.pool = a.pool[layer];
+  u.status = nullptr;
+  quantize_unit_staged<T>(u, a.src_k[layer], a.src_v[layer], a.ks16[layer], a.ks32[layer], a.vs16[layer],
+                          a.vs32[layer], blockIdx.x);
+}
+
+// Several chunks (each <= 128 tokens), all layers, head_dim 128: grid (KV head,
+// chunk x layer); tables and checks as in kvb_quantize_store_batch_kernel.
+template <typename T>
+__global__ void __launch_bounds__(kSThreads) kvb_quantize_store_batch_staged_kernel(const QStoreBatchArgs a) {
+  const int chunk = blockIdx.y / a.L, layer = blockIdx.y - chunk * a.L;
+  QStoreUnit u;
+  u.S = a.num_tokens[chunk];
+  u.nblk = (u.S + 15) / 16;
+  const int64_t si = (static_cast<int64_t>(chunk) * a.L + layer) * 2;
+  const void* src_k = a.src[si];
+  const void* src_v = a.src[si + 1];
+  u.hs = a.src_strides[2 * chunk];
+  u.rs = a.src_strides[2 * chunk + 1];
+  if (u.S < 1 || u.nblk > a.max_blocks || u.hs < 0 || u.rs < 1 || ((u.hs | u.rs) & 7) ||
+      ((reinterpret_cast<uintptr_t>(src_k) | reinterpret_cast<uintptr_t>(src_v)) & 15)) {
+    if (threadIdx.x == 0 && a.status) atomicOr(a.status, KVB_STATUS_BAD_LENGTH);
+    return;
+  }
+  u.block_ids = a.block_ids + static_cast<int64_t>(chunk) * a.max_blocks;
+  u.H = a.H;
+  u.num_pool_blocks = a.num_pool_blocks;
+  u.pool = static_cast<int8_t*>(a.tables[layer]);
+  u.status = a.status;
+  quantize_unit_staged<T>(u, src_k, src_v, static_cast<__half*>(a.tables[a.L + layer]),
+                          static_cast<float*>(a.tables[3 * a.L + layer]),
+                          static_cast<__half*>(a.tables[2 * a.L + layer]),
+                          static_cast<float*>(a.tables[4 * a.L + layer]), blockIdx.x);
+}
+
 // ---- CacheBlend -----------------------------------------------------------------------
 struct BlendArgs {
   void* ck[KVB_MAX_LAYERS];
@@ -792,8 +1058,31 @@ int fail(int code, const std::string& msg) { return kvb_detail_fail(code, msg); 
 
 bool head_dim_ok(int d) { return d == 64 || d == 96 || d == 128; }
 
+// The staged kernels take 64 KB of dynamic shared memory (opted in once per device
+// and kernel: one instantiation per kernel, so each keeps its own flags).
+template <typename T, bool BATCH>
+cudaError_t staged_smem_opt_in() {
+  static int configured[64] = {};
+  const void* kernel = BATCH ? reinterpret_cast<const void*>(kvb_quantize_store_batch_staged_kernel<T>)
+                             : reinterpret_cast<const void*>(kvb_quantize_store_staged_kernel<T>);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (configured[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmem);
+  if (e == cudaSuccess) configured[dev] = 1;
+  return e;
+}
+
 template <typename T, int D>
 cudaError_t launch_qstore(const QStoreArgs& a, int L, cudaStream_t s) {
+  if (D == 128 && a.nblk <= kSTileRows / 16) {
+    cudaError_t e = staged_smem_opt_in<T, false>();
+    if (e != cudaSuccess) return e;
+    kvb_quantize_store_staged_kernel<T><<<dim3(a.H, L), kSThreads, kSSmem, s>>>(a);
+    return cudaGetLastError();
+  }
   const int n_k = (a.nblk * 16 + kQRowsPerCta - 1) / kQRowsPerCta;
   kvb_quantize_store_kernel<T, D><<<dim3(n_k + D / kQVCols, a.H, L), kQThreads, 0, s>>>(a);
   return cudaGetLastError();
@@ -801,6 +1090,12 @@ cudaError_t launch_qstore(const QStoreArgs& a, int L, cudaStream_t s) {
 
 template <typename T, int D>
 cudaError_t launch_qstore_batch(const QStoreBatchArgs& a, int chunks, cudaStream_t s) {
+  if (D == 128 && a.max_blocks <= kSTileRows / 16) {
+    cudaError_t e = staged_smem_opt_in<T, true>();
+    if (e != cudaSuccess) return e;
+    kvb_quantize_store_batch_staged_kernel<T><<<dim3(a.H, chunks * a.L), kSThreads, kSSmem, s>>>(a);
+    return cudaGetLastError();
+  }
   const int n_k = (a.max_blocks * 16 + kQRowsPerCta - 1) / kQRowsPerCta;
   kvb_quantize_store_batch_kernel<T, D><<<dim3(n_k + D / kQVCols, a.H, chunks * a.L), kQThreads, 0, s>>>(a);
   return cudaGetLastError();

@@ -302,12 +302,14 @@ def test_batched_store_matches_oracle(dt):
             _check_layer(alloc, layer, blocks, ks[layer][0], vs[layer][0], name)
 
 
-def test_batched_store_flags_bad_block_and_skips_it():
+@pytest.mark.parametrize("D", [64, 128])
+def test_batched_store_flags_bad_block_and_skips_it(D):
     """A block id outside the pool is skipped on the device (never written) and
-    reported in the status word; the chunk's other blocks are still stored."""
+    reported in the status word; the chunk's other blocks are still stored
+    (head_dim 128 takes the shared-memory-staged kernel, 64 the other one)."""
     from kvboost_b200 import _lib, ops
     from kvboost_b200.paged import DeviceBlockAllocator
-    L, H, S, D = 2, 2, 48, 64
+    L, H, S = 2, 2, 48
     g = torch.Generator().manual_seed(22)
     alloc = DeviceBlockAllocator(L, H, D, 8)
     ops.read_status(torch.device("cuda"))                     # start from 0
