@@ -150,6 +150,10 @@ __device__ __noinline__ uint2 kivi_q8_exact(const float4 x0, const float4 x1, co
   return pack8(q);
 }
 
+__device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
+  return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
+}
+
 template <typename T>
 __device__ __forceinline__ uint2 kivi_q8(const float (&x)[8], const float (&sc)[8], const float (&rc)[8],
                                          bool zero_scale) {
@@ -164,13 +168,18 @@ __device__ __forceinline__ uint2 kivi_q8(const float (&x)[8], const float (&sc)[
     // looks at the dropped 16 bits as the top half of (u - (kHalf - 8)) << 16.
 #pragma unroll
     for (int e = 0; e < 8; e += 2) {
-      const float y0 = x[e] * rc[e], y1 = x[e + 1] * rc[e + 1];
+      uint64_t y2;
+      asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(y2) : "l"(pack_f2(x[e], x[e + 1])), "l"(pack_f2(rc[e], rc[e + 1])));
+      const float y0 = __uint_as_float(static_cast<uint32_t>(y2));
+      const float y1 = __uint_as_float(static_cast<uint32_t>(y2 >> 32));
       uint32_t p;
       asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(y1), "f"(y0));
       const float t0 = fminf(__uint_as_float(p << 16), 127.0f);
       const float t1 = fminf(__uint_as_float(p & 0xffff0000u), 127.0f);
-      w[e] = __float_as_uint(t0 + 12582912.0f);
-      w[e + 1] = __float_as_uint(t1 + 12582912.0f);
+      uint64_t r2;
+      asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r2) : "l"(pack_f2(t0, t1)), "l"(pack_f2(12582912.0f, 12582912.0f)));
+      w[e] = static_cast<uint32_t>(r2);
+      w[e + 1] = static_cast<uint32_t>(r2 >> 32);
       near |= ((__float_as_uint(y0) - (kHalf - 8u)) << 16) <= (16u << 16 | 0xffffu);
       near |= ((__float_as_uint(y1) - (kHalf - 8u)) << 16) <= (16u << 16 | 0xffffu);
     }
@@ -530,11 +539,10 @@ __global__ void __launch_bounds__(kQThreads) kvb_quantize_store_batch_kernel(con
                            static_cast<float*>(a.tables[4 * a.L + layer]), n_k);
 }
 
-// ---- quantise-on-store, staged: one CTA per (chunk, layer, KV head) --------------------
+// ---- quantise-on-store, staged: one CTA per (chunk, layer, KV head, K or V) -------------
 // For chunks of up to 128 tokens at head_dim 128 (the engine's chunks): the CTA
-// copies the chunk's K and V tiles of one head (128 rows x 256 bytes each) into
-// shared memory with cp.async (zero-filled past the chunk's tokens; K and V in
-// two commit groups, so the K pass starts while V is still arriving), then
+// copies the chunk's K or V tile of one head (128 rows x 256 bytes) into shared
+// memory with cp.async (zero-filled past the chunk's tokens), then
 //  K: 8 lanes per token row, 16 elements each, 4 rows per warp and pass, 4 passes;
 //  V: thread = (8-column group cg, token phase tb): tokens tb, tb + 16, ...; the
 //     column maxima reduce over the 16 phases of a half-warp by shuffles, and
@@ -548,7 +556,7 @@ constexpr int kSTileRows = 128;
 constexpr int kSRowBytes = 256;                         // head_dim 128, 16-bit
 constexpr int kSTileBytes = kSTileRows * kSRowBytes;    // 32 KB per operand
 constexpr int kSThreads = 256;
-constexpr int kSSmem = 2 * kSTileBytes;
+constexpr int kSSmem = kSTileBytes;                     // one operand per CTA
 
 __device__ __forceinline__ uint32_t s_piece(int t, int p) {
   return static_cast<uint32_t>(t * kSRowBytes + ((p ^ (t & 15)) << 4));
@@ -560,13 +568,15 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool l
                : "memory");
 }
 
+// Pairwise max(|m|, |w|) in the pair's 16-bit type; the sign bits of the result
+// are not meaningful (clear them with 0x7fff7fff before use).
 template <typename T>
 __device__ __forceinline__ uint32_t max_abs2(uint32_t m, uint32_t w) {
-  uint32_t a = w & 0x7fff7fffu, r;
+  uint32_t r;
   if (std::is_same<T, __nv_bfloat16>::value)
-    asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(a));
+    asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(w));
   else
-    asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(a));
+    asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(w));
   return r;
 }
 
@@ -589,30 +599,32 @@ __device__ __forceinline__ void unpack8s(const uint4& u, float (&x)[8]) {
 template <typename T>
 __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const void* src_k,
                                                      const void* src_v, __half* ks16, float* ks32,
-                                                     __half* vs16, float* vs32, int h) {
+                                                     __half* vs16, float* vs32, int h, int kv) {
   constexpr int D = 128;
   extern __shared__ __align__(128) uint8_t s_tile[];
   const uint32_t sK = static_cast<uint32_t>(__cvta_generic_to_shared(s_tile));
-  const uint32_t sV = sK + kSTileBytes;
+  const uint32_t sV = sK;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int S = u0.S, slots = u0.nblk * 16;
-  // ---- stage: 2048 pieces per operand, 8 per thread each --------------------------------
-#pragma unroll
-  for (int kv = 0; kv < 2; ++kv) {
+  // ---- stage this CTA's operand: 2048 pieces, 8 per thread ------------------------------
+  {
     const T* src = static_cast<const T*>(kv ? src_v : src_k) + h * u0.hs;
 #pragma unroll
     for (int k = 0; k < kSTileBytes / 16 / kSThreads; ++k) {
       const int i = tid + kSThreads * k;
       const int t = i >> 4, pc = i & 15;
       const bool live = t < S;
-      cp_async16((kv ? sV : sK) + s_piece(t, pc), live ? src + t * u0.rs + 8 * pc : src, live);
+      cp_async16(sK + s_piece(t, pc), live ? src + t * u0.rs + 8 * pc : src, live);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
   }
-  // ---- K: per-token scales ------------------------------------------------------------
-  asm volatile("cp.async.wait_group 1;" ::: "memory");
   __syncthreads();
-  {
+  if (kv == 0) {
+    // ---- K: per-token scales ----------------------------------------------------------
+    // (a) row maxima, 8 lanes per row; (b) one thread per row computes its scale,
+    // reciprocal and stored scales; (c) quantise, 8 lanes per row.
+    __shared__ float s_scale[kSTileRows], s_rcp[kSTileRows];
     const int sub = lane & 7;
 #pragma unroll 1
     for (int pass = 0; pass < 4; ++pass) {
@@ -625,29 +637,52 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
       asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
                    : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
                    : "r"(sK + s_piece(t, sub + 8)));
-      uint32_t m2 = 0;
-      m2 = max_abs2<T>(m2, w0.x); m2 = max_abs2<T>(m2, w0.y);
-      m2 = max_abs2<T>(m2, w0.z); m2 = max_abs2<T>(m2, w0.w);
-      m2 = max_abs2<T>(m2, w1.x); m2 = max_abs2<T>(m2, w1.y);
-      m2 = max_abs2<T>(m2, w1.z); m2 = max_abs2<T>(m2, w1.w);
-      const float2 mf = unpack2<T>(m2);
+      uint32_t m2 = max_abs2<T>(max_abs2<T>(max_abs2<T>(w0.x, w0.y), max_abs2<T>(w0.z, w0.w)),
+                                max_abs2<T>(max_abs2<T>(w1.x, w1.y), max_abs2<T>(w1.z, w1.w)));
+      const float2 mf = unpack2<T>(m2 & 0x7fff7fffu);
       float amax = fmaxf(mf.x, mf.y);
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (sub == 0) s_scale[t] = amax;
+    }
+    __syncthreads();
+    if (tid < slots) {
+      const int t = tid;
+      const float scale = t < S ? kivi_scale<T>(s_scale[t]) : 0.0f;
+      s_scale[t] = scale;
+      s_rcp[t] = __frcp_rn(scale);
+      const int blk = u0.block_ids[t >> 4];
+      if (blk >= 0 && blk < u0.num_pool_blocks) {     // flagged by the row writes below
+        const __half s16 = __float2half_rn(scale);
+        const int64_t si = (static_cast<int64_t>(blk) * u0.H + h) * 16 + (t & 15);
+        if (ks16) ks16[si] = s16;
+        if (ks32) ks32[si] = __half2float(s16);
+      }
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int pass = 0; pass < 4; ++pass) {
+      const int t = pass * 32 + warp * 4 + (lane >> 3);
+      if (t >= slots) break;
       const int blk = u0.block_ids[t >> 4], slot = t & 15;
       if (!block_ok(blk, u0)) continue;
-      const bool live = t < S;
-      const float scale = live ? kivi_scale<T>(amax) : 0.0f;
-      const float rcp = __frcp_rn(scale);
-      float sc[8], rc[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        sc[e] = scale;
-        rc[e] = rcp;
-      }
       int8_t* dst = u0.pool + ((static_cast<int64_t>(blk) * 2 + 0) * u0.H + h) * 16 * D + slot * D;
       uint2 q0 = make_uint2(0, 0), q1 = make_uint2(0, 0);
-      if (live) {
+      if (t < S) {
+        uint4 w0, w1;
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w0.x), "=r"(w0.y), "=r"(w0.z), "=r"(w0.w)
+                     : "r"(sK + s_piece(t, sub)));
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
+                     : "r"(sK + s_piece(t, sub + 8)));
+        const float scale = s_scale[t], rcp = s_rcp[t];
+        float sc[8], rc[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          sc[e] = scale;
+          rc[e] = rcp;
+        }
         float x[8];
         unpack8s<T>(w0, x);
         q0 = kivi_q8<T>(x, sc, rc, !(scale > 0.0f));
@@ -656,18 +691,9 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
       }
       *reinterpret_cast<uint2*>(dst + 8 * sub) = q0;
       *reinterpret_cast<uint2*>(dst + 8 * (sub + 8)) = q1;
-      if (sub == 0) {
-        const __half s16 = __float2half_rn(scale);
-        const int64_t si = (static_cast<int64_t>(blk) * u0.H + h) * 16 + slot;
-        if (ks16) ks16[si] = s16;
-        if (ks32) ks32[si] = __half2float(s16);
-      }
     }
-  }
-  // ---- V: per-channel scales over the chunk ---------------------------------------------
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-  __syncthreads();
-  {
+  } else {
+    // ---- V: per-channel scales over the chunk -------------------------------------------
     const int cg = warp * 2 + (lane >> 4), tb = lane & 15;
     uint32_t m2[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -687,19 +713,10 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
       for (int k = 0; k < 4; ++k) m2[k] = max_abs2<T>(m2[k], __shfl_xor_sync(0xffffffffu, m2[k], o));
     // lane tb < 8 owns column cg * 8 + tb
     const uint32_t mine = (tb & 4) ? ((tb & 2) ? m2[3] : m2[2]) : ((tb & 2) ? m2[1] : m2[0]);
-    const float2 mf = unpack2<T>(mine);
+    const float2 mf = unpack2<T>(mine & 0x7fff7fffu);
     const float my_sc = kivi_scale<T>((tb & 1) ? mf.y : mf.x);
     const float my_rc = __frcp_rn(my_sc);
-    if (tb < 8) {
-      const __half s16 = __float2half_rn(my_sc);
-      for (int b = 0; b < u0.nblk; ++b) {
-        const int blk = u0.block_ids[b];
-        if (blk < 0 || blk >= u0.num_pool_blocks) continue;   // flagged by the row writes below
-        const int64_t si = (static_cast<int64_t>(blk) * u0.H + h) * D + cg * 8 + tb;
-        if (vs16) vs16[si] = s16;
-        if (vs32) vs32[si] = __half2float(s16);
-      }
-    }
+    const __half my_s16 = __float2half_rn(my_sc);
     float sc[8], rc[8];
     bool zero_scale = false;
 #pragma unroll
@@ -713,6 +730,11 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
       const int t = tb + 16 * i;
       const int blk = u0.block_ids[i];
       if (!block_ok(blk, u0)) continue;
+      if (tb < 8) {                                // the block's copy of the column scales
+        const int64_t si = (static_cast<int64_t>(blk) * u0.H + h) * D + cg * 8 + tb;
+        if (vs16) vs16[si] = my_s16;
+        if (vs32) vs32[si] = __half2float(my_s16);
+      }
       uint2 q = make_uint2(0, 0);
       if (t < S) {
         uint4 w;
@@ -729,9 +751,9 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
   }
 }
 
-// One chunk (<= 128 tokens), all layers, head_dim 128: grid (KV head, layer).
+// One chunk (<= 128 tokens), all layers, head_dim 128: grid (KV head, layer, K/V).
 template <typename T>
-__global__ void __launch_bounds__(kSThreads) kvb_quantize_store_staged_kernel(const __grid_constant__ QStoreArgs a) {
+__global__ void __launch_bounds__(kSThreads, 5) kvb_quantize_store_staged_kernel(const __grid_constant__ QStoreArgs a) {
   const int layer = blockIdx.y;
   QStoreUnit u;
   u.hs = a.src_head_stride;
@@ -744,13 +766,13 @@ __global__ void __launch_bounds__(kSThreads) kvb_quantize_store_staged_kernel(co
   u.pool = a.pool[layer];
   u.status = nullptr;
   quantize_unit_staged<T>(u, a.src_k[layer], a.src_v[layer], a.ks16[layer], a.ks32[layer], a.vs16[layer],
-                          a.vs32[layer], blockIdx.x);
+                          a.vs32[layer], blockIdx.x, blockIdx.z);
 }
 
 // Several chunks (each <= 128 tokens), all layers, head_dim 128: grid (KV head,
-// chunk x layer); tables and checks as in kvb_quantize_store_batch_kernel.
+// chunk x layer, K/V); tables and checks as in kvb_quantize_store_batch_kernel.
 template <typename T>
-__global__ void __launch_bounds__(kSThreads) kvb_quantize_store_batch_staged_kernel(const QStoreBatchArgs a) {
+__global__ void __launch_bounds__(kSThreads, 5) kvb_quantize_store_batch_staged_kernel(const QStoreBatchArgs a) {
   const int chunk = blockIdx.y / a.L, layer = blockIdx.y - chunk * a.L;
   QStoreUnit u;
   u.S = a.num_tokens[chunk];
@@ -773,7 +795,7 @@ __global__ void __launch_bounds__(kSThreads) kvb_quantize_store_batch_staged_ker
   quantize_unit_staged<T>(u, src_k, src_v, static_cast<__half*>(a.tables[a.L + layer]),
                           static_cast<float*>(a.tables[3 * a.L + layer]),
                           static_cast<__half*>(a.tables[2 * a.L + layer]),
-                          static_cast<float*>(a.tables[4 * a.L + layer]), blockIdx.x);
+                          static_cast<float*>(a.tables[4 * a.L + layer]), blockIdx.x, blockIdx.z);
 }
 
 // ---- CacheBlend -----------------------------------------------------------------------
@@ -1058,8 +1080,9 @@ int fail(int code, const std::string& msg) { return kvb_detail_fail(code, msg); 
 
 bool head_dim_ok(int d) { return d == 64 || d == 96 || d == 128; }
 
-// The staged kernels take 64 KB of dynamic shared memory (opted in once per device
-// and kernel: one instantiation per kernel, so each keeps its own flags).
+// The staged kernels take 32 KB of dynamic shared memory (opted in once per device
+// and kernel -- one instantiation per kernel, so each keeps its own flags -- in
+// case the default limit is lower).
 template <typename T, bool BATCH>
 cudaError_t staged_smem_opt_in() {
   static int configured[64] = {};
@@ -1080,7 +1103,7 @@ cudaError_t launch_qstore(const QStoreArgs& a, int L, cudaStream_t s) {
   if (D == 128 && a.nblk <= kSTileRows / 16) {
     cudaError_t e = staged_smem_opt_in<T, false>();
     if (e != cudaSuccess) return e;
-    kvb_quantize_store_staged_kernel<T><<<dim3(a.H, L), kSThreads, kSSmem, s>>>(a);
+    kvb_quantize_store_staged_kernel<T><<<dim3(a.H, L, 2), kSThreads, kSSmem, s>>>(a);
     return cudaGetLastError();
   }
   const int n_k = (a.nblk * 16 + kQRowsPerCta - 1) / kQRowsPerCta;
@@ -1093,7 +1116,7 @@ cudaError_t launch_qstore_batch(const QStoreBatchArgs& a, int chunks, cudaStream
   if (D == 128 && a.max_blocks <= kSTileRows / 16) {
     cudaError_t e = staged_smem_opt_in<T, true>();
     if (e != cudaSuccess) return e;
-    kvb_quantize_store_batch_staged_kernel<T><<<dim3(a.H, chunks * a.L), kSThreads, kSSmem, s>>>(a);
+    kvb_quantize_store_batch_staged_kernel<T><<<dim3(a.H, chunks * a.L, 2), kSThreads, kSSmem, s>>>(a);
     return cudaGetLastError();
   }
   const int n_k = (a.max_blocks * 16 + kQRowsPerCta - 1) / kQRowsPerCta;
