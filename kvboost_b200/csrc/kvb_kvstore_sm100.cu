@@ -154,12 +154,12 @@ __device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
   return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
 }
 
+// The fast path of kivi_q8: the 8 packed results, and `near` ORed with whether
+// any element needs the exact path.
 template <typename T>
-__device__ __forceinline__ uint2 kivi_q8(const float (&x)[8], const float (&sc)[8], const float (&rc)[8],
-                                         bool zero_scale) {
+__device__ __forceinline__ uint2 kivi_q8_fast(const float (&x)[8], const float (&rc)[8], bool& near) {
   constexpr uint32_t kDrop = RoundBits<T>::kDrop, kHalf = 1u << (kDrop - 1), kMask = (1u << kDrop) - 1;
   uint32_t w[8];
-  bool near = zero_scale;
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
     // bfloat16: the rounding of y to T by the conversion unit (round to nearest
     // even, as the integer rule above), two at a time; only the upper clamp,
@@ -193,13 +193,21 @@ __device__ __forceinline__ uint2 kivi_q8(const float (&x)[8], const float (&sc)[
       near |= ((u - (kHalf - 8u)) & kMask) <= 16u;     // low bits within 8 of the halfway point
     }
   }
+  uint2 p;
+  p.x = __byte_perm(__byte_perm(w[0], w[1], 0x0040), __byte_perm(w[2], w[3], 0x0040), 0x5410);
+  p.y = __byte_perm(__byte_perm(w[4], w[5], 0x0040), __byte_perm(w[6], w[7], 0x0040), 0x5410);
+  return p;
+}
+
+template <typename T>
+__device__ __forceinline__ uint2 kivi_q8(const float (&x)[8], const float (&sc)[8], const float (&rc)[8],
+                                         bool zero_scale) {
+  bool near = zero_scale;
+  const uint2 p = kivi_q8_fast<T>(x, rc, near);
   if (near)
     return kivi_q8_exact<T>(make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]),
                             make_float4(sc[0], sc[1], sc[2], sc[3]), make_float4(sc[4], sc[5], sc[6], sc[7]),
                             make_float4(rc[0], rc[1], rc[2], rc[3]), make_float4(rc[4], rc[5], rc[6], rc[7]));
-  uint2 p;
-  p.x = __byte_perm(__byte_perm(w[0], w[1], 0x0040), __byte_perm(w[2], w[3], 0x0040), 0x5410);
-  p.y = __byte_perm(__byte_perm(w[4], w[5], 0x0040), __byte_perm(w[6], w[7], 0x0040), 0x5410);
   return p;
 }
 
@@ -596,6 +604,37 @@ __device__ __forceinline__ void unpack8s(const uint4& u, float (&x)[8]) {
   }
 }
 
+// Exact paths of the staged kernels, out of line: the 8 elements at shared address
+// `piece`, with one scale (K row) or the 8 columns' scales and reciprocals at
+// shared addresses `sc`, `rc` (V).
+template <typename T>
+__device__ __noinline__ uint2 kivi_q8_exact_row(uint32_t piece, float scale, float rcp) {
+  uint4 w;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+               : "r"(piece));
+  float x[8];
+  unpack8s<T>(w, x);
+  int q[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) q[e] = kivi_q<T>(x[e], scale, rcp);
+  return pack8(q);
+}
+
+template <typename T>
+__device__ __noinline__ uint2 kivi_q8_exact_cols(uint32_t piece, const float* sc, const float* rc) {
+  uint4 w;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+               : "r"(piece));
+  float x[8];
+  unpack8s<T>(w, x);
+  int q[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) q[e] = kivi_q<T>(x[e], sc[e], rc[e]);
+  return pack8(q);
+}
+
 template <typename T>
 __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const void* src_k,
                                                      const void* src_v, __half* ks16, float* ks32,
@@ -677,17 +716,17 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
                      : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
                      : "r"(sK + s_piece(t, sub + 8)));
         const float scale = s_scale[t], rcp = s_rcp[t];
-        float sc[8], rc[8];
+        float rc[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          sc[e] = scale;
-          rc[e] = rcp;
-        }
+        for (int e = 0; e < 8; ++e) rc[e] = rcp;
         float x[8];
+        bool n0 = !(scale > 0.0f), n1 = n0;
         unpack8s<T>(w0, x);
-        q0 = kivi_q8<T>(x, sc, rc, !(scale > 0.0f));
+        q0 = kivi_q8_fast<T>(x, rc, n0);
         unpack8s<T>(w1, x);
-        q1 = kivi_q8<T>(x, sc, rc, !(scale > 0.0f));
+        q1 = kivi_q8_fast<T>(x, rc, n1);
+        if (n0) q0 = kivi_q8_exact_row<T>(sK + s_piece(t, sub), scale, rcp);
+        if (n1) q1 = kivi_q8_exact_row<T>(sK + s_piece(t, sub + 8), scale, rcp);
       }
       *reinterpret_cast<uint2*>(dst + 8 * sub) = q0;
       *reinterpret_cast<uint2*>(dst + 8 * (sub + 8)) = q1;
@@ -717,13 +756,18 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
     const float my_sc = kivi_scale<T>((tb & 1) ? mf.y : mf.x);
     const float my_rc = __frcp_rn(my_sc);
     const __half my_s16 = __float2half_rn(my_sc);
-    float sc[8], rc[8];
+    __shared__ float s_vsc[kSTileRows], s_vrc[kSTileRows];   // per column, for the exact path
+    if (tb < 8) {
+      s_vsc[cg * 8 + tb] = my_sc;
+      s_vrc[cg * 8 + tb] = my_rc;
+    }
+    __syncwarp();
+    float rc[8];
     bool zero_scale = false;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      sc[e] = __shfl_sync(0xffffffffu, my_sc, (lane & 16) + e);
       rc[e] = __shfl_sync(0xffffffffu, my_rc, (lane & 16) + e);
-      zero_scale |= !(sc[e] > 0.0f);
+      zero_scale |= !(__shfl_sync(0xffffffffu, my_sc, (lane & 16) + e) > 0.0f);
     }
 #pragma unroll 1
     for (int i = 0; i < u0.nblk; ++i) {          // token tb + 16 i sits in block i, slot tb
@@ -743,7 +787,9 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
                      : "r"(sV + s_piece(t, cg)));
         float x[8];
         unpack8s<T>(w, x);
-        q = kivi_q8<T>(x, sc, rc, zero_scale);
+        bool nr = zero_scale;
+        q = kivi_q8_fast<T>(x, rc, nr);
+        if (nr) q = kivi_q8_exact_cols<T>(sV + s_piece(t, cg), s_vsc + cg * 8, s_vrc + cg * 8);
       }
       *reinterpret_cast<uint2*>(u0.pool + ((static_cast<int64_t>(blk) * 2 + 1) * u0.H + h) * 16 * D +
                                 tb * D + cg * 8) = q;
