@@ -150,6 +150,13 @@ __device__ __noinline__ uint2 kivi_q8_exact(const float4 x0, const float4 x1, co
   return pack8(q);
 }
 
+// a * b + c (mod 2^32) as one integer multiply-add.
+__device__ __forceinline__ uint32_t imad_u32(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
   return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
 }
@@ -174,14 +181,16 @@ __device__ __forceinline__ uint2 kivi_q8_fast(const float (&x)[8], const float (
       const float y1 = __uint_as_float(static_cast<uint32_t>(y2 >> 32));
       uint32_t p;
       asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(y1), "f"(y0));
-      const float t0 = fminf(__uint_as_float(p << 16), 127.0f);
-      const float t1 = fminf(__uint_as_float(p & 0xffff0000u), 127.0f);
+      asm("min.bf16x2 %0, %0, %1;" : "+r"(p) : "r"(0x42FE42FEu));   // clamp both to 127
+      const float t0 = __uint_as_float(imad_u32(p, 65536u, 0u));
+      const float t1 = __uint_as_float(p & 0xffff0000u);
       uint64_t r2;
       asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r2) : "l"(pack_f2(t0, t1)), "l"(pack_f2(12582912.0f, 12582912.0f)));
       w[e] = static_cast<uint32_t>(r2);
       w[e + 1] = static_cast<uint32_t>(r2 >> 32);
-      near |= ((__float_as_uint(y0) - (kHalf - 8u)) << 16) <= (16u << 16 | 0xffffu);
-      near |= ((__float_as_uint(y1) - (kHalf - 8u)) << 16) <= (16u << 16 | 0xffffu);
+      constexpr uint32_t kOff = (0u - (kHalf - 8u)) << 16;          // (u - (kHalf - 8)) << 16
+      near |= imad_u32(__float_as_uint(y0), 65536u, kOff) <= (16u << 16 | 0xffffu);
+      near |= imad_u32(__float_as_uint(y1), 65536u, kOff) <= (16u << 16 | 0xffffu);
     }
   } else {
 #pragma unroll
@@ -598,9 +607,14 @@ __device__ __forceinline__ void unpack8s(const uint4& u, float (&x)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float2 f = unpack2<T>(w[i]);
-    x[2 * i] = f.x;
-    x[2 * i + 1] = f.y;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {   // low half by a multiply
+      x[2 * i] = __uint_as_float(imad_u32(w[i], 65536u, 0u));
+      x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    } else {
+      const float2 f = unpack2<T>(w[i]);
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    }
   }
 }
 
