@@ -73,9 +73,9 @@ PREWARM_S = 0.5
 # ncu captures (profiles/*.md), per workload.  varlen_d96: the 16-request capture
 # (1 029.9 MB) scaled to the full launch by algorithmic bytes (3 535.4 / 1 004.1 MB).
 NCU_TRAFFIC_BYTES = {"reuse_prefill": 27328000, "varlen_d96": 3626150000,
-                     # the batched 24-chunk launch: 113.3 MB read + 40.4 MB written
+                     # the batched 24-chunk launch (staged kernels): 113.4 MB read + 30.7 MB written
                      # (the rest of the pool writes still in L2 at the end)
-                     "quantize_store": 113305088 + 40395520,
+                     "quantize_store": 113353728 + 30690304,
                      # per step: deviation 113 267 968 + 3 780 096, select 47 616,
                      # patch 16 965 632 + 14 080 (read + write)
                      "cacheblend": 134075392,
