@@ -670,8 +670,11 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
       cp_async16(sK + s_piece(t, pc), live ? src + t * u0.rs + 8 * pc : src, live);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
   }
+  // the chunk's block ids, read once while the tile is in flight
+  __shared__ int s_blk[kSTileRows / 16];
+  if (tid < u0.nblk) s_blk[tid] = u0.block_ids[tid];
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   if (kv == 0) {
     // ---- K: per-token scales ----------------------------------------------------------
@@ -704,7 +707,7 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
       const float scale = t < S ? kivi_scale<T>(s_scale[t]) : 0.0f;
       s_scale[t] = scale;
       s_rcp[t] = __frcp_rn(scale);
-      const int blk = u0.block_ids[t >> 4];
+      const int blk = s_blk[t >> 4];
       if (blk >= 0 && blk < u0.num_pool_blocks) {     // flagged by the row writes below
         const __half s16 = __float2half_rn(scale);
         const int64_t si = (static_cast<int64_t>(blk) * u0.H + h) * 16 + (t & 15);
@@ -717,7 +720,7 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
     for (int pass = 0; pass < 4; ++pass) {
       const int t = pass * 32 + warp * 4 + (lane >> 3);
       if (t >= slots) break;
-      const int blk = u0.block_ids[t >> 4], slot = t & 15;
+      const int blk = s_blk[t >> 4], slot = t & 15;
       if (!block_ok(blk, u0)) continue;
       int8_t* dst = u0.pool + ((static_cast<int64_t>(blk) * 2 + 0) * u0.H + h) * 16 * D + slot * D;
       uint2 q0 = make_uint2(0, 0), q1 = make_uint2(0, 0);
@@ -786,7 +789,7 @@ __device__ __forceinline__ void quantize_unit_staged(const QStoreUnit& u0, const
 #pragma unroll 1
     for (int i = 0; i < u0.nblk; ++i) {          // token tb + 16 i sits in block i, slot tb
       const int t = tb + 16 * i;
-      const int blk = u0.block_ids[i];
+      const int blk = s_blk[i];
       if (!block_ok(blk, u0)) continue;
       if (tb < 8) {                                // the block's copy of the column scales
         const int64_t si = (static_cast<int64_t>(blk) * u0.H + h) * D + cg * 8 + tb;
