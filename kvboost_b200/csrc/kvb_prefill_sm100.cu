@@ -1361,15 +1361,18 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
     }
     const bool row_valid = t < q_rows[sl];
     const float inv_l = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
-    T* obase = reinterpret_cast<T*>(a.o) + hf * DH + (SPLITKV ? vsplit[sl] * pa.o_split_stride : 0) +
+    // dual split-key CTAs merge their two key splits and write one partial (index csplit)
+    const bool merge2 = (DUALOK && dual_dense) || dual_split;
+    const int part = dual_split ? csplit : vsplit[sl];
+    T* obase = reinterpret_cast<T*>(a.o) + hf * DH + (SPLITKV ? part * pa.o_split_stride : 0) +
                (a.cu_q ? (int64_t)q_base * a.o_rs + (int64_t)h * a.o_hs
                        : (int64_t)b * a.o_bs + (int64_t)h * a.o_hs);
     constexpr int NC = DH / 8;                   // 16-byte pieces per row segment
     constexpr int ROT = 8 / (NC % 8 == 0 ? 8 : NC % 4 == 0 ? 4 : 2);
     constexpr int RPS = 32 / NC;                 // rows per store instruction
     const int wrow = (warp & 3) * 32;            // first row of this warp within the tile
-    if (DUALOK && dual_dense) {
-      // Two key halves of one query tile: slot 1 hands each row's maximum and sum
+    if (merge2) {
+      // Two key ranges of one query tile: slot 1 hands each row's maximum and sum
       // to slot 0 (through the exact path's exchange slots, idle now), and slot 0
       // writes O = (O0 2^(m0-m) + O1 2^(m1-m)) / (l0 2^(m0-m) + l1 2^(m1-m)).
       if (sl == 1 && hf == 0) {
@@ -1378,8 +1381,8 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
       }
       ptx::bar_sync(9, 4 * kSlots * H * 32);     // every softmax warp, once
       if (sl == 0) {
-        bool have_o1 = wait_bar(bar(BAR_O_FULL + 1), 0, abort_flag, a.status,
-                                KVB_STATUS_EPILOGUE_WAIT);
+        bool have_o1 = n_t[1] > 0 && wait_bar(bar(BAR_O_FULL + 1), 0, abort_flag, a.status,
+                                              KVB_STATUS_EPILOGUE_WAIT);
         have_o1 = __all_sync(0xffffffffu, have_o1);
         ptx::tc_fence_after();
         const float m1 = xmax[256 + t], l1 = xmax[384 + t];
@@ -1424,7 +1427,8 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
           if (a.cu_q)
             a.lse[(int64_t)h * a.lse_hs + q_base + qi] = lse;
           else
-            a.lse[(int64_t)b * a.lse_bs + (int64_t)h * a.lse_hs + qi] = lse;
+            a.lse[(SPLITKV ? part * pa.lse_split_stride : 0) + (int64_t)b * a.lse_bs +
+                  (int64_t)h * a.lse_hs + qi] = lse;
         }
       }
     } else if (have_o && dual) {
@@ -1485,13 +1489,13 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
 #pragma unroll
       for (int i = 0; i < DH / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
     }
-    if (!(DUALOK && dual_dense) && hf == 0 && row_valid && a.lse != nullptr) {
+    if (!merge2 && hf == 0 && row_valid && a.lse != nullptr) {
       const float lse = (l_tot > 0.f && have_o) ? (m_run + ptx::lg2(l_tot)) * 0.69314718055994531f
                                                 : -INFINITY;
       if (a.cu_q)
         a.lse[(int64_t)h * a.lse_hs + q_base + qi] = lse;
       else
-        a.lse[(SPLITKV ? vsplit[sl] * pa.lse_split_stride : 0) + (int64_t)b * a.lse_bs +
+        a.lse[(SPLITKV ? part * pa.lse_split_stride : 0) + (int64_t)b * a.lse_bs +
               (int64_t)h * a.lse_hs + qi] = lse;
     }
   }
@@ -1769,8 +1773,9 @@ static int launch_decode(const KvbPrefillParams& p, int splits_req, void* ws, cu
   if (e == cudaSuccess) {
     const int64_t rows = (int64_t)p.batch * p.num_kv_heads * packed_rows;
     const int64_t items = rows * (D / 8);
+    // dual CTAs have already merged their two key splits: one partial per CTA
     e = launch_pdl(kvb_split_merge_kernel<T, D>, dim3((unsigned)((items + 255) / 256)), 256, 0,
-                   stream, a, sp, parts, rows);
+                   stream, a, sp, dual ? ctas : parts, rows);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(KVB_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
