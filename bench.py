@@ -81,8 +81,9 @@ NCU_TRAFFIC_BYTES = {"reuse_prefill": 27328000, "varlen_d96": 3626150000,
                      "cacheblend": 134075392,
                      # split-key kernel, 33 647 616 read (the merged partials stay in L2)
                      "decode": 33647616,
-                     # split-key kernel: 270 195 200 read + 11 918 592 partials written
-                     "short_suffix": 282113792}
+                     # split-key kernel (dual CTAs merging in-kernel): 269 853 952 read
+                     # + 11 240 192 written
+                     "short_suffix": 281094144}
 
 
 def parse():
