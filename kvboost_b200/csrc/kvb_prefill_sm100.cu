@@ -976,7 +976,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
   } else if (!PAGED && warp == kWarpTma) {
     // ================================================================ TMA
     if (lane == 0 && n_max > 0) {
-      // Q of slot 0, then K0, then Q of slot 1: the first S waits for two tiles, not three
+      // Q of slot 0, then K0, then (once K0 has landed) Q of slot 1
       auto load_q = [&](int sl) {
         if (n_t[sl] == 0) return;
         ptx::mbar_arrive_expect_tx(bar(BAR_Q_FULL + sl), G::TILE_BYTES);
@@ -1015,17 +1015,15 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
             ptx::tma_load_4d(ptx::smem_u32(kdst + at * G::ATOM_BYTES), &tm_k,
                              at * 64, ky, kvh, tb, bar(BAR_K_FULL + st));
           last_k[st] = (int)ph;
-          if (j == 0 && t == 0) {
-            if (!dual)
-              for (int sl = 1; sl < kSlots; ++sl) load_q(sl);
-            // V0 and the next K tiles are needed only after the first softmax:
-            // hold them back until K0 has landed, so that the first S MMAs'
-            // operands do not share DRAM bandwidth with them at launch.
-            if (!dual &&
-                !wait_bar(bar(BAR_K_FULL), 0, abort_flag, a.status, KVB_STATUS_LOAD_WAIT)) {
+          if (j == 0 && t == 0 && !dual) {
+            // Q of slot 1, V0 and the next K tiles are needed only after slot 0's
+            // first S: hold them back until K0 has landed, so that the first S
+            // MMA's operands do not share DRAM bandwidth with them at launch.
+            if (!wait_bar(bar(BAR_K_FULL), 0, abort_flag, a.status, KVB_STATUS_LOAD_WAIT)) {
               go = false;
               break;
             }
+            for (int sl = 1; sl < kSlots; ++sl) load_q(sl);
           }
         }
 #pragma unroll 1
