@@ -560,14 +560,17 @@ __global__ void __launch_bounds__(kQThreads) kvb_quantize_store_batch_kernel(con
 // For chunks of up to 128 tokens at head_dim 128 (the engine's chunks): the CTA
 // copies the chunk's K or V tile of one head (128 rows x 256 bytes) into shared
 // memory with cp.async (zero-filled past the chunk's tokens), then
-//  K: 8 lanes per token row, 16 elements each, 4 rows per warp and pass, 4 passes;
+//  K: row maxima with 8 lanes per token row (16 elements each, 4 rows per warp
+//     and pass, 4 passes), one thread per row for its scale and reciprocal, then
+//     the same 8-lanes-per-row walk quantises;
 //  V: thread = (8-column group cg, token phase tb): tokens tb, tb + 16, ...; the
 //     column maxima reduce over the 16 phases of a half-warp by shuffles, and
 //     lanes tb < 8 compute column cg * 8 + tb's scale once.
 // Row t's 16-byte piece p sits at t * 256 + ((p ^ (t & 15)) << 4): the copies,
 // the K reads (one row per 8 lanes) and the V reads (16 rows, one per lane, per
 // column group) all spread over the 32 banks.  Maxima are taken on packed pairs
-// with the sign bits cleared.  Output bytes and scales are those of
+// (max.xorsign.abs; sign bits cleared at the end).  48 registers and 33 KB of
+// shared memory: 5 CTAs per SM.  Output bytes and scales are those of
 // quantize_store_k / quantize_store_v.
 constexpr int kSTileRows = 128;
 constexpr int kSRowBytes = 256;                         // head_dim 128, 16-bit
