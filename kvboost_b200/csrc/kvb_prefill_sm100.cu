@@ -1429,27 +1429,6 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads)
                   (int64_t)h * a.lse_hs + qi] = lse;
         }
       }
-    } else if (have_o && dual) {
-      // dual split-key mode: the Q tile and slot 1's Q buffer may still be read
-      // by the other slot's MMAs, so each thread stores its own row segment
-      T* orow = obase + (int64_t)qi * a.o_rs;
-#pragma unroll 1
-      for (int c = 0; c < DH; c += OCW) {
-        uint32_t r[OCW];
-        tmem_ld_cw<OCW>(tO + c, r);
-        ptx::tmem_wait_ld();
-        if (row_valid) {
-          uint32_t pk[OCW / 2];
-#pragma unroll
-          for (int i = 0; i < OCW / 2; ++i)
-            pk[i] = pack2<T>(__uint_as_float(r[2 * i]) * inv_l,
-                             __uint_as_float(r[2 * i + 1]) * inv_l);
-          uint4* dst = reinterpret_cast<uint4*>(orow + c);
-#pragma unroll
-          for (int i = 0; i < OCW / 8; ++i)
-            dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-        }
-      }
     } else if (have_o) {
       // The warp's 32 output row segments go through shared memory, so that the
       // global stores write whole segments (NC lanes per row) instead of one
